@@ -1,0 +1,239 @@
+"""
+Per-block recompute of a region (``CompileConfig.checkpoint``).
+
+Semantics follow src/create_graph/checkpoint.py:1-334. The region runs
+eagerly, and each submodule whose path matches the pattern (``re.fullmatch``
+over ``named_modules()``) becomes one ``BlockFn`` node of the autograd graph:
+
+- forward: the block runs without grad; only its inputs are kept;
+- force pass (``forces_pass()`` is active): the node's backward returns the
+  input cotangents from a ``VjpFn`` node, which runs the block's forward and
+  VJP without keeping anything;
+- parameter backward: ``VjpFn`` recomputes forward + VJP with grad and
+  differentiates it (backward2); ``BlockFn`` recomputes the forward and returns
+  its first-order gradients.
+
+So a block's forward runs four times and its VJP twice, and at most one
+block's activations are alive at a time. The block's fused ops are the same
+sm_100a kernels as elsewhere; the recompute runs under the region's config,
+so its memory budget applies inside the blocks too.
+"""
+
+from __future__ import annotations
+
+import contextlib
+import re
+from collections.abc import Iterable
+
+import torch
+from torch import Tensor, nn
+
+from create_graph_b200.compile_config import compile_context
+from create_graph_b200.errors import ContractError
+from create_graph_b200.pytree import flatten, is_float, unflatten
+
+_grad = torch.autograd.grad
+
+FORCES_PASS: list[bool] = [False]
+
+
+@contextlib.contextmanager
+def forces_pass():
+    """Marks the region's force pass (the VJP create_graph computes)."""
+    FORCES_PASS.append(True)
+    try:
+        yield
+    finally:
+        FORCES_PASS.pop()
+
+
+def in_forces_pass() -> bool:
+    return FORCES_PASS[-1]
+
+
+class _BlockCall:
+    """One call of a checkpointed block: its arguments, differentiable slots
+    and outputs."""
+
+    def __init__(self, block: nn.Module, config, args, kwargs):
+        self.block = block
+        self.config = config
+        self.leaves, self.spec = flatten((args, kwargs))
+        self.slots = tuple(i for i, x in enumerate(self.leaves) if is_float(x) and x.requires_grad)
+        self.params = [p for p in block.parameters() if p.requires_grad]
+        self.out_leaves: list = []
+        self.out_spec = None
+        self.out_slots: tuple[int, ...] = ()
+
+    @property
+    def inputs(self) -> list[Tensor]:
+        return [self.leaves[i] for i in self.slots]
+
+    def run(self, tensors):
+        """The block's own forward on ``tensors`` in its differentiable slots."""
+        leaves = list(self.leaves)
+        for i, t in zip(self.slots, tensors):
+            leaves[i] = t
+        args, kwargs = unflatten(self.spec, leaves)
+        with compile_context(self.config):
+            return type(self.block).forward(self.block, *args, **kwargs)
+
+    def vjp(self, tensors, g_outs, create: bool):
+        """Cotangents of the block inputs for output cotangents ``g_outs``."""
+        with torch.enable_grad():
+            outs = self.selected(self.run(tensors))
+            pairs = [(o, g) for o, g in zip(outs, g_outs) if o.requires_grad]
+            if not pairs:
+                return [None] * len(tensors)
+            return _grad(
+                [o for o, _ in pairs],
+                list(tensors),
+                [g for _, g in pairs],
+                create_graph=create,
+                allow_unused=True,
+            )
+
+    def keep_output(self, out) -> tuple[Tensor, ...]:
+        """The block's float outputs become the node's outputs, except tensors it
+        passes through unchanged from non-differentiable arguments."""
+        self.out_leaves, self.out_spec = flatten(out)
+        constant = {
+            id(x)
+            for i, x in enumerate(self.leaves)
+            if isinstance(x, Tensor) and i not in set(self.slots)
+        }
+        self.out_slots = tuple(
+            i for i, x in enumerate(self.out_leaves) if is_float(x) and id(x) not in constant
+        )
+        return tuple(self.out_leaves[i] for i in self.out_slots)
+
+    def selected(self, out) -> list[Tensor]:
+        leaves = flatten(out)[0]
+        return [leaves[i] for i in self.out_slots]
+
+    def rebuild(self, tensors):
+        leaves = list(self.out_leaves)
+        for i, t in zip(self.out_slots, tensors):
+            leaves[i] = t
+        self.out_leaves = []  # the node keeps the call alive: drop the forward's outputs
+        return unflatten(self.out_spec, leaves)
+
+
+def _leaf(t: Tensor, requires_grad: bool | None = None) -> Tensor:
+    flag = t.requires_grad if requires_grad is None else requires_grad
+    return t.detach().requires_grad_(flag)
+
+
+class VjpFn(torch.autograd.Function):
+    """The block's VJP as a node: input cotangents from (inputs, output
+    cotangents, parameters); its backward is the block's backward2."""
+
+    @staticmethod
+    def forward(ctx, call: _BlockCall, n_out: int, *tensors):
+        n = len(call.slots)
+        inputs, g_outs = tensors[:n], tensors[n : n + n_out]
+        ctx.call = call
+        ctx.save_for_backward(*inputs, *g_outs)
+        grads = call.vjp([_leaf(t, True) for t in inputs], [g.detach() for g in g_outs], False)
+        return tuple(torch.zeros_like(t) if g is None else g for g, t in zip(grads, inputs))
+
+    @staticmethod
+    def backward(ctx, *ggs):
+        call: _BlockCall = ctx.call
+        saved = ctx.saved_tensors
+        n = len(call.slots)
+        inputs, g_outs = saved[:n], saved[n:]
+        with torch.enable_grad():
+            li = [_leaf(t, True) for t in inputs]
+            lg = [_leaf(g, True) for g in g_outs]
+            outs = call.vjp(li, lg, True)
+            pairs = [
+                (o, gg)
+                for o, gg in zip(outs, ggs)
+                if o is not None and gg is not None and o.requires_grad
+            ]
+            wanted = [*li, *lg, *call.params]
+            if pairs:
+                grads = _grad([o for o, _ in pairs], wanted, [gg for _, gg in pairs], allow_unused=True)
+            else:
+                grads = [None] * len(wanted)
+        return (None, None, *grads)
+
+
+class BlockFn(torch.autograd.Function):
+    """A checkpointed block: keeps its inputs only."""
+
+    @staticmethod
+    def forward(ctx, call: _BlockCall, *tensors):
+        inputs = tensors[: len(call.slots)]
+        ctx.call = call
+        ctx.save_for_backward(*inputs)
+        with torch.no_grad():
+            out = call.run([t.detach() for t in inputs])
+        return call.keep_output(out)
+
+    @staticmethod
+    def backward(ctx, *g_outs):
+        call: _BlockCall = ctx.call
+        inputs = ctx.saved_tensors
+        n_params = len(call.params)
+        if in_forces_pass():
+            grads_in = VjpFn.apply(call, len(g_outs), *inputs, *g_outs, *call.params)
+            return (None, *grads_in, *([None] * n_params))
+        with torch.enable_grad():
+            leaves = [_leaf(t) for t in inputs]
+            outs = call.selected(call.run(leaves))
+            pairs = [(o, g) for o, g in zip(outs, g_outs) if g is not None and o.requires_grad]
+            every = [*leaves, *call.params]
+            wanted = [t for t in every if t.requires_grad]
+            if pairs and wanted:
+                found = iter(_grad([o for o, _ in pairs], wanted, [g for _, g in pairs], allow_unused=True))
+            else:
+                found = iter([None] * len(wanted))
+            grads = [next(found) if t.requires_grad else None for t in every]
+        return (None, *grads)
+
+
+def _wrapped_forward(block: nn.Module, config):
+    def forward(*args, **kwargs):
+        call = _BlockCall(block, config, args, kwargs)
+        outs = BlockFn.apply(call, *call.inputs, *call.params)
+        return call.rebuild(outs)
+
+    return forward
+
+
+def matching_blocks(roots: Iterable[nn.Module], pattern: str) -> list[nn.Module]:
+    """Submodules whose path ``re.fullmatch``es ``pattern``; a match nested in an
+    earlier match belongs to that block (src/create_graph/checkpoint.py:302-314)."""
+    found: list[nn.Module] = []
+    seen: set[int] = set()
+    for root in roots:
+        for name, module in root.named_modules():
+            if id(module) in seen or not re.fullmatch(pattern, name):
+                continue
+            if any(module in set(outer.modules()) for outer in found):
+                continue
+            seen.add(id(module))
+            found.append(module)
+    return found
+
+
+@contextlib.contextmanager
+def checkpointed_blocks(roots: list[nn.Module], config):
+    pattern = config.checkpoint
+    blocks = matching_blocks(roots, pattern)
+    if not blocks:
+        names = ", ".join(type(r).__name__ for r in roots) or "no nn.Module"
+        raise ContractError(
+            f"create_graph: CompileConfig(checkpoint={pattern!r}) matched no submodule of the "
+            f"region's modules ({names}). The pattern is matched with re.fullmatch against "
+            "names from named_modules() of the region's self and module arguments."
+        )
+    for block in blocks:
+        block.forward = _wrapped_forward(block, config)
+    try:
+        yield blocks
+    finally:
+        for block in blocks:
+            del block.forward

@@ -1,0 +1,58 @@
+// Shared helpers of the sm_100a library: error reporting through the C ABI,
+// launch checks and small device utilities.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+namespace cg {
+
+// Last error message of the calling host thread (read through cg_last_error()).
+void set_error(const char* fmt, ...);
+
+// Codes returned by every entry point.
+enum Status : int {
+  kOk = 0,
+  kBadArgument = 1,
+  kCudaError = 2,
+  kUnsupported = 3,
+};
+
+#define CG_REQUIRE(cond, ...)                 \
+  do {                                        \
+    if (!(cond)) {                            \
+      ::cg::set_error(__VA_ARGS__);           \
+      return ::cg::kBadArgument;              \
+    }                                         \
+  } while (0)
+
+#define CG_CUDA(call)                                                            \
+  do {                                                                           \
+    cudaError_t err_ = (call);                                                   \
+    if (err_ != cudaSuccess) {                                                   \
+      ::cg::set_error("%s failed: %s (%s:%d)", #call, cudaGetErrorString(err_),  \
+                      __FILE__, __LINE__);                                       \
+      return ::cg::kCudaError;                                                   \
+    }                                                                            \
+  } while (0)
+
+#define CG_LAUNCHED(name)                                                                 \
+  do {                                                                                    \
+    cudaError_t err_ = cudaGetLastError();                                                \
+    if (err_ != cudaSuccess) {                                                            \
+      ::cg::set_error("launch of %s failed: %s", name, cudaGetErrorString(err_));         \
+      return ::cg::kCudaError;                                                            \
+    }                                                                                     \
+  } while (0)
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+template <typename T>
+__host__ __device__ inline T ceil_div(T a, T b) { return (a + b - 1) / b; }
+
+}  // namespace cg

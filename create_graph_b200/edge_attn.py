@@ -1,0 +1,229 @@
+"""
+Masked edge attention ``out = softmax(q k^T * scale + bias) v`` as a fused op.
+
+The reference registers this op with ``cg.custom_op`` and PyTorch bodies
+(kernels/edge_attn/ops.py:57-108) and says a faster version "replaces the
+bodies, the registration stays" (:14-15). That is what this module does: the
+same class shape (outputs ``out, lse``; saved ``q, k, v, bias, lse``; ``lse``
+a statistic), registered through ``cg.custom_op`` as ``cg_b200::edge_attn``,
+with forward1 / backward1 / backward2 bodies that call the sm_100a kernels
+``cg_edge_attn_fwd1/bwd1/bwd2`` through the C ABI.
+
+q, k, v are (..., S, D) with S <= 32 tokens and D <= 64; the bias broadcasts to
+the scores (..., S, S). Rows whose keys are all -inf get zero probabilities.
+``key_counts`` (model path, ``edge_attention_masked``) masks keys
+j >= key_counts[n] without a -inf bias.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+from torch import Tensor
+
+from create_graph_b200 import native
+from create_graph_b200.errors import NativeError
+from create_graph_b200.ops import custom_op
+
+
+def _grid(q: Tensor) -> tuple[tuple[int, ...], int, int]:
+    """Leading dims of q and their split into the kernel's (n, h) slice grid."""
+    lead = tuple(q.shape[:-2])
+    if not lead:
+        return lead, 1, 1
+    h = lead[-1]
+    n = math.prod(lead[:-1])
+    return lead, n, h
+
+
+def _as_nhsd(t: Tensor, n: int, h: int) -> Tensor:
+    """(n, h, S, D) view of t with unit column stride (a copy only if needed)."""
+    v = t.reshape(n, h, t.shape[-2], t.shape[-1])
+    if v.stride(-1) != 1:
+        v = v.contiguous()
+    return v
+
+
+def _mat(t: Tensor | None) -> native.Mat:
+    if t is None:
+        return native.Mat(None, 0, 0, 0)
+    return native.Mat(t.data_ptr(), t.stride(0), t.stride(1), t.stride(2))
+
+
+def _bias_view(bias: Tensor, lead, n: int, h: int, s: int) -> tuple[Tensor, bool]:
+    """(n, h, s, s) view of the broadcast bias (stride 0 where it broadcasts), or
+    a materialised copy when the leading dims cannot be merged as a view."""
+    expanded = bias.expand(*lead, s, s)
+    try:
+        return expanded.view(n, h, s, s), False
+    except RuntimeError:
+        return expanded.reshape(n, h, s, s).contiguous(), True
+
+
+def _bias(t: Tensor | None) -> native.Bias:
+    if t is None:
+        return native.Bias(None, 0, 0, 0, 0)
+    return native.Bias(t.data_ptr(), t.stride(0), t.stride(1), t.stride(2), t.stride(3))
+
+
+def _reduce_to(grad: Tensor, like: Tensor) -> Tensor:
+    """Sum a score-shaped tensor down to ``like``'s broadcast shape (used only for
+    bias layouts whose leading dims cannot be merged into a strided view)."""
+    while grad.ndim > like.ndim:
+        grad = grad.sum(dim=0)
+    for dim, size in enumerate(like.shape):
+        if size == 1 and grad.shape[dim] != 1:
+            grad = grad.sum(dim=dim, keepdim=True)
+    return grad
+
+
+class _Call:
+    """Argument block of one kernel call plus the tensors it points into."""
+
+    def __init__(self, q: Tensor, k: Tensor, v: Tensor, bias: Tensor | None, scale: float, key_counts=None):
+        native.require_cuda(q, k, v, bias)
+        if not (q.dtype == k.dtype == v.dtype and (bias is None or bias.dtype == q.dtype)):
+            raise NativeError("edge_attn: q, k, v and bias must share one dtype")
+        self.lead, self.n, self.h = _grid(q)
+        self.s, self.d = q.shape[-2], q.shape[-1]
+        if k.shape != q.shape or v.shape[:-1] != q.shape[:-1] or v.shape[-1] != self.d:
+            raise NativeError(
+                f"edge_attn: q {tuple(q.shape)}, k {tuple(k.shape)}, v {tuple(v.shape)} must match"
+            )
+        self.q = _as_nhsd(q, self.n, self.h)
+        self.k = _as_nhsd(k, self.n, self.h)
+        self.v = _as_nhsd(v, self.n, self.h)
+        self.bias_src = bias
+        self.bias, self.bias_copied = (None, False)
+        if bias is not None:
+            self.bias, self.bias_copied = _bias_view(bias, self.lead, self.n, self.h, self.s)
+        self.args = native.EdgeAttnArgs()
+        a = self.args
+        a.n, a.h, a.k, a.d = self.n, self.h, self.s, self.d
+        a.dtype = native.dtype_code(q)
+        a.scale = float(scale)
+        a.key_count = None if key_counts is None else key_counts.data_ptr()
+        a.q, a.k_, a.v = _mat(self.q), _mat(self.k), _mat(self.v)
+        a.bias = _bias(self.bias)
+        self.keep = [key_counts]
+
+    def new(self, *shape) -> Tensor:
+        return torch.empty(shape, dtype=self.q.dtype, device=self.q.device)
+
+    def run(self, fn) -> None:
+        lib = native.lib()
+        args = ctypes.byref(self.args)
+        scratch_bytes = lib.cg_edge_attn_scratch_bytes(args)
+        if scratch_bytes > 0:
+            scratch = torch.empty(scratch_bytes, dtype=torch.uint8, device=self.q.device)
+            self.args.scratch = scratch.data_ptr()
+            self.keep.append(scratch)
+        native.check(getattr(lib, fn)(args, native.stream_ptr(self.q.device)))
+
+    def dbias_buffer(self) -> Tensor | None:
+        """dbias in the reduced (n_b, h_b, ki, kj) layout the kernel writes."""
+        if self.bias is None:
+            return None
+        b = self.bias
+        shape = tuple(1 if b.stride(i) == 0 else b.shape[i] for i in range(4))
+        out = self.new(*shape)
+        self.args.dbias = native.Bias(out.data_ptr(), *(out.stride(i) for i in range(4)))
+        return out
+
+    def finish_dbias(self, dbias: Tensor | None) -> Tensor | None:
+        if dbias is None:
+            return None
+        if self.bias_copied:
+            full = dbias.reshape(*self.lead, self.s, self.s)
+            return _reduce_to(full, self.bias_src).contiguous()
+        return dbias.reshape(self.bias_src.shape)
+
+    def set_hb(self, hb: Tensor | None) -> None:
+        if hb is None or self.bias is None:
+            return
+        view, _ = _bias_view(hb, self.lead, self.n, self.h, self.s)
+        if view.stride(-1) != 1 and view.stride(-1) != 0:
+            view = view.contiguous()
+        self.keep.append(view)
+        self.args.hb = _bias(view)
+
+    def mat_arg(self, name: str, t: Tensor) -> Tensor:
+        view = _as_nhsd(t, self.n, self.h)
+        self.keep.append(view)
+        setattr(self.args, name, _mat(view))
+        return view
+
+
+def attn_forward1(q, k, v, bias, scale, key_counts=None) -> tuple[Tensor, Tensor]:
+    c = _Call(q, k, v, bias, scale, key_counts)
+    out = c.new(c.n, c.h, c.s, c.d)
+    lse = c.new(c.n, c.h, c.s)
+    c.args.out = _mat(out)
+    c.args.lse = lse.data_ptr()
+    c.run("cg_edge_attn_fwd1")
+    return out.view(*c.lead, c.s, c.d), lse.view(*c.lead, c.s)
+
+
+def attn_backward1(q, k, v, bias, lse, grad_out, scale, key_counts=None):
+    c = _Call(q, k, v, bias, scale, key_counts)
+    lse_c = lse.reshape(c.n, c.h, c.s).contiguous()
+    c.keep.append(lse_c)
+    c.args.lse = lse_c.data_ptr()
+    c.mat_arg("grad_out", grad_out)
+    dq, dk, dv = (c.new(c.n, c.h, c.s, c.d) for _ in range(3))
+    c.args.dq, c.args.dk, c.args.dv = _mat(dq), _mat(dk), _mat(dv)
+    dbias = c.dbias_buffer()
+    c.run("cg_edge_attn_bwd1")
+    shape = (*c.lead, c.s, c.d)
+    return dq.view(shape), dk.view(shape), dv.view(shape), c.finish_dbias(dbias)
+
+
+def attn_backward2(q, k, v, bias, lse, grad_out, scale, hq, hk, hv, hb, key_counts=None):
+    c = _Call(q, k, v, bias, scale, key_counts)
+    lse_c = lse.reshape(c.n, c.h, c.s).contiguous()
+    c.keep.append(lse_c)
+    c.args.lse = lse_c.data_ptr()
+    c.mat_arg("grad_out", grad_out)
+    c.mat_arg("hq", hq)
+    c.mat_arg("hk", hk)
+    c.mat_arg("hv", hv)
+    c.set_hb(hb)
+    dq, dk, dv, dg = (c.new(c.n, c.h, c.s, c.d) for _ in range(4))
+    c.args.dq, c.args.dk, c.args.dv, c.args.dgrad_out = _mat(dq), _mat(dk), _mat(dv), _mat(dg)
+    dbias = c.dbias_buffer()
+    c.run("cg_edge_attn_bwd2")
+    shape = (*c.lead, c.s, c.d)
+    return dq.view(shape), dk.view(shape), dv.view(shape), c.finish_dbias(dbias), dg.view(shape)
+
+
+@custom_op("cg_b200::edge_attn")
+class EdgeAttention:
+    """The reference's EdgeAttention (kernels/edge_attn/ops.py:57-104) with
+    sm_100a kernel bodies."""
+
+    outputs = ("out", "lse")
+    save = ("q", "k", "v", "bias", "lse")
+    nondiff = ("lse",)
+
+    @staticmethod
+    def forward1(q: Tensor, k: Tensor, v: Tensor, bias: Tensor, scale: float) -> tuple[Tensor, Tensor]:
+        return attn_forward1(q, k, v, bias, scale)
+
+    @staticmethod
+    def fake(q, k, v, bias, scale):
+        return q.new_empty((*q.shape[:-1], v.shape[-1])), q.new_empty(q.shape[:-1])
+
+    @staticmethod
+    def backward1(q, k, v, bias, lse, grad_out, scale):
+        return attn_backward1(q, k, v, bias, lse, grad_out, scale)
+
+    @staticmethod
+    def backward2(q, k, v, bias, lse, grad_out, scale, hq, hk, hv, hb):
+        return attn_backward2(q, k, v, bias, lse, grad_out, scale, hq, hk, hv, hb)
+
+
+def edge_attention(q, k, v, bias, scale: float) -> Tensor:
+    """``softmax(q k^T * scale + bias) v`` through the fused op."""
+    return EdgeAttention(q, k, v, bias, scale)[0]

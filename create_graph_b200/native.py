@@ -1,0 +1,133 @@
+"""
+ctypes binding of libcg_b200.so (declared in include/cg_b200.h).
+
+This is the only module that talks to the sm_100a library. ``lib()`` loads it
+once and fails loudly when it is missing or when CUDA is unavailable: the
+fused ops have no CPU or library fallback. Every call passes raw device
+pointers and the current torch CUDA stream, and raises ``NativeError`` with the
+library's message on a non-zero status.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import functools
+import pathlib
+
+import torch
+
+from create_graph_b200.errors import NativeError
+
+LIB_PATH = pathlib.Path(__file__).resolve().parent / "_lib" / "libcg_b200.so"
+ABI_VERSION = 1
+F32, F64 = 0, 1
+_DTYPES = {torch.float32: F32, torch.float64: F64}
+
+i64 = ctypes.c_int64
+i32 = ctypes.c_int32
+vp = ctypes.c_void_p
+
+
+class Mat(ctypes.Structure):
+    _fields_ = [("ptr", vp), ("sn", i64), ("sh", i64), ("sr", i64)]
+
+
+class Bias(ctypes.Structure):
+    _fields_ = [("ptr", vp), ("sn", i64), ("sh", i64), ("si", i64), ("sj", i64)]
+
+
+class EdgeAttnArgs(ctypes.Structure):
+    _fields_ = [
+        ("n", i64),
+        ("h", i64),
+        ("k", i32),
+        ("d", i32),
+        ("dtype", i32),
+        ("pad0", i32),
+        ("scale", ctypes.c_double),
+        ("key_count", vp),
+        ("q", Mat),
+        ("k_", Mat),
+        ("v", Mat),
+        ("bias", Bias),
+        ("lse", vp),
+        ("grad_out", Mat),
+        ("hq", Mat),
+        ("hk", Mat),
+        ("hv", Mat),
+        ("hb", Bias),
+        ("out", Mat),
+        ("dq", Mat),
+        ("dk", Mat),
+        ("dv", Mat),
+        ("dbias", Bias),
+        ("dgrad_out", Mat),
+        ("scratch", vp),
+    ]
+
+
+# name -> (restype, argtypes)
+_SIGNATURES = {
+    "cg_last_error": (ctypes.c_char_p, []),
+    "cg_version": (ctypes.c_int, []),
+    "cg_edge_attn_fwd1": (ctypes.c_int, [ctypes.POINTER(EdgeAttnArgs), vp]),
+    "cg_edge_attn_bwd1": (ctypes.c_int, [ctypes.POINTER(EdgeAttnArgs), vp]),
+    "cg_edge_attn_bwd2": (ctypes.c_int, [ctypes.POINTER(EdgeAttnArgs), vp]),
+    "cg_edge_attn_scratch_bytes": (i64, [ctypes.POINTER(EdgeAttnArgs)]),
+}
+
+
+def exported_symbols() -> list[str]:
+    """Every symbol the Python side binds (each one is declared in include/cg_b200.h)."""
+    return sorted(_SIGNATURES)
+
+
+@functools.cache
+def load_library() -> ctypes.CDLL:
+    """Load libcg_b200.so without touching the GPU (CPU-side checks use this)."""
+    if not LIB_PATH.exists():
+        raise NativeError(
+            f"{LIB_PATH} is missing: build it with `python -m create_graph_b200.build` "
+            "(the fused ops have no fallback)"
+        )
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, (res, args) in _SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if lib.cg_version() != ABI_VERSION:
+        raise NativeError(f"libcg_b200.so has ABI {lib.cg_version()}, expected {ABI_VERSION}")
+    return lib
+
+
+def lib() -> ctypes.CDLL:
+    """The library, for a compute call: CUDA must be available."""
+    if not torch.cuda.is_available():
+        raise NativeError("create_graph_b200 fused ops need a CUDA device (sm_100a); none is visible")
+    return load_library()
+
+
+def check(status: int) -> None:
+    if status != 0:
+        message = load_library().cg_last_error().decode(errors="replace")
+        raise NativeError(message or f"libcg_b200 call failed with status {status}")
+
+
+def stream_ptr(device: torch.device | None = None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise NativeError(f"unsupported dtype {t.dtype}: float32 or float64 expected") from None
+
+
+def require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise NativeError(
+                "create_graph_b200 fused ops run on CUDA tensors only (no CPU fallback); got a "
+                f"{t.device} tensor"
+            )

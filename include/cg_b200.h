@@ -1,0 +1,103 @@
+/*
+ * cg_b200.h -- C ABI of the create_graph_b200 sm_100a library (libcg_b200.so).
+ *
+ * Every entry point takes plain device pointers, sizes and strides (in
+ * elements, not bytes) and a cudaStream_t passed as void*; it launches on that
+ * stream and returns 0, or a non-zero status whose text cg_last_error() gives.
+ * Nothing here allocates device memory: callers pass every output and, where a
+ * *_scratch_bytes() query says so, a scratch buffer.
+ *
+ * The reference (create_graph) is pure Python: its fused-op boundary is
+ * `cg.custom_op` (src/create_graph/ops.py:82-212), whose forward1 / backward1 /
+ * backward2 bodies for the masked edge attention are the PyTorch code of
+ * kernels/edge_attn/ops.py. Each function below names the reference code it
+ * replaces. The Python package calls these through ctypes
+ * (create_graph_b200/native.py); other hosts bind the same symbols.
+ */
+#ifndef CG_B200_H
+#define CG_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CG_B200_ABI_VERSION 1
+
+/* dtype codes */
+#define CG_F32 0
+#define CG_F64 1
+
+/* Text of the last error raised on the calling thread ("" if none). */
+const char* cg_last_error(void);
+/* CG_B200_ABI_VERSION of the loaded library. */
+int cg_version(void);
+
+/* ------------------------------------------------------------------------
+ * Masked edge attention, per slice (n, h) of k tokens with head dim d:
+ *   logits = q k^T * scale + bias,  keys j >= key_count[n] masked (-inf);
+ *   probs  = softmax over finite logits (all-masked rows give zeros);
+ *   out    = probs v,  lse = row logsumexp (-inf for all-masked rows).
+ * A matrix operand's row r of slice (n, h) starts at
+ *   ptr + n*sn + h*sh + r*sr   (elements; columns contiguous).
+ * bias / hb / dbias use (sn, sh, si, sj); a stride of 0 broadcasts that
+ * dimension, and dbias is then summed over it (deterministically).
+ * Limits: 1 <= k <= 32, 1 <= d <= 64 (d <= 16 for float64).
+ * ---------------------------------------------------------------------- */
+typedef struct cg_mat {
+  void* ptr;
+  int64_t sn, sh, sr;
+} cg_mat;
+
+typedef struct cg_bias {
+  void* ptr;
+  int64_t sn, sh, si, sj;
+} cg_bias;
+
+typedef struct cg_edge_attn_args {
+  int64_t n, h;           /* slice grid */
+  int32_t k, d;           /* tokens per slice, head dim */
+  int32_t dtype;          /* CG_F32 or CG_F64 */
+  int32_t pad0;
+  double scale;
+  const int32_t* key_count; /* optional (n,): valid keys per n; NULL = all k */
+  /* inputs */
+  cg_mat q, k_, v;
+  cg_bias bias;           /* ptr may be NULL: no bias */
+  void* lse;              /* (n, h, k) contiguous: output of fwd1, input of bwd1/bwd2 */
+  cg_mat grad_out;        /* bwd1, bwd2 */
+  cg_mat hq, hk, hv;      /* bwd2: cotangents of dq, dk, dv */
+  cg_bias hb;             /* bwd2: cotangent of dbias (bias's broadcast shape), may be NULL */
+  /* outputs */
+  cg_mat out;             /* fwd1 */
+  cg_mat dq, dk, dv;      /* bwd1, bwd2 */
+  cg_bias dbias;          /* bwd1, bwd2; strides of broadcast dims ignored; NULL = skip */
+  cg_mat dgrad_out;       /* bwd2 */
+  void* scratch;          /* cg_edge_attn_scratch_bytes() bytes, or NULL if that is 0 */
+} cg_edge_attn_args;
+
+/* Replaces EdgeAttention.forward1 (kernels/edge_attn/ops.py:64-68, with
+ * _scores at :26-34): writes out and lse. */
+int cg_edge_attn_fwd1(const cg_edge_attn_args* a, void* stream);
+
+/* Replaces EdgeAttention.backward1 (kernels/edge_attn/ops.py:75-76 via _first
+ * at :47-54, bias reduction _reduce at :37-44): rebuilds probs from lse,
+ * writes dq, dk, dv and dbias. */
+int cg_edge_attn_bwd1(const cg_edge_attn_args* a, void* stream);
+
+/* Replaces EdgeAttention.backward2 (kernels/edge_attn/ops.py:79-104): the
+ * gradients of <hq,dq>+<hk,dk>+<hv,dv>+<hb,dbias> w.r.t. q, k, v, bias and
+ * grad_out; writes dq, dk, dv, dbias and dgrad_out. */
+int cg_edge_attn_bwd2(const cg_edge_attn_args* a, void* stream);
+
+/* Scratch bytes bwd1 / bwd2 need for a dbias broadcast over n or h (the
+ * per-slice partial sums reduced in a fixed order); 0 otherwise. Replaces the
+ * cross-batch part of _reduce (kernels/edge_attn/ops.py:37-44). */
+int64_t cg_edge_attn_scratch_bytes(const cg_edge_attn_args* a);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CG_B200_H */

@@ -1,0 +1,100 @@
+"""
+Generate the golden vectors under tests/golden/ by running the reference itself.
+
+    python tests/golden/make_golden.py [--reference /root/reference]
+
+Imports the reference package read-only from its source tree (``src/`` and the
+repository root for ``kernels.edge_attn``) and records, for seeded inputs, what
+its own ``cg_kernels::edge_attn`` operators (forward1 / backward1 / backward2,
+kernels/edge_attn/ops.py) and its ``create_graph`` step (examples/mlp.py-style
+model) return. The fixtures are small ``.npz`` files; the GPU box never needs
+the reference. Re-running this script reproduces them bit for bit.
+"""
+
+from __future__ import annotations
+
+import argparse
+import pathlib
+import sys
+
+import numpy as np
+import torch
+
+HERE = pathlib.Path(__file__).resolve().parent
+
+
+def import_reference(root: str):
+    sys.path[:0] = [f"{root}/src", root]
+    import create_graph as ref_cg  # noqa: PLC0415
+    from kernels.edge_attn import EdgeAttention  # noqa: PLC0415
+
+    return ref_cg, EdgeAttention
+
+
+def attn_case(op, q, k, v, bias, scale, gen):
+    """Inputs, cotangents and the reference op's three outputs."""
+    out, lse = op.op(q, k, v, bias, scale)
+    grad_out = torch.randn(out.shape, generator=gen, dtype=q.dtype)
+    b1 = op.backward1_op(q, k, v, bias, lse, grad_out, scale)
+    hq, hk, hv = (torch.randn(q.shape, generator=gen, dtype=q.dtype) for _ in range(3))
+    hb = torch.randn(bias.shape, generator=gen, dtype=q.dtype)
+    hb = torch.where(torch.isfinite(bias), hb, torch.zeros_like(hb))
+    b2 = op.backward2_op(q, k, v, bias, lse, grad_out, scale, hq, hk, hv, hb)
+    arrays = dict(
+        q=q, k=k, v=v, bias=bias, scale=torch.tensor(scale, dtype=torch.float64),
+        out=out, lse=lse, grad_out=grad_out,
+        b1_dq=b1[0], b1_dk=b1[1], b1_dv=b1[2], b1_dbias=b1[3],
+        hq=hq, hk=hk, hv=hv, hb=hb,
+        b2_dq=b2[0], b2_dk=b2[1], b2_dv=b2[2], b2_dbias=b2[3], b2_dgrad_out=b2[4],
+    )
+    return {name: t.detach().numpy() for name, t in arrays.items()}
+
+
+def edge_attn_fixtures(op) -> dict[str, dict]:
+    cases = {}
+    # the reference test's own shapes (tests/test_custom_ops.py:24-39): fp64,
+    # q/k/v (2,3,5,4), bias (2,1,1,5) broadcast, scale 0.5, with and without -inf keys
+    for masked in (False, True):
+        gen = torch.Generator().manual_seed(0)
+        q, k, v = (torch.randn(2, 3, 5, 4, generator=gen, dtype=torch.float64) for _ in range(3))
+        bias = torch.randn(2, 1, 1, 5, generator=gen, dtype=torch.float64)
+        if masked:
+            bias[0, 0, 0, 1] = -torch.inf
+            bias[1, 0, 0, 4] = -torch.inf
+        cases[f"edge_attn_testshape_{'masked' if masked else 'plain'}"] = attn_case(
+            op, q, k, v, bias, 0.5, gen
+        )
+    # the microbenchmark's distribution at a small n: K=32, H=8, D=32,
+    # bias ~ N(0, 0.1) per (n, h, i, j), keys j >= c_n masked, c_n ~ U{8..32}
+    gen = torch.Generator().manual_seed(0)
+    n, h, s, d = 6, 2, 32, 32
+    q, k, v = (torch.randn(n, h, s, d, generator=gen, dtype=torch.float64) for _ in range(3))
+    bias = 0.1 * torch.randn(n, h, s, s, generator=gen, dtype=torch.float64)
+    counts = torch.randint(8, s + 1, (n,), generator=gen)
+    keymask = torch.arange(s)[None, :] >= counts[:, None]  # (n, s)
+    bias = bias.masked_fill(keymask[:, None, None, :], -torch.inf)
+    case = attn_case(op, q, k, v, bias, 1.0 / np.sqrt(d), gen)
+    case["key_counts"] = counts.numpy().astype(np.int32)
+    cases["edge_attn_cfg2_small"] = case
+    # the model's layout: bias (n, h, 1, s) broadcast over queries, all rows valid
+    gen = torch.Generator().manual_seed(1)
+    n, h, s, d = 3, 2, 30, 64
+    q, k, v = (torch.randn(n, h, s, d, generator=gen, dtype=torch.float64) for _ in range(3))
+    bias = torch.randn(n, h, 1, s, generator=gen, dtype=torch.float64)
+    cases["edge_attn_keybias"] = attn_case(op, q, k, v, bias, 0.125, gen)
+    return cases
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--reference", default="/root/reference")
+    args = parser.parse_args()
+    _, op = import_reference(args.reference)
+    for name, arrays in edge_attn_fixtures(op).items():
+        path = HERE / f"{name}.npz"
+        np.savez_compressed(path, **arrays)
+        print(path, {k: v.shape for k, v in arrays.items()})
+
+
+if __name__ == "__main__":
+    main()
