@@ -83,7 +83,7 @@ def build(verbose: bool = False, jobs: int | None = None) -> pathlib.Path:
     objs = [obj for obj, _ in results]
     if not LIB.exists() or any(o.stat().st_mtime > LIB.stat().st_mtime for o in objs):
         tmp = LIB.with_suffix(".so.tmp")
-        cmd = [compiler, *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-lcuda"]
+        cmd = [compiler, *ARCH, "-shared", "-o", str(tmp), *map(str, objs)]
         run = subprocess.run(cmd, capture_output=True, text=True)
         if run.returncode != 0:
             raise RuntimeError(f"linking libcg_b200.so failed:\n{run.stderr}")

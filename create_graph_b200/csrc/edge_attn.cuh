@@ -90,27 +90,45 @@ __device__ inline void load_mat(T* s, const cg_mat& m, int64_t n, int64_t h, int
   }
 }
 
-// Write one row of d values held by this lane (registers acc[0..DP)).
-template <typename T, int DP>
-__device__ inline void store_row(const cg_mat& m, int64_t n, int64_t h, int r, int d,
-                                 const T* acc, bool vec) {
+// Row r of output m for slice (n, h): computed 16 bytes at a time by `chunk`
+// (a functor filling acc[0..V::n) for columns [c, c + V::n)) and stored at
+// once, so no d-wide accumulator array lives in registers.
+template <typename T, int DP, typename Chunk>
+__device__ inline void emit_row(const cg_mat& m, int64_t n, int64_t h, int r, int d, bool vec,
+                                Chunk chunk) {
   using V = V16<T>;
   T* dst = out_row<T>(m, n, h, r);
-  if (vec) {
-#pragma unroll
-    for (int c = 0; c < DP; c += V::n) {
+#pragma unroll 1
+  for (int c = 0; c < DP; c += V::n) {
+    T acc[V::n];
+    chunk(c, acc);
+    if (vec) {
       typename V::type v;
       if constexpr (V::n == 4) {
-        v.x = acc[c]; v.y = acc[c + 1]; v.z = acc[c + 2]; v.w = acc[c + 3];
+        v.x = acc[0]; v.y = acc[1]; v.z = acc[2]; v.w = acc[3];
       } else {
-        v.x = acc[c]; v.y = acc[c + 1];
+        v.x = acc[0]; v.y = acc[1];
       }
       *reinterpret_cast<typename V::type*>(dst + c) = v;
-    }
-  } else {
+    } else {
 #pragma unroll
-    for (int c = 0; c < DP; ++c)
-      if (c < d) dst[c] = acc[c];
+      for (int e = 0; e < V::n; ++e)
+        if (c + e < d) dst[c + e] = acc[e];
+    }
+  }
+}
+
+// acc[e] += sum_j w[j] * s[j][c + e] over j < k (broadcast reads of s rows).
+template <typename T, int LD>
+__device__ inline void combine(T* acc, const T (&w)[KMAX], const T* s, int c, int k) {
+  using V = V16<T>;
+#pragma unroll
+  for (int j = 0; j < KMAX; ++j) {
+    if (j < k) {
+      const typename V::type sv = *reinterpret_cast<const typename V::type*>(s + j * LD + c);
+#pragma unroll
+      for (int e = 0; e < V::n; ++e) acc[e] = fma(w[j], V::get(sv, e), acc[e]);
+    }
   }
 }
 
@@ -120,7 +138,7 @@ __device__ inline void row_dots(T (&dots)[KMAX], const T* x, const T* s, int k) 
   using V = V16<T>;
 #pragma unroll
   for (int j = 0; j < KMAX; ++j) dots[j] = T(0);
-#pragma unroll
+#pragma unroll 1
   for (int c = 0; c < DP; c += V::n) {
     const typename V::type xv = *reinterpret_cast<const typename V::type*>(x + c);
 #pragma unroll
@@ -134,38 +152,18 @@ __device__ inline void row_dots(T (&dots)[KMAX], const T* x, const T* s, int k) 
   }
 }
 
-// acc[c] += sum_j w[j] * s[j][c] (broadcast reads of s rows).
-template <typename T, int DP, int LD>
-__device__ inline void row_combine(T* acc, const T (&w)[KMAX], const T* s, int k) {
-  using V = V16<T>;
+// w[i] = M[i][col] for i < k (a column of a k x k matrix of pitch KLD), else 0.
+template <typename T>
+__device__ inline void load_col(T (&w)[KMAX], const T* M, int col, int k) {
 #pragma unroll
-  for (int j = 0; j < KMAX; ++j) {
-    if (j < k) {
-      const T wj = w[j];
-#pragma unroll
-      for (int c = 0; c < DP; c += V::n) {
-        const typename V::type sv = *reinterpret_cast<const typename V::type*>(s + j * LD + c);
-#pragma unroll
-        for (int e = 0; e < V::n; ++e) acc[c + e] = fma(wj, V::get(sv, e), acc[c + e]);
-      }
-    }
-  }
+  for (int i = 0; i < KMAX; ++i) w[i] = i < k ? M[i * KLD + col] : T(0);
 }
 
-// acc[c] += sum_i M[i][lane] * s[i][c]: the transposed product for key row `lane`.
-template <typename T, int DP, int LD>
-__device__ inline void col_combine(T* acc, const T* M, const T* s, int k, int lane) {
-  using V = V16<T>;
-#pragma unroll 4
-  for (int i = 0; i < k; ++i) {
-    const T w = M[i * KLD + lane];
+// w[j] = M[row][j] for j < k, else 0.
+template <typename T>
+__device__ inline void load_row(T (&w)[KMAX], const T* M, int row, int k) {
 #pragma unroll
-    for (int c = 0; c < DP; c += V::n) {
-      const typename V::type sv = *reinterpret_cast<const typename V::type*>(s + i * LD + c);
-#pragma unroll
-      for (int e = 0; e < V::n; ++e) acc[c + e] = fma(w, V::get(sv, e), acc[c + e]);
-    }
-  }
+  for (int j = 0; j < KMAX; ++j) w[j] = j < k ? M[row * KLD + j] : T(0);
 }
 
 // Bias row i of slice (n, h) into b[0..k) (0 where there is no bias).
@@ -284,19 +282,24 @@ __global__ void __launch_bounds__(128) fwd1_kernel(const Params P) {
     load_mat<T, DP, LD>(sV, a.v, n, h, k, d, P.vec_ok, lane);
     __syncwarp();
     const int kc = valid_keys<T>(P, n);
-    const int i = lane;
-    T dots[KMAX], b[KMAX], logit[KMAX], p[KMAX];
-    row_dots<T, DP, LD>(dots, sQ + (i < k ? i : 0) * LD, sK, k);
-    bias_row<T>(b, a.bias, n, h, i < k ? i : 0, k);
-    make_logits<T>(logit, dots, b, scale);
-    const T lse = softmax_row<T>(p, logit, k, kc, nullptr);
-    T acc[DP];
+    const int i = lane < k ? lane : 0;
+    T p[KMAX];
+    T lse;
+    {
+      T dots[KMAX], b[KMAX];
+      row_dots<T, DP, LD>(dots, sQ + i * LD, sK, k);
+      bias_row<T>(b, a.bias, n, h, i, k);
 #pragma unroll
-    for (int c = 0; c < DP; ++c) acc[c] = T(0);
-    row_combine<T, DP, LD>(acc, p, sV, k);
-    if (i < k) {
-      store_row<T, DP>(a.out, n, h, i, d, acc, P.vec_ok);
-      reinterpret_cast<T*>(a.lse)[s * k + i] = lse;
+      for (int j = 0; j < KMAX; ++j) dots[j] = dots[j] * scale + b[j];
+      lse = softmax_row<T>(p, dots, k, kc, nullptr);
+    }
+    if (lane < k) {
+      emit_row<T, DP>(a.out, n, h, lane, d, P.vec_ok, [&](int c, T* acc) {
+#pragma unroll
+        for (int e = 0; e < V16<T>::n; ++e) acc[e] = T(0);
+        combine<T, LD>(acc, p, sV, c, k);
+      });
+      reinterpret_cast<T*>(a.lse)[s * k + lane] = lse;
     }
   }
 }
@@ -330,27 +333,31 @@ __global__ void __launch_bounds__(128) bwd1_kernel(const Params P) {
     const int kc = valid_keys<T>(P, n);
     const int i = lane < k ? lane : 0;
     {
-      T dots[KMAX], b[KMAX], logit[KMAX], p[KMAX], gp[KMAX];
-      row_dots<T, DP, LD>(dots, sQ + i * LD, sK, k);
-      bias_row<T>(b, a.bias, n, h, i, k);
-      make_logits<T>(logit, dots, b, scale);
-      const T* lse_in = reinterpret_cast<const T*>(a.lse) + s * k + i;
-      softmax_row<T>(p, logit, k, kc, lse_in);
-      row_dots<T, DP, LD>(gp, sG + i * LD, sV, k);  // grad_probs = grad_out v^T
-      T rs = T(0);
+      T p[KMAX], gl[KMAX];
+      {
+        T dots[KMAX], b[KMAX];
+        row_dots<T, DP, LD>(dots, sQ + i * LD, sK, k);
+        bias_row<T>(b, a.bias, n, h, i, k);
 #pragma unroll
-      for (int j = 0; j < KMAX; ++j) rs = fma(p[j], gp[j], rs);
-      T gl[KMAX];
+        for (int j = 0; j < KMAX; ++j) dots[j] = dots[j] * scale + b[j];
+        const T* lse_in = reinterpret_cast<const T*>(a.lse) + s * k + i;
+        softmax_row<T>(p, dots, k, kc, lse_in);
+        row_dots<T, DP, LD>(gl, sG + i * LD, sV, k);  // grad_probs = grad_out v^T
+        T rs = T(0);
 #pragma unroll
-      for (int j = 0; j < KMAX; ++j) gl[j] = p[j] * (gp[j] - rs);
-      T acc[DP];
+        for (int j = 0; j < KMAX; ++j) rs = fma(p[j], gl[j], rs);
 #pragma unroll
-      for (int c = 0; c < DP; ++c) acc[c] = T(0);
-      row_combine<T, DP, LD>(acc, gl, sK, k);  // grad_q = scale * grad_logits k
-#pragma unroll
-      for (int c = 0; c < DP; ++c) acc[c] *= scale;
+        for (int j = 0; j < KMAX; ++j) gl[j] = p[j] * (gl[j] - rs);  // grad_logits
+      }
       if (lane < k) {
-        store_row<T, DP>(a.dq, n, h, lane, d, acc, P.vec_ok);
+        // grad_q = scale * grad_logits k
+        emit_row<T, DP>(a.dq, n, h, lane, d, P.vec_ok, [&](int c, T* acc) {
+#pragma unroll
+          for (int e = 0; e < V16<T>::n; ++e) acc[e] = T(0);
+          combine<T, LD>(acc, gl, sK, c, k);
+#pragma unroll
+          for (int e = 0; e < V16<T>::n; ++e) acc[e] *= scale;
+        });
 #pragma unroll
         for (int j = 0; j < KMAX; ++j) {
           sP[lane * KLD + j] = p[j];
@@ -360,17 +367,21 @@ __global__ void __launch_bounds__(128) bwd1_kernel(const Params P) {
     }
     __syncwarp();
     if (lane < k) {
-      T acc[DP];
+      T w[KMAX];
+      load_col<T>(w, sP, lane, k);  // grad_v = probs^T grad_out
+      emit_row<T, DP>(a.dv, n, h, lane, d, P.vec_ok, [&](int c, T* acc) {
 #pragma unroll
-      for (int c = 0; c < DP; ++c) acc[c] = T(0);
-      col_combine<T, DP, LD>(acc, sP, sG, k, lane);  // grad_v = probs^T grad_out
-      store_row<T, DP>(a.dv, n, h, lane, d, acc, P.vec_ok);
+        for (int e = 0; e < V16<T>::n; ++e) acc[e] = T(0);
+        combine<T, LD>(acc, w, sG, c, k);
+      });
+      load_col<T>(w, sD, lane, k);  // grad_k = scale * grad_logits^T q
+      emit_row<T, DP>(a.dk, n, h, lane, d, P.vec_ok, [&](int c, T* acc) {
 #pragma unroll
-      for (int c = 0; c < DP; ++c) acc[c] = T(0);
-      col_combine<T, DP, LD>(acc, sD, sQ, k, lane);  // grad_k = scale * grad_logits^T q
+        for (int e = 0; e < V16<T>::n; ++e) acc[e] = T(0);
+        combine<T, LD>(acc, w, sQ, c, k);
 #pragma unroll
-      for (int c = 0; c < DP; ++c) acc[c] *= scale;
-      store_row<T, DP>(a.dk, n, h, lane, d, acc, P.vec_ok);
+        for (int e = 0; e < V16<T>::n; ++e) acc[e] *= scale;
+      });
     }
     write_dbias<T>(P, sD, n, h, s, lane);
   }
@@ -433,21 +444,20 @@ __global__ void __launch_bounds__(128) bwd2_kernel(const Params P) {
       row_dots<T, DP, LD>(x, sHQ + i * LD, sK, k);
       row_dots<T, DP, LD>(y, sQ + i * LD, sHK, k);
       bias_row<T>(b, a.hb, n, h, i, k);
-      T dl[KMAX];
 #pragma unroll
-      for (int j = 0; j < KMAX; ++j) dl[j] = scale * (x[j] + y[j]) + b[j];
-      // d_rowsum = -sum(d_logits * probs); d_gp = d_logits*p + d_rowsum*p
+      for (int j = 0; j < KMAX; ++j) b[j] = scale * (x[j] + y[j]) + b[j];  // d_logits
+      // d_rowsum = -sum(d_logits * probs)
       T drs = T(0);
 #pragma unroll
-      for (int j = 0; j < KMAX; ++j) drs = fma(dl[j], p[j], drs);
+      for (int j = 0; j < KMAX; ++j) drs = fma(b[j], p[j], drs);
       drs = -drs;
-      // d_probs = d_logits*cen + d_rowsum*gp + grad_out hv^T
+      // d_probs = d_logits*cen + d_rowsum*gp + grad_out hv^T; d_gp = (d_logits + d_rowsum)*p
       row_dots<T, DP, LD>(x, sG + i * LD, sHV, k);
 #pragma unroll
       for (int j = 0; j < KMAX; ++j) {
         const T gp = cen[j] + rs;
-        y[j] = dl[j] * cen[j] + drs * gp + x[j];       // d_probs
-        x[j] = dl[j] * p[j] + drs * p[j];              // d_grad_probs
+        y[j] = b[j] * cen[j] + drs * gp + x[j];       // d_probs
+        x[j] = b[j] * p[j] + drs * p[j];              // d_grad_probs
       }
       T rs2 = T(0);
 #pragma unroll
@@ -462,42 +472,45 @@ __global__ void __launch_bounds__(128) bwd2_kernel(const Params P) {
       }
     }
     __syncwarp();
-    T acc[DP];
     if (lane < k) {
+      T w1[KMAX], w2[KMAX];
       // grad_q = scale * (grad_logits hk + d_scores k)
-      T w[KMAX];
+      load_row<T>(w1, sGL, lane, k);
+      load_row<T>(w2, sDS, lane, k);
+      emit_row<T, DP>(a.dq, n, h, lane, d, P.vec_ok, [&](int c, T* acc) {
 #pragma unroll
-      for (int c = 0; c < DP; ++c) acc[c] = T(0);
+        for (int e = 0; e < V16<T>::n; ++e) acc[e] = T(0);
+        combine<T, LD>(acc, w1, sHK, c, k);
+        combine<T, LD>(acc, w2, sK, c, k);
 #pragma unroll
-      for (int j = 0; j < KMAX; ++j) w[j] = sGL[lane * KLD + j];
-      row_combine<T, DP, LD>(acc, w, sHK, k);
-#pragma unroll
-      for (int j = 0; j < KMAX; ++j) w[j] = sDS[lane * KLD + j];
-      row_combine<T, DP, LD>(acc, w, sK, k);
-#pragma unroll
-      for (int c = 0; c < DP; ++c) acc[c] *= scale;
-      store_row<T, DP>(a.dq, n, h, lane, d, acc, P.vec_ok);
+        for (int e = 0; e < V16<T>::n; ++e) acc[e] *= scale;
+      });
       // grad_out cotangent = d_grad_probs v + probs hv
+      load_row<T>(w1, sDG, lane, k);
+      emit_row<T, DP>(a.dgrad_out, n, h, lane, d, P.vec_ok, [&](int c, T* acc) {
 #pragma unroll
-      for (int c = 0; c < DP; ++c) acc[c] = T(0);
-#pragma unroll
-      for (int j = 0; j < KMAX; ++j) w[j] = sDG[lane * KLD + j];
-      row_combine<T, DP, LD>(acc, w, sV, k);
-      row_combine<T, DP, LD>(acc, p, sHV, k);
-      store_row<T, DP>(a.dgrad_out, n, h, lane, d, acc, P.vec_ok);
+        for (int e = 0; e < V16<T>::n; ++e) acc[e] = T(0);
+        combine<T, LD>(acc, w1, sV, c, k);
+        combine<T, LD>(acc, p, sHV, c, k);
+      });
       // grad_k = scale * (grad_logits^T hq + d_scores^T q)
+      load_col<T>(w1, sGL, lane, k);
+      load_col<T>(w2, sDS, lane, k);
+      emit_row<T, DP>(a.dk, n, h, lane, d, P.vec_ok, [&](int c, T* acc) {
 #pragma unroll
-      for (int c = 0; c < DP; ++c) acc[c] = T(0);
-      col_combine<T, DP, LD>(acc, sGL, sHQ, k, lane);
-      col_combine<T, DP, LD>(acc, sDS, sQ, k, lane);
+        for (int e = 0; e < V16<T>::n; ++e) acc[e] = T(0);
+        combine<T, LD>(acc, w1, sHQ, c, k);
+        combine<T, LD>(acc, w2, sQ, c, k);
 #pragma unroll
-      for (int c = 0; c < DP; ++c) acc[c] *= scale;
-      store_row<T, DP>(a.dk, n, h, lane, d, acc, P.vec_ok);
+        for (int e = 0; e < V16<T>::n; ++e) acc[e] *= scale;
+      });
       // grad_v = d_grad_probs^T grad_out
+      load_col<T>(w1, sDG, lane, k);
+      emit_row<T, DP>(a.dv, n, h, lane, d, P.vec_ok, [&](int c, T* acc) {
 #pragma unroll
-      for (int c = 0; c < DP; ++c) acc[c] = T(0);
-      col_combine<T, DP, LD>(acc, sDG, sG, k, lane);
-      store_row<T, DP>(a.dv, n, h, lane, d, acc, P.vec_ok);
+        for (int e = 0; e < V16<T>::n; ++e) acc[e] = T(0);
+        combine<T, LD>(acc, w1, sG, c, k);
+      });
     }
     write_dbias<T>(P, sDS, n, h, s, lane);
   }

@@ -1,0 +1,303 @@
+// Dense projections on the 5th-generation tensor cores: C = epilogue(A . B^T)
+// with kind::tf32 UMMA (fp32 in, fp32 accumulate in TMEM).
+//
+// One CTA computes one BM x BN tile (BM = 128, BN in {64, 128, 256}):
+//   warp 0        TMA producer: A and B k-slices of 32 fp32 (128 B, 128B
+//                 swizzle) into a ring of STAGES shared-memory stages;
+//   warp 1        allocates TMEM; one thread issues 4 UMMAs (K = 8) per stage
+//                 and commits each stage back to the producer;
+//   warps 2..5    epilogue: tcgen05.ld of the accumulator (one TMEM lane =
+//                 one output row per thread), bias / SiLU / SiLU-derivative /
+//                 accumulate, and stores.
+// A and B are each either K-major (rows contiguous along K) or MN-major
+// (contiguous along M / N), so the forward (x W^T), the data gradient (g W)
+// and the weight gradient (g^T x) all read their operands in place.
+// Every mbarrier wait is bounded: on timeout the kernel records an error in
+// the device error word and unwinds, freeing its TMEM.
+#include <cudaTypedefs.h>
+#include <math.h>
+
+#include "common.cuh"
+#include "sm100.cuh"
+#include "../../include/cg_b200.h"
+
+namespace cg {
+namespace gemm {
+
+// device error word of this translation unit's kernels
+__device__ int g_gemm_error = 0;
+
+using namespace cg::sm100;
+
+constexpr int BM = 128;
+constexpr int BK = 32;  // fp32 elements per k-slice: one 128-byte swizzle row
+constexpr int kThreads = 192;
+
+struct Epilogue {
+  float* c;
+  int64_t ldc;
+  const float* bias;    // (N,) or null
+  const float* aux_in;  // (M, N) pre-activation for the SiLU derivative, ld = ld_aux
+  float* aux_out;       // (M, N) pre-activation written by the SiLU forward, ld = ld_aux
+  int64_t ld_aux;
+  int act;              // CG_ACT_*
+  int accumulate;       // C += result
+  float alpha;
+};
+
+__device__ inline float silu(float z) { return z / (1.0f + expf(-z)); }
+__device__ inline float silu_grad(float z) {
+  const float s = 1.0f / (1.0f + expf(-z));
+  return s * (1.0f + z * (1.0f - s));
+}
+
+template <int BN, int STAGES>
+struct Smem {
+  static constexpr int kA = BM * BK * 4;
+  static constexpr int kB = BN * BK * 4;
+  static constexpr int kStage = kA + kB;
+  static constexpr int kTiles = STAGES * kStage;
+  static constexpr int kBytes = kTiles + 1024 /*alignment*/ + 256 /*barriers*/;
+};
+
+template <int BN, int STAGES, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tf32_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                     int M, int N, int K, Epilogue ep) {
+  using S = Smem<BN, STAGES>;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // tiles need 1024-byte alignment for the 128B swizzle pattern
+  unsigned char* tiles = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(tiles + S::kTiles);
+  uint64_t* empty = full + STAGES;
+  uint64_t* done = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+  const int ktiles = (K + BK - 1) / BK;
+  constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    prefetch_tmap(&map_a);
+    prefetch_tmap(&map_b);
+    for (int kt = 0; kt < ktiles && ok; ++kt) {
+      const int s = kt % STAGES;
+      const uint32_t round = kt / STAGES;
+      if (kt >= STAGES) ok = mbar_wait(&empty[s], (round - 1) & 1, &g_gemm_error);
+      if (!ok) break;
+      unsigned char* sa = tiles + s * S::kStage;
+      unsigned char* sb = sa + S::kA;
+      mbar_arrive_expect_tx(&full[s], S::kStage);
+      const int k0 = kt * BK;
+      if (!A_MN) {
+        tma_load_2d(sa, &map_a, &full[s], k0, m0);
+      } else {
+#pragma unroll
+        for (int c = 0; c < BM / 32; ++c) tma_load_2d(sa + c * (BK * 128), &map_a, &full[s], m0 + 32 * c, k0);
+      }
+      if (!B_MN) {
+        tma_load_2d(sb, &map_b, &full[s], k0, n0);
+      } else {
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) tma_load_2d(sb + c * (BK * 128), &map_b, &full[s], n0 + 32 * c, k0);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- UMMA issuer ----------------
+    constexpr uint32_t idesc = idesc_tf32(BM, BN, A_MN, B_MN);
+    for (int kt = 0; kt < ktiles && ok; ++kt) {
+      const int s = kt % STAGES;
+      ok = mbar_wait(&full[s], (kt / STAGES) & 1, &g_gemm_error);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t sa = smem_u32(tiles + s * S::kStage);
+      const uint32_t sb = sa + S::kA;
+#pragma unroll
+      for (int kk = 0; kk < BK / 8; ++kk) {
+        // K-major (128B swizzle, 8-row groups at 1024 B): advance 32 bytes
+        // along the row. MN-major (128B swizzle with 32 B granules, 4-row K
+        // groups at 512 B, 32-wide MN groups at BK * 128 B): advance 8 rows.
+        const uint64_t ad = A_MN ? smem_desc(sa + kk * 1024, BK * 128, 512, kSwizzle128BBase32B)
+                                 : smem_desc(sa + kk * 32, 16, 1024, kSwizzle128B);
+        const uint64_t bd = B_MN ? smem_desc(sb + kk * 1024, BK * 128, 512, kSwizzle128BBase32B)
+                                 : smem_desc(sb + kk * 32, 16, 1024, kSwizzle128B);
+        umma_tf32(tmem, ad, bd, idesc, kt > 0 || kk > 0);
+      }
+      umma_commit(&empty[s]);
+    }
+    umma_commit(done);
+  } else if (warp >= 2) {
+    // ---------------- epilogue ----------------
+    const int quarter = warp & 3;  // TMEM lanes this warp may read
+    const int row = m0 + quarter * 32 + lane;
+    if (mbar_wait(done, 0, &g_gemm_error)) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        float v[32];
+        tmem_load_32(tmem + ((uint32_t)(quarter * 32) << 16) + c0, v);
+        if (row < M) {
+          float* crow = ep.c + (int64_t)row * ep.ldc;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int col = n0 + c0 + j;
+            if (col < N) {
+              float x = v[j] * ep.alpha;
+              if (ep.bias) x += ep.bias[col];
+              if (ep.act == CG_ACT_SILU) {
+                if (ep.aux_out) ep.aux_out[(int64_t)row * ep.ld_aux + col] = x;
+                x = silu(x);
+              } else if (ep.act == CG_ACT_SILU_GRAD) {
+                x *= silu_grad(ep.aux_in[(int64_t)row * ep.ld_aux + col]);
+              }
+              if (ep.accumulate) x += crow[col];
+              crow[col] = x;
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2D fp32 tensor map over `rows` x `cols` (cols contiguous, row pitch `ld`),
+// box = box_cols x box_rows, 128-byte swizzle with 16-byte granules
+// (K-major tiles) or 32-byte granules (MN-major tiles).
+static int make_map(CUtensorMap* map, const float* ptr, int64_t rows, int64_t cols, int64_t ld,
+                    int box_cols, int box_rows, bool mn_major) {
+  auto fn = encode_fn();
+  CG_REQUIRE(fn != nullptr, "gemm: cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 4)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CG_REQUIRE(r == CUDA_SUCCESS, "gemm: cuTensorMapEncodeTiled failed (%d): rows %lld cols %lld ld %lld",
+             (int)r, (long long)rows, (long long)cols, (long long)ld);
+  return kOk;
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN>
+static int launch(const cg_gemm_args& g, cudaStream_t stream) {
+  CUtensorMap ma, mb;
+  int rc;
+  // A as stored: K-major (M rows x K cols) or MN-major (K rows x M cols)
+  if ((rc = A_MN ? make_map(&ma, g.a, g.k, g.m, g.lda, 32, BK, true)
+                 : make_map(&ma, g.a, g.m, g.k, g.lda, BK, BM, false)))
+    return rc;
+  if ((rc = B_MN ? make_map(&mb, g.b, g.k, g.n, g.ldb, 32, BK, true)
+                 : make_map(&mb, g.b, g.n, g.k, g.ldb, BK, BN, false)))
+    return rc;
+  Epilogue ep;
+  ep.c = g.c;
+  ep.ldc = g.ldc;
+  ep.bias = g.bias;
+  ep.aux_in = g.aux_in;
+  ep.aux_out = g.aux_out;
+  ep.ld_aux = g.ld_aux;
+  ep.act = g.act;
+  ep.accumulate = g.accumulate;
+  ep.alpha = g.alpha;
+  using S = Smem<BN, STAGES>;
+  auto kernel = gemm_tf32_kernel<BN, STAGES, A_MN, B_MN>;
+  CG_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes));
+  dim3 grid((unsigned)ceil_div<int64_t>(g.m, BM), (unsigned)ceil_div<int64_t>(g.n, BN));
+  kernel<<<grid, kThreads, S::kBytes, stream>>>(ma, mb, (int)g.m, (int)g.n, (int)g.k, ep);
+  CG_LAUNCHED("gemm_tf32");
+  return kOk;
+}
+
+template <int BN, int STAGES>
+static int launch_majors(const cg_gemm_args& g, cudaStream_t s) {
+  if (!g.a_mn_major && !g.b_mn_major) return launch<BN, STAGES, false, false>(g, s);
+  if (!g.a_mn_major && g.b_mn_major) return launch<BN, STAGES, false, true>(g, s);
+  if (g.a_mn_major && !g.b_mn_major) return launch<BN, STAGES, true, false>(g, s);
+  return launch<BN, STAGES, true, true>(g, s);
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+static int run(const cg_gemm_args* args, void* stream) {
+  CG_REQUIRE(args != nullptr, "gemm: args is NULL");
+  const cg_gemm_args& g = *args;
+  CG_REQUIRE(g.m >= 0 && g.n >= 0 && g.k >= 0, "gemm: negative size");
+  if (g.m == 0 || g.n == 0) return kOk;
+  CG_REQUIRE(g.k >= 1, "gemm: k must be >= 1 (use a fill for k = 0)");
+  CG_REQUIRE(g.m < (1ll << 31) && g.n < (1ll << 31) && g.k < (1ll << 31), "gemm: size too large");
+  CG_REQUIRE(g.a && g.b && g.c, "gemm: a, b and c must be non-null");
+  CG_REQUIRE(aligned16(g.a) && aligned16(g.b), "gemm: a and b must be 16-byte aligned");
+  CG_REQUIRE(g.lda % 4 == 0 && g.ldb % 4 == 0, "gemm: lda and ldb must be multiples of 4 floats");
+  CG_REQUIRE(g.lda >= (g.a_mn_major ? g.m : g.k) && g.ldb >= (g.b_mn_major ? g.n : g.k),
+             "gemm: leading dimension smaller than the contiguous extent");
+  CG_REQUIRE(g.act == CG_ACT_NONE || g.act == CG_ACT_SILU || g.act == CG_ACT_SILU_GRAD, "gemm: bad act");
+  CG_REQUIRE(g.act != CG_ACT_SILU_GRAD || g.aux_in != nullptr, "gemm: SiLU gradient needs aux_in");
+  cudaStream_t s = as_stream(stream);
+  // wider tiles for wide outputs; 64-wide tiles keep small-N problems spread over the SMs
+  if (g.n >= 256 && ceil_div<int64_t>(g.m, BM) * ceil_div<int64_t>(g.n, 256) >= sm_count())
+    return launch_majors<256, 4>(g, s);
+  if (g.n > 64) return launch_majors<128, 6>(g, s);
+  return launch_majors<64, 8>(g, s);
+}
+
+}  // namespace gemm
+}  // namespace cg
+
+extern "C" {
+
+int cg_gemm_tf32(const cg_gemm_args* args, void* stream) { return cg::gemm::run(args, stream); }
+
+int cg_device_error(int* out, int reset) {
+  int v = 0;
+  CG_CUDA(cudaMemcpyFromSymbol(&v, cg::gemm::g_gemm_error, sizeof(int)));
+  if (reset) {
+    const int zero = 0;
+    CG_CUDA(cudaMemcpyToSymbol(cg::gemm::g_gemm_error, &zero, sizeof(int)));
+  }
+  if (out) *out = v;
+  return cg::kOk;
+}
+
+}  // extern "C"

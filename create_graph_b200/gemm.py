@@ -1,0 +1,88 @@
+"""
+The tcgen05 GEMM of the dense projections (``cg_gemm_tf32``), on torch tensors.
+
+``gemm(a, b)`` computes ``a @ b.T`` for a (M, K) and b (N, K); ``a_t=True``
+takes ``a`` as (K, M) and ``b_t=True`` takes ``b`` as (K, N), read in place
+(MN-major operands), so x W^T, g W and g^T x need no transposed copies.
+Arithmetic: tf32 products (fp32 operands rounded by the tensor core), fp32
+accumulation.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+from torch import Tensor
+
+from create_graph_b200 import native
+from create_graph_b200.errors import NativeError
+
+ACT_NONE, ACT_SILU, ACT_SILU_GRAD = native.ACT_NONE, native.ACT_SILU, native.ACT_SILU_GRAD
+
+
+def _operand(t: Tensor, name: str) -> Tensor:
+    if t.dtype != torch.float32:
+        raise NativeError(f"gemm: {name} must be float32, got {t.dtype}")
+    if t.dim() != 2:
+        raise NativeError(f"gemm: {name} must be 2-D, got {tuple(t.shape)}")
+    if t.stride(1) != 1 or t.stride(0) % 4 != 0 or t.data_ptr() % 16 != 0 or t.stride(0) < t.shape[1]:
+        t = t.contiguous()
+        if t.shape[1] % 4 != 0:
+            pitch = (t.shape[1] + 3) // 4 * 4
+            padded = torch.zeros(t.shape[0], pitch, dtype=t.dtype, device=t.device)
+            padded[:, : t.shape[1]] = t
+            t = padded[:, : t.shape[1]]
+    return t
+
+
+def gemm(
+    a: Tensor,
+    b: Tensor,
+    *,
+    a_t: bool = False,
+    b_t: bool = False,
+    bias: Tensor | None = None,
+    act: int = ACT_NONE,
+    aux_in: Tensor | None = None,
+    aux_out: Tensor | None = None,
+    out: Tensor | None = None,
+    accumulate: bool = False,
+    alpha: float = 1.0,
+) -> Tensor:
+    native.require_cuda(a, b, bias, aux_in, aux_out, out)
+    a = _operand(a, "a")
+    b = _operand(b, "b")
+    m, k = (a.shape[1], a.shape[0]) if a_t else (a.shape[0], a.shape[1])
+    n, kb = (b.shape[1], b.shape[0]) if b_t else (b.shape[0], b.shape[1])
+    if k != kb:
+        raise NativeError(f"gemm: inner dimensions differ ({k} vs {kb})")
+    if out is None:
+        if accumulate:
+            raise NativeError("gemm: accumulate needs out")
+        out = torch.empty(m, n, dtype=torch.float32, device=a.device)
+    if out.shape != (m, n) or out.stride(1) != 1:
+        raise NativeError(f"gemm: out must be ({m}, {n}) with unit column stride")
+    if k == 0:
+        if not accumulate:
+            out.zero_()
+        return out
+    args = native.GemmArgs()
+    args.m, args.n, args.k = m, n, k
+    args.a, args.lda = a.data_ptr(), a.stride(0)
+    args.b, args.ldb = b.data_ptr(), b.stride(0)
+    args.c, args.ldc = out.data_ptr(), out.stride(0)
+    if bias is not None:
+        bias = bias.contiguous()
+        args.bias = bias.data_ptr()
+    aux = aux_in if aux_in is not None else aux_out
+    if aux is not None:
+        if aux.shape != (m, n) or aux.stride(1) != 1:
+            raise NativeError(f"gemm: aux must be ({m}, {n}) with unit column stride")
+        args.ld_aux = aux.stride(0)
+    args.aux_in = None if aux_in is None else aux_in.data_ptr()
+    args.aux_out = None if aux_out is None else aux_out.data_ptr()
+    args.a_mn_major, args.b_mn_major = int(a_t), int(b_t)
+    args.act, args.accumulate, args.alpha = act, int(accumulate), float(alpha)
+    native.check(native.lib().cg_gemm_tf32(ctypes.byref(args), native.stream_ptr(a.device)))
+    return out

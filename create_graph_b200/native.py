@@ -66,6 +66,32 @@ class EdgeAttnArgs(ctypes.Structure):
     ]
 
 
+class GemmArgs(ctypes.Structure):
+    _fields_ = [
+        ("m", i64),
+        ("n", i64),
+        ("k", i64),
+        ("a", vp),
+        ("lda", i64),
+        ("b", vp),
+        ("ldb", i64),
+        ("c", vp),
+        ("ldc", i64),
+        ("bias", vp),
+        ("aux_in", vp),
+        ("aux_out", vp),
+        ("ld_aux", i64),
+        ("a_mn_major", i32),
+        ("b_mn_major", i32),
+        ("act", i32),
+        ("accumulate", i32),
+        ("alpha", ctypes.c_float),
+        ("pad0", i32),
+    ]
+
+
+ACT_NONE, ACT_SILU, ACT_SILU_GRAD = 0, 1, 2
+
 # name -> (restype, argtypes)
 _SIGNATURES = {
     "cg_last_error": (ctypes.c_char_p, []),
@@ -74,6 +100,8 @@ _SIGNATURES = {
     "cg_edge_attn_bwd1": (ctypes.c_int, [ctypes.POINTER(EdgeAttnArgs), vp]),
     "cg_edge_attn_bwd2": (ctypes.c_int, [ctypes.POINTER(EdgeAttnArgs), vp]),
     "cg_edge_attn_scratch_bytes": (i64, [ctypes.POINTER(EdgeAttnArgs)]),
+    "cg_gemm_tf32": (ctypes.c_int, [ctypes.POINTER(GemmArgs), vp]),
+    "cg_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
 }
 
 
@@ -131,3 +159,10 @@ def require_cuda(*tensors: torch.Tensor) -> None:
                 "create_graph_b200 fused ops run on CUDA tensors only (no CPU fallback); got a "
                 f"{t.device} tensor"
             )
+
+
+def device_error(reset: bool = False) -> int:
+    """The device error word (non-zero: a kernel's bounded wait gave up)."""
+    out = ctypes.c_int(0)
+    check(lib().cg_device_error(ctypes.byref(out), int(reset)))
+    return out.value

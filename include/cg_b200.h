@@ -96,6 +96,50 @@ int cg_edge_attn_bwd2(const cg_edge_attn_args* a, void* stream);
  * cross-batch part of _reduce (kernels/edge_attn/ops.py:37-44). */
 int64_t cg_edge_attn_scratch_bytes(const cg_edge_attn_args* a);
 
+/* ------------------------------------------------------------------------
+ * Dense projections on the tcgen05 tensor cores (kind::tf32: fp32 operands
+ * rounded to tf32, fp32 accumulation in TMEM):
+ *   C[m, n] = epi( alpha * sum_k A(m, k) B(n, k) )
+ * A(m, k) is a[m*lda + k] (K-major) or a[k*lda + m] (a_mn_major);
+ * B(n, k) is b[n*ldb + k] (K-major) or b[k*ldb + n] (b_mn_major).
+ * epi adds bias[n], then per act:
+ *   CG_ACT_NONE       nothing;
+ *   CG_ACT_SILU       aux_out[m, n] = x (pre-activation), x = silu(x);
+ *   CG_ACT_SILU_GRAD  x *= silu'(aux_in[m, n]);
+ * then C = x, or C += x with accumulate. a, b 16-byte aligned; lda, ldb
+ * multiples of 4. Replaces the nn.Linear (+ activation) GEMMs Inductor
+ * generates inside a compiled region (src/create_graph/region.py:191-198).
+ * ---------------------------------------------------------------------- */
+#define CG_ACT_NONE 0
+#define CG_ACT_SILU 1
+#define CG_ACT_SILU_GRAD 2
+
+typedef struct cg_gemm_args {
+  int64_t m, n, k;
+  const float* a;
+  int64_t lda;
+  const float* b;
+  int64_t ldb;
+  float* c;
+  int64_t ldc;
+  const float* bias;     /* (n,) or NULL */
+  const float* aux_in;   /* CG_ACT_SILU_GRAD: pre-activation, pitch ld_aux */
+  float* aux_out;        /* CG_ACT_SILU: pre-activation out, pitch ld_aux; may be NULL */
+  int64_t ld_aux;
+  int32_t a_mn_major, b_mn_major;
+  int32_t act, accumulate;
+  float alpha;
+  int32_t pad0;
+} cg_gemm_args;
+
+int cg_gemm_tf32(const cg_gemm_args* args, void* stream);
+
+/* The device error word kernels set when a bounded wait gave up (0: none);
+ * reset != 0 clears it. Synchronises with the device. No reference
+ * counterpart: the reference's kernels are generated by Inductor and have no
+ * waits. */
+int cg_device_error(int* out, int reset);
+
 #ifdef __cplusplus
 }
 #endif

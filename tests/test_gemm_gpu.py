@@ -1,0 +1,81 @@
+"""
+The tcgen05 tf32 GEMM (cg_gemm_tf32) against float64 torch matmul.
+
+tf32 keeps 10 explicit mantissa bits per operand and accumulates in fp32, so
+the stated bound is a norm-wise relative error below 3e-3 (observed ~5e-4).
+Covers the four operand layouts (x W^T, g W, g^T x, and both transposed),
+partial tiles, every tile width, bias, the SiLU and SiLU-derivative epilogues,
+accumulation, and that no bounded wait fired.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from create_graph_b200 import native
+from create_graph_b200.gemm import ACT_SILU, ACT_SILU_GRAD, gemm
+
+pytestmark = pytest.mark.gpu
+TF32_TOL = 3e-3
+
+
+def rel(a, b):
+    a, b = a.double(), b.double()
+    return ((a - b).norm() / b.norm()).item()
+
+
+def operands(m, n, k, a_t, b_t, seed=0):
+    gen = torch.Generator().manual_seed(seed)
+    a = torch.randn(m, k, generator=gen)
+    b = torch.randn(n, k, generator=gen)
+    a_dev = (a.t().contiguous() if a_t else a).cuda()
+    b_dev = (b.t().contiguous() if b_t else b).cuda()
+    return a, b, a_dev, b_dev
+
+
+@pytest.mark.parametrize("a_t", [False, True])
+@pytest.mark.parametrize("b_t", [False, True])
+@pytest.mark.parametrize("mnk", [(128, 64, 32), (300, 200, 100), (1000, 2304, 768), (768, 768, 4100), (77, 3072, 768)])
+def test_layouts_and_sizes(a_t, b_t, mnk):
+    m, n, k = mnk
+    a, b, a_dev, b_dev = operands(m, n, k, a_t, b_t)
+    got = gemm(a_dev, b_dev, a_t=a_t, b_t=b_t)
+    torch.cuda.synchronize()
+    assert native.device_error() == 0
+    assert rel(got.cpu(), a.double() @ b.double().T) < TF32_TOL
+
+
+def test_bias_silu_and_saved_preactivation():
+    m, n, k = 513, 384, 256
+    a, b, a_dev, b_dev = operands(m, n, k, False, False, seed=1)
+    bias = torch.randn(n)
+    pre = torch.empty(m, n, device="cuda")
+    got = gemm(a_dev, b_dev, bias=bias.cuda(), act=ACT_SILU, aux_out=pre)
+    z = a.double() @ b.double().T + bias.double()
+    assert rel(pre.cpu(), z) < TF32_TOL
+    assert rel(got.cpu(), torch.nn.functional.silu(z)) < TF32_TOL
+
+
+def test_silu_gradient_epilogue_and_accumulate():
+    m, n, k = 256, 640, 96
+    a, b, a_dev, b_dev = operands(m, n, k, False, True, seed=2)
+    z = torch.randn(m, n)
+    s = torch.sigmoid(z.double())
+    dsilu = s * (1 + z.double() * (1 - s))
+    got = gemm(a_dev, b_dev, b_t=True, act=ACT_SILU_GRAD, aux_in=z.cuda())
+    assert rel(got.cpu(), (a.double() @ b.double().T) * dsilu) < TF32_TOL
+    base = torch.randn(m, n)
+    acc = base.clone().cuda()
+    gemm(a_dev, b_dev, b_t=True, out=acc, accumulate=True, alpha=0.5)
+    assert rel(acc.cpu(), base.double() + 0.5 * a.double() @ b.double().T) < TF32_TOL
+
+
+def test_strided_operands_in_place():
+    """Column slices of wider tensors (a (M, 3C) activation, a sub-block of W)."""
+    gen = torch.Generator().manual_seed(3)
+    big = torch.randn(400, 3 * 96, generator=gen).cuda()
+    w = torch.randn(64, 96, generator=gen).cuda()
+    x = big[:, 96:192]
+    got = gemm(x, w)
+    assert rel(got.cpu(), x.double().cpu() @ w.double().cpu().T) < TF32_TOL
