@@ -133,6 +133,8 @@ def is_python_function_node(node) -> bool:
     """
     if not isinstance(node, torch.autograd.function.BackwardCFunction):
         return False
+    if getattr(getattr(node, "_forward_cls", None), "_cg_fused", False):
+        return False
     name = type(node).__name__
     return not name.startswith("GeneratedBackwardFor")
 
@@ -141,7 +143,12 @@ def gradient_edge(t: torch.Tensor):
     """The autograd node a gradient for ``t`` flows into (None if ``t`` needs none)."""
     if not t.requires_grad:
         return None
-    return torch.autograd.graph.get_gradient_edge(t).node
+    try:
+        return torch.autograd.graph.get_gradient_edge(t).node
+    except AssertionError:
+        # a view made in no-grad mode (inside a backward without create_graph):
+        # the op recording it is never differentiated again
+        return None
 
 
 def engine_will_execute(node) -> bool:

@@ -55,4 +55,10 @@ int sm_count();
 template <typename T>
 __host__ __device__ inline T ceil_div(T a, T b) { return (a + b - 1) / b; }
 
+namespace seg {
+// Row chunking of the two-pass column reductions (segment.cu): `chunks`
+// partial rows of `cols` floats each.
+void colsum_plan(int64_t rows, int64_t cols, int64_t* chunks, int64_t* rows_per);
+}  // namespace seg
+
 }  // namespace cg

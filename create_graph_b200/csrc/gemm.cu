@@ -207,6 +207,11 @@ static int make_map(CUtensorMap* map, const float* ptr, int64_t rows, int64_t co
                     int box_cols, int box_rows, bool mn_major) {
   auto fn = encode_fn();
   CG_REQUIRE(fn != nullptr, "gemm: cuTensorMapEncodeTiled is unavailable");
+  // the driver call needs a current context; threads such as autograd's
+  // backward workers may not have bound the runtime's primary context yet
+  int dev = 0;
+  CG_CUDA(cudaGetDevice(&dev));
+  CG_CUDA(cudaSetDevice(dev));
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(ld * 4)};
   cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};

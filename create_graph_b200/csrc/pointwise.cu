@@ -1,0 +1,332 @@
+// Elementwise and per-row kernels of the energy network: the SiLU derivative
+// family, column scale/shift (LayerNorm's affine part), column dot products,
+// the row normalisation of LayerNorm with its first and second derivatives,
+// and the envelope pooling family (pool / outer / dot).
+//
+// Row kernels put one warp on one row (lanes over the columns), so every row
+// reduction is a fixed-order warp tree: deterministic.
+#include <math.h>
+
+#include "common.cuh"
+#include "../../include/cg_b200.h"
+
+namespace cg {
+namespace pw {
+
+__device__ inline float sigm(float z) { return 1.0f / (1.0f + expf(-z)); }
+// silu(z) = z s, silu' = s (1 + z (1 - s)), silu'' = s (1 - s) (2 + z (1 - 2 s))
+__device__ inline float silu_d1(float z) {
+  const float s = sigm(z);
+  return s * (1.0f + z * (1.0f - s));
+}
+__device__ inline float silu_d2(float z) {
+  const float s = sigm(z);
+  return s * (1.0f - s) * (2.0f + z * (1.0f - 2.0f * s));
+}
+
+__device__ inline float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+inline int blocks_for(int64_t n, int threads) {
+  const int64_t b = ceil_div<int64_t>(n, threads);
+  const int64_t cap = (int64_t)sm_count() * 32;
+  return (int)(b < 1 ? 1 : (b < cap ? b : cap));
+}
+
+// mode 0: out = a * silu'(z); mode 1: out = a * b * silu''(z)
+__global__ void silu_grad_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                                 const float* __restrict__ z, float* __restrict__ out, int64_t n,
+                                 int mode) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    out[i] = mode == 0 ? a[i] * silu_d1(z[i]) : a[i] * b[i] * silu_d2(z[i]);
+  }
+}
+
+// out[r, c] = x[r, c] * (gamma ? gamma[c] : 1) + (beta ? beta[c] : 0)
+__global__ void scale_shift_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+                                   const float* __restrict__ beta, float* __restrict__ out,
+                                   int64_t rows, int64_t cols) {
+  const int64_t n = rows * cols;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c = i % cols;
+    float v = x[i];
+    if (gamma) v *= gamma[c];
+    if (beta) v += beta[c];
+    out[i] = v;
+  }
+}
+
+// partial[chunk, c] = sum over the chunk's rows of a[r, c] * b[r, c]
+__global__ void coldot_partial_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                                      int64_t rows, int64_t cols, int64_t rows_per,
+                                      float* __restrict__ partial) {
+  __shared__ float red[8][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t c = blockIdx.x * 32ll + tx;
+  const int64_t r0 = blockIdx.y * rows_per;
+  const int64_t r1 = r0 + rows_per < rows ? r0 + rows_per : rows;
+  float acc = 0.0f;
+  if (c < cols)
+    for (int64_t r = r0 + ty; r < r1; r += 8) acc += a[r * cols + c] * b[r * cols + c];
+  red[ty][tx] = acc;
+  __syncthreads();
+  if (ty == 0 && c < cols) {
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += red[i][tx];
+    partial[blockIdx.y * cols + c] = s;
+  }
+}
+
+__global__ void partial_final_kernel(const float* __restrict__ partial, int64_t chunks, int64_t cols,
+                                     float* __restrict__ out, bool accumulate) {
+  const int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  float s = 0.0f;
+  for (int64_t k = 0; k < chunks; ++k) s += partial[k * cols + c];
+  out[c] = accumulate ? out[c] + s : s;
+}
+
+// ---- row normalisation: xhat = (x - mean) / sqrt(var + eps) -----------------
+// Per row stats: mean, rstd. One warp per row.
+__global__ void rownorm_fwd_kernel(const float* __restrict__ x, int64_t rows, int cols, float eps,
+                                   float* __restrict__ xhat, float* __restrict__ rstd_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp; r < rows; r += warps) {
+    const float* xr = x + r * cols;
+    float s = 0.0f;
+    for (int c = lane; c < cols; c += 32) s += xr[c];
+    const float mean = warp_sum(s) / cols;
+    float v = 0.0f;
+    for (int c = lane; c < cols; c += 32) {
+      const float d = xr[c] - mean;
+      v += d * d;
+    }
+    const float rstd = rsqrtf(warp_sum(v) / cols + eps);
+    for (int c = lane; c < cols; c += 32) xhat[r * cols + c] = (xr[c] - mean) * rstd;
+    if (lane == 0 && rstd_out) rstd_out[r] = rstd;
+  }
+}
+
+// gx = rstd * (g - mean(g) - xhat * mean(g * xhat))
+// With h (second-order mode), also d_g = rstd * (h - mean(h) - xhat mean(h xhat)) and
+// d_x = -xhat (mean(h g) - mean(g) mean(h)) rstd^2 - rstd (c gx' + b hx') + b c xhat rstd^2
+// where b = mean(g xhat), c = mean(h xhat), gx' = rstd (g - mean g - xhat b),
+// hx' = rstd (h - mean h - xhat c).
+__global__ void rownorm_bwd_kernel(const float* __restrict__ x, const float* __restrict__ g,
+                                   const float* __restrict__ h, int64_t rows, int cols, float eps,
+                                   float* __restrict__ out_a, float* __restrict__ out_b) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp; r < rows; r += warps) {
+    const float* xr = x + r * cols;
+    const float* gr = g + r * cols;
+    float s = 0.0f;
+    for (int c = lane; c < cols; c += 32) s += xr[c];
+    const float mean = warp_sum(s) / cols;
+    float v = 0.0f;
+    for (int c = lane; c < cols; c += 32) {
+      const float d = xr[c] - mean;
+      v += d * d;
+    }
+    const float rstd = rsqrtf(warp_sum(v) / cols + eps);
+    float sg = 0.0f, sgx = 0.0f;
+    for (int c = lane; c < cols; c += 32) {
+      const float xh = (xr[c] - mean) * rstd;
+      sg += gr[c];
+      sgx += gr[c] * xh;
+    }
+    const float a = warp_sum(sg) / cols, b = warp_sum(sgx) / cols;
+    if (h == nullptr) {
+      for (int c = lane; c < cols; c += 32) {
+        const float xh = (xr[c] - mean) * rstd;
+        out_a[r * cols + c] = rstd * (gr[c] - a - xh * b);
+      }
+      continue;
+    }
+    const float* hr = h + r * cols;
+    float sh = 0.0f, shx = 0.0f, shg = 0.0f;
+    for (int c = lane; c < cols; c += 32) {
+      const float xh = (xr[c] - mean) * rstd;
+      sh += hr[c];
+      shx += hr[c] * xh;
+      shg += hr[c] * gr[c];
+    }
+    const float mh = warp_sum(sh) / cols, cc = warp_sum(shx) / cols, mhg = warp_sum(shg) / cols;
+    const float r2 = rstd * rstd;
+    for (int c = lane; c < cols; c += 32) {
+      const float xh = (xr[c] - mean) * rstd;
+      const float gx = rstd * (gr[c] - a - xh * b);
+      const float hx = rstd * (hr[c] - mh - xh * cc);
+      out_b[r * cols + c] = hx;  // d_g
+      out_a[r * cols + c] = -xh * (mhg - a * mh) * r2 - (cc * gx + b * hx) * rstd + b * cc * xh * r2;
+    }
+  }
+}
+
+// ---- envelope pooling over the k tokens of each n ------------------------------
+// pool:  out[n, c]    = sum_s w[n, s] x[n, s, c]
+// outer: out[n, s, c] = w[n, s] g[n, c]
+// dot:   out[n, s]    = sum_c g[n, c] x[n, s, c]
+__global__ void pool_kernel(const float* __restrict__ x, const float* __restrict__ w, int64_t n,
+                            int k, int64_t cols, float* __restrict__ out) {
+  const int64_t total = n * cols;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / cols, c = i % cols;
+    const float* xr = x + r * k * cols + c;
+    const float* wr = w + r * k;
+    float acc = 0.0f;
+    for (int s = 0; s < k; ++s) acc += wr[s] * xr[(int64_t)s * cols];
+    out[i] = acc;
+  }
+}
+
+__global__ void outer_kernel(const float* __restrict__ w, const float* __restrict__ g, int64_t n, int k,
+                             int64_t cols, float* __restrict__ out) {
+  const int64_t total = n * k * cols;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c = i % cols, rs = i / cols, r = rs / k;
+    out[i] = w[rs] * g[r * cols + c];
+  }
+}
+
+__global__ void dot_kernel(const float* __restrict__ g, const float* __restrict__ x, int64_t n, int k,
+                           int64_t cols, float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t rs = warp; rs < n * k; rs += warps) {
+    const int64_t r = rs / k;
+    const float* xr = x + rs * cols;
+    const float* gr = g + r * cols;
+    float acc = 0.0f;
+    for (int64_t c = lane; c < cols; c += 32) acc += gr[c] * xr[c];
+    acc = warp_sum(acc);
+    if (lane == 0) out[rs] = acc;
+  }
+}
+
+}  // namespace pw
+}  // namespace cg
+
+extern "C" {
+
+using namespace cg;
+
+int cg_silu_grad(const float* a, const float* z, float* out, int64_t n, void* stream) {
+  CG_REQUIRE(n >= 0, "silu_grad: negative size");
+  if (n == 0) return kOk;
+  pw::silu_grad_kernel<<<pw::blocks_for(n, 256), 256, 0, as_stream(stream)>>>(a, nullptr, z, out, n, 0);
+  CG_LAUNCHED("silu_grad");
+  return kOk;
+}
+
+int cg_silu_grad2(const float* a, const float* b, const float* z, float* out, int64_t n, void* stream) {
+  CG_REQUIRE(n >= 0, "silu_grad2: negative size");
+  if (n == 0) return kOk;
+  pw::silu_grad_kernel<<<pw::blocks_for(n, 256), 256, 0, as_stream(stream)>>>(a, b, z, out, n, 1);
+  CG_LAUNCHED("silu_grad2");
+  return kOk;
+}
+
+int cg_scale_shift(const float* x, const float* gamma, const float* beta, float* out, int64_t rows,
+                   int64_t cols, void* stream) {
+  CG_REQUIRE(rows >= 0 && cols >= 0, "scale_shift: negative size");
+  if (rows * cols == 0) return kOk;
+  pw::scale_shift_kernel<<<pw::blocks_for(rows * cols, 256), 256, 0, as_stream(stream)>>>(x, gamma, beta,
+                                                                                          out, rows, cols);
+  CG_LAUNCHED("scale_shift");
+  return kOk;
+}
+
+int64_t cg_coldot_scratch_bytes(int64_t rows, int64_t cols) { return cg_colsum_scratch_bytes(rows, cols); }
+
+int cg_coldot(const float* a, const float* b, int64_t rows, int64_t cols, float* out, int accumulate,
+              float* scratch, void* stream) {
+  CG_REQUIRE(rows >= 0 && cols >= 0, "coldot: negative size");
+  if (cols == 0) return kOk;
+  if (rows == 0) {
+    if (!accumulate) CG_CUDA(cudaMemsetAsync(out, 0, cols * sizeof(float), as_stream(stream)));
+    return kOk;
+  }
+  CG_REQUIRE(a && b && out && scratch, "coldot: null pointer");
+  int64_t chunks, per;
+  cg::seg::colsum_plan(rows, cols, &chunks, &per);
+  dim3 grid((unsigned)ceil_div<int64_t>(cols, 32), (unsigned)chunks);
+  pw::coldot_partial_kernel<<<grid, 256, 0, as_stream(stream)>>>(a, b, rows, cols, per, scratch);
+  CG_LAUNCHED("coldot_partial");
+  pw::partial_final_kernel<<<(unsigned)ceil_div<int64_t>(cols, 256), 256, 0, as_stream(stream)>>>(
+      scratch, chunks, cols, out, accumulate != 0);
+  CG_LAUNCHED("coldot_final");
+  return kOk;
+}
+
+int cg_rownorm_fwd(const float* x, int64_t rows, int64_t cols, float eps, float* xhat, float* rstd,
+                   void* stream) {
+  CG_REQUIRE(rows >= 0 && cols >= 1 && cols < (1 << 30), "rownorm: bad size");
+  if (rows == 0) return kOk;
+  pw::rownorm_fwd_kernel<<<pw::blocks_for(rows * 32, 256), 256, 0, as_stream(stream)>>>(x, rows, (int)cols,
+                                                                                        eps, xhat, rstd);
+  CG_LAUNCHED("rownorm_fwd");
+  return kOk;
+}
+
+int cg_rownorm_bwd1(const float* x, const float* g, int64_t rows, int64_t cols, float eps, float* gx,
+                    void* stream) {
+  CG_REQUIRE(rows >= 0 && cols >= 1 && cols < (1 << 30), "rownorm: bad size");
+  if (rows == 0) return kOk;
+  pw::rownorm_bwd_kernel<<<pw::blocks_for(rows * 32, 256), 256, 0, as_stream(stream)>>>(
+      x, g, nullptr, rows, (int)cols, eps, gx, nullptr);
+  CG_LAUNCHED("rownorm_bwd1");
+  return kOk;
+}
+
+int cg_rownorm_bwd2(const float* x, const float* g, const float* h, int64_t rows, int64_t cols, float eps,
+                    float* d_x, float* d_g, void* stream) {
+  CG_REQUIRE(rows >= 0 && cols >= 1 && cols < (1 << 30), "rownorm: bad size");
+  if (rows == 0) return kOk;
+  CG_REQUIRE(h != nullptr, "rownorm_bwd2: h is NULL");
+  pw::rownorm_bwd_kernel<<<pw::blocks_for(rows * 32, 256), 256, 0, as_stream(stream)>>>(
+      x, g, h, rows, (int)cols, eps, d_x, d_g);
+  CG_LAUNCHED("rownorm_bwd2");
+  return kOk;
+}
+
+int cg_pool(const float* x, const float* w, int64_t n, int64_t k, int64_t cols, float* out, void* stream) {
+  CG_REQUIRE(n >= 0 && k >= 0 && cols >= 0 && k < (1 << 30), "pool: bad size");
+  if (n * cols == 0) return kOk;
+  pw::pool_kernel<<<pw::blocks_for(n * cols, 256), 256, 0, as_stream(stream)>>>(x, w, n, (int)k, cols, out);
+  CG_LAUNCHED("pool");
+  return kOk;
+}
+
+int cg_pool_outer(const float* w, const float* g, int64_t n, int64_t k, int64_t cols, float* out,
+                  void* stream) {
+  CG_REQUIRE(n >= 0 && k >= 0 && cols >= 0 && k < (1 << 30), "pool_outer: bad size");
+  if (n * k * cols == 0) return kOk;
+  pw::outer_kernel<<<pw::blocks_for(n * k * cols, 256), 256, 0, as_stream(stream)>>>(w, g, n, (int)k, cols,
+                                                                                     out);
+  CG_LAUNCHED("pool_outer");
+  return kOk;
+}
+
+int cg_pool_dot(const float* g, const float* x, int64_t n, int64_t k, int64_t cols, float* out,
+                void* stream) {
+  CG_REQUIRE(n >= 0 && k >= 0 && cols >= 0 && k < (1 << 30), "pool_dot: bad size");
+  if (n * k == 0) return kOk;
+  pw::dot_kernel<<<pw::blocks_for(n * k * 32, 256), 256, 0, as_stream(stream)>>>(g, x, n, (int)k, cols, out);
+  CG_LAUNCHED("pool_dot");
+  return kOk;
+}
+
+}  // extern "C"

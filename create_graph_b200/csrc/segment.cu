@@ -1,0 +1,192 @@
+// Deterministic segment sums over a sorted CSR layout, their transpose (row
+// gathers), and column sums.
+//
+// The reference's models reduce edges to atoms and atoms to systems with
+// index_add (tests/test_semantics.py:68-69 there), which on a GPU is an
+// atomic scatter whose summation order changes from run to run. Here every
+// reduction reads its terms in a fixed order: one warp owns one output row
+// and walks its CSR segment sequentially, lanes spread over the columns with
+// 16-byte accesses, so results are bitwise reproducible.
+#include "common.cuh"
+#include "../../include/cg_b200.h"
+
+namespace cg {
+namespace seg {
+
+// out[e, :] = index[e] >= 0 ? src[index[e], :] : 0
+__global__ void gather_rows_kernel(const float* __restrict__ src, int64_t ld_src,
+                                   const int32_t* __restrict__ index, int64_t n_out, int64_t cols,
+                                   float* __restrict__ out, int64_t ld_out, bool vec) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t e = warp; e < n_out; e += warps) {
+    const int32_t r = index[e];
+    float* dst = out + e * ld_out;
+    if (vec) {
+      const float4* s4 = reinterpret_cast<const float4*>(src + (int64_t)(r < 0 ? 0 : r) * ld_src);
+      float4* d4 = reinterpret_cast<float4*>(dst);
+      for (int64_t c = lane; c < cols / 4; c += 32) d4[c] = r >= 0 ? __ldg(s4 + c) : make_float4(0, 0, 0, 0);
+    } else {
+      for (int64_t c = lane; c < cols; c += 32) dst[c] = r >= 0 ? src[(int64_t)r * ld_src + c] : 0.0f;
+    }
+  }
+}
+
+// out[r, :] (+)= sum over e in [row_ptr[r], row_ptr[r+1]) of src[perm ? perm[e] : e, :],
+// in increasing e.
+__global__ void segment_sum_kernel(const float* __restrict__ src, int64_t ld_src,
+                                   const int32_t* __restrict__ row_ptr,
+                                   const int32_t* __restrict__ perm, int64_t n_rows, int64_t cols,
+                                   float* __restrict__ out, int64_t ld_out, bool accumulate, bool vec) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp; r < n_rows; r += warps) {
+    const int32_t e0 = row_ptr[r], e1 = row_ptr[r + 1];
+    float* dst = out + r * ld_out;
+    if (vec) {
+      float4* d4 = reinterpret_cast<float4*>(dst);
+      for (int64_t c = lane; c < cols / 4; c += 32) {
+        float4 acc = accumulate ? d4[c] : make_float4(0, 0, 0, 0);
+        for (int32_t e = e0; e < e1; ++e) {
+          const int64_t s = perm ? perm[e] : e;
+          const float4 v = __ldg(reinterpret_cast<const float4*>(src + s * ld_src) + c);
+          acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+        }
+        d4[c] = acc;
+      }
+    } else {
+      for (int64_t c = lane; c < cols; c += 32) {
+        float acc = accumulate ? dst[c] : 0.0f;
+        for (int32_t e = e0; e < e1; ++e) {
+          const int64_t s = perm ? perm[e] : e;
+          acc += src[s * ld_src + c];
+        }
+        dst[c] = acc;
+      }
+    }
+  }
+}
+
+// Column sums in two fixed-order passes: block (cb, chunk) sums rows
+// [chunk*rows_per, (chunk+1)*rows_per) of 32 columns into partial[chunk, :];
+// then one thread per column adds the partials in chunk order.
+constexpr int kColTile = 32;
+constexpr int kRowsPerThread = 8;
+
+__global__ void colsum_partial_kernel(const float* __restrict__ src, int64_t ld, int64_t rows,
+                                      int64_t cols, int64_t rows_per, float* __restrict__ partial) {
+  __shared__ float red[8][kColTile + 1];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
+  const int64_t c = blockIdx.x * (int64_t)kColTile + tx;
+  const int64_t r0 = blockIdx.y * rows_per;
+  const int64_t r1 = r0 + rows_per < rows ? r0 + rows_per : rows;
+  float acc = 0.0f;
+  if (c < cols)
+    for (int64_t r = r0 + ty; r < r1; r += 8) acc += src[r * ld + c];
+  red[ty][tx] = acc;
+  __syncthreads();
+  if (ty == 0 && c < cols) {
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += red[i][tx];
+    partial[blockIdx.y * cols + c] = s;
+  }
+}
+
+__global__ void colsum_final_kernel(const float* __restrict__ partial, int64_t chunks, int64_t cols,
+                                    float* __restrict__ out, bool accumulate) {
+  const int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  float s = 0.0f;
+  for (int64_t k = 0; k < chunks; ++k) s += partial[k * cols + c];
+  out[c] = accumulate ? out[c] + s : s;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+static int grid_for_warps(int64_t items) {
+  const int64_t blocks = ceil_div<int64_t>(items, 8);  // 8 warps per 256-thread block
+  const int64_t cap = (int64_t)sm_count() * 16;
+  return (int)(blocks < 1 ? 1 : (blocks < cap ? blocks : cap));
+}
+
+void colsum_plan(int64_t rows, int64_t cols, int64_t* chunks, int64_t* rows_per) {
+  // enough row chunks to fill the GPU, each at least 64 rows
+  const int64_t col_blocks = ceil_div<int64_t>(cols, kColTile);
+  int64_t want = ceil_div<int64_t>((int64_t)sm_count() * 8, col_blocks);
+  int64_t per = ceil_div<int64_t>(rows, want < 1 ? 1 : want);
+  if (per < 64) per = 64;
+  *rows_per = per;
+  *chunks = ceil_div<int64_t>(rows, per);
+}
+
+int colsum_launch(const float* src, int64_t ld, int64_t rows, int64_t cols, float* out, int accumulate,
+                  float* partial, cudaStream_t s) {
+  int64_t chunks, per;
+  colsum_plan(rows, cols, &chunks, &per);
+  dim3 grid((unsigned)ceil_div<int64_t>(cols, kColTile), (unsigned)chunks);
+  colsum_partial_kernel<<<grid, 256, 0, s>>>(src, ld, rows, cols, per, partial);
+  CG_LAUNCHED("colsum_partial");
+  colsum_final_kernel<<<(unsigned)ceil_div<int64_t>(cols, 256), 256, 0, s>>>(partial, chunks, cols, out,
+                                                                               accumulate != 0);
+  CG_LAUNCHED("colsum_final");
+  return kOk;
+}
+
+}  // namespace seg
+}  // namespace cg
+
+extern "C" {
+
+int cg_gather_rows(const float* src, int64_t ld_src, const int32_t* index, int64_t n_out, int64_t cols,
+                   float* out, int64_t ld_out, void* stream) {
+  using namespace cg;
+  CG_REQUIRE(n_out >= 0 && cols >= 0, "gather_rows: negative size");
+  if (n_out == 0 || cols == 0) return kOk;
+  CG_REQUIRE(src && index && out, "gather_rows: null pointer");
+  const bool vec = cols % 4 == 0 && ld_src % 4 == 0 && ld_out % 4 == 0 && seg::aligned16(src) &&
+                   seg::aligned16(out);
+  seg::gather_rows_kernel<<<seg::grid_for_warps(n_out), 256, 0, as_stream(stream)>>>(
+      src, ld_src, index, n_out, cols, out, ld_out, vec);
+  CG_LAUNCHED("gather_rows");
+  return kOk;
+}
+
+int cg_segment_sum(const float* src, int64_t ld_src, const int32_t* row_ptr, const int32_t* perm,
+                   int64_t n_rows, int64_t cols, float* out, int64_t ld_out, int accumulate,
+                   void* stream) {
+  using namespace cg;
+  CG_REQUIRE(n_rows >= 0 && cols >= 0, "segment_sum: negative size");
+  if (n_rows == 0 || cols == 0) return kOk;
+  CG_REQUIRE(src && row_ptr && out, "segment_sum: null pointer");
+  const bool vec = cols % 4 == 0 && ld_src % 4 == 0 && ld_out % 4 == 0 && seg::aligned16(src) &&
+                   seg::aligned16(out);
+  seg::segment_sum_kernel<<<seg::grid_for_warps(n_rows), 256, 0, as_stream(stream)>>>(
+      src, ld_src, row_ptr, perm, n_rows, cols, out, ld_out, accumulate != 0, vec);
+  CG_LAUNCHED("segment_sum");
+  return kOk;
+}
+
+int64_t cg_colsum_scratch_bytes(int64_t rows, int64_t cols) {
+  if (rows <= 0 || cols <= 0) return 0;
+  int64_t chunks, per;
+  cg::seg::colsum_plan(rows, cols, &chunks, &per);
+  return chunks * cols * (int64_t)sizeof(float);
+}
+
+int cg_colsum(const float* src, int64_t ld, int64_t rows, int64_t cols, float* out, int accumulate,
+              float* scratch, void* stream) {
+  using namespace cg;
+  CG_REQUIRE(rows >= 0 && cols >= 0, "colsum: negative size");
+  if (cols == 0) return kOk;
+  if (rows == 0) {
+    if (!accumulate) CG_CUDA(cudaMemsetAsync(out, 0, cols * sizeof(float), as_stream(stream)));
+    return kOk;
+  }
+  CG_REQUIRE(src && out && scratch, "colsum: null pointer (scratch: cg_colsum_scratch_bytes bytes)");
+  return seg::colsum_launch(src, ld, rows, cols, out, accumulate, scratch, as_stream(stream));
+}
+
+}  // extern "C"

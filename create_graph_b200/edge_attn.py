@@ -227,3 +227,90 @@ class EdgeAttention:
 def edge_attention(q, k, v, bias, scale: float) -> Tensor:
     """``softmax(q k^T * scale + bias) v`` through the fused op."""
     return EdgeAttention(q, k, v, bias, scale)[0]
+
+
+# ---------------------------------------------------------------------------
+# Token layout of the energy network: per atom n, k edge tokens, each row of
+# tok (n*k, 3*h*d) holding [q | k | v] with heads contiguous; the per-key
+# bias is (n*k, h); keys j >= counts[n] are masked.
+# ---------------------------------------------------------------------------
+
+
+def _token_mats(t: Tensor, n: int, k: int, heads: int, d: int, parts: int):
+    """cg_mat views of the `parts` blocks of a token tensor (n*k, parts*h*d)."""
+    c = heads * d
+    width = parts * c
+    esz = t.element_size()
+    return [native.Mat(t.data_ptr() + p * c * esz, k * width, d, width) for p in range(parts)]
+
+
+def _token_bias(t: Tensor | None, k: int, heads: int) -> native.Bias:
+    if t is None:
+        return native.Bias(None, 0, 0, 0, 0)
+    return native.Bias(t.data_ptr(), k * heads, 1, 0, heads)
+
+
+def _token_args(tok: Tensor, bias: Tensor, counts: Tensor, heads: int, scale: float):
+    native.require_cuda(tok, bias, counts)
+    if tok.dtype != torch.float32 or bias.dtype != torch.float32 or counts.dtype != torch.int32:
+        raise NativeError("token attention: tok and bias float32, counts int32")
+    n = counts.shape[0]
+    k = tok.shape[0] // max(n, 1)
+    d = tok.shape[1] // (3 * heads)
+    if tok.shape[0] != n * k or tok.shape[1] != 3 * heads * d or bias.shape[0] != n * k or bias.shape[-1] != heads:
+        raise NativeError(f"token attention: tok {tuple(tok.shape)}, bias {tuple(bias.shape)}, counts {n}")
+    a = native.EdgeAttnArgs()
+    a.n, a.h, a.k, a.d = n, heads, k, d
+    a.dtype = native.F32
+    a.scale = float(scale)
+    a.key_count = counts.data_ptr()
+    a.q, a.k_, a.v = _token_mats(tok, n, k, heads, d, 3)
+    a.bias = _token_bias(bias, k, heads)
+    return a, n, k, d
+
+
+def _run(fn: str, a, device) -> None:
+    native.check(getattr(native.lib(), fn)(ctypes.byref(a), native.stream_ptr(device)))
+
+
+def token_attention_forward1(tok, bias, counts, heads, scale):
+    tok, bias = tok.contiguous(), bias.contiguous()
+    a, n, k, d = _token_args(tok, bias, counts, heads, scale)
+    out = torch.empty(n, k, heads * d, device=tok.device)
+    lse = torch.empty(n, heads, k, device=tok.device)
+    (a.out,) = _token_mats(out, n, k, heads, d, 1)
+    a.lse = lse.data_ptr()
+    _run("cg_edge_attn_fwd1", a, tok.device)
+    return out, lse
+
+
+def token_attention_backward1(tok, bias, lse, g, counts, heads, scale):
+    tok, bias, g = tok.contiguous(), bias.contiguous(), g.contiguous()
+    a, n, k, d = _token_args(tok, bias, counts, heads, scale)
+    a.lse = lse.data_ptr()
+    (a.grad_out,) = _token_mats(g, n, k, heads, d, 1)
+    dtok = torch.empty_like(tok)
+    dbias = torch.empty_like(bias)
+    a.dq, a.dk, a.dv = _token_mats(dtok, n, k, heads, d, 3)
+    a.dbias = _token_bias(dbias, k, heads)
+    _run("cg_edge_attn_bwd1", a, tok.device)
+    return dtok, dbias
+
+
+def token_attention_backward2(tok, bias, lse, g, h_tok, h_bias, counts, heads, scale):
+    tok, bias, g, h_tok = tok.contiguous(), bias.contiguous(), g.contiguous(), h_tok.contiguous()
+    a, n, k, d = _token_args(tok, bias, counts, heads, scale)
+    a.lse = lse.data_ptr()
+    (a.grad_out,) = _token_mats(g, n, k, heads, d, 1)
+    a.hq, a.hk, a.hv = _token_mats(h_tok, n, k, heads, d, 3)
+    if h_bias is not None:
+        h_bias = h_bias.contiguous()
+        a.hb = _token_bias(h_bias, k, heads)
+    dtok = torch.empty_like(tok)
+    dbias = torch.empty_like(bias)
+    dg = torch.empty_like(g)
+    a.dq, a.dk, a.dv = _token_mats(dtok, n, k, heads, d, 3)
+    a.dbias = _token_bias(dbias, k, heads)
+    (a.dgrad_out,) = _token_mats(dg, n, k, heads, d, 1)
+    _run("cg_edge_attn_bwd2", a, tok.device)
+    return dtok, dbias, dg

@@ -90,7 +90,23 @@ class GemmArgs(ctypes.Structure):
     ]
 
 
+class GeomArgs(ctypes.Structure):
+    _fields_ = [
+        ("pos", vp),
+        ("nbr", vp),
+        ("rev_ptr", vp),
+        ("rev_idx", vp),
+        ("n_atoms", i64),
+        ("k", i32),
+        ("n_rbf", i32),
+        ("cutoff", ctypes.c_float),
+        ("gamma", ctypes.c_float),
+    ]
+
+
 ACT_NONE, ACT_SILU, ACT_SILU_GRAD = 0, 1, 2
+f32 = ctypes.c_float
+_I = ctypes.c_int
 
 # name -> (restype, argtypes)
 _SIGNATURES = {
@@ -102,6 +118,24 @@ _SIGNATURES = {
     "cg_edge_attn_scratch_bytes": (i64, [ctypes.POINTER(EdgeAttnArgs)]),
     "cg_gemm_tf32": (ctypes.c_int, [ctypes.POINTER(GemmArgs), vp]),
     "cg_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
+    "cg_gather_rows": (_I, [vp, i64, vp, i64, i64, vp, i64, vp]),
+    "cg_segment_sum": (_I, [vp, i64, vp, vp, i64, i64, vp, i64, _I, vp]),
+    "cg_colsum_scratch_bytes": (i64, [i64, i64]),
+    "cg_colsum": (_I, [vp, i64, i64, i64, vp, _I, vp, vp]),
+    "cg_coldot_scratch_bytes": (i64, [i64, i64]),
+    "cg_coldot": (_I, [vp, vp, i64, i64, vp, _I, vp, vp]),
+    "cg_silu_grad": (_I, [vp, vp, vp, i64, vp]),
+    "cg_silu_grad2": (_I, [vp, vp, vp, vp, i64, vp]),
+    "cg_scale_shift": (_I, [vp, vp, vp, vp, i64, i64, vp]),
+    "cg_rownorm_fwd": (_I, [vp, i64, i64, f32, vp, vp, vp]),
+    "cg_rownorm_bwd1": (_I, [vp, vp, i64, i64, f32, vp, vp]),
+    "cg_rownorm_bwd2": (_I, [vp, vp, vp, i64, i64, f32, vp, vp, vp]),
+    "cg_pool": (_I, [vp, vp, i64, i64, i64, vp, vp]),
+    "cg_pool_outer": (_I, [vp, vp, i64, i64, i64, vp, vp]),
+    "cg_pool_dot": (_I, [vp, vp, i64, i64, i64, vp, vp]),
+    "cg_edge_geom_fwd": (_I, [ctypes.POINTER(GeomArgs), vp, vp, vp]),
+    "cg_edge_geom_bwd1": (_I, [ctypes.POINTER(GeomArgs), vp, vp, vp, vp, vp]),
+    "cg_edge_geom_bwd2": (_I, [ctypes.POINTER(GeomArgs), vp, vp, vp, vp, vp, vp, vp, vp]),
 }
 
 
@@ -166,3 +200,13 @@ def device_error(reset: bool = False) -> int:
     out = ctypes.c_int(0)
     check(lib().cg_device_error(ctypes.byref(out), int(reset)))
     return out.value
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    """Device address of a tensor (None for None)."""
+    return None if t is None else t.data_ptr()
+
+
+def call(name: str, *args) -> None:
+    """Call a status-returning entry point; the last argument is the stream."""
+    check(getattr(lib(), name)(*args))

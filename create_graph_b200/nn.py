@@ -1,0 +1,607 @@
+"""
+Fused, twice-differentiable ops of the energy network and the modules built
+from them.
+
+Every op is an autograd Function whose forward and backward run sm_100a
+kernels from libcg_b200.so. Under ``cg.create_graph`` the force pass is
+autograd calling these backwards with ``create_graph=True``, and
+``loss.backward()`` differentiates them once more:
+
+- bilinear ops (``mm`` on the tcgen05 GEMM, gather / segment sum over a
+  sorted CSR, envelope pooling, column scale / dot / sum) write their
+  backward with ops of the same family, so their second derivative is again
+  those kernels;
+- nonlinear ops (edge attention, edge geometry, row normalisation, the SiLU
+  derivative) have explicit backward2 kernels.
+
+Backwards skip the gradients nobody asked for: during the force pass the
+parameters' gradients are not computed (``engine_will_execute``), which
+removes the weight-gradient GEMMs from it.
+
+These Functions are the package's own fused kernels, not user
+``torch.autograd.Function``s, so regions accept them on the differentiated
+path (``_cg_fused``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import dataclasses
+import math
+
+import torch
+from torch import Tensor, nn
+
+from create_graph_b200 import native
+from create_graph_b200.compile_config import engine_will_execute, gradient_edge
+from create_graph_b200.edge_attn import token_attention_backward1, token_attention_backward2, token_attention_forward1
+from create_graph_b200.errors import NativeError
+from create_graph_b200.gemm import ACT_SILU, gemm
+
+Function = torch.autograd.Function
+
+
+def _stream() -> int:
+    return native.stream_ptr()
+
+
+class _Fused(Function):
+    """Marker base: the package's fused ops (accepted on the differentiated path)."""
+
+    _cg_fused = True
+
+
+def _edges(*tensors):
+    return [gradient_edge(t) if isinstance(t, Tensor) else None for t in tensors]
+
+
+def _wanted(ctx, i: int) -> bool:
+    """Whether input i's gradient is needed by the backward pass running now."""
+    return ctx.needs_input_grad[i] and engine_will_execute(ctx.edges[i])
+
+
+def _f32(t: Tensor, name: str) -> Tensor:
+    native.require_cuda(t)
+    if t.dtype != torch.float32:
+        raise NativeError(f"{name}: float32 expected, got {t.dtype}")
+    return t if t.is_contiguous() else t.contiguous()
+
+
+# ---------------------------------------------------------------------------
+# GEMM family: mm(a, b) = a @ b.T on the tcgen05 kernel
+# ---------------------------------------------------------------------------
+
+
+def _mm_operand(t: Tensor) -> tuple[Tensor, bool]:
+    """(tensor, mn_major) for a logical (rows, K) operand: row-contiguous tensors
+    are K-major, transposed views of row-contiguous tensors are MN-major."""
+    if t.stride(-1) == 1 and t.stride(0) >= t.shape[1]:
+        return t, False
+    if t.stride(0) == 1 and t.stride(1) >= t.shape[0]:
+        return t.t(), True
+    return t.contiguous(), False
+
+
+def mm_raw(a: Tensor, b: Tensor, **kw) -> Tensor:
+    A, at = _mm_operand(a)
+    B, bt = _mm_operand(b)
+    return gemm(A, B, a_t=at, b_t=bt, **kw)
+
+
+class MM(_Fused):
+    """C = a @ b.T (a (M, K), b (N, K)); backward: g @ b and g.T @ a."""
+
+    @staticmethod
+    def forward(ctx, a, b):
+        ctx.save_for_backward(a, b)
+        ctx.edges = _edges(a, b)
+        return mm_raw(a, b)
+
+    @staticmethod
+    def backward(ctx, g):
+        a, b = ctx.saved_tensors
+        ga = MM.apply(g, b.t()) if _wanted(ctx, 0) else None
+        gb = MM.apply(g.t(), a.t()) if _wanted(ctx, 1) else None
+        return ga, gb
+
+
+def mm(a: Tensor, b: Tensor) -> Tensor:
+    return MM.apply(a, b)
+
+
+class ColSum(_Fused):
+    """out[c] = sum_r x[r, c] (deterministic two-pass reduction)."""
+
+    @staticmethod
+    def forward(ctx, x):
+        x = _f32(x, "colsum")
+        ctx.rows = x.shape[0]
+        out = torch.empty(x.shape[1], device=x.device)
+        nbytes = native.lib().cg_colsum_scratch_bytes(x.shape[0], x.shape[1])
+        scratch = torch.empty(max(nbytes // 4, 1), device=x.device)
+        native.call("cg_colsum", x.data_ptr(), x.stride(0), x.shape[0], x.shape[1], out.data_ptr(), 0,
+                    scratch.data_ptr(), _stream())
+        return out
+
+    @staticmethod
+    def backward(ctx, h):
+        return h.expand(ctx.rows, h.shape[0])
+
+
+class ColDot(_Fused):
+    """out[c] = sum_r a[r, c] b[r, c]."""
+
+    @staticmethod
+    def forward(ctx, a, b):
+        a, b = _f32(a, "coldot"), _f32(b, "coldot")
+        ctx.save_for_backward(a, b)
+        out = torch.empty(a.shape[1], device=a.device)
+        nbytes = native.lib().cg_coldot_scratch_bytes(a.shape[0], a.shape[1])
+        scratch = torch.empty(max(nbytes // 4, 1), device=a.device)
+        native.call("cg_coldot", a.data_ptr(), b.data_ptr(), a.shape[0], a.shape[1], out.data_ptr(), 0,
+                    scratch.data_ptr(), _stream())
+        return out
+
+    @staticmethod
+    def backward(ctx, h):
+        a, b = ctx.saved_tensors
+        ga = ScaleShift.apply(b, h, None) if ctx.needs_input_grad[0] else None
+        gb = ScaleShift.apply(a, h, None) if ctx.needs_input_grad[1] else None
+        return ga, gb
+
+
+class ScaleShift(_Fused):
+    """y[r, c] = x[r, c] * gamma[c] + beta[c] (beta optional)."""
+
+    @staticmethod
+    def forward(ctx, x, gamma, beta):
+        x = _f32(x, "scale_shift")
+        out = torch.empty_like(x)
+        native.call("cg_scale_shift", x.data_ptr(), native.ptr(gamma), native.ptr(beta), out.data_ptr(),
+                    x.shape[0], x.shape[1], _stream())
+        ctx.save_for_backward(x, gamma)
+        ctx.edges = _edges(x, gamma, beta)
+        ctx.has_beta = beta is not None
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        x, gamma = ctx.saved_tensors
+        gx = ScaleShift.apply(g, gamma, None) if _wanted(ctx, 0) else None
+        gg = ColDot.apply(g, x) if _wanted(ctx, 1) else None
+        gb = ColSum.apply(g) if ctx.has_beta and _wanted(ctx, 2) else None
+        return gx, gg, gb
+
+
+# ---------------------------------------------------------------------------
+# Linear layers (bias and SiLU fused into the GEMM epilogue)
+# ---------------------------------------------------------------------------
+
+
+def _linear_backward(ctx, g, x, w, has_bias):
+    gx = MM.apply(g, w.t()) if _wanted(ctx, 0) else None
+    gw = MM.apply(g.t(), x.t()) if _wanted(ctx, 1) else None
+    gb = ColSum.apply(g) if has_bias and _wanted(ctx, 2) else None
+    return gx, gw, gb
+
+
+class LinearFn(_Fused):
+    """y = x @ w.T + b."""
+
+    @staticmethod
+    def forward(ctx, x, w, b):
+        ctx.save_for_backward(x, w)
+        ctx.edges = _edges(x, w, b)
+        ctx.has_bias = b is not None
+        return mm_raw(x, w, bias=b)
+
+    @staticmethod
+    def backward(ctx, g):
+        x, w = ctx.saved_tensors
+        return _linear_backward(ctx, g, x, w, ctx.has_bias)
+
+
+class SiluGrad(_Fused):
+    """out = g * silu'(z)."""
+
+    @staticmethod
+    def forward(ctx, g, z):
+        g, z = _f32(g, "silu_grad"), _f32(z, "silu_grad")
+        out = torch.empty_like(g)
+        native.call("cg_silu_grad", g.data_ptr(), z.data_ptr(), out.data_ptr(), g.numel(), _stream())
+        ctx.save_for_backward(g, z)
+        return out
+
+    @staticmethod
+    def backward(ctx, h):
+        g, z = ctx.saved_tensors
+        dg = SiluGrad.apply(h, z) if ctx.needs_input_grad[0] else None
+        dz = None
+        if ctx.needs_input_grad[1]:
+            h = _f32(h, "silu_grad2")
+            dz = torch.empty_like(h)
+            native.call("cg_silu_grad2", h.data_ptr(), g.data_ptr(), z.data_ptr(), dz.data_ptr(), h.numel(),
+                        _stream())
+        return dg, dz
+
+
+class LinearSiluFn(_Fused):
+    """(y, z) with z = x @ w.T + b and y = silu(z), from one GEMM."""
+
+    @staticmethod
+    def forward(ctx, x, w, b):
+        z = torch.empty(x.shape[0], w.shape[0], device=x.device)
+        y = mm_raw(x, w, bias=b, act=ACT_SILU, aux_out=z)
+        ctx.save_for_backward(x, w, z)
+        ctx.edges = _edges(x, w, b)
+        ctx.has_bias = b is not None
+        return y, z
+
+    @staticmethod
+    def backward(ctx, gy, gz):
+        x, w, z = ctx.saved_tensors
+        g = None
+        if gy is not None:
+            g = SiluGrad.apply(gy, z)
+        if gz is not None:
+            g = gz if g is None else g + gz
+        if g is None:
+            return None, None, None
+        return _linear_backward(ctx, g, x, w, ctx.has_bias)
+
+
+# ---------------------------------------------------------------------------
+# Row normalisation (LayerNorm without its affine part)
+# ---------------------------------------------------------------------------
+
+
+class RowNorm(_Fused):
+    @staticmethod
+    def forward(ctx, x, eps):
+        x = _f32(x, "rownorm")
+        out = torch.empty_like(x)
+        native.call("cg_rownorm_fwd", x.data_ptr(), x.shape[0], x.shape[1], eps, out.data_ptr(), None,
+                    _stream())
+        ctx.save_for_backward(x)
+        ctx.eps = eps
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        (x,) = ctx.saved_tensors
+        return RowNormGrad.apply(g, x, ctx.eps), None
+
+
+class RowNormGrad(_Fused):
+    """gx = J(x)^T g of the row normalisation; backward is the bwd2 kernel."""
+
+    @staticmethod
+    def forward(ctx, g, x, eps):
+        g, x = _f32(g, "rownorm_bwd1"), _f32(x, "rownorm_bwd1")
+        out = torch.empty_like(g)
+        native.call("cg_rownorm_bwd1", x.data_ptr(), g.data_ptr(), x.shape[0], x.shape[1], eps, out.data_ptr(),
+                    _stream())
+        ctx.save_for_backward(g, x)
+        ctx.eps = eps
+        return out
+
+    @staticmethod
+    def backward(ctx, h):
+        g, x = ctx.saved_tensors
+        h = _f32(h, "rownorm_bwd2")
+        dx, dg = torch.empty_like(x), torch.empty_like(g)
+        native.call("cg_rownorm_bwd2", x.data_ptr(), g.data_ptr(), h.data_ptr(), x.shape[0], x.shape[1], ctx.eps,
+                    dx.data_ptr(), dg.data_ptr(), _stream())
+        return dg, dx, None
+
+
+# ---------------------------------------------------------------------------
+# Gather / segment sum over a sorted CSR
+# ---------------------------------------------------------------------------
+
+
+@dataclasses.dataclass
+class Csr:
+    """A many-to-one map: element e goes to row index[e] (-1: nowhere). row_ptr
+    (rows + 1) and perm (the elements grouped by row, ascending within a row)
+    make the reduction direction a fixed-order segment sum."""
+
+    index: Tensor      # (elements,) int32
+    row_ptr: Tensor    # (rows + 1,) int32
+    perm: Tensor       # (elements mapped somewhere,) int32
+    rows: int
+
+    @staticmethod
+    def from_index(index: Tensor, rows: int) -> Csr:
+        """Build on the index's device with a stable sort (deterministic)."""
+        index = index.to(torch.int64)
+        valid = index >= 0
+        order = torch.argsort(torch.where(valid, index, rows), stable=True)
+        counts = torch.bincount(index[valid], minlength=rows)
+        row_ptr = torch.zeros(rows + 1, dtype=torch.int64, device=index.device)
+        row_ptr[1:] = torch.cumsum(counts, 0)
+        nnz = int(valid.sum())
+        return Csr(index.to(torch.int32), row_ptr.to(torch.int32), order[:nnz].to(torch.int32).contiguous(), rows)
+
+
+def gather_raw(src: Tensor, csr: Csr) -> Tensor:
+    src = _f32(src, "gather_rows")
+    out = torch.empty(csr.index.shape[0], src.shape[1], device=src.device)
+    native.call("cg_gather_rows", src.data_ptr(), src.stride(0), csr.index.data_ptr(), out.shape[0], src.shape[1],
+                out.data_ptr(), out.stride(0), _stream())
+    return out
+
+
+def segment_sum_raw(src: Tensor, csr: Csr) -> Tensor:
+    src = _f32(src, "segment_sum")
+    out = torch.empty(csr.rows, src.shape[1], device=src.device)
+    native.call("cg_segment_sum", src.data_ptr(), src.stride(0), csr.row_ptr.data_ptr(), csr.perm.data_ptr(),
+                csr.rows, src.shape[1], out.data_ptr(), out.stride(0), 0, _stream())
+    return out
+
+
+class Gather(_Fused):
+    """out[e] = src[csr.index[e]]; backward: segment sum."""
+
+    @staticmethod
+    def forward(ctx, src, csr):
+        ctx.csr = csr
+        return gather_raw(src, csr)
+
+    @staticmethod
+    def backward(ctx, g):
+        return SegmentSum.apply(g, ctx.csr), None
+
+
+class SegmentSum(_Fused):
+    """out[r] = sum of src[e] over index[e] == r, in ascending e; backward: gather."""
+
+    @staticmethod
+    def forward(ctx, src, csr):
+        ctx.csr = csr
+        return segment_sum_raw(src, csr)
+
+    @staticmethod
+    def backward(ctx, g):
+        return Gather.apply(g, ctx.csr), None
+
+
+# ---------------------------------------------------------------------------
+# Envelope pooling over the k tokens of each atom
+# ---------------------------------------------------------------------------
+
+
+class Pool(_Fused):
+    """m[n, c] = sum_s w[n, s] x[n, s, c]."""
+
+    @staticmethod
+    def forward(ctx, x, w):
+        x, w = _f32(x, "pool"), _f32(w, "pool")
+        n, k, c = x.shape
+        out = torch.empty(n, c, device=x.device)
+        native.call("cg_pool", x.data_ptr(), w.data_ptr(), n, k, c, out.data_ptr(), _stream())
+        ctx.save_for_backward(x, w)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        x, w = ctx.saved_tensors
+        gx = Outer.apply(w, g) if ctx.needs_input_grad[0] else None
+        gw = Dot.apply(g, x) if ctx.needs_input_grad[1] else None
+        return gx, gw
+
+
+class Outer(_Fused):
+    """y[n, s, c] = w[n, s] g[n, c]."""
+
+    @staticmethod
+    def forward(ctx, w, g):
+        w, g = _f32(w, "pool_outer"), _f32(g, "pool_outer")
+        n, k = w.shape
+        out = torch.empty(n, k, g.shape[1], device=w.device)
+        native.call("cg_pool_outer", w.data_ptr(), g.data_ptr(), n, k, g.shape[1], out.data_ptr(), _stream())
+        ctx.save_for_backward(w, g)
+        return out
+
+    @staticmethod
+    def backward(ctx, h):
+        w, g = ctx.saved_tensors
+        gw = Dot.apply(g, h) if ctx.needs_input_grad[0] else None
+        gg = Pool.apply(h, w) if ctx.needs_input_grad[1] else None
+        return gw, gg
+
+
+class Dot(_Fused):
+    """y[n, s] = sum_c g[n, c] x[n, s, c]."""
+
+    @staticmethod
+    def forward(ctx, g, x):
+        g, x = _f32(g, "pool_dot"), _f32(x, "pool_dot")
+        n, k, c = x.shape
+        out = torch.empty(n, k, device=x.device)
+        native.call("cg_pool_dot", g.data_ptr(), x.data_ptr(), n, k, c, out.data_ptr(), _stream())
+        ctx.save_for_backward(g, x)
+        return out
+
+    @staticmethod
+    def backward(ctx, h):
+        g, x = ctx.saved_tensors
+        gg = Pool.apply(x, h) if ctx.needs_input_grad[0] else None
+        gx = Outer.apply(h, g) if ctx.needs_input_grad[1] else None
+        return gg, gx
+
+
+# ---------------------------------------------------------------------------
+# Edge geometry
+# ---------------------------------------------------------------------------
+
+
+@dataclasses.dataclass
+class NeighborGraph:
+    """Padded neighbour layout of a batch: slot e = i*k + s holds neighbour
+    nbr[i, s] of atom i (-1 past counts[i]); ``tokens`` maps slots to their
+    neighbour (the gather of per-atom features into edge tokens) and back."""
+
+    nbr: Tensor        # (n, k) int32
+    counts: Tensor     # (n,) int32
+    tokens: Csr        # index = nbr.flatten(); rows = n
+    k: int
+
+    @property
+    def n_atoms(self) -> int:
+        return self.nbr.shape[0]
+
+
+def _geom_args(pos: Tensor, graph: NeighborGraph, n_rbf: int, cutoff: float, gamma: float):
+    a = native.GeomArgs()
+    a.pos = pos.data_ptr()
+    a.nbr = graph.nbr.data_ptr()
+    a.rev_ptr = graph.tokens.row_ptr.data_ptr()
+    a.rev_idx = graph.tokens.perm.data_ptr()
+    a.n_atoms = graph.n_atoms
+    a.k = graph.k
+    a.n_rbf = n_rbf
+    a.cutoff = cutoff
+    a.gamma = gamma
+    return a
+
+
+class EdgeGeometry(_Fused):
+    """(rbf (n*k, n_rbf), env (n*k,)) of the neighbour edges of pos."""
+
+    @staticmethod
+    def forward(ctx, pos, graph, n_rbf, cutoff, gamma):
+        pos = _f32(pos, "edge_geom")
+        e = graph.n_atoms * graph.k
+        rbf = torch.empty(e, n_rbf, device=pos.device)
+        env = torch.empty(e, device=pos.device)
+        args = _geom_args(pos, graph, n_rbf, cutoff, gamma)
+        native.check(native.lib().cg_edge_geom_fwd(ctypes.byref(args), rbf.data_ptr(), env.data_ptr(), _stream()))
+        ctx.save_for_backward(pos)
+        ctx.meta = (graph, n_rbf, cutoff, gamma)
+        return rbf, env
+
+    @staticmethod
+    def backward(ctx, g_rbf, g_env):
+        (pos,) = ctx.saved_tensors
+        graph, n_rbf, cutoff, gamma = ctx.meta
+        if g_rbf is None:
+            g_rbf = torch.zeros(graph.n_atoms * graph.k, n_rbf, device=pos.device)
+        return EdgeGeometryGrad.apply(pos, g_rbf, g_env, ctx.meta), None, None, None, None
+
+
+class EdgeGeometryGrad(_Fused):
+    """g_pos of (g_rbf, g_env); backward: the second-derivative kernel."""
+
+    @staticmethod
+    def forward(ctx, pos, g_rbf, g_env, meta):
+        graph, n_rbf, cutoff, gamma = meta
+        g_rbf = _f32(g_rbf, "edge_geom_bwd1")
+        g_env = None if g_env is None else _f32(g_env, "edge_geom_bwd1")
+        gvec = torch.empty(graph.n_atoms * graph.k, 3, device=pos.device)
+        g_pos = torch.empty_like(pos)
+        args = _geom_args(pos, graph, n_rbf, cutoff, gamma)
+        native.check(native.lib().cg_edge_geom_bwd1(ctypes.byref(args), g_rbf.data_ptr(), native.ptr(g_env),
+                                                    gvec.data_ptr(), g_pos.data_ptr(), _stream()))
+        ctx.save_for_backward(pos, g_rbf, g_env)
+        ctx.meta = meta
+        return g_pos
+
+    @staticmethod
+    def backward(ctx, h):
+        pos, g_rbf, g_env = ctx.saved_tensors
+        graph, n_rbf, cutoff, gamma = ctx.meta
+        h = _f32(h, "edge_geom_bwd2")
+        e = graph.n_atoms * graph.k
+        gvec = torch.empty(e, 3, device=pos.device)
+        d_pos = torch.empty_like(pos)
+        d_g_rbf = torch.empty(e, n_rbf, device=pos.device)
+        d_g_env = torch.empty(e, device=pos.device)
+        args = _geom_args(pos, graph, n_rbf, cutoff, gamma)
+        native.check(native.lib().cg_edge_geom_bwd2(ctypes.byref(args), g_rbf.data_ptr(), native.ptr(g_env),
+                                                    h.data_ptr(), gvec.data_ptr(), d_pos.data_ptr(),
+                                                    d_g_rbf.data_ptr(), d_g_env.data_ptr(), _stream()))
+        return d_pos, d_g_rbf, (d_g_env if g_env is not None else None), None
+
+
+# ---------------------------------------------------------------------------
+# Edge attention over gathered tokens
+# ---------------------------------------------------------------------------
+
+
+class TokenAttention(_Fused):
+    """Attention among the k edge tokens of each atom.
+
+    tok (n*k, 3*h*d) holds [q | k | v] per token (heads contiguous), bias
+    (n*k, h) the per-key additive bias, counts (n,) the valid keys per atom.
+    Returns the token outputs (n, k, h*d), heads concatenated.
+    """
+
+    @staticmethod
+    def forward(ctx, tok, bias, counts, heads, scale):
+        out, lse = token_attention_forward1(tok, bias, counts, heads, scale)
+        ctx.save_for_backward(tok, bias, lse)
+        ctx.meta = (counts, heads, scale)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        tok, bias, lse = ctx.saved_tensors
+        counts, heads, scale = ctx.meta
+        dtok, dbias = TokenAttentionGrad.apply(tok, bias, lse, g, ctx.meta)
+        return dtok, dbias, None, None, None
+
+
+class TokenAttentionGrad(_Fused):
+    """backward1 of TokenAttention; its backward is the backward2 kernel."""
+
+    @staticmethod
+    def forward(ctx, tok, bias, lse, g, meta):
+        counts, heads, scale = meta
+        dtok, dbias = token_attention_backward1(tok, bias, lse, g, counts, heads, scale)
+        ctx.save_for_backward(tok, bias, lse, g)
+        ctx.meta = meta
+        return dtok, dbias
+
+    @staticmethod
+    def backward(ctx, h_tok, h_bias):
+        tok, bias, lse, g = ctx.saved_tensors
+        counts, heads, scale = ctx.meta
+        if h_tok is None:
+            h_tok = torch.zeros_like(tok)
+        dtok, dbias, dg = token_attention_backward2(tok, bias, lse, g, h_tok, h_bias, counts, heads, scale)
+        return dtok, dbias, None, dg, None
+
+
+# ---------------------------------------------------------------------------
+# modules
+# ---------------------------------------------------------------------------
+
+
+class Linear(nn.Module):
+    """nn.Linear on the tcgen05 GEMM (optionally with a fused SiLU)."""
+
+    def __init__(self, fan_in: int, fan_out: int, bias: bool = True, silu: bool = False):
+        super().__init__()
+        bound = 1.0 / math.sqrt(fan_in)
+        self.weight = nn.Parameter(torch.empty(fan_out, fan_in).uniform_(-bound, bound))
+        self.bias = nn.Parameter(torch.empty(fan_out).uniform_(-bound, bound)) if bias else None
+        self.silu = silu
+
+    def forward(self, x: Tensor) -> Tensor:
+        if self.silu:
+            return LinearSiluFn.apply(x, self.weight, self.bias)[0]
+        return LinearFn.apply(x, self.weight, self.bias)
+
+
+class LayerNorm(nn.Module):
+    """nn.LayerNorm over the last dimension: row normalisation + column affine."""
+
+    def __init__(self, dim: int, eps: float = 1e-5):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(dim))
+        self.bias = nn.Parameter(torch.zeros(dim))
+        self.eps = eps
+
+    def forward(self, x: Tensor) -> Tensor:
+        return ScaleShift.apply(RowNorm.apply(x, self.eps), self.weight, self.bias)

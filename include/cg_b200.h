@@ -134,6 +134,87 @@ typedef struct cg_gemm_args {
 
 int cg_gemm_tf32(const cg_gemm_args* args, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Segment sums over a sorted CSR, their transpose, column reductions.
+ * The reference's models reduce with index_add (tests/test_semantics.py:68-69
+ * there), an atomic scatter on GPUs; these read every segment in a fixed
+ * order, so results are bitwise reproducible.
+ * ---------------------------------------------------------------------- */
+/* out[e, :] = index[e] >= 0 ? src[index[e], :] : 0 (the transpose of
+ * cg_segment_sum); replaces the tensor indexing pos[src] / h[index]. */
+int cg_gather_rows(const float* src, int64_t ld_src, const int32_t* index, int64_t n_out, int64_t cols,
+                   float* out, int64_t ld_out, void* stream);
+/* out[r, :] (+)= sum_{e in [row_ptr[r], row_ptr[r+1])} src[perm ? perm[e] : e, :],
+ * in increasing e; replaces index_add (tests/test_semantics.py:68-69 there). */
+int cg_segment_sum(const float* src, int64_t ld_src, const int32_t* row_ptr, const int32_t* perm,
+                   int64_t n_rows, int64_t cols, float* out, int64_t ld_out, int accumulate,
+                   void* stream);
+/* out[c] (+)= sum_r src[r*ld + c], two fixed-order passes through `scratch`
+ * (cg_colsum_scratch_bytes bytes); the bias gradients of nn.Linear. */
+int64_t cg_colsum_scratch_bytes(int64_t rows, int64_t cols);
+int cg_colsum(const float* src, int64_t ld, int64_t rows, int64_t cols, float* out, int accumulate,
+              float* scratch, void* stream);
+/* out[c] (+)= sum_r a[r, c] b[r, c] (contiguous rows), as cg_colsum. */
+int64_t cg_coldot_scratch_bytes(int64_t rows, int64_t cols);
+int cg_coldot(const float* a, const float* b, int64_t rows, int64_t cols, float* out, int accumulate,
+              float* scratch, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Pointwise and per-row kernels of the energy network (nn.SiLU, nn.LayerNorm
+ * of the reference's test models, tests/test_semantics.py:51-69 there).
+ * ---------------------------------------------------------------------- */
+/* out = a * silu'(z) */
+int cg_silu_grad(const float* a, const float* z, float* out, int64_t n, void* stream);
+/* out = a * b * silu''(z) */
+int cg_silu_grad2(const float* a, const float* b, const float* z, float* out, int64_t n, void* stream);
+/* out[r, c] = x[r, c] * gamma[c] + beta[c] (either may be NULL) */
+int cg_scale_shift(const float* x, const float* gamma, const float* beta, float* out, int64_t rows,
+                   int64_t cols, void* stream);
+/* xhat = (x - mean) / sqrt(var + eps) per row (rstd may be NULL) */
+int cg_rownorm_fwd(const float* x, int64_t rows, int64_t cols, float eps, float* xhat, float* rstd,
+                   void* stream);
+/* gx = d xhat / dx applied to g */
+int cg_rownorm_bwd1(const float* x, const float* g, int64_t rows, int64_t cols, float eps, float* gx,
+                    void* stream);
+/* gradients of <h, gx(x, g)> w.r.t. x (d_x) and g (d_g) */
+int cg_rownorm_bwd2(const float* x, const float* g, const float* h, int64_t rows, int64_t cols, float eps,
+                    float* d_x, float* d_g, void* stream);
+/* Envelope pooling of k tokens per row n (x contiguous (n, k, cols)):
+ * pool: out[n, c] = sum_s w[n, s] x[n, s, c];  outer: out[n, s, c] = w[n, s] g[n, c];
+ * dot: out[n, s] = sum_c g[n, c] x[n, s, c]. A family closed under differentiation. */
+int cg_pool(const float* x, const float* w, int64_t n, int64_t k, int64_t cols, float* out, void* stream);
+int cg_pool_outer(const float* w, const float* g, int64_t n, int64_t k, int64_t cols, float* out,
+                  void* stream);
+int cg_pool_dot(const float* g, const float* x, int64_t n, int64_t k, int64_t cols, float* out,
+                void* stream);
+
+/* ------------------------------------------------------------------------
+ * Edge geometry of the padded (n_atoms, k) neighbour layout: slot e = i*k + s
+ * holds neighbour nbr[e] of centre i (or -1). vec = pos[nbr] - pos[i],
+ * d = |vec|, rbf[e, r] = exp(-gamma (d - r*cutoff/(n_rbf-1))^2),
+ * env[e] = (cos(pi d / cutoff) + 1) / 2 inside the cutoff. rev_ptr/rev_idx:
+ * reverse CSR (slots grouped by neighbour, ascending). Replaces the eager
+ * geometry before the reference's region (README.md:28,
+ * tests/test_semantics.py:46-48 there) and its autograd double backward.
+ * ---------------------------------------------------------------------- */
+typedef struct cg_geom_args {
+  const float* pos;        /* (n_atoms, 3) */
+  const int32_t* nbr;      /* (n_atoms, k) */
+  const int32_t* rev_ptr;  /* (n_atoms + 1) */
+  const int32_t* rev_idx;  /* (valid slots) */
+  int64_t n_atoms;
+  int32_t k, n_rbf;
+  float cutoff, gamma;
+} cg_geom_args;
+
+int cg_edge_geom_fwd(const cg_geom_args* a, float* rbf, float* env, void* stream);
+/* g_pos from (g_rbf, g_env); gvec: (n_atoms*k, 3) scratch */
+int cg_edge_geom_bwd1(const cg_geom_args* a, const float* g_rbf, const float* g_env, float* gvec,
+                      float* g_pos, void* stream);
+/* gradients of <h_pos, g_pos(pos, g_rbf, g_env)> w.r.t. pos, g_rbf, g_env */
+int cg_edge_geom_bwd2(const cg_geom_args* a, const float* g_rbf, const float* g_env, const float* h_pos,
+                      float* gvec, float* d_pos, float* d_g_rbf, float* d_g_env, void* stream);
+
 /* The device error word kernels set when a bounded wait gave up (0: none);
  * reset != 0 clears it. Synchronises with the device. No reference
  * counterpart: the reference's kernels are generated by Inductor and have no

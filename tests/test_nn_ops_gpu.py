@@ -1,0 +1,146 @@
+"""
+The fused ops of the energy network (create_graph_b200.nn) against float64
+torch composites of the same functions, at all three levels create_graph
+uses: forward, the force-pass gradient (create_graph=True) and the
+parameter backward through it (tests/twice.py).
+
+Tolerances: float32 kernels at 1e-5 relative (norm-wise); ops on the tf32
+GEMM at the stated tf32 bound 3e-3.
+"""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from create_graph_b200 import nn as cgnn
+from tests.twice import twice_errors
+
+pytestmark = pytest.mark.gpu
+F32_TOL = 1e-5
+TF32_TOL = 3e-3
+
+
+def check(errors, tol):
+    bad = {k: v for k, v in errors.items() if not v <= tol}
+    assert not bad, f"above {tol}: {bad} (all {errors})"
+
+
+def randn(*shape, seed=0, scale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return (scale * torch.randn(*shape, generator=g)).cuda()
+
+
+def test_mm_and_linear():
+    x, w, b = randn(300, 96, seed=1), randn(200, 96, seed=2), randn(200, seed=3)
+    check(twice_errors(cgnn.mm, lambda a, c: a @ c.T, [x, w]), TF32_TOL)
+    check(twice_errors(lambda *a: cgnn.LinearFn.apply(*a), F.linear, [x, w, b]), TF32_TOL)
+    silu_lin = lambda *a: cgnn.LinearSiluFn.apply(*a)[0]  # noqa: E731
+    check(twice_errors(silu_lin, lambda *a: F.silu(F.linear(*a)), [x, w, b]), TF32_TOL)
+
+
+def test_layer_norm():
+    x = randn(257, 192, seed=4, scale=2.0) + 0.5
+    gamma, beta = randn(192, seed=5), randn(192, seed=6)
+    mine = lambda x, g, b: cgnn.ScaleShift.apply(cgnn.RowNorm.apply(x, 1e-5), g, b)  # noqa: E731
+    ref = lambda x, g, b: F.layer_norm(x, (x.shape[-1],), g, b, 1e-5)  # noqa: E731
+    check(twice_errors(mine, ref, [x, gamma, beta]), F32_TOL)
+
+
+def test_column_ops():
+    a, b = randn(1000, 40, seed=7), randn(1000, 40, seed=8)
+    check(twice_errors(lambda a: cgnn.ColSum.apply(a), lambda a: a.sum(0), [a]), F32_TOL)
+    check(twice_errors(lambda a, b: cgnn.ColDot.apply(a, b), lambda a, b: (a * b).sum(0), [a, b]), F32_TOL)
+
+
+def test_gather_and_segment_sum():
+    n, e = 50, 400
+    g = torch.Generator().manual_seed(9)
+    index = torch.randint(-1, n, (e,), generator=g).cuda()
+    csr = cgnn.Csr.from_index(index, n)
+    src = randn(n, 24, seed=10)
+    rows = randn(e, 24, seed=11)
+
+    def ref_gather(s):
+        out = s[index.clamp_min(0).long()]
+        return out * (index >= 0)[:, None].to(out.dtype)
+
+    def ref_segsum(r):
+        out = torch.zeros(n, r.shape[1], dtype=r.dtype, device=r.device)
+        keep = index >= 0
+        return out.index_add(0, index[keep].long(), r[keep])
+
+    check(twice_errors(lambda s: cgnn.Gather.apply(s, csr), ref_gather, [src]), F32_TOL)
+    check(twice_errors(lambda r: cgnn.SegmentSum.apply(r, csr), ref_segsum, [rows]), F32_TOL)
+    # deterministic: bitwise equal on repeat
+    a = cgnn.segment_sum_raw(rows, csr)
+    assert torch.equal(a, cgnn.segment_sum_raw(rows, csr))
+
+
+def test_pool_family():
+    x, w = randn(37, 30, 64, seed=12), randn(37, 30, seed=13)
+    check(twice_errors(lambda x, w: cgnn.Pool.apply(x, w), lambda x, w: (w[..., None] * x).sum(1), [x, w]), F32_TOL)
+
+
+def neighbor_case(n=40, k=12, seed=14):
+    g = torch.Generator().manual_seed(seed)
+    pos = (3.0 * torch.rand(n, 3, generator=g)).cuda()
+    counts = torch.randint(0, k + 1, (n,), generator=g, dtype=torch.int32)
+    nbr = torch.full((n, k), -1, dtype=torch.int32)
+    for i in range(n):
+        others = torch.tensor([j for j in range(n) if j != i])
+        pick = others[torch.randperm(n - 1, generator=g)[: int(counts[i])]]
+        nbr[i, : int(counts[i])] = pick.to(torch.int32)
+    nbr = nbr.cuda()
+    graph = cgnn.NeighborGraph(nbr, counts.cuda(), cgnn.Csr.from_index(nbr.flatten(), n), k)
+    return pos, graph
+
+
+def ref_geometry(pos, nbr, n_rbf, cutoff, gamma):
+    n, k = nbr.shape
+    valid = (nbr >= 0).flatten()
+    i = torch.arange(n, device=pos.device).repeat_interleave(k)
+    # padded slots point at another atom so the masked terms stay finite
+    j = torch.where(valid, nbr.flatten().long(), (i + 1) % n)
+    vec = pos[j] - pos[i]
+    d = vec.norm(dim=-1)
+    mu = torch.arange(n_rbf, device=pos.device, dtype=pos.dtype) * (cutoff / (n_rbf - 1))
+    rbf = torch.exp(-gamma * (d[:, None] - mu) ** 2) * valid[:, None]
+    env = 0.5 * (torch.cos(math.pi * d / cutoff) + 1) * (d < cutoff) * valid
+    return rbf, env
+
+
+def test_edge_geometry():
+    pos, graph = neighbor_case()
+    args = (16, 2.5, 4.0)
+    mine = lambda p: cgnn.EdgeGeometry.apply(p, graph, *args)  # noqa: E731
+    ref = lambda p: ref_geometry(p, graph.nbr, *args)  # noqa: E731
+    check(twice_errors(mine, ref, [pos]), F32_TOL)
+
+
+def ref_token_attention(tok, bias, counts, heads, scale):
+    n = counts.shape[0]
+    k = tok.shape[0] // n
+    d = tok.shape[1] // (3 * heads)
+    t = tok.view(n, k, 3, heads, d)
+    q, kk, v = (t[:, :, i].permute(0, 2, 1, 3) for i in range(3))
+    b = bias.view(n, k, heads).permute(0, 2, 1)[:, :, None, :]
+    mask = torch.arange(k, device=tok.device)[None, :] >= counts[:, None].long()
+    b = b.masked_fill(mask[:, None, None, :], -torch.inf)
+    logits = q @ kk.transpose(-1, -2) * scale + b
+    p = torch.softmax(logits, -1).nan_to_num(0.0)
+    return (p @ v).permute(0, 2, 1, 3).reshape(n, k, heads * d)
+
+
+def test_token_attention():
+    n, k, heads, d = 24, 30, 4, 16
+    g = torch.Generator().manual_seed(15)
+    tok = torch.randn(n * k, 3 * heads * d, generator=g).cuda()
+    bias = torch.randn(n * k, heads, generator=g).cuda()
+    counts = torch.randint(1, k + 1, (n,), generator=g, dtype=torch.int32).cuda()
+    mine = lambda t, b: cgnn.TokenAttention.apply(t, b, counts, heads, 0.25)  # noqa: E731
+    ref = lambda t, b: ref_token_attention(t, b, counts, heads, 0.25)  # noqa: E731
+    check(twice_errors(mine, ref, [tok, bias]), F32_TOL)
