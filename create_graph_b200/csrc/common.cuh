@@ -38,8 +38,12 @@ enum Status : int {
     }                                                                            \
   } while (0)
 
+// Kernels launched by this library (host-side count, all threads).
+void note_launch();
+
 #define CG_LAUNCHED(name)                                                                 \
   do {                                                                                    \
+    ::cg::note_launch();                                                                  \
     cudaError_t err_ = cudaGetLastError();                                                \
     if (err_ != cudaSuccess) {                                                            \
       ::cg::set_error("launch of %s failed: %s", name, cudaGetErrorString(err_));         \

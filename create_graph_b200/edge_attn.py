@@ -120,7 +120,7 @@ class _Call:
             scratch = torch.empty(scratch_bytes, dtype=torch.uint8, device=self.q.device)
             self.args.scratch = scratch.data_ptr()
             self.keep.append(scratch)
-        native.check(getattr(lib, fn)(args, native.stream_ptr(self.q.device)))
+        native.invoke(fn, args, native.stream_ptr(self.q.device), info=_info(self.args))
 
     def dbias_buffer(self) -> Tensor | None:
         """dbias in the reduced (n_b, h_b, ki, kj) layout the kernel writes."""
@@ -269,8 +269,12 @@ def _token_args(tok: Tensor, bias: Tensor, counts: Tensor, heads: int, scale: fl
     return a, n, k, d
 
 
+def _info(a) -> tuple[int, int, int, int]:
+    return (int(a.n), int(a.h), int(a.k), int(a.d))
+
+
 def _run(fn: str, a, device) -> None:
-    native.check(getattr(native.lib(), fn)(ctypes.byref(a), native.stream_ptr(device)))
+    native.invoke(fn, ctypes.byref(a), native.stream_ptr(device), info=_info(a))
 
 
 def token_attention_forward1(tok, bias, counts, heads, scale):

@@ -84,5 +84,5 @@ def gemm(
     args.aux_out = None if aux_out is None else aux_out.data_ptr()
     args.a_mn_major, args.b_mn_major = int(a_t), int(b_t)
     args.act, args.accumulate, args.alpha = act, int(accumulate), float(alpha)
-    native.check(native.lib().cg_gemm_tf32(ctypes.byref(args), native.stream_ptr(a.device)))
+    native.invoke("cg_gemm_tf32", ctypes.byref(args), native.stream_ptr(a.device), info=(m, n, k))
     return out

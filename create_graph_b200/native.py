@@ -112,6 +112,7 @@ _I = ctypes.c_int
 _SIGNATURES = {
     "cg_last_error": (ctypes.c_char_p, []),
     "cg_version": (ctypes.c_int, []),
+    "cg_launch_count": (i64, []),
     "cg_edge_attn_fwd1": (ctypes.c_int, [ctypes.POINTER(EdgeAttnArgs), vp]),
     "cg_edge_attn_bwd1": (ctypes.c_int, [ctypes.POINTER(EdgeAttnArgs), vp]),
     "cg_edge_attn_bwd2": (ctypes.c_int, [ctypes.POINTER(EdgeAttnArgs), vp]),
@@ -136,6 +137,8 @@ _SIGNATURES = {
     "cg_edge_geom_fwd": (_I, [ctypes.POINTER(GeomArgs), vp, vp, vp]),
     "cg_edge_geom_bwd1": (_I, [ctypes.POINTER(GeomArgs), vp, vp, vp, vp, vp]),
     "cg_edge_geom_bwd2": (_I, [ctypes.POINTER(GeomArgs), vp, vp, vp, vp, vp, vp, vp, vp]),
+    "cg_neighbor_list_workspace": (_I, [i64]),
+    "cg_neighbor_list": (_I, [vp, vp, i64, i64, i64, f32, i32, vp, vp, vp, vp, vp, vp]),
 }
 
 
@@ -207,6 +210,37 @@ def ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
-def call(name: str, *args) -> None:
-    """Call a status-returning entry point; the last argument is the stream."""
-    check(getattr(lib(), name)(*args))
+# entry point name -> list of (start, end, info) CUDA event pairs, for the
+# entry points a benchmark asked to time (``time_entry_points``)
+TIMED: dict[str, list] = {}
+
+
+def time_entry_points(names, enable: bool = True) -> None:
+    """Record CUDA events around every call of the named entry points."""
+    for name in names:
+        if enable:
+            TIMED.setdefault(name, [])
+        else:
+            TIMED.pop(name, None)
+
+
+def invoke(name: str, *args, info=None) -> None:
+    """Call a status-returning entry point (the last argument is the stream)."""
+    fn = getattr(lib(), name)
+    slot = TIMED.get(name)
+    if slot is None:
+        check(fn(*args))
+        return
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    check(fn(*args))
+    end.record()
+    slot.append((start, end, info))
+
+
+call = invoke
+
+
+def launch_count() -> int:
+    """Kernels libcg_b200.so has launched in this process."""
+    return int(load_library().cg_launch_count())

@@ -476,7 +476,7 @@ class EdgeGeometry(_Fused):
         rbf = torch.empty(e, n_rbf, device=pos.device)
         env = torch.empty(e, device=pos.device)
         args = _geom_args(pos, graph, n_rbf, cutoff, gamma)
-        native.check(native.lib().cg_edge_geom_fwd(ctypes.byref(args), rbf.data_ptr(), env.data_ptr(), _stream()))
+        native.invoke("cg_edge_geom_fwd", ctypes.byref(args), rbf.data_ptr(), env.data_ptr(), _stream())
         ctx.save_for_backward(pos)
         ctx.meta = (graph, n_rbf, cutoff, gamma)
         return rbf, env
@@ -501,8 +501,8 @@ class EdgeGeometryGrad(_Fused):
         gvec = torch.empty(graph.n_atoms * graph.k, 3, device=pos.device)
         g_pos = torch.empty_like(pos)
         args = _geom_args(pos, graph, n_rbf, cutoff, gamma)
-        native.check(native.lib().cg_edge_geom_bwd1(ctypes.byref(args), g_rbf.data_ptr(), native.ptr(g_env),
-                                                    gvec.data_ptr(), g_pos.data_ptr(), _stream()))
+        native.invoke("cg_edge_geom_bwd1", ctypes.byref(args), g_rbf.data_ptr(), native.ptr(g_env), gvec.data_ptr(),
+                      g_pos.data_ptr(), _stream())
         ctx.save_for_backward(pos, g_rbf, g_env)
         ctx.meta = meta
         return g_pos
@@ -518,9 +518,8 @@ class EdgeGeometryGrad(_Fused):
         d_g_rbf = torch.empty(e, n_rbf, device=pos.device)
         d_g_env = torch.empty(e, device=pos.device)
         args = _geom_args(pos, graph, n_rbf, cutoff, gamma)
-        native.check(native.lib().cg_edge_geom_bwd2(ctypes.byref(args), g_rbf.data_ptr(), native.ptr(g_env),
-                                                    h.data_ptr(), gvec.data_ptr(), d_pos.data_ptr(),
-                                                    d_g_rbf.data_ptr(), d_g_env.data_ptr(), _stream()))
+        native.invoke("cg_edge_geom_bwd2", ctypes.byref(args), g_rbf.data_ptr(), native.ptr(g_env), h.data_ptr(),
+                      gvec.data_ptr(), d_pos.data_ptr(), d_g_rbf.data_ptr(), d_g_env.data_ptr(), _stream())
         return d_pos, d_g_rbf, (d_g_env if g_env is not None else None), None
 
 

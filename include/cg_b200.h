@@ -33,6 +33,9 @@ extern "C" {
 const char* cg_last_error(void);
 /* CG_B200_ABI_VERSION of the loaded library. */
 int cg_version(void);
+/* Kernels this library has launched in this process (all threads). No
+ * reference counterpart: it lets a benchmark report its own launches. */
+int64_t cg_launch_count(void);
 
 /* ------------------------------------------------------------------------
  * Masked edge attention, per slice (n, h) of k tokens with head dim d:
@@ -214,6 +217,22 @@ int cg_edge_geom_bwd1(const cg_geom_args* a, const float* g_rbf, const float* g_
 /* gradients of <h_pos, g_pos(pos, g_rbf, g_env)> w.r.t. pos, g_rbf, g_env */
 int cg_edge_geom_bwd2(const cg_geom_args* a, const float* g_rbf, const float* g_env, const float* h_pos,
                       float* gvec, float* d_pos, float* d_g_rbf, float* d_g_env, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Neighbour lists of a batch of non-periodic systems (atoms sorted by system,
+ * system b = atoms [sys_ptr[b], sys_ptr[b+1])). For atom i: the other atoms
+ * of its system with d2 < cutoff^2, d2 = (dx*dx + dy*dy) + dz*dz in
+ * round-to-nearest single operations (no FMA), the k nearest by (d2, j) in
+ * that order; nbr (n_atoms, k) padded with -1, counts (n_atoms). rev_ptr
+ * (n_atoms + 1) / rev_idx (sum of counts) is the reverse CSR, slots grouped by
+ * neighbour in ascending slot order. workspace: cg_neighbor_list_workspace()
+ * int32s. Bit-exact and deterministic. The reference leaves neighbour lists
+ * to model code before its region (README.md:28 there).
+ * ---------------------------------------------------------------------- */
+int cg_neighbor_list_workspace(int64_t n_systems);
+int cg_neighbor_list(const float* pos, const int32_t* sys_ptr, int64_t n_systems, int64_t n_atoms,
+                     int64_t max_atoms_per_system, float cutoff, int32_t k, int32_t* nbr, int32_t* counts,
+                     int32_t* rev_ptr, int32_t* rev_idx, int32_t* workspace, void* stream);
 
 /* The device error word kernels set when a bounded wait gave up (0: none);
  * reset != 0 clears it. Synchronises with the device. No reference
