@@ -1,0 +1,70 @@
+// Launchers of the tensor-core edge-attention kernels (attn_tc.cuh): the
+// float32 path of cg_edge_attn_fwd1 / bwd1 / bwd2.
+#include "attn_tc.cuh"
+
+namespace cg {
+namespace attn_tc {
+
+// Sum the per-slice partial dbias over the broadcast n and/or h dimensions in
+// a fixed order (deterministic), one thread per dbias element.
+__global__ void dbias_reduce_tc(const Params P, int64_t outs) {
+  const cg_edge_attn_args& a = P.a;
+  const int64_t per = (int64_t)P.ki * P.kj;
+  const bool bn = a.bias.sn == 0, bh = a.bias.sh == 0;
+  const int64_t hh = bh ? 1 : a.h;
+  for (int64_t o = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; o < outs; o += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t f = o % per, nh = o / per;
+    const int64_t n0 = nh / hh, h0 = nh % hh;
+    const float* part = reinterpret_cast<const float*>(a.scratch);
+    float v = 0.0f;
+    for (int64_t n = bn ? 0 : n0; n < (bn ? a.n : n0 + 1); ++n)
+      for (int64_t h = bh ? 0 : h0; h < (bh ? a.h : h0 + 1); ++h) v += part[(n * a.h + h) * per + f];
+    const int i = (int)(f / P.kj), j = (int)(f % P.kj);
+    const cg_bias& db = a.dbias;
+    reinterpret_cast<float*>(db.ptr)[n0 * db.sn + h0 * db.sh + (int64_t)i * db.si + (int64_t)j * db.sj] = v;
+  }
+}
+
+template <int DP>
+static int launch_dp(int which, const Params& P, cudaStream_t stream) {
+  const int smem = smem_bytes<DP>(which);
+  void (*kernel)(const Params) = which == 0 ? fwd1_tc<DP> : which == 1 ? bwd1_tc<DP> : bwd2_tc<DP>;
+  CG_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int64_t slices = P.a.n * P.a.h;
+  int per_sm = (220 * 1024) / smem;
+  if (per_sm < 1) per_sm = 1;
+  if (per_sm > 16) per_sm = 16;
+  const int64_t cap = (int64_t)sm_count() * per_sm;
+  const int grid = (int)(slices < cap ? slices : cap);
+  kernel<<<grid, kThreads, smem, stream>>>(P);
+  CG_LAUNCHED("edge_attn_tc");
+  if (which != 0 && P.dbias_mode == 2) {
+    const bool bn = P.a.bias.sn == 0, bh = P.a.bias.sh == 0;
+    const int64_t outs = (bn ? 1 : P.a.n) * (bh ? 1 : P.a.h) * (int64_t)P.ki * P.kj;
+    const int64_t blocks = ceil_div<int64_t>(outs, 256);
+    dbias_reduce_tc<<<(int)(blocks < 4096 ? blocks : 4096), 256, 0, stream>>>(P, outs);
+    CG_LAUNCHED("edge_attn_tc dbias reduction");
+  }
+  return kOk;
+}
+
+int launch(int which, const cg_edge_attn_args& a, int dbias_mode, int ki, int kj, int vec_ok, int dp,
+           cudaStream_t stream) {
+  Params P;
+  P.a = a;
+  P.dbias_mode = dbias_mode;
+  P.ki = ki;
+  P.kj = kj;
+  P.vec_ok = vec_ok;
+  switch (dp) {
+    case 8: return launch_dp<8>(which, P, stream);
+    case 16: return launch_dp<16>(which, P, stream);
+    case 32: return launch_dp<32>(which, P, stream);
+    case 64: return launch_dp<64>(which, P, stream);
+  }
+  set_error("edge_attn: no tensor-core variant for padded head dim %d", dp);
+  return kUnsupported;
+}
+
+}  // namespace attn_tc
+}  // namespace cg

@@ -1,0 +1,529 @@
+// Masked edge attention (float32) on the tensor cores.
+//
+// Same arithmetic as the CUDA-core kernels in edge_attn.cuh (the reference's
+// kernels/edge_attn/ops.py:26-104), organised for mma.sync m16n8k8 tf32 with
+// a three-term split of every operand (x = hi + lo, hi = tf32(x),
+// lo = tf32(x - hi); a*b ~ hi*hi + hi*lo + lo*hi), which keeps fp32-level
+// accuracy (~1e-6 relative) while the products run on the tensor pipe.
+//
+// One CTA of two warps owns one slice (n, h) of k <= 32 tokens: warp w holds
+// query rows [16w, 16w + 16) of every k x k matrix as mma accumulator
+// fragments, so row reductions of the softmax are quad shuffles. The k x d
+// operands sit in shared memory with a 4-float row pad; k x k intermediates
+// (probs, grad_logits, d_scores, d_grad_probs) are written to shared memory
+// once, then read back as A fragments, straight for the row products
+// (dq, grad_out) and transposed for the key products (dk, dv) after a CTA
+// barrier. Rows past k and columns past d are zero in shared memory.
+#pragma once
+
+#include <math.h>
+
+#include "common.cuh"
+#include "../../include/cg_b200.h"
+
+namespace cg {
+namespace attn_tc {
+
+constexpr int KP = 32;    // padded tokens per slice
+constexpr int LDP = 36;   // pitch of k x k matrices
+constexpr int kThreads = 64;
+
+struct Params {
+  cg_edge_attn_args a;
+  int dbias_mode;  // 0 none, 1 direct, 2 per-slice partials into scratch
+  int ki, kj;
+  int vec_ok;
+};
+
+// ---- mma.sync tf32 with a 3-term split ---------------------------------------
+__device__ inline uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+struct Split {
+  uint32_t hi, lo;
+};
+
+__device__ inline Split split(float x) {
+  const uint32_t h = to_tf32(x);
+  return {h, to_tf32(x - __uint_as_float(h))};
+}
+
+__device__ inline void mma(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// acc[nt] += A(16 x 8*KT) * B(8*KT x 8*NT) for one 16-row band.
+// la(m, k): A element (m < 16); lb(k, n): B element. Fragment layout of
+// m16n8k8: A a0 (g, t) a1 (g+8, t) a2 (g, t+4) a3 (g+8, t+4); B b0 (t, g)
+// b1 (t+4, g); C c0 (g, 2t) c1 (g, 2t+1) c2 (g+8, 2t) c3 (g+8, 2t+1).
+template <int NT, int KT, class LA, class LB>
+__device__ inline void band_mma(float (&acc)[NT][4], LA la, LB lb, int g, int t) {
+#pragma unroll 1
+  for (int kt = 0; kt < KT; ++kt) {
+    const int k0 = kt * 8;
+    const Split a0 = split(la(g, k0 + t)), a1 = split(la(g + 8, k0 + t));
+    const Split a2 = split(la(g, k0 + t + 4)), a3 = split(la(g + 8, k0 + t + 4));
+    const uint32_t ahi[4] = {a0.hi, a1.hi, a2.hi, a3.hi};
+    const uint32_t alo[4] = {a0.lo, a1.lo, a2.lo, a3.lo};
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const Split b0 = split(lb(k0 + t, nt * 8 + g)), b1 = split(lb(k0 + t + 4, nt * 8 + g));
+      const uint32_t bhi[2] = {b0.hi, b1.hi};
+      const uint32_t blo[2] = {b0.lo, b1.lo};
+      mma(acc[nt], alo, bhi);
+      mma(acc[nt], ahi, blo);
+      mma(acc[nt], ahi, bhi);
+    }
+  }
+}
+
+template <int NT>
+__device__ inline void zero(float (&acc)[NT][4]) {
+#pragma unroll
+  for (int i = 0; i < NT; ++i)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[i][e] = 0.0f;
+}
+
+// C-fragment element e of tile nt: row (within the band) and column.
+__device__ inline int frag_row(int g, int e) { return g + 8 * (e >> 1); }
+__device__ inline int frag_col(int nt, int t, int e) { return nt * 8 + 2 * t + (e & 1); }
+
+// Sum over the quad (the four lanes sharing g): a full row of a k x k band.
+__device__ inline float quad_sum(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  v += __shfl_xor_sync(0xffffffffu, v, 2);
+  return v;
+}
+__device__ inline float quad_max(float v) {
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+  return v;
+}
+
+// ---- shared-memory staging -------------------------------------------------------
+template <int DP>
+__device__ inline void load_op(float* s, const cg_mat& m, int64_t n, int64_t h, int k, int d, bool vec) {
+  constexpr int LD = DP + 4;
+  const float* base = reinterpret_cast<const float*>(m.ptr) + n * m.sn + h * m.sh;
+  if (vec) {
+    constexpr int VPR = DP / 4;
+    for (int f = threadIdx.x; f < KP * VPR; f += kThreads) {
+      const int r = f / VPR, c = (f % VPR) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (r < k) v = __ldg(reinterpret_cast<const float4*>(base + (int64_t)r * m.sr + c));
+      *reinterpret_cast<float4*>(s + r * LD + c) = v;
+    }
+  } else {
+    for (int f = threadIdx.x; f < KP * DP; f += kThreads) {
+      const int r = f / DP, c = f % DP;
+      s[r * LD + c] = (r < k && c < d) ? base[(int64_t)r * m.sr + c] : 0.0f;
+    }
+  }
+}
+
+// k x k tile of a broadcastable bias (zeros outside [0,k)^2 or without bias).
+__device__ inline void load_bias(float* s, const cg_bias& b, int64_t n, int64_t h, int k) {
+  for (int f = threadIdx.x; f < KP * KP; f += kThreads) {
+    const int i = f / KP, j = f % KP;
+    float v = 0.0f;
+    if (b.ptr != nullptr && i < k && j < k)
+      v = reinterpret_cast<const float*>(b.ptr)[n * b.sn + h * b.sh + (int64_t)i * b.si + (int64_t)j * b.sj];
+    s[i * LDP + j] = v;
+  }
+}
+
+// Store a 16 x 8*NT band (rows 16*band + ...) of a k x d output.
+template <int NT>
+__device__ inline void store_band(const cg_mat& m, int64_t n, int64_t h, int band, int k, int d,
+                                  const float (&acc)[NT][4], int g, int t, float scale) {
+  float* base = reinterpret_cast<float*>(m.ptr) + n * m.sn + h * m.sh;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int r = band * 16 + g + 8 * half;
+      const int c = nt * 8 + 2 * t;
+      if (r < k) {
+        float* dst = base + (int64_t)r * m.sr + c;
+        if (c + 1 < d) {
+          dst[0] = acc[nt][2 * half] * scale;
+          dst[1] = acc[nt][2 * half + 1] * scale;
+        } else if (c < d) {
+          dst[0] = acc[nt][2 * half] * scale;
+        }
+      }
+    }
+  }
+}
+
+__device__ inline int valid_keys(const Params& P, int64_t n) {
+  const int k = P.a.k;
+  if (P.a.key_count == nullptr) return k;
+  const int c = P.a.key_count[n];
+  return c < 0 ? 0 : (c > k ? k : c);
+}
+
+// Per-slice dbias from a k x k matrix M in shared memory (pitch LDP), reduced
+// over i and/or j when the bias broadcasts them; to dbias or scratch.
+__device__ inline void write_dbias(const Params& P, const float* M, int64_t n, int64_t h, int64_t slice) {
+  if (P.dbias_mode == 0) return;
+  const int k = P.a.k, ki = P.ki, kj = P.kj;
+  for (int f = threadIdx.x; f < ki * kj; f += kThreads) {
+    const int i = f / kj, j = f % kj;
+    float v = 0.0f;
+    if (ki == k && kj == k) {
+      v = M[i * LDP + j];
+    } else if (ki == 1 && kj == k) {
+      for (int r = 0; r < k; ++r) v += M[r * LDP + j];
+    } else if (ki == k && kj == 1) {
+      for (int c = 0; c < k; ++c) v += M[i * LDP + c];
+    } else {
+      for (int r = 0; r < k; ++r)
+        for (int c = 0; c < k; ++c) v += M[r * LDP + c];
+    }
+    if (P.dbias_mode == 1) {
+      const cg_bias& db = P.a.dbias;
+      reinterpret_cast<float*>(db.ptr)[n * db.sn + h * db.sh + (int64_t)i * db.si + (int64_t)j * db.sj] = v;
+    } else {
+      reinterpret_cast<float*>(P.a.scratch)[slice * (ki * kj) + f] = v;
+    }
+  }
+}
+
+// Logits of the band from the S accumulator: scale * S + bias, masked to -inf
+// for keys past kc and non-finite values. Returns probabilities in `p`
+// (exp(l - lse)) and, when lse_in is null, computes the row lse.
+__device__ inline void band_softmax(float (&p)[4][4], const float (&s)[4][4], const float* sbias, int band,
+                                    int g, int t, float scale, int kc, const float* lse_in, float (&lse)[2]) {
+  float l[4][4];
+  bool ok[4][4];
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int r = band * 16 + frag_row(g, e), c = frag_col(nt, t, e);
+      const float v = s[nt][e] * scale + sbias[r * LDP + c];
+      l[nt][e] = v;
+      ok[nt][e] = c < kc && isfinite(v);
+    }
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    if (lse_in != nullptr) {
+      lse[half] = lse_in[band * 16 + g + 8 * half];
+    } else {
+      float m = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e2 = 0; e2 < 2; ++e2)
+          if (ok[nt][2 * half + e2]) m = fmaxf(m, l[nt][2 * half + e2]);
+      m = quad_max(m);
+      float sum = 0.0f;
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e2 = 0; e2 < 2; ++e2)
+          if (ok[nt][2 * half + e2]) sum += expf(l[nt][2 * half + e2] - m);
+      sum = quad_sum(sum);
+      lse[half] = m == -INFINITY ? -INFINITY : m + logf(sum);
+    }
+  }
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float ls = lse[e >> 1];
+      p[nt][e] = (ok[nt][e] && isfinite(ls)) ? expf(l[nt][e] - ls) : 0.0f;
+    }
+}
+
+// Write a band of a k x k fragment matrix to shared memory.
+__device__ inline void put_band(float* M, const float (&v)[4][4], int band, int g, int t) {
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) M[(band * 16 + frag_row(g, e)) * LDP + frag_col(nt, t, e)] = v[nt][e];
+}
+
+// row sums of a band (both halves) of a product of two fragment matrices
+__device__ inline void row_dot(float (&out)[2], const float (&a)[4][4], const float (&b)[4][4]) {
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    float s = 0.0f;
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) s += a[nt][2 * half] * b[nt][2 * half] + a[nt][2 * half + 1] * b[nt][2 * half + 1];
+    out[half] = quad_sum(s);
+  }
+}
+
+// ---------------------------------------------------------------------------
+template <int DP>
+struct Layout {
+  static constexpr int LD = DP + 4;
+  static constexpr int OP = KP * LD;     // floats per k x d operand
+  static constexpr int KK = KP * LDP;    // floats per k x k matrix
+};
+
+template <int DP>
+__global__ void __launch_bounds__(kThreads) fwd1_tc(const Params P) {
+  using L = Layout<DP>;
+  extern __shared__ __align__(16) float smem[];
+  float* sQ = smem;
+  float* sK = sQ + L::OP;
+  float* sV = sK + L::OP;
+  float* sP = sV + L::OP;  // bias tile, then probabilities
+  const cg_edge_attn_args& a = P.a;
+  const int k = a.k, d = a.d;
+  const float scale = (float)a.scale;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  for (int64_t s = blockIdx.x; s < a.n * a.h; s += gridDim.x) {
+    const int64_t n = s / a.h, h = s % a.h;
+    __syncthreads();
+    load_op<DP>(sQ, a.q, n, h, k, d, P.vec_ok);
+    load_op<DP>(sK, a.k_, n, h, k, d, P.vec_ok);
+    load_op<DP>(sV, a.v, n, h, k, d, P.vec_ok);
+    load_bias(sP, a.bias, n, h, k);
+    __syncthreads();
+    const int kc = valid_keys(P, n);
+    const int band = warp;
+    float S[4][4], p[4][4], lse[2];
+    zero(S);
+    band_mma<4, DP / 8>(S, [&](int m, int kk) { return sQ[(band * 16 + m) * L::LD + kk]; },
+                        [&](int kk, int j) { return sK[j * L::LD + kk]; }, g, t);
+    band_softmax(p, S, sP, band, g, t, scale, kc, nullptr, lse);
+    __syncwarp();
+    put_band(sP, p, band, g, t);
+    __syncwarp();
+    float O[DP / 8][4];
+    zero(O);
+    band_mma<DP / 8, 4>(O, [&](int m, int j) { return sP[(band * 16 + m) * LDP + j]; },
+                        [&](int j, int c) { return sV[j * L::LD + c]; }, g, t);
+    store_band<DP / 8>(a.out, n, h, band, k, d, O, g, t, 1.0f);
+    if (t == 0) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int r = band * 16 + g + 8 * half;
+        if (r < k) reinterpret_cast<float*>(a.lse)[s * k + r] = lse[half];
+      }
+    }
+  }
+}
+
+template <int DP>
+__global__ void __launch_bounds__(kThreads) bwd1_tc(const Params P) {
+  using L = Layout<DP>;
+  extern __shared__ __align__(16) float smem[];
+  float* sQ = smem;
+  float* sK = sQ + L::OP;
+  float* sV = sK + L::OP;
+  float* sG = sV + L::OP;
+  float* sP = sG + L::OP;
+  float* sGL = sP + L::KK;  // bias tile, then grad_logits
+  float* sLse = sGL + L::KK;
+  const cg_edge_attn_args& a = P.a;
+  const int k = a.k, d = a.d;
+  const float scale = (float)a.scale;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  for (int64_t s = blockIdx.x; s < a.n * a.h; s += gridDim.x) {
+    const int64_t n = s / a.h, h = s % a.h;
+    __syncthreads();
+    load_op<DP>(sQ, a.q, n, h, k, d, P.vec_ok);
+    load_op<DP>(sK, a.k_, n, h, k, d, P.vec_ok);
+    load_op<DP>(sV, a.v, n, h, k, d, P.vec_ok);
+    load_op<DP>(sG, a.grad_out, n, h, k, d, P.vec_ok);
+    load_bias(sGL, a.bias, n, h, k);
+    if (threadIdx.x < KP) sLse[threadIdx.x] = threadIdx.x < k ? reinterpret_cast<const float*>(a.lse)[s * k + threadIdx.x] : 0.0f;
+    __syncthreads();
+    const int kc = valid_keys(P, n);
+    const int band = warp;
+    {
+      float S[4][4], p[4][4], lse[2];
+      zero(S);
+      band_mma<4, DP / 8>(S, [&](int m, int kk) { return sQ[(band * 16 + m) * L::LD + kk]; },
+                          [&](int kk, int j) { return sK[j * L::LD + kk]; }, g, t);
+      band_softmax(p, S, sGL, band, g, t, scale, kc, sLse, lse);
+      float GP[4][4];
+      zero(GP);
+      band_mma<4, DP / 8>(GP, [&](int m, int kk) { return sG[(band * 16 + m) * L::LD + kk]; },
+                          [&](int kk, int j) { return sV[j * L::LD + kk]; }, g, t);
+      float rs[2];
+      row_dot(rs, p, GP);
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) GP[nt][e] = p[nt][e] * (GP[nt][e] - rs[e >> 1]);  // grad_logits
+      __syncwarp();
+      put_band(sP, p, band, g, t);
+      put_band(sGL, GP, band, g, t);
+      __syncwarp();
+    }
+    {
+      float O[DP / 8][4];
+      zero(O);  // grad_q = scale * grad_logits k
+      band_mma<DP / 8, 4>(O, [&](int m, int j) { return sGL[(band * 16 + m) * LDP + j]; },
+                          [&](int j, int c) { return sK[j * L::LD + c]; }, g, t);
+      store_band<DP / 8>(a.dq, n, h, band, k, d, O, g, t, scale);
+    }
+    __syncthreads();
+    {
+      float O[DP / 8][4];
+      zero(O);  // grad_v = probs^T grad_out (rows: keys of this band)
+      band_mma<DP / 8, 4>(O, [&](int m, int i) { return sP[i * LDP + band * 16 + m]; },
+                          [&](int i, int c) { return sG[i * L::LD + c]; }, g, t);
+      store_band<DP / 8>(a.dv, n, h, band, k, d, O, g, t, 1.0f);
+      zero(O);  // grad_k = scale * grad_logits^T q
+      band_mma<DP / 8, 4>(O, [&](int m, int i) { return sGL[i * LDP + band * 16 + m]; },
+                          [&](int i, int c) { return sQ[i * L::LD + c]; }, g, t);
+      store_band<DP / 8>(a.dk, n, h, band, k, d, O, g, t, scale);
+    }
+    write_dbias(P, sGL, n, h, s);
+  }
+}
+
+template <int DP>
+__global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
+  using L = Layout<DP>;
+  extern __shared__ __align__(16) float smem[];
+  float* sQ = smem;
+  float* sK = sQ + L::OP;
+  float* sV = sK + L::OP;
+  float* sG = sV + L::OP;
+  float* sHQ = sG + L::OP;
+  float* sHK = sHQ + L::OP;
+  float* sHV = sHK + L::OP;
+  float* sP = sHV + L::OP;
+  float* sDG = sP + L::KK;
+  float* sGL = sDG + L::KK;  // bias tile, then grad_logits
+  float* sDS = sGL + L::KK;  // hb tile, then d_scores
+  float* sLse = sDS + L::KK;
+  const cg_edge_attn_args& a = P.a;
+  const int k = a.k, d = a.d;
+  const float scale = (float)a.scale;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  for (int64_t s = blockIdx.x; s < a.n * a.h; s += gridDim.x) {
+    const int64_t n = s / a.h, h = s % a.h;
+    __syncthreads();
+    load_op<DP>(sQ, a.q, n, h, k, d, P.vec_ok);
+    load_op<DP>(sK, a.k_, n, h, k, d, P.vec_ok);
+    load_op<DP>(sV, a.v, n, h, k, d, P.vec_ok);
+    load_op<DP>(sG, a.grad_out, n, h, k, d, P.vec_ok);
+    load_op<DP>(sHQ, a.hq, n, h, k, d, P.vec_ok);
+    load_op<DP>(sHK, a.hk, n, h, k, d, P.vec_ok);
+    load_op<DP>(sHV, a.hv, n, h, k, d, P.vec_ok);
+    load_bias(sGL, a.bias, n, h, k);
+    load_bias(sDS, a.hb, n, h, k);
+    if (threadIdx.x < KP) sLse[threadIdx.x] = threadIdx.x < k ? reinterpret_cast<const float*>(a.lse)[s * k + threadIdx.x] : 0.0f;
+    __syncthreads();
+    const int kc = valid_keys(P, n);
+    const int band = warp;
+    {
+      float p[4][4], lse[2], A[4][4], B[4][4];
+      zero(A);  // scores
+      band_mma<4, DP / 8>(A, [&](int m, int kk) { return sQ[(band * 16 + m) * L::LD + kk]; },
+                          [&](int kk, int j) { return sK[j * L::LD + kk]; }, g, t);
+      band_softmax(p, A, sGL, band, g, t, scale, kc, sLse, lse);
+      zero(B);  // grad_probs = grad_out v^T
+      band_mma<4, DP / 8>(B, [&](int m, int kk) { return sG[(band * 16 + m) * L::LD + kk]; },
+                          [&](int kk, int j) { return sV[j * L::LD + kk]; }, g, t);
+      float rs[2];
+      row_dot(rs, p, B);
+      float cen[4][4];
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) cen[nt][e] = B[nt][e] - rs[e >> 1];
+      zero(A);  // d_logits = scale * (hq k^T + q hk^T) + hb
+      band_mma<4, DP / 8>(A, [&](int m, int kk) { return sHQ[(band * 16 + m) * L::LD + kk]; },
+                          [&](int kk, int j) { return sK[j * L::LD + kk]; }, g, t);
+      band_mma<4, DP / 8>(A, [&](int m, int kk) { return sQ[(band * 16 + m) * L::LD + kk]; },
+                          [&](int kk, int j) { return sHK[j * L::LD + kk]; }, g, t);
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          A[nt][e] = scale * A[nt][e] + sDS[(band * 16 + frag_row(g, e)) * LDP + frag_col(nt, t, e)];
+      float drs[2];
+      row_dot(drs, A, p);
+      zero(B);  // grad_out hv^T
+      band_mma<4, DP / 8>(B, [&](int m, int kk) { return sG[(band * 16 + m) * L::LD + kk]; },
+                          [&](int kk, int j) { return sHV[j * L::LD + kk]; }, g, t);
+      float dg[4][4];
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float dr = -drs[e >> 1];
+          const float gp = cen[nt][e] + rs[e >> 1];
+          B[nt][e] = A[nt][e] * cen[nt][e] + dr * gp + B[nt][e];  // d_probs
+          dg[nt][e] = (A[nt][e] + dr) * p[nt][e];                  // d_grad_probs
+        }
+      float rs2[2];
+      row_dot(rs2, p, B);
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          A[nt][e] = p[nt][e] * (B[nt][e] - rs2[e >> 1]);  // d_scores
+          cen[nt][e] = p[nt][e] * cen[nt][e];              // grad_logits
+        }
+      __syncwarp();
+      put_band(sP, p, band, g, t);
+      put_band(sDG, dg, band, g, t);
+      put_band(sGL, cen, band, g, t);
+      put_band(sDS, A, band, g, t);
+      __syncwarp();
+    }
+    {
+      float O[DP / 8][4];
+      zero(O);  // grad_q = scale * (grad_logits hk + d_scores k)
+      band_mma<DP / 8, 4>(O, [&](int m, int j) { return sGL[(band * 16 + m) * LDP + j]; },
+                          [&](int j, int c) { return sHK[j * L::LD + c]; }, g, t);
+      band_mma<DP / 8, 4>(O, [&](int m, int j) { return sDS[(band * 16 + m) * LDP + j]; },
+                          [&](int j, int c) { return sK[j * L::LD + c]; }, g, t);
+      store_band<DP / 8>(a.dq, n, h, band, k, d, O, g, t, scale);
+      zero(O);  // grad_out cotangent = d_grad_probs v + probs hv
+      band_mma<DP / 8, 4>(O, [&](int m, int j) { return sDG[(band * 16 + m) * LDP + j]; },
+                          [&](int j, int c) { return sV[j * L::LD + c]; }, g, t);
+      band_mma<DP / 8, 4>(O, [&](int m, int j) { return sP[(band * 16 + m) * LDP + j]; },
+                          [&](int j, int c) { return sHV[j * L::LD + c]; }, g, t);
+      store_band<DP / 8>(a.dgrad_out, n, h, band, k, d, O, g, t, 1.0f);
+    }
+    __syncthreads();
+    {
+      float O[DP / 8][4];
+      zero(O);  // grad_k = scale * (grad_logits^T hq + d_scores^T q)
+      band_mma<DP / 8, 4>(O, [&](int m, int i) { return sGL[i * LDP + band * 16 + m]; },
+                          [&](int i, int c) { return sHQ[i * L::LD + c]; }, g, t);
+      band_mma<DP / 8, 4>(O, [&](int m, int i) { return sDS[i * LDP + band * 16 + m]; },
+                          [&](int i, int c) { return sQ[i * L::LD + c]; }, g, t);
+      store_band<DP / 8>(a.dk, n, h, band, k, d, O, g, t, scale);
+      zero(O);  // grad_v = d_grad_probs^T grad_out
+      band_mma<DP / 8, 4>(O, [&](int m, int i) { return sDG[i * LDP + band * 16 + m]; },
+                          [&](int i, int c) { return sG[i * L::LD + c]; }, g, t);
+      store_band<DP / 8>(a.dv, n, h, band, k, d, O, g, t, 1.0f);
+    }
+    write_dbias(P, sDS, n, h, s);
+  }
+}
+
+// shared memory per CTA (bytes)
+template <int DP>
+inline int smem_bytes(int which) {
+  using L = Layout<DP>;
+  switch (which) {
+    case 0: return (3 * L::OP + L::KK) * 4;
+    case 1: return (4 * L::OP + 2 * L::KK + KP) * 4;
+    default: return (7 * L::OP + 4 * L::KK + KP) * 4;
+  }
+}
+
+}  // namespace attn_tc
+}  // namespace cg

@@ -1,8 +1,13 @@
-// Masked edge attention: argument checks and the C entry points. Kernels are
-// in edge_attn.cuh, instantiated per dtype in edge_attn_f32.cu / edge_attn_f64.cu.
+// Masked edge attention: argument checks and the C entry points. float32 runs
+// the tensor-core kernels (attn_tc.cuh); float64 the CUDA-core kernels of
+// edge_attn.cuh (edge_attn_f64.cu), kept for 1e-10 parity with the reference.
 #include "edge_attn.cuh"
 
 namespace cg {
+namespace attn_tc {
+int launch(int which, const cg_edge_attn_args& a, int dbias_mode, int ki, int kj, int vec_ok, int dp,
+           cudaStream_t stream);
+}
 namespace attn {
 
 static int run(Which w, const cg_edge_attn_args* args, void* stream) {
@@ -55,7 +60,11 @@ static int run(Which w, const cg_edge_attn_args* args, void* stream) {
       P.dbias_mode = kDbiasDirect;
     }
   }
-  if (a.dtype == CG_F32) return dispatch_f32(w, P, dp, as_stream(stream));
+  if (a.dtype == CG_F32) {
+    // float32: tensor-core kernels (3-term tf32 split, fp32-level accuracy)
+    const int which = w == kFwd1 ? 0 : w == kBwd1 ? 1 : 2;
+    return attn_tc::launch(which, a, P.dbias_mode, P.ki, P.kj, P.vec_ok, dp, as_stream(stream));
+  }
   return dispatch_f64(w, P, dp, as_stream(stream));
 }
 

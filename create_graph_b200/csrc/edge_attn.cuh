@@ -616,7 +616,6 @@ inline int launch_typed(Which w, const Params& P, cudaStream_t stream) {
   return kOk;
 }
 
-int dispatch_f32(Which w, const Params& P, int dp, cudaStream_t stream);
 int dispatch_f64(Which w, const Params& P, int dp, cudaStream_t stream);
 
 }  // namespace attn

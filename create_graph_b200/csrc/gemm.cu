@@ -58,12 +58,31 @@ struct Smem {
   static constexpr int kStage = kA + kB;
   static constexpr int kTiles = STAGES * kStage;
   static constexpr int kBytes = kTiles + 1024 /*alignment*/ + 256 /*barriers*/;
+  static_assert(kStage >= 4 * 32 * 33 * 4, "epilogue staging must fit in one stage");
 };
 
+// Epilogue of one output element x = alpha * acc at (row, col).
+__device__ inline void epilogue_store(const Epilogue& ep, int64_t row, int col, float x) {
+  x *= ep.alpha;
+  if (ep.bias) x += ep.bias[col];
+  if (ep.act == CG_ACT_SILU) {
+    if (ep.aux_out) ep.aux_out[row * ep.ld_aux + col] = x;
+    x = silu(x);
+  } else if (ep.act == CG_ACT_SILU_GRAD) {
+    x *= silu_grad(ep.aux_in[row * ep.ld_aux + col]);
+  }
+  float* c = ep.c + row * ep.ldc + col;
+  if (ep.accumulate) x += *c;
+  *c = x;
+}
+
+// Split-K: CTA z of gridDim.z accumulates k-tiles [z * kt_per, (z+1) * kt_per)
+// and, when `partial` is set, stores its raw fp32 tile to partial[z] (M x N);
+// cg_gemm's reduction pass then adds the splits in z order (deterministic).
 template <int BN, int STAGES, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                     int M, int N, int K, Epilogue ep) {
+                     int M, int N, int K, int kt_per, float* partial, Epilogue ep) {
   using S = Smem<BN, STAGES>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // tiles need 1024-byte alignment for the 128B swizzle pattern
@@ -76,7 +95,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
-  const int ktiles = (K + BK - 1) / BK;
+  const int ktiles_all = (K + BK - 1) / BK;
+  const int kt_begin = blockIdx.z * kt_per;
+  const int kt_end = kt_begin + kt_per < ktiles_all ? kt_begin + kt_per : ktiles_all;
+  const int ktiles = kt_end - kt_begin;
   constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
 
   if (threadIdx.x == 0) {
@@ -98,15 +120,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- TMA producer ----------------
     prefetch_tmap(&map_a);
     prefetch_tmap(&map_b);
-    for (int kt = 0; kt < ktiles && ok; ++kt) {
-      const int s = kt % STAGES;
-      const uint32_t round = kt / STAGES;
-      if (kt >= STAGES) ok = mbar_wait(&empty[s], (round - 1) & 1, &g_gemm_error);
+    for (int i = 0; i < ktiles && ok; ++i) {
+      const int s = i % STAGES;
+      const uint32_t round = i / STAGES;
+      if (i >= STAGES) ok = mbar_wait(&empty[s], (round - 1) & 1, &g_gemm_error);
       if (!ok) break;
       unsigned char* sa = tiles + s * S::kStage;
       unsigned char* sb = sa + S::kA;
       mbar_arrive_expect_tx(&full[s], S::kStage);
-      const int k0 = kt * BK;
+      const int k0 = (kt_begin + i) * BK;
       if (!A_MN) {
         tma_load_2d(sa, &map_a, &full[s], k0, m0);
       } else {
@@ -123,9 +145,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1 && lane == 0) {
     // ---------------- UMMA issuer ----------------
     constexpr uint32_t idesc = idesc_tf32(BM, BN, A_MN, B_MN);
-    for (int kt = 0; kt < ktiles && ok; ++kt) {
-      const int s = kt % STAGES;
-      ok = mbar_wait(&full[s], (kt / STAGES) & 1, &g_gemm_error);
+    for (int i = 0; i < ktiles && ok; ++i) {
+      const int s = i % STAGES;
+      ok = mbar_wait(&full[s], (i / STAGES) & 1, &g_gemm_error);
       if (!ok) break;
       tc_fence_after();
       const uint32_t sa = smem_u32(tiles + s * S::kStage);
@@ -139,40 +161,44 @@ __global__ void __launch_bounds__(kThreads, 1)
                                  : smem_desc(sa + kk * 32, 16, 1024, kSwizzle128B);
         const uint64_t bd = B_MN ? smem_desc(sb + kk * 1024, BK * 128, 512, kSwizzle128BBase32B)
                                  : smem_desc(sb + kk * 32, 16, 1024, kSwizzle128B);
-        umma_tf32(tmem, ad, bd, idesc, kt > 0 || kk > 0);
+        umma_tf32(tmem, ad, bd, idesc, i > 0 || kk > 0);
       }
       umma_commit(&empty[s]);
     }
     umma_commit(done);
   } else if (warp >= 2) {
     // ---------------- epilogue ----------------
-    const int quarter = warp & 3;  // TMEM lanes this warp may read
-    const int row = m0 + quarter * 32 + lane;
+    // Each warp owns 32 accumulator rows (its TMEM lane quarter). Per 32-column
+    // chunk: tcgen05.ld (thread = row), transpose through shared memory (the
+    // pipeline stages are free once `done` fired), then store row by row with
+    // the lanes along the columns: every store is one coalesced 128-byte line.
+    const int quarter = warp & 3;
+    float* stage = reinterpret_cast<float*>(tiles) + quarter * 32 * 33;
+    const int64_t mn = (int64_t)M * N;
     if (mbar_wait(done, 0, &g_gemm_error)) {
       tc_fence_after();
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         float v[32];
         tmem_load_32(tmem + ((uint32_t)(quarter * 32) << 16) + c0, v);
-        if (row < M) {
-          float* crow = ep.c + (int64_t)row * ep.ldc;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int col = n0 + c0 + j;
-            if (col < N) {
-              float x = v[j] * ep.alpha;
-              if (ep.bias) x += ep.bias[col];
-              if (ep.act == CG_ACT_SILU) {
-                if (ep.aux_out) ep.aux_out[(int64_t)row * ep.ld_aux + col] = x;
-                x = silu(x);
-              } else if (ep.act == CG_ACT_SILU_GRAD) {
-                x *= silu_grad(ep.aux_in[(int64_t)row * ep.ld_aux + col]);
-              }
-              if (ep.accumulate) x += crow[col];
-              crow[col] = x;
+        for (int j = 0; j < 32; ++j) stage[lane * 33 + j] = v[j];
+        __syncwarp();
+        const int col = n0 + c0 + lane;
+        const bool col_ok = c0 + lane < BN && col < N;
+#pragma unroll 4
+        for (int r = 0; r < 32; ++r) {
+          const int row = m0 + quarter * 32 + r;
+          if (col_ok && row < M) {
+            const float x = stage[r * 33 + lane];
+            if (partial) {
+              partial[blockIdx.z * mn + (int64_t)row * N + col] = x;
+            } else {
+              epilogue_store(ep, row, col, x);
             }
           }
         }
+        __syncwarp();
       }
     }
   }
@@ -181,6 +207,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// C = epi(alpha * sum_z partial[z]) in z order; one thread per element.
+__global__ void splitk_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N, Epilogue ep) {
+  const int64_t mn = (int64_t)M * N;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < mn; i += (int64_t)gridDim.x * blockDim.x) {
+    float x = 0.0f;
+    for (int z = 0; z < splits; ++z) x += partial[z * mn + i];
+    epilogue_store(ep, i / N, (int)(i % N), x);
   }
 }
 
@@ -225,8 +261,44 @@ static int make_map(CUtensorMap* map, const float* ptr, int64_t rows, int64_t co
   return kOk;
 }
 
+struct Plan {
+  int bn;
+  int splits;
+  int kt_per;
+};
+
+// Tile width and split-K factor of a problem: tiles as wide as N allows; when
+// the output tiles cannot fill the SMs and K is long, split K so that about
+// one wave of CTAs runs, each with at least 4 k-tiles.
+static Plan plan_of(const cg_gemm_args& g) {
+  Plan p;
+  const int64_t mt = ceil_div<int64_t>(g.m, BM);
+  if (g.n <= 16 && !g.b_mn_major) p.bn = 16;
+  else if (g.n <= 32) p.bn = 32;
+  else if (g.n <= 64) p.bn = 64;
+  else if (g.n >= 256 && mt * ceil_div<int64_t>(g.n, 256) >= sm_count()) p.bn = 256;
+  else p.bn = 128;
+  const int64_t tiles = mt * ceil_div<int64_t>(g.n, p.bn);
+  const int64_t ktiles = ceil_div<int64_t>(g.k, BK);
+  int64_t splits = 1;
+  if (tiles < sm_count() && ktiles >= 8) {
+    splits = ceil_div<int64_t>(sm_count(), tiles);
+    const int64_t cap = ktiles / 4;
+    if (splits > cap) splits = cap;
+    if (splits < 1) splits = 1;
+  }
+  p.kt_per = (int)ceil_div<int64_t>(ktiles, splits);
+  p.splits = (int)ceil_div<int64_t>(ktiles, p.kt_per);
+  return p;
+}
+
+static int64_t workspace_bytes(const cg_gemm_args& g) {
+  const Plan p = plan_of(g);
+  return p.splits > 1 ? (int64_t)p.splits * g.m * g.n * (int64_t)sizeof(float) : 0;
+}
+
 template <int BN, int STAGES, bool A_MN, bool B_MN>
-static int launch(const cg_gemm_args& g, cudaStream_t stream) {
+static int launch(const cg_gemm_args& g, const Plan& p, cudaStream_t stream) {
   CUtensorMap ma, mb;
   int rc;
   // A as stored: K-major (M rows x K cols) or MN-major (K rows x M cols)
@@ -246,21 +318,35 @@ static int launch(const cg_gemm_args& g, cudaStream_t stream) {
   ep.act = g.act;
   ep.accumulate = g.accumulate;
   ep.alpha = g.alpha;
+  float* partial = nullptr;
+  if (p.splits > 1) {
+    CG_REQUIRE(g.workspace != nullptr && g.workspace_bytes >= workspace_bytes(g),
+               "gemm: this shape splits K %d ways and needs %lld workspace bytes (cg_gemm_workspace_bytes)",
+               p.splits, (long long)workspace_bytes(g));
+    partial = g.workspace;
+  }
   using S = Smem<BN, STAGES>;
   auto kernel = gemm_tf32_kernel<BN, STAGES, A_MN, B_MN>;
   CG_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes));
-  dim3 grid((unsigned)ceil_div<int64_t>(g.m, BM), (unsigned)ceil_div<int64_t>(g.n, BN));
-  kernel<<<grid, kThreads, S::kBytes, stream>>>(ma, mb, (int)g.m, (int)g.n, (int)g.k, ep);
+  dim3 grid((unsigned)ceil_div<int64_t>(g.m, BM), (unsigned)ceil_div<int64_t>(g.n, BN), (unsigned)p.splits);
+  kernel<<<grid, kThreads, S::kBytes, stream>>>(ma, mb, (int)g.m, (int)g.n, (int)g.k, p.kt_per, partial, ep);
   CG_LAUNCHED("gemm_tf32");
+  if (p.splits > 1) {
+    const int64_t mn = g.m * g.n;
+    const int64_t blocks = ceil_div<int64_t>(mn, 256);
+    splitk_reduce_kernel<<<(unsigned)(blocks < 8192 ? blocks : 8192), 256, 0, stream>>>(partial, p.splits, (int)g.m,
+                                                                                        (int)g.n, ep);
+    CG_LAUNCHED("gemm_tf32 split-K reduction");
+  }
   return kOk;
 }
 
 template <int BN, int STAGES>
-static int launch_majors(const cg_gemm_args& g, cudaStream_t s) {
-  if (!g.a_mn_major && !g.b_mn_major) return launch<BN, STAGES, false, false>(g, s);
-  if (!g.a_mn_major && g.b_mn_major) return launch<BN, STAGES, false, true>(g, s);
-  if (g.a_mn_major && !g.b_mn_major) return launch<BN, STAGES, true, false>(g, s);
-  return launch<BN, STAGES, true, true>(g, s);
+static int launch_majors(const cg_gemm_args& g, const Plan& p, cudaStream_t s) {
+  if (!g.a_mn_major && !g.b_mn_major) return launch<BN, STAGES, false, false>(g, p, s);
+  if (!g.a_mn_major && g.b_mn_major) return launch<BN, STAGES, false, true>(g, p, s);
+  if (g.a_mn_major && !g.b_mn_major) return launch<BN, STAGES, true, false>(g, p, s);
+  return launch<BN, STAGES, true, true>(g, p, s);
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -280,11 +366,14 @@ static int run(const cg_gemm_args* args, void* stream) {
   CG_REQUIRE(g.act == CG_ACT_NONE || g.act == CG_ACT_SILU || g.act == CG_ACT_SILU_GRAD, "gemm: bad act");
   CG_REQUIRE(g.act != CG_ACT_SILU_GRAD || g.aux_in != nullptr, "gemm: SiLU gradient needs aux_in");
   cudaStream_t s = as_stream(stream);
-  // wider tiles for wide outputs; 64-wide tiles keep small-N problems spread over the SMs
-  if (g.n >= 256 && ceil_div<int64_t>(g.m, BM) * ceil_div<int64_t>(g.n, 256) >= sm_count())
-    return launch_majors<256, 4>(g, s);
-  if (g.n > 64) return launch_majors<128, 6>(g, s);
-  return launch_majors<64, 8>(g, s);
+  const Plan p = plan_of(g);
+  switch (p.bn) {
+    case 16: return g.a_mn_major ? launch<16, 10, true, false>(g, p, s) : launch<16, 10, false, false>(g, p, s);
+    case 32: return launch_majors<32, 9>(g, p, s);
+    case 64: return launch_majors<64, 8>(g, p, s);
+    case 128: return launch_majors<128, 6>(g, p, s);
+    default: return launch_majors<256, 4>(g, p, s);
+  }
 }
 
 }  // namespace gemm
@@ -293,6 +382,11 @@ static int run(const cg_gemm_args* args, void* stream) {
 extern "C" {
 
 int cg_gemm_tf32(const cg_gemm_args* args, void* stream) { return cg::gemm::run(args, stream); }
+
+int64_t cg_gemm_workspace_bytes(const cg_gemm_args* args) {
+  if (args == nullptr || args->m <= 0 || args->n <= 0 || args->k <= 0) return 0;
+  return cg::gemm::workspace_bytes(*args);
+}
 
 int cg_device_error(int* out, int reset) {
   int v = 0;

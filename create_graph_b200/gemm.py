@@ -84,5 +84,10 @@ def gemm(
     args.aux_out = None if aux_out is None else aux_out.data_ptr()
     args.a_mn_major, args.b_mn_major = int(a_t), int(b_t)
     args.act, args.accumulate, args.alpha = act, int(accumulate), float(alpha)
+    ws_bytes = native.lib().cg_gemm_workspace_bytes(ctypes.byref(args))
+    workspace = None
+    if ws_bytes > 0:
+        workspace = torch.empty(ws_bytes // 4, dtype=torch.float32, device=a.device)
+        args.workspace, args.workspace_bytes = workspace.data_ptr(), ws_bytes
     native.invoke("cg_gemm_tf32", ctypes.byref(args), native.stream_ptr(a.device), info=(m, n, k))
     return out

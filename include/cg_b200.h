@@ -133,9 +133,16 @@ typedef struct cg_gemm_args {
   int32_t act, accumulate;
   float alpha;
   int32_t pad0;
+  float* workspace;         /* split-K partial tiles; cg_gemm_workspace_bytes() bytes */
+  int64_t workspace_bytes;
 } cg_gemm_args;
 
+/* When the output tiles cannot fill the GPU and K is long (the weight
+ * gradients, K = atoms or edges), K is split across CTAs; their partial tiles
+ * go to `workspace` and are added in a fixed order (deterministic). */
 int cg_gemm_tf32(const cg_gemm_args* args, void* stream);
+/* Workspace bytes cg_gemm_tf32 needs for these args (0: no split). */
+int64_t cg_gemm_workspace_bytes(const cg_gemm_args* args);
 
 /* ------------------------------------------------------------------------
  * Segment sums over a sorted CSR, their transpose, column reductions.

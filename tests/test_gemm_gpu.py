@@ -36,7 +36,11 @@ def operands(m, n, k, a_t, b_t, seed=0):
 
 @pytest.mark.parametrize("a_t", [False, True])
 @pytest.mark.parametrize("b_t", [False, True])
-@pytest.mark.parametrize("mnk", [(128, 64, 32), (300, 200, 100), (1000, 2304, 768), (768, 768, 4100), (77, 3072, 768)])
+@pytest.mark.parametrize(
+    "mnk",
+    [(128, 64, 32), (300, 200, 100), (1000, 2304, 768), (768, 768, 4100), (77, 3072, 768), (12, 128, 20000),
+     (128, 12, 20000), (5000, 12, 128), (5000, 128, 12), (40, 24, 300)],
+)
 def test_layouts_and_sizes(a_t, b_t, mnk):
     m, n, k = mnk
     a, b, a_dev, b_dev = operands(m, n, k, a_t, b_t)
@@ -69,6 +73,18 @@ def test_silu_gradient_epilogue_and_accumulate():
     acc = base.clone().cuda()
     gemm(a_dev, b_dev, b_t=True, out=acc, accumulate=True, alpha=0.5)
     assert rel(acc.cpu(), base.double() + 0.5 * a.double() @ b.double().T) < TF32_TOL
+
+
+def test_split_k_is_deterministic_and_uses_the_epilogue():
+    """Weight-gradient shapes (small M x N, K = edges) split K across CTAs; the
+    partial tiles are added in a fixed order."""
+    m, n, k = 12, 128, 50000
+    a, b, a_dev, b_dev = operands(m, n, k, True, True, seed=5)
+    bias = torch.randn(n)
+    first = gemm(a_dev, b_dev, a_t=True, b_t=True, bias=bias.cuda())
+    second = gemm(a_dev, b_dev, a_t=True, b_t=True, bias=bias.cuda())
+    assert torch.equal(first, second)
+    assert rel(first.cpu(), a.double() @ b.double().T + bias.double()) < TF32_TOL
 
 
 def test_strided_operands_in_place():
