@@ -376,10 +376,60 @@ static int run(const cg_gemm_args* args, void* stream) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// The allocation-free variant (cg_gemm_tf32_noalloc). Its split-K partial
+// tiles live in this file-scope device array instead of a caller workspace.
+// Every GPU that loads the library keeps the array for the life of the
+// process. Host code must not pass the symbol itself to a kernel (on the host
+// it is only a stand-in); the device address comes from cudaGetSymbolAddress.
+// ---------------------------------------------------------------------------
+constexpr int64_t kNoAllocScratchFloats = 2 * 1024 * 1024;  // 8 MiB per device
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+
+// Device address of the array on the current device, looked up once per device
+// (the first call on a device therefore runs a runtime query; make it before
+// any stream capture).
+static int noalloc_scratch(float** out) {
+  static float* cached[64] = {nullptr};
+  int dev = -1;
+  CG_CUDA(cudaGetDevice(&dev));
+  CG_REQUIRE(dev >= 0 && dev < 64, "gemm_noalloc: device index %d out of range", dev);
+  if (cached[dev] == nullptr) {
+    void* p = nullptr;
+    CG_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    cached[dev] = static_cast<float*>(p);
+  }
+  *out = cached[dev];
+  return kOk;
+}
+
+static int run_noalloc(const cg_gemm_args* args, void* stream) {
+  CG_REQUIRE(args != nullptr, "gemm_noalloc: args is NULL");
+  cg_gemm_args local = *args;
+  local.workspace = nullptr;
+  local.workspace_bytes = 0;
+  if (local.m > 0 && local.n > 0 && local.k > 0) {
+    const int64_t need = workspace_bytes(local);
+    const int64_t have = kNoAllocScratchFloats * (int64_t)sizeof(float);
+    CG_REQUIRE(need <= have,
+               "gemm_noalloc: this shape splits K and needs %lld bytes of scratch, more than the %lld-byte "
+               "static buffer; call cg_gemm_tf32 with a workspace instead",
+               (long long)need, (long long)have);
+    if (need > 0) {
+      int rc = noalloc_scratch(&local.workspace);
+      if (rc) return rc;
+      local.workspace_bytes = have;
+    }
+  }
+  return run(&local, stream);
+}
+
 }  // namespace gemm
 }  // namespace cg
 
 extern "C" {
+
+int cg_gemm_tf32_noalloc(const cg_gemm_args* args, void* stream) { return cg::gemm::run_noalloc(args, stream); }
 
 int cg_gemm_tf32(const cg_gemm_args* args, void* stream) { return cg::gemm::run(args, stream); }
 

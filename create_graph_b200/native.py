@@ -121,6 +121,7 @@ _SIGNATURES = {
     "cg_edge_attn_scratch_bytes": (i64, [ctypes.POINTER(EdgeAttnArgs)]),
     "cg_gemm_tf32": (ctypes.c_int, [ctypes.POINTER(GemmArgs), vp]),
     "cg_gemm_workspace_bytes": (i64, [ctypes.POINTER(GemmArgs)]),
+    "cg_gemm_tf32_noalloc": (ctypes.c_int, [ctypes.POINTER(GemmArgs), vp]),
     "cg_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
     "cg_gather_rows": (_I, [vp, i64, vp, i64, i64, vp, i64, vp]),
     "cg_segment_sum": (_I, [vp, i64, vp, vp, i64, i64, vp, i64, _I, vp]),

@@ -143,6 +143,20 @@ typedef struct cg_gemm_args {
 int cg_gemm_tf32(const cg_gemm_args* args, void* stream);
 /* Workspace bytes cg_gemm_tf32 needs for these args (0: no split). */
 int64_t cg_gemm_workspace_bytes(const cg_gemm_args* args);
+/* cg_gemm_tf32 for callers that cannot allocate device memory: hosts whose
+ * device memory belongs to another allocator (a framework's caching pool, or
+ * a Go / JVM / Node service that hands its libraries fixed buffers) and that
+ * forbid cudaMalloc, which synchronises the device and can fail under memory
+ * pressure. The split-K partial tiles of the weight-gradient shapes go to one
+ * static 8 MiB device buffer inside the library instead of args->workspace
+ * (ignored); every GPU that loads the library holds that buffer until exit.
+ * Shapes needing more scratch are rejected with an error before any launch.
+ * The call allocates nothing; its first call on a device looks up the
+ * buffer's address (make it before any stream capture). All calls share the
+ * buffer, so calls that overlap on the GPU (other streams, other threads)
+ * race; each call writes every scratch element it later reads, so nothing
+ * needs clearing between calls. No counterpart in the reference. */
+int cg_gemm_tf32_noalloc(const cg_gemm_args* args, void* stream);
 
 /* ------------------------------------------------------------------------
  * Segment sums over a sorted CSR, their transpose, column reductions.
