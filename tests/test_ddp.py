@@ -1,0 +1,130 @@
+"""
+Data parallelism on CPU ranks (gloo, 2 processes, float64): each rank runs
+cg.create_graph on its own systems, gradients live in one flat buffer
+(create_graph_b200.ddp.FlatGradients) and one all-reduce averages them. The
+reduced gradients must be identical on both ranks and equal the mean of the
+per-rank eager create_graph gradients -- the property the reference's DDP
+test asserts (tests/test_ddp.py there). A second case has one rank raise
+before the collective and checks the other fails with an error instead of
+waiting forever.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+import tempfile
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+from torch import nn
+
+import create_graph_b200 as cg
+from create_graph_b200.ddp import FlatGradients
+
+pytestmark = [pytest.mark.ddp, pytest.mark.slow]
+
+
+class Net(nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.layers = nn.ModuleList(nn.Linear(32, 32) for _ in range(3))
+        self.inp, self.out = nn.Linear(4, 32), nn.Linear(32, 1)
+        self.region = cg.compile(self._energy)
+
+    def _energy(self, vec, dist):
+        h = torch.tanh(self.inp(torch.cat([vec, dist[:, None]], dim=-1)))
+        for layer in self.layers:
+            h = h + nn.functional.silu(layer(h))
+        return self.out(h).sum().reshape(1)
+
+    def forward(self, data):
+        vec = data["pos"][data["src"]] - data["pos"][data["dst"]]
+        return {"energy": self.region(vec, vec.norm(dim=-1))}
+
+
+def rank_data(rank):
+    gen = torch.Generator().manual_seed(100 + rank)
+    n = 9
+    src = torch.randint(0, n, (24,), generator=gen)
+    return {
+        "pos": torch.randn(n, 3, generator=gen, dtype=torch.float64),
+        "src": src,
+        "dst": (src + torch.randint(1, n, (24,), generator=gen)) % n,
+    }
+
+
+def step(model, data, exact=False):
+    out, grads = cg.create_graph(model, data, exact=exact)
+    (out["energy"].sum() + grads["pos"].square().sum()).backward()
+
+
+def worker(rank, world, port, path, fail_rank):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
+    torch.set_default_dtype(torch.float64)
+    torch.manual_seed(0)
+    model = Net()
+    grads = FlatGradients(model.parameters(), world)
+    try:
+        grads.zero()
+        step(model, rank_data(rank))
+        if rank == fail_rank:
+            raise RuntimeError("injected failure before the all-reduce")
+        grads.allreduce()
+        flat = grads.flat.clone()
+        gathered = [torch.empty_like(flat) for _ in range(world)]
+        dist.all_gather(gathered, flat)
+        if rank == 0:
+            torch.save({"flat": flat, "identical": all(torch.equal(gathered[0], g) for g in gathered[1:])}, path)
+    except RuntimeError as error:
+        torch.save({"error": str(error)}, f"{path}.{rank}")
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:  # noqa: BLE001 - the group may already be broken
+            pass
+
+
+def free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def expected_flat():
+    torch.set_default_dtype(torch.float64)
+    try:
+        torch.manual_seed(0)
+        model = Net()
+        total = None
+        for rank in range(2):
+            model.zero_grad()
+            step(model, rank_data(rank), exact=True)
+            flat = torch.cat([p.grad.flatten() for p in model.parameters()])
+            total = flat if total is None else total + flat
+        return total / 2
+    finally:
+        torch.set_default_dtype(torch.float32)
+
+
+def test_averaged_gradients_match_eager_mean():
+    want = expected_flat()
+    with tempfile.TemporaryDirectory() as tmp:
+        path = os.path.join(tmp, "out.pt")
+        mp.spawn(worker, args=(2, free_port(), path, -1), nprocs=2, join=True)
+        got = torch.load(path)
+    assert got["identical"]
+    assert ((got["flat"] - want).norm() / want.norm()).item() < 1e-10
+
+
+def test_failing_rank_ends_the_other_with_an_error():
+    with tempfile.TemporaryDirectory() as tmp:
+        path = os.path.join(tmp, "out.pt")
+        mp.spawn(worker, args=(2, free_port(), path, 1), nprocs=2, join=True)
+        assert "injected failure" in torch.load(f"{path}.1")["error"]
+        # rank 0 is left alone in the collective: gloo ends it with an error, not a hang
+        assert os.path.exists(f"{path}.0")
