@@ -243,6 +243,17 @@ def run_mine(args):
             "clocks": clocks.summary(),
             "loss": float(loss.item()),
         }
+        # the metric's second part: edge-attention backward2 against its HBM roofline at the
+        # microbenchmark shape (4096 atoms x 8 heads x 32 tokens x 32 dims, fp32)
+        from create_graph_b200 import microbench
+
+        mb = microbench.attn(4096, iters=10, hbm_gbs=hbm, which=("bwd2",))["bwd2"]
+        line["edge_attn_bwd2"] = {
+            "shape": "(4096, 8, 32, 32) fp32, keys masked past U{8..32}",
+            "roofline": {"bound": "hbm", "achieved": mb["gb_s"], "peak": hbm, "unit": "GB/s",
+                         "frac": mb["gb_s"] / hbm, "traffic": None, "algorithmic_bytes": mb["bytes"],
+                         "us_per_launch": mb["us"], "peak_source": f"{src} hbm_gbs"},
+        }
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(spec, sizes, pos_h, species_h, sys_ptr_h, e_t_h, f_t_h, model)
         print(json.dumps(line), flush=True)

@@ -1,0 +1,107 @@
+"""
+Microbenchmarks of the hot kernels, timed with CUDA events.
+
+    python -m create_graph_b200.microbench attn [--n 4096] [--iters 10]
+    python -m create_graph_b200.microbench gemm M N K [--silu]
+
+``attn``: the masked edge-attention microbenchmark: n atoms x 8 heads x 32
+tokens x 32 dims, fp32, q/k/v ~ N(0, 1), bias ~ N(0, 0.1) per (n, h, i, j),
+keys j >= c_n masked with c_n ~ U{8..32}; forward1, backward1 and backward2,
+each against its algorithmic bytes (every operand read or written once).
+``gemm``: one tcgen05 tf32 GEMM shape (bias, optionally the SiLU epilogue).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from create_graph_b200.edge_attn import attn_backward1, attn_backward2, attn_forward1
+from create_graph_b200.gemm import ACT_SILU, gemm
+
+
+def attn_inputs(n: int, h: int = 8, s: int = 32, d: int = 32, seed: int = 0):
+    gen = torch.Generator().manual_seed(seed)
+    q, k, v = (torch.randn(n, h, s, d, generator=gen).cuda() for _ in range(3))
+    bias = (0.1 * torch.randn(n, h, s, s, generator=gen)).cuda()
+    counts = torch.randint(8, s + 1, (n,), generator=gen, dtype=torch.int32).cuda()
+    g, hq, hk, hv = (torch.randn(n, h, s, d, generator=gen).cuda() for _ in range(4))
+    hb = torch.randn(n, h, s, s, generator=gen).cuda()
+    return q, k, v, bias, counts, g, hq, hk, hv, hb, d**-0.5
+
+
+def attn_algorithmic_bytes(n: int, h: int = 8, s: int = 32, d: int = 32) -> dict[str, int]:
+    t, tb, lse = n * h * s * d * 4, n * h * s * s * 4, n * h * s * 4
+    return {
+        "fwd1": 3 * t + tb + t + lse,
+        "bwd1": 4 * t + tb + lse + 3 * t + tb,
+        "bwd2": 7 * t + 2 * tb + lse + 4 * t + tb,
+    }
+
+
+def _time(fn, iters: int) -> float:
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    return sorted(times)[len(times) // 2]
+
+
+def attn(n: int = 4096, iters: int = 10, hbm_gbs: float | None = None, which=("fwd1", "bwd1", "bwd2")) -> dict:
+    """Median launch time and achieved GB/s of each kernel at (n, 8, 32, 32)."""
+    q, k, v, bias, counts, g, hq, hk, hv, hb, scale = attn_inputs(n)
+    _, lse = attn_forward1(q, k, v, bias, scale, counts)
+    fns = {
+        "fwd1": lambda: attn_forward1(q, k, v, bias, scale, counts),
+        "bwd1": lambda: attn_backward1(q, k, v, bias, lse, g, scale, counts),
+        "bwd2": lambda: attn_backward2(q, k, v, bias, lse, g, scale, hq, hk, hv, hb, counts),
+    }
+    nbytes = attn_algorithmic_bytes(n)
+    out = {}
+    for name in which:
+        ms = _time(fns[name], iters)
+        gbs = nbytes[name] / (ms / 1e3) / 1e9
+        out[name] = {"us": ms * 1e3, "bytes": nbytes[name], "gb_s": gbs}
+        if hbm_gbs:
+            out[name]["frac"] = gbs / hbm_gbs
+    return out
+
+
+def gemm_bench(m: int, n: int, k: int, silu: bool = False, iters: int = 20) -> dict:
+    a = torch.randn(m, k, device="cuda")
+    b = torch.randn(n, k, device="cuda")
+    bias = torch.randn(n, device="cuda")
+    kw = {"bias": bias}
+    if silu:
+        kw.update(act=ACT_SILU, aux_out=torch.empty(m, n, device="cuda"))
+    ms = _time(lambda: gemm(a, b, **kw), iters)
+    return {"shape": [m, n, k], "silu": silu, "us": ms * 1e3, "tflops": 2 * m * n * k / (ms / 1e3) / 1e12}
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    sub = parser.add_subparsers(dest="what", required=True)
+    p_attn = sub.add_parser("attn")
+    p_attn.add_argument("--n", type=int, default=4096)
+    p_attn.add_argument("--iters", type=int, default=10)
+    p_gemm = sub.add_parser("gemm")
+    p_gemm.add_argument("shape", type=int, nargs=3)
+    p_gemm.add_argument("--silu", action="store_true")
+    args = parser.parse_args()
+    if args.what == "attn":
+        print(json.dumps(attn(args.n, args.iters)))
+    else:
+        print(json.dumps(gemm_bench(*args.shape, silu=args.silu)))
+
+
+if __name__ == "__main__":
+    main()
