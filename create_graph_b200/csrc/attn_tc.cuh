@@ -129,6 +129,38 @@ __device__ inline void load_op(float* s, const cg_mat& m, int64_t n, int64_t h, 
   }
 }
 
+// Asynchronous version of load_op for the aligned layout: 16-byte cp.async
+// copies (rows past k zero-filled by a source size of 0), completed by
+// cp_async_wait<N>() + __syncthreads() before use. Unaligned layouts fall back
+// to load_op.
+__device__ inline void cp_async16(void* dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ inline void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ inline void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <int DP>
+__device__ inline void load_op_async(float* s, const cg_mat& m, int64_t n, int64_t h, int k, int d, bool vec) {
+  if (!vec) {
+    load_op<DP>(s, m, n, h, k, d, false);
+    return;
+  }
+  constexpr int LD = DP + 4;
+  constexpr int VPR = DP / 4;
+  const float* base = reinterpret_cast<const float*>(m.ptr) + n * m.sn + h * m.sh;
+  for (int f = threadIdx.x; f < KP * VPR; f += kThreads) {
+    const int r = f / VPR, c = (f % VPR) * 4;
+    const float* src = r < k ? base + (int64_t)r * m.sr + c : base;
+    cp_async16(s + r * LD + c, src, r < k ? 16 : 0);
+  }
+}
+
 // k x k tile of a broadcastable bias (zeros outside [0,k)^2 or without bias).
 __device__ inline void load_bias(float* s, const cg_bias& b, int64_t n, int64_t h, int k) {
   for (int f = threadIdx.x; f < KP * KP; f += kThreads) {
@@ -287,10 +319,13 @@ __global__ void __launch_bounds__(kThreads) fwd1_tc(const Params P) {
   for (int64_t s = blockIdx.x; s < a.n * a.h; s += gridDim.x) {
     const int64_t n = s / a.h, h = s % a.h;
     __syncthreads();
-    load_op<DP>(sQ, a.q, n, h, k, d, P.vec_ok);
-    load_op<DP>(sK, a.k_, n, h, k, d, P.vec_ok);
-    load_op<DP>(sV, a.v, n, h, k, d, P.vec_ok);
+    load_op_async<DP>(sQ, a.q, n, h, k, d, P.vec_ok);
+    load_op_async<DP>(sK, a.k_, n, h, k, d, P.vec_ok);
+    cp_async_commit();
+    load_op_async<DP>(sV, a.v, n, h, k, d, P.vec_ok);
+    cp_async_commit();
     load_bias(sP, a.bias, n, h, k);
+    cp_async_wait<1>();
     __syncthreads();
     const int kc = valid_keys(P, n);
     const int band = warp;
@@ -299,6 +334,8 @@ __global__ void __launch_bounds__(kThreads) fwd1_tc(const Params P) {
     band_mma<4, DP / 8>(S, [&](int m, int kk) { return sQ[(band * 16 + m) * L::LD + kk]; },
                         [&](int kk, int j) { return sK[j * L::LD + kk]; }, g, t);
     band_softmax(p, S, sP, band, g, t, scale, kc, nullptr, lse);
+    cp_async_wait<0>();
+    __syncthreads();
     __syncwarp();
     put_band(sP, p, band, g, t);
     __syncwarp();
@@ -335,12 +372,15 @@ __global__ void __launch_bounds__(kThreads) bwd1_tc(const Params P) {
   for (int64_t s = blockIdx.x; s < a.n * a.h; s += gridDim.x) {
     const int64_t n = s / a.h, h = s % a.h;
     __syncthreads();
-    load_op<DP>(sQ, a.q, n, h, k, d, P.vec_ok);
-    load_op<DP>(sK, a.k_, n, h, k, d, P.vec_ok);
-    load_op<DP>(sV, a.v, n, h, k, d, P.vec_ok);
-    load_op<DP>(sG, a.grad_out, n, h, k, d, P.vec_ok);
+    load_op_async<DP>(sQ, a.q, n, h, k, d, P.vec_ok);
+    load_op_async<DP>(sK, a.k_, n, h, k, d, P.vec_ok);
+    cp_async_commit();
+    load_op_async<DP>(sV, a.v, n, h, k, d, P.vec_ok);
+    load_op_async<DP>(sG, a.grad_out, n, h, k, d, P.vec_ok);
+    cp_async_commit();
     load_bias(sGL, a.bias, n, h, k);
     if (threadIdx.x < KP) sLse[threadIdx.x] = threadIdx.x < k ? reinterpret_cast<const float*>(a.lse)[s * k + threadIdx.x] : 0.0f;
+    cp_async_wait<1>();
     __syncthreads();
     const int kc = valid_keys(P, n);
     const int band = warp;
@@ -350,6 +390,8 @@ __global__ void __launch_bounds__(kThreads) bwd1_tc(const Params P) {
       band_mma<4, DP / 8>(S, [&](int m, int kk) { return sQ[(band * 16 + m) * L::LD + kk]; },
                           [&](int kk, int j) { return sK[j * L::LD + kk]; }, g, t);
       band_softmax(p, S, sGL, band, g, t, scale, kc, sLse, lse);
+      cp_async_wait<0>();
+      __syncthreads();
       float GP[4][4];
       zero(GP);
       band_mma<4, DP / 8>(GP, [&](int m, int kk) { return sG[(band * 16 + m) * L::LD + kk]; },
@@ -411,16 +453,22 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
   for (int64_t s = blockIdx.x; s < a.n * a.h; s += gridDim.x) {
     const int64_t n = s / a.h, h = s % a.h;
     __syncthreads();
-    load_op<DP>(sQ, a.q, n, h, k, d, P.vec_ok);
-    load_op<DP>(sK, a.k_, n, h, k, d, P.vec_ok);
-    load_op<DP>(sV, a.v, n, h, k, d, P.vec_ok);
-    load_op<DP>(sG, a.grad_out, n, h, k, d, P.vec_ok);
-    load_op<DP>(sHQ, a.hq, n, h, k, d, P.vec_ok);
-    load_op<DP>(sHK, a.hk, n, h, k, d, P.vec_ok);
-    load_op<DP>(sHV, a.hv, n, h, k, d, P.vec_ok);
+    // operands in the order the products need them, four cp.async groups
+    load_op_async<DP>(sQ, a.q, n, h, k, d, P.vec_ok);
+    load_op_async<DP>(sK, a.k_, n, h, k, d, P.vec_ok);
+    cp_async_commit();
+    load_op_async<DP>(sG, a.grad_out, n, h, k, d, P.vec_ok);
+    load_op_async<DP>(sV, a.v, n, h, k, d, P.vec_ok);
+    cp_async_commit();
+    load_op_async<DP>(sHQ, a.hq, n, h, k, d, P.vec_ok);
+    load_op_async<DP>(sHK, a.hk, n, h, k, d, P.vec_ok);
+    cp_async_commit();
+    load_op_async<DP>(sHV, a.hv, n, h, k, d, P.vec_ok);
+    cp_async_commit();
     load_bias(sGL, a.bias, n, h, k);
     load_bias(sDS, a.hb, n, h, k);
     if (threadIdx.x < KP) sLse[threadIdx.x] = threadIdx.x < k ? reinterpret_cast<const float*>(a.lse)[s * k + threadIdx.x] : 0.0f;
+    cp_async_wait<3>();
     __syncthreads();
     const int kc = valid_keys(P, n);
     const int band = warp;
@@ -430,6 +478,8 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
       band_mma<4, DP / 8>(A, [&](int m, int kk) { return sQ[(band * 16 + m) * L::LD + kk]; },
                           [&](int kk, int j) { return sK[j * L::LD + kk]; }, g, t);
       band_softmax(p, A, sGL, band, g, t, scale, kc, sLse, lse);
+      cp_async_wait<2>();
+      __syncthreads();
       zero(B);  // grad_probs = grad_out v^T
       band_mma<4, DP / 8>(B, [&](int m, int kk) { return sG[(band * 16 + m) * L::LD + kk]; },
                           [&](int kk, int j) { return sV[j * L::LD + kk]; }, g, t);
@@ -440,6 +490,8 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
       for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) cen[nt][e] = B[nt][e] - rs[e >> 1];
+      cp_async_wait<1>();
+      __syncthreads();
       zero(A);  // d_logits = scale * (hq k^T + q hk^T) + hb
       band_mma<4, DP / 8>(A, [&](int m, int kk) { return sHQ[(band * 16 + m) * L::LD + kk]; },
                           [&](int kk, int j) { return sK[j * L::LD + kk]; }, g, t);
@@ -452,6 +504,8 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
           A[nt][e] = scale * A[nt][e] + sDS[(band * 16 + frag_row(g, e)) * LDP + frag_col(nt, t, e)];
       float drs[2];
       row_dot(drs, A, p);
+      cp_async_wait<0>();
+      __syncthreads();
       zero(B);  // grad_out hv^T
       band_mma<4, DP / 8>(B, [&](int m, int kk) { return sG[(band * 16 + m) * L::LD + kk]; },
                           [&](int kk, int j) { return sHV[j * L::LD + kk]; }, g, t);

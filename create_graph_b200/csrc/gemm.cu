@@ -1,14 +1,17 @@
 // Dense projections on the 5th-generation tensor cores: C = epilogue(A . B^T)
 // with kind::tf32 UMMA (fp32 in, fp32 accumulate in TMEM).
 //
-// One CTA computes one BM x BN tile (BM = 128, BN in {64, 128, 256}):
+// Persistent: one CTA per SM walks the BM x BN output tiles (BM = 128,
+// BN in {16, 32, 64, 128, 256}) and k-splits:
 //   warp 0        TMA producer: A and B k-slices of 32 fp32 (128 B, 128B
 //                 swizzle) into a ring of STAGES shared-memory stages;
-//   warp 1        allocates TMEM; one thread issues 4 UMMAs (K = 8) per stage
-//                 and commits each stage back to the producer;
+//   warp 1        allocates TMEM (two accumulators); one thread issues 4 UMMAs
+//                 (K = 8) per stage and commits each stage back to the producer
+//                 and each finished accumulator to the epilogue;
 //   warps 2..5    epilogue: tcgen05.ld of the accumulator (one TMEM lane =
-//                 one output row per thread), bias / SiLU / SiLU-derivative /
-//                 accumulate, and stores.
+//                 one output row per thread), a shared-memory transpose,
+//                 bias / SiLU / SiLU-derivative / accumulate and coalesced
+//                 stores, overlapping the next tile's UMMAs.
 // A and B are each either K-major (rows contiguous along K) or MN-major
 // (contiguous along M / N), so the forward (x W^T), the data gradient (g W)
 // and the weight gradient (g^T x) all read their operands in place.
@@ -32,6 +35,7 @@ using namespace cg::sm100;
 constexpr int BM = 128;
 constexpr int BK = 32;  // fp32 elements per k-slice: one 128-byte swizzle row
 constexpr int kThreads = 192;
+constexpr int kStagePitch = 36;  // floats per staged row: 16-byte rows, conflict-free 128-bit access
 
 struct Epilogue {
   float* c;
@@ -43,6 +47,7 @@ struct Epilogue {
   int act;              // CG_ACT_*
   int accumulate;       // C += result
   float alpha;
+  int vec;              // 16-byte column groups: N, ldc, ld_aux multiples of 4, pointers aligned
 };
 
 __device__ inline float silu(float z) { return z / (1.0f + expf(-z)); }
@@ -57,8 +62,9 @@ struct Smem {
   static constexpr int kB = BN * BK * 4;
   static constexpr int kStage = kA + kB;
   static constexpr int kTiles = STAGES * kStage;
-  static constexpr int kBytes = kTiles + 1024 /*alignment*/ + 256 /*barriers*/;
-  static_assert(kStage >= 4 * 32 * 33 * 4, "epilogue staging must fit in one stage");
+  static constexpr int kStaging = 4 * 32 * kStagePitch * 4;  // epilogue transpose, one 32 x 36 block per warp
+  static constexpr int kBytes = kTiles + kStaging + 1024 /*alignment*/ + 256 /*barriers*/;
+  static_assert(kBytes <= 227 * 1024, "shared memory budget");
 };
 
 // Epilogue of one output element x = alpha * acc at (row, col).
@@ -76,37 +82,68 @@ __device__ inline void epilogue_store(const Epilogue& ep, int64_t row, int col, 
   *c = x;
 }
 
-// Split-K: CTA z of gridDim.z accumulates k-tiles [z * kt_per, (z+1) * kt_per)
-// and, when `partial` is set, stores its raw fp32 tile to partial[z] (M x N);
-// cg_gemm's reduction pass then adds the splits in z order (deterministic).
+// Epilogue of four consecutive columns (col % 4 == 0, all in range).
+__device__ inline void epilogue_store4(const Epilogue& ep, int64_t row, int col, float4 x, float4 bias) {
+  float v[4] = {x.x * ep.alpha + bias.x, x.y * ep.alpha + bias.y, x.z * ep.alpha + bias.z, x.w * ep.alpha + bias.w};
+  if (ep.act == CG_ACT_SILU) {
+    if (ep.aux_out) *reinterpret_cast<float4*>(ep.aux_out + row * ep.ld_aux + col) = make_float4(v[0], v[1], v[2], v[3]);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = silu(v[e]);
+  } else if (ep.act == CG_ACT_SILU_GRAD) {
+    const float4 z = *reinterpret_cast<const float4*>(ep.aux_in + row * ep.ld_aux + col);
+    v[0] *= silu_grad(z.x);
+    v[1] *= silu_grad(z.y);
+    v[2] *= silu_grad(z.z);
+    v[3] *= silu_grad(z.w);
+  }
+  float4* c = reinterpret_cast<float4*>(ep.c + row * ep.ldc + col);
+  if (ep.accumulate) {
+    const float4 old = *c;
+    v[0] += old.x;
+    v[1] += old.y;
+    v[2] += old.z;
+    v[3] += old.w;
+  }
+  *c = make_float4(v[0], v[1], v[2], v[3]);
+}
+
+// Persistent kernel: CTA b processes work items b, b + gridDim.x, ... where an
+// item is (m-tile, n-tile, k-split z). Split z accumulates k-tiles
+// [z * kt_per, (z+1) * kt_per) and, when `partial` is set, stores its raw fp32
+// tile to partial[z] (M x N); the reduction pass adds the splits in z order.
+// Two TMEM accumulators (2 * BN columns) let the epilogue of item j overlap
+// the UMMAs of item j + 1.
 template <int BN, int STAGES, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                     int M, int N, int K, int kt_per, float* partial, Epilogue ep) {
+                     int M, int N, int K, int kt_per, int splits, float* partial, Epilogue ep) {
   using S = Smem<BN, STAGES>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // tiles need 1024-byte alignment for the 128B swizzle pattern
   unsigned char* tiles = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(tiles + S::kTiles);
+  float* staging = reinterpret_cast<float*>(tiles + S::kTiles);
+  uint64_t* full = reinterpret_cast<uint64_t*>(tiles + S::kTiles + S::kStaging);
   uint64_t* empty = full + STAGES;
-  uint64_t* done = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+  const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + BN - 1) / BN;
   const int ktiles_all = (K + BK - 1) / BK;
-  const int kt_begin = blockIdx.z * kt_per;
-  const int kt_end = kt_begin + kt_per < ktiles_all ? kt_begin + kt_per : ktiles_all;
-  const int ktiles = kt_end - kt_begin;
-  constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
+  const int items = m_tiles * n_tiles * splits;
+  constexpr uint32_t kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(done, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+    }
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
@@ -114,92 +151,145 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  bool ok = true;
+
+  auto item_coords = [&](int w, int& m0, int& n0, int& kt0, int& kt1) {
+    const int mn = m_tiles * n_tiles;
+    const int z = w / mn, t = w % mn;
+    m0 = (t % m_tiles) * BM;
+    n0 = (t / m_tiles) * BN;
+    kt0 = z * kt_per;
+    kt1 = kt0 + kt_per < ktiles_all ? kt0 + kt_per : ktiles_all;
+  };
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer ----------------
     prefetch_tmap(&map_a);
     prefetch_tmap(&map_b);
-    for (int i = 0; i < ktiles && ok; ++i) {
-      const int s = i % STAGES;
-      const uint32_t round = i / STAGES;
-      if (i >= STAGES) ok = mbar_wait(&empty[s], (round - 1) & 1, &g_gemm_error);
-      if (!ok) break;
-      unsigned char* sa = tiles + s * S::kStage;
-      unsigned char* sb = sa + S::kA;
-      mbar_arrive_expect_tx(&full[s], S::kStage);
-      const int k0 = (kt_begin + i) * BK;
-      if (!A_MN) {
-        tma_load_2d(sa, &map_a, &full[s], k0, m0);
-      } else {
+    bool ok = true;
+    uint32_t it = 0;
+    for (int w = blockIdx.x; w < items && ok; w += gridDim.x) {
+      int m0, n0, kt0, kt1;
+      item_coords(w, m0, n0, kt0, kt1);
+      for (int kt = kt0; kt < kt1; ++kt, ++it) {
+        const int s = it % STAGES;
+        const uint32_t round = it / STAGES;
+        if (it >= STAGES && !(ok = mbar_wait(&empty[s], (round - 1) & 1, &g_gemm_error))) break;
+        unsigned char* sa = tiles + s * S::kStage;
+        unsigned char* sb = sa + S::kA;
+        mbar_arrive_expect_tx(&full[s], S::kStage);
+        const int k0 = kt * BK;
+        if (!A_MN) {
+          tma_load_2d(sa, &map_a, &full[s], k0, m0);
+        } else {
 #pragma unroll
-        for (int c = 0; c < BM / 32; ++c) tma_load_2d(sa + c * (BK * 128), &map_a, &full[s], m0 + 32 * c, k0);
-      }
-      if (!B_MN) {
-        tma_load_2d(sb, &map_b, &full[s], k0, n0);
-      } else {
+          for (int c = 0; c < BM / 32; ++c) tma_load_2d(sa + c * (BK * 128), &map_a, &full[s], m0 + 32 * c, k0);
+        }
+        if (!B_MN) {
+          tma_load_2d(sb, &map_b, &full[s], k0, n0);
+        } else {
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c) tma_load_2d(sb + c * (BK * 128), &map_b, &full[s], n0 + 32 * c, k0);
+          for (int c = 0; c < BN / 32; ++c) tma_load_2d(sb + c * (BK * 128), &map_b, &full[s], n0 + 32 * c, k0);
+        }
       }
     }
   } else if (warp == 1 && lane == 0) {
     // ---------------- UMMA issuer ----------------
     constexpr uint32_t idesc = idesc_tf32(BM, BN, A_MN, B_MN);
-    for (int i = 0; i < ktiles && ok; ++i) {
-      const int s = i % STAGES;
-      ok = mbar_wait(&full[s], (i / STAGES) & 1, &g_gemm_error);
-      if (!ok) break;
+    bool ok = true;
+    uint32_t it = 0;
+    int j = 0;
+    for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++j) {
+      int m0, n0, kt0, kt1;
+      item_coords(w, m0, n0, kt0, kt1);
+      const int b = j & 1, use = j >> 1;
+      if (use > 0 && !(ok = mbar_wait(&acc_empty[b], (use - 1) & 1, &g_gemm_error))) break;
       tc_fence_after();
-      const uint32_t sa = smem_u32(tiles + s * S::kStage);
-      const uint32_t sb = sa + S::kA;
+      const uint32_t acc = tmem + b * BN;
+      for (int kt = kt0; kt < kt1; ++kt, ++it) {
+        const int s = it % STAGES;
+        if (!(ok = mbar_wait(&full[s], (it / STAGES) & 1, &g_gemm_error))) break;
+        tc_fence_after();
+        const uint32_t sa = smem_u32(tiles + s * S::kStage);
+        const uint32_t sb = sa + S::kA;
 #pragma unroll
-      for (int kk = 0; kk < BK / 8; ++kk) {
-        // K-major (128B swizzle, 8-row groups at 1024 B): advance 32 bytes
-        // along the row. MN-major (128B swizzle with 32 B granules, 4-row K
-        // groups at 512 B, 32-wide MN groups at BK * 128 B): advance 8 rows.
-        const uint64_t ad = A_MN ? smem_desc(sa + kk * 1024, BK * 128, 512, kSwizzle128BBase32B)
-                                 : smem_desc(sa + kk * 32, 16, 1024, kSwizzle128B);
-        const uint64_t bd = B_MN ? smem_desc(sb + kk * 1024, BK * 128, 512, kSwizzle128BBase32B)
-                                 : smem_desc(sb + kk * 32, 16, 1024, kSwizzle128B);
-        umma_tf32(tmem, ad, bd, idesc, i > 0 || kk > 0);
+        for (int kk = 0; kk < BK / 8; ++kk) {
+          // K-major (128B swizzle, 8-row groups at 1024 B): advance 32 bytes
+          // along the row. MN-major (128B swizzle with 32 B granules, 4-row K
+          // groups at 512 B, 32-wide MN groups at BK * 128 B): advance 8 rows.
+          const uint64_t ad = A_MN ? smem_desc(sa + kk * 1024, BK * 128, 512, kSwizzle128BBase32B)
+                                   : smem_desc(sa + kk * 32, 16, 1024, kSwizzle128B);
+          const uint64_t bd = B_MN ? smem_desc(sb + kk * 1024, BK * 128, 512, kSwizzle128BBase32B)
+                                   : smem_desc(sb + kk * 32, 16, 1024, kSwizzle128B);
+          umma_tf32(acc, ad, bd, idesc, kt > kt0 || kk > 0);
+        }
+        umma_commit(&empty[s]);
       }
-      umma_commit(&empty[s]);
+      umma_commit(&acc_full[b]);
     }
-    umma_commit(done);
   } else if (warp >= 2) {
     // ---------------- epilogue ----------------
     // Each warp owns 32 accumulator rows (its TMEM lane quarter). Per 32-column
-    // chunk: tcgen05.ld (thread = row), transpose through shared memory (the
-    // pipeline stages are free once `done` fired), then store row by row with
-    // the lanes along the columns: every store is one coalesced 128-byte line.
+    // chunk: tcgen05.ld (thread = row), transpose through shared memory, then
+    // store row by row with the lanes along the columns: every store is one
+    // coalesced 128-byte line.
     const int quarter = warp & 3;
-    float* stage = reinterpret_cast<float*>(tiles) + quarter * 32 * 33;
+    float* stage = staging + quarter * 32 * kStagePitch;
     const int64_t mn = (int64_t)M * N;
-    if (mbar_wait(done, 0, &g_gemm_error)) {
+    int j = 0;
+    for (int w = blockIdx.x; w < items; w += gridDim.x, ++j) {
+      int m0, n0, kt0, kt1;
+      item_coords(w, m0, n0, kt0, kt1);
+      const int z = w / (m_tiles * n_tiles);
+      const int b = j & 1, use = j >> 1;
+      if (!mbar_wait(&acc_full[b], use & 1, &g_gemm_error)) break;
       tc_fence_after();
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         float v[32];
-        tmem_load_32(tmem + ((uint32_t)(quarter * 32) << 16) + c0, v);
+        tmem_load_32(tmem + b * BN + ((uint32_t)(quarter * 32) << 16) + c0, v);
+        // row `lane` of the warp's 32 x 32 block, as 8 16-byte stores
 #pragma unroll
-        for (int j = 0; j < 32; ++j) stage[lane * 33 + j] = v[j];
+        for (int q = 0; q < 8; ++q)
+          *reinterpret_cast<float4*>(stage + lane * kStagePitch + 4 * q) =
+              make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
         __syncwarp();
-        const int col = n0 + c0 + lane;
-        const bool col_ok = c0 + lane < BN && col < N;
-#pragma unroll 4
-        for (int r = 0; r < 32; ++r) {
-          const int row = m0 + quarter * 32 + r;
-          if (col_ok && row < M) {
-            const float x = stage[r * 33 + lane];
+        // each store instruction writes 4 full rows of 32 columns (8 lanes x 16 B per row)
+        const int cl = (lane & 7) * 4;
+        const int col = n0 + c0 + cl;
+        if (ep.vec && c0 + cl < BN && col < N) {
+          const float4 bias = ep.bias ? *reinterpret_cast<const float4*>(ep.bias + col) : make_float4(0, 0, 0, 0);
+#pragma unroll 2
+          for (int r = lane >> 3; r < 32; r += 4) {
+            const int row = m0 + quarter * 32 + r;
+            if (row >= M) break;
+            const float4 x = *reinterpret_cast<const float4*>(stage + r * kStagePitch + cl);
             if (partial) {
-              partial[blockIdx.z * mn + (int64_t)row * N + col] = x;
+              *reinterpret_cast<float4*>(partial + z * mn + (int64_t)row * N + col) = x;
             } else {
-              epilogue_store(ep, row, col, x);
+              epilogue_store4(ep, row, col, x, bias);
+            }
+          }
+        } else if (!ep.vec) {
+          // unaligned or ragged outputs: one column per lane, one row per step
+          const int colc = n0 + c0 + lane;
+          const bool ok_c = c0 + lane < BN && colc < N;
+          for (int r = 0; r < 32; ++r) {
+            const int row = m0 + quarter * 32 + r;
+            if (!ok_c || row >= M) continue;
+            const float x = stage[r * kStagePitch + lane];
+            if (partial) {
+              partial[z * mn + (int64_t)row * N + colc] = x;
+            } else {
+              epilogue_store(ep, row, colc, x);
             }
           }
         }
         __syncwarp();
       }
+      // the accumulator may be overwritten once every epilogue warp has read it
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
     }
   }
   tc_fence_before();
@@ -318,6 +408,12 @@ static int launch(const cg_gemm_args& g, const Plan& p, cudaStream_t stream) {
   ep.act = g.act;
   ep.accumulate = g.accumulate;
   ep.alpha = g.alpha;
+  {
+    auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    const bool aux = g.aux_in != nullptr || g.aux_out != nullptr;
+    ep.vec = g.n % 4 == 0 && g.ldc % 4 == 0 && al(g.c) && (g.bias == nullptr || al(g.bias)) &&
+             (!aux || (g.ld_aux % 4 == 0 && al(g.aux_in) && al(g.aux_out)));
+  }
   float* partial = nullptr;
   if (p.splits > 1) {
     CG_REQUIRE(g.workspace != nullptr && g.workspace_bytes >= workspace_bytes(g),
@@ -328,8 +424,11 @@ static int launch(const cg_gemm_args& g, const Plan& p, cudaStream_t stream) {
   using S = Smem<BN, STAGES>;
   auto kernel = gemm_tf32_kernel<BN, STAGES, A_MN, B_MN>;
   CG_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes));
-  dim3 grid((unsigned)ceil_div<int64_t>(g.m, BM), (unsigned)ceil_div<int64_t>(g.n, BN), (unsigned)p.splits);
-  kernel<<<grid, kThreads, S::kBytes, stream>>>(ma, mb, (int)g.m, (int)g.n, (int)g.k, p.kt_per, partial, ep);
+  const int64_t items = ceil_div<int64_t>(g.m, BM) * ceil_div<int64_t>(g.n, BN) * p.splits;
+  CG_REQUIRE(items < (1ll << 31), "gemm: too many tiles");
+  const int grid = (int)(items < sm_count() ? items : sm_count());
+  kernel<<<grid, kThreads, S::kBytes, stream>>>(ma, mb, (int)g.m, (int)g.n, (int)g.k, p.kt_per, p.splits, partial,
+                                                ep);
   CG_LAUNCHED("gemm_tf32");
   if (p.splits > 1) {
     const int64_t mn = g.m * g.n;

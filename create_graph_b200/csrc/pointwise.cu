@@ -30,6 +30,11 @@ __device__ inline float warp_sum(float v) {
   return v;
 }
 
+// 16-byte column vectors: both row-major operands aligned and cols % 4 == 0
+inline bool vec_ok(const float* a, const float* b, int64_t cols) {
+  return (cols & 3) == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0 && (reinterpret_cast<uintptr_t>(b) & 15) == 0;
+}
+
 inline int blocks_for(int64_t n, int threads) {
   const int64_t b = ceil_div<int64_t>(n, threads);
   const int64_t cap = (int64_t)sm_count() * 32;
@@ -176,43 +181,81 @@ __global__ void rownorm_bwd_kernel(const float* __restrict__ x, const float* __r
 // pool:  out[n, c]    = sum_s w[n, s] x[n, s, c]
 // outer: out[n, s, c] = w[n, s] g[n, c]
 // dot:   out[n, s]    = sum_c g[n, c] x[n, s, c]
-__global__ void pool_kernel(const float* __restrict__ x, const float* __restrict__ w, int64_t n,
-                            int k, int64_t cols, float* __restrict__ out) {
-  const int64_t total = n * cols;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / cols, c = i % cols;
-    const float* xr = x + r * k * cols + c;
+// One warp per row n (pool, outer) or per (n, s) pair (dot); lanes walk the
+// columns in 16-byte vectors when cols % 4 == 0, with no per-element division.
+__global__ void pool_kernel(const float* __restrict__ x, const float* __restrict__ w, int64_t n, int k,
+                            int64_t cols, float* __restrict__ out, bool vec) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp; r < n; r += warps) {
+    const float* xr = x + r * k * cols;
     const float* wr = w + r * k;
-    float acc = 0.0f;
-    for (int s = 0; s < k; ++s) acc += wr[s] * xr[(int64_t)s * cols];
-    out[i] = acc;
+    float* dst = out + r * cols;
+    if (vec) {
+      for (int64_t c = lane * 4; c < cols; c += 128) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s = 0; s < k; ++s) {
+          const float ws = __ldg(wr + s);
+          const float4 v = __ldg(reinterpret_cast<const float4*>(xr + (int64_t)s * cols + c));
+          acc.x += ws * v.x; acc.y += ws * v.y; acc.z += ws * v.z; acc.w += ws * v.w;
+        }
+        *reinterpret_cast<float4*>(dst + c) = acc;
+      }
+    } else {
+      for (int64_t c = lane; c < cols; c += 32) {
+        float acc = 0.0f;
+        for (int s = 0; s < k; ++s) acc += wr[s] * xr[(int64_t)s * cols + c];
+        dst[c] = acc;
+      }
+    }
   }
 }
 
 __global__ void outer_kernel(const float* __restrict__ w, const float* __restrict__ g, int64_t n, int k,
-                             int64_t cols, float* __restrict__ out) {
-  const int64_t total = n * k * cols;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t c = i % cols, rs = i / cols, r = rs / k;
-    out[i] = w[rs] * g[r * cols + c];
+                             int64_t cols, float* __restrict__ out, bool vec) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp; r < n; r += warps) {
+    const float* gr = g + r * cols;
+    for (int s = 0; s < k; ++s) {
+      const float ws = __ldg(w + r * k + s);
+      float* dst = out + (r * k + s) * cols;
+      if (vec) {
+        for (int64_t c = lane * 4; c < cols; c += 128) {
+          const float4 v = __ldg(reinterpret_cast<const float4*>(gr + c));
+          *reinterpret_cast<float4*>(dst + c) = make_float4(ws * v.x, ws * v.y, ws * v.z, ws * v.w);
+        }
+      } else {
+        for (int64_t c = lane; c < cols; c += 32) dst[c] = ws * gr[c];
+      }
+    }
   }
 }
 
 __global__ void dot_kernel(const float* __restrict__ g, const float* __restrict__ x, int64_t n, int k,
-                           int64_t cols, float* __restrict__ out) {
+                           int64_t cols, float* __restrict__ out, bool vec) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t rs = warp; rs < n * k; rs += warps) {
-    const int64_t r = rs / k;
-    const float* xr = x + rs * cols;
+  for (int64_t r = warp; r < n; r += warps) {
     const float* gr = g + r * cols;
-    float acc = 0.0f;
-    for (int64_t c = lane; c < cols; c += 32) acc += gr[c] * xr[c];
-    acc = warp_sum(acc);
-    if (lane == 0) out[rs] = acc;
+    for (int s = 0; s < k; ++s) {
+      const float* xr = x + (r * k + s) * cols;
+      float acc = 0.0f;
+      if (vec) {
+        for (int64_t c = lane * 4; c < cols; c += 128) {
+          const float4 a = __ldg(reinterpret_cast<const float4*>(gr + c));
+          const float4 b = __ldg(reinterpret_cast<const float4*>(xr + c));
+          acc += a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+        }
+      } else {
+        for (int64_t c = lane; c < cols; c += 32) acc += gr[c] * xr[c];
+      }
+      acc = warp_sum(acc);
+      if (lane == 0) out[r * k + s] = acc;
+    }
   }
 }
 
@@ -305,7 +348,8 @@ int cg_rownorm_bwd2(const float* x, const float* g, const float* h, int64_t rows
 int cg_pool(const float* x, const float* w, int64_t n, int64_t k, int64_t cols, float* out, void* stream) {
   CG_REQUIRE(n >= 0 && k >= 0 && cols >= 0 && k < (1 << 30), "pool: bad size");
   if (n * cols == 0) return kOk;
-  pw::pool_kernel<<<pw::blocks_for(n * cols, 256), 256, 0, as_stream(stream)>>>(x, w, n, (int)k, cols, out);
+  pw::pool_kernel<<<pw::blocks_for(n * 32, 256), 256, 0, as_stream(stream)>>>(x, w, n, (int)k, cols, out,
+                                                                                     pw::vec_ok(x, out, cols));
   CG_LAUNCHED("pool");
   return kOk;
 }
@@ -314,8 +358,8 @@ int cg_pool_outer(const float* w, const float* g, int64_t n, int64_t k, int64_t 
                   void* stream) {
   CG_REQUIRE(n >= 0 && k >= 0 && cols >= 0 && k < (1 << 30), "pool_outer: bad size");
   if (n * k * cols == 0) return kOk;
-  pw::outer_kernel<<<pw::blocks_for(n * k * cols, 256), 256, 0, as_stream(stream)>>>(w, g, n, (int)k, cols,
-                                                                                     out);
+  pw::outer_kernel<<<pw::blocks_for(n * 32, 256), 256, 0, as_stream(stream)>>>(w, g, n, (int)k, cols, out,
+                                                                                      pw::vec_ok(g, out, cols));
   CG_LAUNCHED("pool_outer");
   return kOk;
 }
@@ -324,7 +368,8 @@ int cg_pool_dot(const float* g, const float* x, int64_t n, int64_t k, int64_t co
                 void* stream) {
   CG_REQUIRE(n >= 0 && k >= 0 && cols >= 0 && k < (1 << 30), "pool_dot: bad size");
   if (n * k == 0) return kOk;
-  pw::dot_kernel<<<pw::blocks_for(n * k * 32, 256), 256, 0, as_stream(stream)>>>(g, x, n, (int)k, cols, out);
+  pw::dot_kernel<<<pw::blocks_for(n * 32, 256), 256, 0, as_stream(stream)>>>(g, x, n, (int)k, cols, out,
+                                                                                    pw::vec_ok(g, x, cols));
   CG_LAUNCHED("pool_dot");
   return kOk;
 }
