@@ -55,7 +55,8 @@ int launch(int which, const cg_edge_attn_args& a, int dbias_mode, int ki, int kj
   P.dbias_mode = dbias_mode;
   P.ki = ki;
   P.kj = kj;
-  P.vec_ok = vec_ok;
+  // 16-byte operand loads need rows of exactly the padded width
+  P.vec_ok = vec_ok && a.d == dp;
   switch (dp) {
     case 8: return launch_dp<8>(which, P, stream);
     case 16: return launch_dp<16>(which, P, stream);
