@@ -2,7 +2,7 @@
 //
 // Same arithmetic as the CUDA-core kernels in edge_attn.cuh (the reference's
 // kernels/edge_attn/ops.py:26-104), organised for mma.sync m16n8k8 tf32 with
-// a three-term split of every operand (x = hi + lo, hi = tf32(x),
+// a three-term split of every operand (x = hi + lo, hi = x truncated to tf32,
 // lo = tf32(x - hi); a*b ~ hi*hi + hi*lo + lo*hi), which keeps fp32-level
 // accuracy (~1e-6 relative) while the products run on the tensor pipe.
 //
@@ -36,19 +36,18 @@ struct Params {
 };
 
 // ---- mma.sync tf32 with a 3-term split ---------------------------------------
-__device__ inline uint32_t to_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
-}
 
 struct Split {
   uint32_t hi, lo;
 };
 
+// hi: x truncated to tf32 (mantissa bits below the 10 kept ones cleared);
+// lo: the exact remainder x - hi rounded to tf32 by adding half an ulp to its
+// bit pattern before clearing. Integer and FADD work only: no conversions.
 __device__ inline Split split(float x) {
-  const uint32_t h = to_tf32(x);
-  return {h, to_tf32(x - __uint_as_float(h))};
+  const uint32_t hi = __float_as_uint(x) & 0xffffe000u;
+  const float rem = x - __uint_as_float(hi);
+  return {hi, (__float_as_uint(rem) + 0x1000u) & 0xffffe000u};
 }
 
 __device__ inline void mma(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
@@ -109,22 +108,45 @@ __device__ inline float quad_max(float v) {
 }
 
 // ---- shared-memory staging -------------------------------------------------------
+// Row r of a slice operand, or null for a zero row: plain rows
+// ptr + n*sn + h*sh + r*sr, or, with the slice's token index staged in shared
+// memory (sidx[r] = token_index[n*k + r]), the gathered row
+// ptr + sidx[r]*sr + h*sh (negative index: zero row).
+__device__ inline const float* op_row(const cg_mat& m, const int32_t* sidx, int64_t n, int64_t h, int r, int k) {
+  if (r >= k) return nullptr;
+  const float* base = reinterpret_cast<const float*>(m.ptr) + h * m.sh;
+  if (sidx == nullptr) return base + n * m.sn + (int64_t)r * m.sr;
+  const int32_t j = sidx[r];
+  return j < 0 ? nullptr : base + (int64_t)j * m.sr;
+}
+
+// Stage the slice's token index in shared memory (all threads; a barrier
+// follows before use). Returns the pointer the loads take, or null.
+__device__ inline const int32_t* stage_index(int32_t* sidx, const int32_t* token_index, int64_t n, int k) {
+  if (token_index == nullptr) return nullptr;
+  if (threadIdx.x < KP) sidx[threadIdx.x] = threadIdx.x < k ? token_index[n * k + threadIdx.x] : -1;
+  __syncthreads();
+  return sidx;
+}
+
 template <int DP>
-__device__ inline void load_op(float* s, const cg_mat& m, int64_t n, int64_t h, int k, int d, bool vec) {
+__device__ inline void load_op(float* s, const cg_mat& m, int64_t n, int64_t h, int k, int d, bool vec,
+                               const int32_t* idx = nullptr) {
   constexpr int LD = DP + 4;
-  const float* base = reinterpret_cast<const float*>(m.ptr) + n * m.sn + h * m.sh;
   if (vec) {
     constexpr int VPR = DP / 4;
     for (int f = threadIdx.x; f < KP * VPR; f += kThreads) {
       const int r = f / VPR, c = (f % VPR) * 4;
+      const float* row = op_row(m, idx, n, h, r, k);
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (r < k) v = __ldg(reinterpret_cast<const float4*>(base + (int64_t)r * m.sr + c));
+      if (row) v = __ldg(reinterpret_cast<const float4*>(row + c));
       *reinterpret_cast<float4*>(s + r * LD + c) = v;
     }
   } else {
     for (int f = threadIdx.x; f < KP * DP; f += kThreads) {
       const int r = f / DP, c = f % DP;
-      s[r * LD + c] = (r < k && c < d) ? base[(int64_t)r * m.sr + c] : 0.0f;
+      const float* row = op_row(m, idx, n, h, r, k);
+      s[r * LD + c] = (row && c < d) ? row[c] : 0.0f;
     }
   }
 }
@@ -146,18 +168,18 @@ __device__ inline void cp_async_wait() {
 }
 
 template <int DP>
-__device__ inline void load_op_async(float* s, const cg_mat& m, int64_t n, int64_t h, int k, int d, bool vec) {
+__device__ inline void load_op_async(float* s, const cg_mat& m, int64_t n, int64_t h, int k, int d, bool vec,
+                                     const int32_t* idx = nullptr) {
   if (!vec) {
-    load_op<DP>(s, m, n, h, k, d, false);
+    load_op<DP>(s, m, n, h, k, d, false, idx);
     return;
   }
   constexpr int LD = DP + 4;
   constexpr int VPR = DP / 4;
-  const float* base = reinterpret_cast<const float*>(m.ptr) + n * m.sn + h * m.sh;
   for (int f = threadIdx.x; f < KP * VPR; f += kThreads) {
     const int r = f / VPR, c = (f % VPR) * 4;
-    const float* src = r < k ? base + (int64_t)r * m.sr + c : base;
-    cp_async16(s + r * LD + c, src, r < k ? 16 : 0);
+    const float* row = op_row(m, idx, n, h, r, k);
+    cp_async16(s + r * LD + c, row ? row + c : reinterpret_cast<const float*>(m.ptr), row ? 16 : 0);
   }
 }
 
@@ -312,6 +334,7 @@ __global__ void __launch_bounds__(kThreads) fwd1_tc(const Params P) {
   float* sK = sQ + L::OP;
   float* sV = sK + L::OP;
   float* sP = sV + L::OP;  // bias tile, then probabilities
+  int32_t* sIdx = reinterpret_cast<int32_t*>(sP + L::KK);
   const cg_edge_attn_args& a = P.a;
   const int k = a.k, d = a.d;
   const float scale = (float)a.scale;
@@ -319,10 +342,11 @@ __global__ void __launch_bounds__(kThreads) fwd1_tc(const Params P) {
   for (int64_t s = blockIdx.x; s < a.n * a.h; s += gridDim.x) {
     const int64_t n = s / a.h, h = s % a.h;
     __syncthreads();
-    load_op_async<DP>(sQ, a.q, n, h, k, d, P.vec_ok);
-    load_op_async<DP>(sK, a.k_, n, h, k, d, P.vec_ok);
+    const int32_t* tix = stage_index(sIdx, a.token_index, n, k);
+    load_op_async<DP>(sQ, a.q, n, h, k, d, P.vec_ok, tix);
+    load_op_async<DP>(sK, a.k_, n, h, k, d, P.vec_ok, tix);
     cp_async_commit();
-    load_op_async<DP>(sV, a.v, n, h, k, d, P.vec_ok);
+    load_op_async<DP>(sV, a.v, n, h, k, d, P.vec_ok, tix);
     cp_async_commit();
     load_bias(sP, a.bias, n, h, k);
     cp_async_wait<1>();
@@ -365,6 +389,7 @@ __global__ void __launch_bounds__(kThreads) bwd1_tc(const Params P) {
   float* sP = sG + L::OP;
   float* sGL = sP + L::KK;  // bias tile, then grad_logits
   float* sLse = sGL + L::KK;
+  int32_t* sIdx = reinterpret_cast<int32_t*>(sLse + KP);
   const cg_edge_attn_args& a = P.a;
   const int k = a.k, d = a.d;
   const float scale = (float)a.scale;
@@ -372,10 +397,11 @@ __global__ void __launch_bounds__(kThreads) bwd1_tc(const Params P) {
   for (int64_t s = blockIdx.x; s < a.n * a.h; s += gridDim.x) {
     const int64_t n = s / a.h, h = s % a.h;
     __syncthreads();
-    load_op_async<DP>(sQ, a.q, n, h, k, d, P.vec_ok);
-    load_op_async<DP>(sK, a.k_, n, h, k, d, P.vec_ok);
+    const int32_t* tix = stage_index(sIdx, a.token_index, n, k);
+    load_op_async<DP>(sQ, a.q, n, h, k, d, P.vec_ok, tix);
+    load_op_async<DP>(sK, a.k_, n, h, k, d, P.vec_ok, tix);
     cp_async_commit();
-    load_op_async<DP>(sV, a.v, n, h, k, d, P.vec_ok);
+    load_op_async<DP>(sV, a.v, n, h, k, d, P.vec_ok, tix);
     load_op_async<DP>(sG, a.grad_out, n, h, k, d, P.vec_ok);
     cp_async_commit();
     load_bias(sGL, a.bias, n, h, k);
@@ -446,6 +472,7 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
   float* sGL = sDG + L::KK;  // bias tile, then grad_logits
   float* sDS = sGL + L::KK;  // hb tile, then d_scores
   float* sLse = sDS + L::KK;
+  int32_t* sIdx = reinterpret_cast<int32_t*>(sLse + KP);
   const cg_edge_attn_args& a = P.a;
   const int k = a.k, d = a.d;
   const float scale = (float)a.scale;
@@ -453,17 +480,18 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
   for (int64_t s = blockIdx.x; s < a.n * a.h; s += gridDim.x) {
     const int64_t n = s / a.h, h = s % a.h;
     __syncthreads();
+    const int32_t* tix = stage_index(sIdx, a.token_index, n, k);
     // operands in the order the products need them, four cp.async groups
-    load_op_async<DP>(sQ, a.q, n, h, k, d, P.vec_ok);
-    load_op_async<DP>(sK, a.k_, n, h, k, d, P.vec_ok);
+    load_op_async<DP>(sQ, a.q, n, h, k, d, P.vec_ok, tix);
+    load_op_async<DP>(sK, a.k_, n, h, k, d, P.vec_ok, tix);
     cp_async_commit();
     load_op_async<DP>(sG, a.grad_out, n, h, k, d, P.vec_ok);
-    load_op_async<DP>(sV, a.v, n, h, k, d, P.vec_ok);
+    load_op_async<DP>(sV, a.v, n, h, k, d, P.vec_ok, tix);
     cp_async_commit();
-    load_op_async<DP>(sHQ, a.hq, n, h, k, d, P.vec_ok);
-    load_op_async<DP>(sHK, a.hk, n, h, k, d, P.vec_ok);
+    load_op_async<DP>(sHQ, a.hq, n, h, k, d, P.vec_ok, tix);
+    load_op_async<DP>(sHK, a.hk, n, h, k, d, P.vec_ok, tix);
     cp_async_commit();
-    load_op_async<DP>(sHV, a.hv, n, h, k, d, P.vec_ok);
+    load_op_async<DP>(sHV, a.hv, n, h, k, d, P.vec_ok, tix);
     cp_async_commit();
     load_bias(sGL, a.bias, n, h, k);
     load_bias(sDS, a.hb, n, h, k);
@@ -573,9 +601,9 @@ template <int DP>
 inline int smem_bytes(int which) {
   using L = Layout<DP>;
   switch (which) {
-    case 0: return (3 * L::OP + L::KK) * 4;
-    case 1: return (4 * L::OP + 2 * L::KK + KP) * 4;
-    default: return (7 * L::OP + 4 * L::KK + KP) * 4;
+    case 0: return (3 * L::OP + L::KK + KP) * 4;
+    case 1: return (4 * L::OP + 2 * L::KK + 2 * KP) * 4;
+    default: return (7 * L::OP + 4 * L::KK + 2 * KP) * 4;
   }
 }
 

@@ -37,6 +37,7 @@ static int run(Which w, const cg_edge_attn_args* args, void* stream) {
         (rc = check_mat(a.hv, "hv", true)) || (rc = check_mat(a.dgrad_out, "dgrad_out", true)))
       return rc;
   }
+  CG_REQUIRE(a.token_index == nullptr || a.dtype == CG_F32, "edge_attn: token_index needs float32");
   Params P;
   P.a = a;
   const int es = a.dtype == CG_F32 ? 4 : 8;

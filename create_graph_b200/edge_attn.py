@@ -230,9 +230,12 @@ def edge_attention(q, k, v, bias, scale: float) -> Tensor:
 
 
 # ---------------------------------------------------------------------------
-# Token layout of the energy network: per atom n, k edge tokens, each row of
-# tok (n*k, 3*h*d) holding [q | k | v] with heads contiguous; the per-key
-# bias is (n*k, h); keys j >= counts[n] are masked.
+# Token layout of the energy network: per atom n, k edge tokens; token (n, s)
+# holds [q | k | v] (heads contiguous) of atom index[n*k + s], read by the
+# kernels straight from the per-atom qkv rows (n_atoms, 3*h*d) through the
+# index (no materialised token tensor). The per-key bias is (n*k, h); keys
+# j >= counts[n] are masked. Token-level outputs (attention output, its
+# gradient, and the per-token q/k/v gradients) are (n, k, ...) tensors.
 # ---------------------------------------------------------------------------
 
 
@@ -244,29 +247,40 @@ def _token_mats(t: Tensor, n: int, k: int, heads: int, d: int, parts: int):
     return [native.Mat(t.data_ptr() + p * c * esz, k * width, d, width) for p in range(parts)]
 
 
+def _atom_mats(t: Tensor, heads: int, d: int):
+    """cg_mat views of q, k, v in per-atom rows (n_atoms, 3*h*d), read through the token index."""
+    c = heads * d
+    esz = t.element_size()
+    return [native.Mat(t.data_ptr() + p * c * esz, 0, d, 3 * c) for p in range(3)]
+
+
 def _token_bias(t: Tensor | None, k: int, heads: int) -> native.Bias:
     if t is None:
         return native.Bias(None, 0, 0, 0, 0)
     return native.Bias(t.data_ptr(), k * heads, 1, 0, heads)
 
 
-def _token_args(tok: Tensor, bias: Tensor, counts: Tensor, heads: int, scale: float):
-    native.require_cuda(tok, bias, counts)
-    if tok.dtype != torch.float32 or bias.dtype != torch.float32 or counts.dtype != torch.int32:
-        raise NativeError("token attention: tok and bias float32, counts int32")
+def _gathered_args(qkv: Tensor, bias: Tensor, index: Tensor, counts: Tensor, k: int, heads: int, scale: float):
+    native.require_cuda(qkv, bias, counts, index)
+    if qkv.dtype != torch.float32 or bias.dtype != torch.float32:
+        raise NativeError("token attention: qkv and bias must be float32")
+    if counts.dtype != torch.int32 or index.dtype != torch.int32:
+        raise NativeError("token attention: counts and index must be int32")
     n = counts.shape[0]
-    k = tok.shape[0] // max(n, 1)
-    d = tok.shape[1] // (3 * heads)
-    if tok.shape[0] != n * k or tok.shape[1] != 3 * heads * d or bias.shape[0] != n * k or bias.shape[-1] != heads:
-        raise NativeError(f"token attention: tok {tuple(tok.shape)}, bias {tuple(bias.shape)}, counts {n}")
+    d = qkv.shape[1] // (3 * heads)
+    if qkv.shape[1] != 3 * heads * d or index.numel() != n * k or bias.shape[0] != n * k or bias.shape[-1] != heads:
+        raise NativeError(
+            f"token attention: qkv {tuple(qkv.shape)}, bias {tuple(bias.shape)}, index {index.numel()}, n {n}, k {k}"
+        )
     a = native.EdgeAttnArgs()
     a.n, a.h, a.k, a.d = n, heads, k, d
     a.dtype = native.F32
     a.scale = float(scale)
     a.key_count = counts.data_ptr()
-    a.q, a.k_, a.v = _token_mats(tok, n, k, heads, d, 3)
+    a.token_index = index.data_ptr()
+    a.q, a.k_, a.v = _atom_mats(qkv, heads, d)
     a.bias = _token_bias(bias, k, heads)
-    return a, n, k, d
+    return a, n, d
 
 
 def _info(a) -> tuple[int, int, int, int]:
@@ -277,44 +291,49 @@ def _run(fn: str, a, device) -> None:
     native.invoke(fn, ctypes.byref(a), native.stream_ptr(device), info=_info(a))
 
 
-def token_attention_forward1(tok, bias, counts, heads, scale):
-    tok, bias = tok.contiguous(), bias.contiguous()
-    a, n, k, d = _token_args(tok, bias, counts, heads, scale)
-    out = torch.empty(n, k, heads * d, device=tok.device)
-    lse = torch.empty(n, heads, k, device=tok.device)
+def token_attention_forward1(qkv, bias, index, counts, k, heads, scale):
+    """(out (n, k, h*d), lse (n, h, k)) of the gathered tokens."""
+    qkv, bias = qkv.contiguous(), bias.contiguous()
+    a, n, d = _gathered_args(qkv, bias, index, counts, k, heads, scale)
+    out = torch.empty(n, k, heads * d, device=qkv.device)
+    lse = torch.empty(n, heads, k, device=qkv.device)
     (a.out,) = _token_mats(out, n, k, heads, d, 1)
     a.lse = lse.data_ptr()
-    _run("cg_edge_attn_fwd1", a, tok.device)
+    _run("cg_edge_attn_fwd1", a, qkv.device)
     return out, lse
 
 
-def token_attention_backward1(tok, bias, lse, g, counts, heads, scale):
-    tok, bias, g = tok.contiguous(), bias.contiguous(), g.contiguous()
-    a, n, k, d = _token_args(tok, bias, counts, heads, scale)
+def token_attention_backward1(qkv, bias, lse, g, index, counts, k, heads, scale):
+    """(dtok (n*k, 3*h*d) per-token q/k/v gradients, dbias (n*k, h))."""
+    qkv, bias, g = qkv.contiguous(), bias.contiguous(), g.contiguous()
+    a, n, d = _gathered_args(qkv, bias, index, counts, k, heads, scale)
     a.lse = lse.data_ptr()
     (a.grad_out,) = _token_mats(g, n, k, heads, d, 1)
-    dtok = torch.empty_like(tok)
+    dtok = torch.empty(n * k, qkv.shape[1], device=qkv.device)
     dbias = torch.empty_like(bias)
     a.dq, a.dk, a.dv = _token_mats(dtok, n, k, heads, d, 3)
     a.dbias = _token_bias(dbias, k, heads)
-    _run("cg_edge_attn_bwd1", a, tok.device)
+    _run("cg_edge_attn_bwd1", a, qkv.device)
     return dtok, dbias
 
 
-def token_attention_backward2(tok, bias, lse, g, h_tok, h_bias, counts, heads, scale):
-    tok, bias, g, h_tok = tok.contiguous(), bias.contiguous(), g.contiguous(), h_tok.contiguous()
-    a, n, k, d = _token_args(tok, bias, counts, heads, scale)
+def token_attention_backward2(qkv, bias, lse, g, h_qkv, h_bias, index, counts, k, heads, scale):
+    """Second derivative: per-token (dtok, dbias, dg) for the per-atom
+    cotangent h_qkv of the q/k/v gradient (read through the same index) and
+    the cotangent h_bias of dbias."""
+    qkv, bias, g, h_qkv = qkv.contiguous(), bias.contiguous(), g.contiguous(), h_qkv.contiguous()
+    a, n, d = _gathered_args(qkv, bias, index, counts, k, heads, scale)
     a.lse = lse.data_ptr()
     (a.grad_out,) = _token_mats(g, n, k, heads, d, 1)
-    a.hq, a.hk, a.hv = _token_mats(h_tok, n, k, heads, d, 3)
+    a.hq, a.hk, a.hv = _atom_mats(h_qkv, heads, d)
     if h_bias is not None:
         h_bias = h_bias.contiguous()
         a.hb = _token_bias(h_bias, k, heads)
-    dtok = torch.empty_like(tok)
+    dtok = torch.empty(n * k, qkv.shape[1], device=qkv.device)
     dbias = torch.empty_like(bias)
     dg = torch.empty_like(g)
     a.dq, a.dk, a.dv = _token_mats(dtok, n, k, heads, d, 3)
     a.dbias = _token_bias(dbias, k, heads)
     (a.dgrad_out,) = _token_mats(dg, n, k, heads, d, 1)
-    _run("cg_edge_attn_bwd2", a, tok.device)
+    _run("cg_edge_attn_bwd2", a, qkv.device)
     return dtok, dbias, dg

@@ -8,7 +8,7 @@ here and the CPU oracle in oracle/step.py, which restates it in plain torch.
     species embedding                               h (n, C)
     per block (x n_blocks):
         x   = LN(h);  qkv = x Wqkv^T + b            (n, 3C)       tcgen05 GEMM
-        tok = qkv[nbr]                              (n*k, 3C)     CSR gather
+        tok = qkv[nbr]  (read in place by the attention kernels through the index)
         bias = rbf Wb^T + bb                        (n*k, H)      per-key RBF bias
         o   = attention among the k tokens of each atom, keys past counts masked
         m   = sum_s env[i, s] o[i, s]               (n, C)        envelope pooling
@@ -81,9 +81,8 @@ class Block(nn.Module):
 
     def forward(self, h: Tensor, rbf: Tensor, env: Tensor, graph: cgnn.NeighborGraph) -> Tensor:
         n = h.shape[0]
-        tok = cgnn.Gather.apply(self.qkv(self.norm1(h)), graph.tokens)
         bias = self.rbf_bias(rbf)
-        o = cgnn.TokenAttention.apply(tok, bias, graph.counts, self.heads, self.scale)
+        o = cgnn.TokenAttention.apply(self.qkv(self.norm1(h)), bias, graph, self.heads, self.scale)
         m = cgnn.Pool.apply(o, env.view(n, graph.k))
         h = h + self.out(m)
         return h + self.ffn2(self.ffn1(self.norm2(h)))

@@ -63,6 +63,7 @@ class EdgeAttnArgs(ctypes.Structure):
         ("dbias", Bias),
         ("dgrad_out", Mat),
         ("scratch", vp),
+        ("token_index", vp),
     ]
 
 

@@ -531,45 +531,51 @@ class EdgeGeometryGrad(_Fused):
 class TokenAttention(_Fused):
     """Attention among the k edge tokens of each atom.
 
-    tok (n*k, 3*h*d) holds [q | k | v] per token (heads contiguous), bias
-    (n*k, h) the per-key additive bias, counts (n,) the valid keys per atom.
-    Returns the token outputs (n, k, h*d), heads concatenated.
+    Token (n, s) is [q | k | v] of atom graph.tokens.index[n*k + s], read by
+    the kernels straight from the per-atom qkv rows (n_atoms, 3*h*d); bias
+    (n*k, h) is the per-key additive bias and keys past graph.counts[n] are
+    masked. Returns the token outputs (n, k, h*d), heads concatenated. The
+    per-token q/k/v gradients are reduced to atoms by the deterministic CSR
+    segment sum (the transpose of the gather).
     """
 
     @staticmethod
-    def forward(ctx, tok, bias, counts, heads, scale):
-        out, lse = token_attention_forward1(tok, bias, counts, heads, scale)
-        ctx.save_for_backward(tok, bias, lse)
-        ctx.meta = (counts, heads, scale)
+    def forward(ctx, qkv, bias, graph, heads, scale):
+        meta = (graph, heads, scale)
+        out, lse = token_attention_forward1(qkv, bias, graph.tokens.index, graph.counts, graph.k, heads, scale)
+        ctx.save_for_backward(qkv, bias, lse)
+        ctx.meta = meta
         return out
 
     @staticmethod
     def backward(ctx, g):
-        tok, bias, lse = ctx.saved_tensors
-        counts, heads, scale = ctx.meta
-        dtok, dbias = TokenAttentionGrad.apply(tok, bias, lse, g, ctx.meta)
-        return dtok, dbias, None, None, None
+        qkv, bias, lse = ctx.saved_tensors
+        d_qkv, dbias = TokenAttentionGrad.apply(qkv, bias, lse, g, ctx.meta)
+        return d_qkv, dbias, None, None, None
 
 
 class TokenAttentionGrad(_Fused):
-    """backward1 of TokenAttention; its backward is the backward2 kernel."""
+    """backward1 of TokenAttention (per-atom q/k/v and bias gradients); its
+    backward is the backward2 kernel followed by the same segment sum."""
 
     @staticmethod
-    def forward(ctx, tok, bias, lse, g, meta):
-        counts, heads, scale = meta
-        dtok, dbias = token_attention_backward1(tok, bias, lse, g, counts, heads, scale)
-        ctx.save_for_backward(tok, bias, lse, g)
+    def forward(ctx, qkv, bias, lse, g, meta):
+        graph, heads, scale = meta
+        dtok, dbias = token_attention_backward1(qkv, bias, lse, g, graph.tokens.index, graph.counts, graph.k,
+                                                heads, scale)
+        ctx.save_for_backward(qkv, bias, lse, g)
         ctx.meta = meta
-        return dtok, dbias
+        return segment_sum_raw(dtok, graph.tokens), dbias
 
     @staticmethod
-    def backward(ctx, h_tok, h_bias):
-        tok, bias, lse, g = ctx.saved_tensors
-        counts, heads, scale = ctx.meta
-        if h_tok is None:
-            h_tok = torch.zeros_like(tok)
-        dtok, dbias, dg = token_attention_backward2(tok, bias, lse, g, h_tok, h_bias, counts, heads, scale)
-        return dtok, dbias, None, dg, None
+    def backward(ctx, h_qkv, h_bias):
+        qkv, bias, lse, g = ctx.saved_tensors
+        graph, heads, scale = ctx.meta
+        if h_qkv is None:
+            h_qkv = torch.zeros_like(qkv)
+        dtok, dbias, dg = token_attention_backward2(qkv, bias, lse, g, h_qkv, h_bias, graph.tokens.index,
+                                                    graph.counts, graph.k, heads, scale)
+        return segment_sum_raw(dtok, graph.tokens), dbias, None, dg, None
 
 
 # ---------------------------------------------------------------------------

@@ -78,6 +78,11 @@ typedef struct cg_edge_attn_args {
   cg_bias dbias;          /* bwd1, bwd2; strides of broadcast dims ignored; NULL = skip */
   cg_mat dgrad_out;       /* bwd2 */
   void* scratch;          /* cg_edge_attn_scratch_bytes() bytes, or NULL if that is 0 */
+  /* optional (n, k) token index (float32 only): when set, row r of q, k, v,
+   * hq, hk, hv for slice (n, h) is read at ptr + token_index[n*k + r]*sr + h*sh
+   * (sn unused; index < 0 reads zeros): the kernels gather the edge tokens
+   * from per-atom rows instead of a materialised (n*k, ...) token tensor. */
+  const int32_t* token_index;
 } cg_edge_attn_args;
 
 /* Replaces EdgeAttention.forward1 (kernels/edge_attn/ops.py:64-68, with

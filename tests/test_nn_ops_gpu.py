@@ -121,26 +121,31 @@ def test_edge_geometry():
     check(twice_errors(mine, ref, [pos]), F32_TOL)
 
 
-def ref_token_attention(tok, bias, counts, heads, scale):
+def ref_token_attention(qkv, bias, index, counts, heads, scale):
     n = counts.shape[0]
-    k = tok.shape[0] // n
-    d = tok.shape[1] // (3 * heads)
+    k = index.numel() // n
+    d = qkv.shape[1] // (3 * heads)
+    valid = (index >= 0)[:, None].to(qkv.dtype)
+    tok = qkv[index.clamp_min(0).long()] * valid
     t = tok.view(n, k, 3, heads, d)
     q, kk, v = (t[:, :, i].permute(0, 2, 1, 3) for i in range(3))
     b = bias.view(n, k, heads).permute(0, 2, 1)[:, :, None, :]
     mask = torch.arange(k, device=tok.device)[None, :] >= counts[:, None].long()
     b = b.masked_fill(mask[:, None, None, :], -torch.inf)
     logits = q @ kk.transpose(-1, -2) * scale + b
-    p = torch.softmax(logits, -1).nan_to_num(0.0)
+    row_ok = (~mask).any(-1)[:, None, None, None]  # atoms without neighbours give zeros
+    p = torch.softmax(torch.where(row_ok, logits, torch.zeros_like(logits)), -1) * row_ok
     return (p @ v).permute(0, 2, 1, 3).reshape(n, k, heads * d)
 
 
 def test_token_attention():
-    n, k, heads, d = 24, 30, 4, 16
+    """Tokens gathered from per-atom qkv rows through the neighbour index (padded
+    slots read zeros); per-token gradients reduced back to atoms."""
+    pos, graph = neighbor_case(n=40, k=12)
+    heads, d = 4, 16
     g = torch.Generator().manual_seed(15)
-    tok = torch.randn(n * k, 3 * heads * d, generator=g).cuda()
-    bias = torch.randn(n * k, heads, generator=g).cuda()
-    counts = torch.randint(1, k + 1, (n,), generator=g, dtype=torch.int32).cuda()
-    mine = lambda t, b: cgnn.TokenAttention.apply(t, b, counts, heads, 0.25)  # noqa: E731
-    ref = lambda t, b: ref_token_attention(t, b, counts, heads, 0.25)  # noqa: E731
-    check(twice_errors(mine, ref, [tok, bias]), F32_TOL)
+    qkv = torch.randn(40, 3 * heads * d, generator=g).cuda()
+    bias = torch.randn(40 * 12, heads, generator=g).cuda()
+    mine = lambda q, b: cgnn.TokenAttention.apply(q, b, graph, heads, 0.25)  # noqa: E731
+    ref = lambda q, b: ref_token_attention(q, b, graph.tokens.index, graph.counts, heads, 0.25)  # noqa: E731
+    check(twice_errors(mine, ref, [qkv, bias]), F32_TOL)
