@@ -85,12 +85,68 @@ def edge_attn_fixtures(op) -> dict[str, dict]:
     return cases
 
 
+def mlp_step_fixture(ref_cg) -> dict:
+    """One config-1 training step through the reference's own create_graph:
+    4 molecules x 32 atoms, pos ~ N(0, 1.5 A) from seed 0, each molecule
+    centred eagerly outside the region; per-atom MLP 3 -> 64 -> 64 -> 1 with
+    SiLU inside cg.compile; E = per-molecule sum; loss = MSE(E) + MSE(F),
+    F = -dE/dpos. Float64, default (compiled) backend and exact=True."""
+    from torch import nn
+
+    torch.manual_seed(0)
+
+    class Network(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.l1, self.l2, self.l3 = nn.Linear(3, 64), nn.Linear(64, 64), nn.Linear(64, 1)
+
+        def forward(self, x, mol):
+            h = torch.nn.functional.silu(self.l1(x))
+            h = torch.nn.functional.silu(self.l2(h))
+            e_atom = self.l3(h)[:, 0]
+            return torch.zeros(4, dtype=x.dtype).index_add(0, mol, e_atom)
+
+    class Model(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.network = ref_cg.compile(Network(), config=ref_cg.CompileConfig(backend="aot_eager"))
+
+        def forward(self, batch):
+            pos = batch["pos"].view(4, 32, 3)
+            centred = (pos - pos.mean(dim=1, keepdim=True)).view(128, 3)
+            return {"energy": self.network(centred, batch["mol"])}
+
+    model = Model().double()
+    gen = torch.Generator().manual_seed(0)
+    pos = 1.5 * torch.randn(128, 3, generator=gen, dtype=torch.float64)
+    mol = torch.arange(128) // 32
+    e_target = torch.randn(4, generator=gen, dtype=torch.float64)
+    f_target = torch.randn(128, 3, generator=gen, dtype=torch.float64)
+    out = {"pos": pos.numpy(), "e_target": e_target.numpy(), "f_target": f_target.numpy()}
+    for name, p in model.network.module.named_parameters():
+        out[f"param.{name}"] = p.detach().numpy().copy()
+    for label, exact in (("compiled", False), ("exact", True)):
+        model.zero_grad()
+        res, grads = ref_cg.create_graph(model, {"pos": pos, "mol": mol}, exact=exact)
+        forces = -grads["pos"]
+        loss = (res["energy"] - e_target).square().mean() + (forces - f_target).square().mean()
+        loss.backward()
+        out[f"{label}.energy"] = res["energy"].detach().numpy()
+        out[f"{label}.forces"] = forces.detach().numpy()
+        out[f"{label}.loss"] = loss.detach().numpy()
+        for name, p in model.network.module.named_parameters():
+            out[f"{label}.grad.{name}"] = p.grad.detach().numpy().copy()
+    return out
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--reference", default="/root/reference")
     args = parser.parse_args()
-    _, op = import_reference(args.reference)
-    for name, arrays in edge_attn_fixtures(op).items():
+    ref_cg, op = import_reference(args.reference)
+    fixtures = edge_attn_fixtures(op)
+    fixtures["mlp_step"] = mlp_step_fixture(ref_cg)
+    for name, arrays in fixtures.items():
         path = HERE / f"{name}.npz"
         np.savez_compressed(path, **arrays)
         print(path, {k: v.shape for k, v in arrays.items()})
