@@ -224,7 +224,7 @@ def run_mine(args):
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": "f32 (tf32 GEMM operands)",
+            "dtype": "f32 (tf32 tensor-core products in the GEMMs and the edge attention, fp32 accumulation)",
             "data": "synthetic (seeded random systems, random-init weights)",
             "config": {
                 "workload": f"{CONFIG_NAME}: ~{args.atoms} atoms/GPU as systems of U{{20..200}} atoms, "
@@ -233,6 +233,8 @@ def run_mine(args):
                 "atoms_per_step": total_atoms,
                 "systems_rank0": len(sizes),
                 "parallelism": f"dp{world}",
+                "allreduce": (f"{len(grads.buckets)} buckets (<= 64 MiB) of the flat fp32 gradients, NCCL "
+                              "all-reduce launched from backward hooks" if world > 1 else "none (1 rank)"),
                 "l2": "working set of several GB per step (larger than L2)",
             },
             "e2e": e2e,
@@ -244,16 +246,17 @@ def run_mine(args):
             "loss": float(loss.item()),
         }
         # the metric's second part: edge-attention backward2 against its HBM roofline at the
-        # microbenchmark shape (4096 atoms x 8 heads x 32 tokens x 32 dims, fp32)
+        # microbenchmark shape (4096 atoms x 8 heads x 32 tokens x 32 dims, fp32 storage), in the
+        # tf32 precision the model runs (headline) and the fp32 (three-term split) precision
         from create_graph_b200 import microbench
 
-        mb = microbench.attn(4096, iters=10, hbm_gbs=hbm, which=("bwd2",))["bwd2"]
-        line["edge_attn_bwd2"] = {
-            "shape": "(4096, 8, 32, 32) fp32, keys masked past U{8..32}",
-            "roofline": {"bound": "hbm", "achieved": mb["gb_s"], "peak": hbm, "unit": "GB/s",
-                         "frac": mb["gb_s"] / hbm, "traffic": None, "algorithmic_bytes": mb["bytes"],
-                         "us_per_launch": mb["us"], "peak_source": f"{src} hbm_gbs"},
-        }
+        line["edge_attn_bwd2"] = {"shape": "(4096, 8, 32, 32) fp32, keys masked past U{8..32}"}
+        for prec in ("tf32", "fp32"):
+            mb = microbench.attn(4096, iters=10, hbm_gbs=hbm, which=("bwd2",), precision=prec)["bwd2"]
+            entry = {"bound": "hbm", "achieved": mb["gb_s"], "peak": hbm, "unit": "GB/s",
+                     "frac": mb["gb_s"] / hbm, "traffic": None, "algorithmic_bytes": mb["bytes"],
+                     "us_per_launch": mb["us"], "peak_source": f"{src} hbm_gbs", "precision": prec}
+            line["edge_attn_bwd2"]["roofline" if prec == "tf32" else "roofline_fp32"] = entry
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(spec, sizes, pos_h, species_h, sys_ptr_h, e_t_h, f_t_h, model)
         print(json.dumps(line), flush=True)

@@ -1,5 +1,6 @@
 // Launchers of the tensor-core edge-attention kernels (attn_tc.cuh): the
-// float32 path of cg_edge_attn_fwd1 / bwd1 / bwd2.
+// float32 path of cg_edge_attn_fwd1 / bwd1 / bwd2, fp32-precision
+// instantiations and the precision dispatch.
 #include "attn_tc.cuh"
 
 namespace cg {
@@ -25,27 +26,17 @@ __global__ void dbias_reduce_tc(const Params P, int64_t outs) {
   }
 }
 
-template <int DP>
-static int launch_dp(int which, const Params& P, cudaStream_t stream) {
-  const int smem = smem_bytes<DP>(which);
-  void (*kernel)(const Params) = which == 0 ? fwd1_tc<DP> : which == 1 ? bwd1_tc<DP> : bwd2_tc<DP>;
-  CG_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  const int64_t slices = P.a.n * P.a.h;
-  int per_sm = (220 * 1024) / smem;
-  if (per_sm < 1) per_sm = 1;
-  if (per_sm > 16) per_sm = 16;
-  const int64_t cap = (int64_t)sm_count() * per_sm;
-  const int grid = (int)(slices < cap ? slices : cap);
-  kernel<<<grid, kThreads, smem, stream>>>(P);
-  CG_LAUNCHED("edge_attn_tc");
-  if (which != 0 && P.dbias_mode == 2) {
-    const bool bn = P.a.bias.sn == 0, bh = P.a.bias.sh == 0;
-    const int64_t outs = (bn ? 1 : P.a.n) * (bh ? 1 : P.a.h) * (int64_t)P.ki * P.kj;
-    const int64_t blocks = ceil_div<int64_t>(outs, 256);
-    dbias_reduce_tc<<<(int)(blocks < 4096 ? blocks : 4096), 256, 0, stream>>>(P, outs);
-    CG_LAUNCHED("edge_attn_tc dbias reduction");
-  }
+int reduce_dbias(const Params& P, cudaStream_t stream) {
+  const bool bn = P.a.bias.sn == 0, bh = P.a.bias.sh == 0;
+  const int64_t outs = (bn ? 1 : P.a.n) * (bh ? 1 : P.a.h) * (int64_t)P.ki * P.kj;
+  const int64_t blocks = ceil_div<int64_t>(outs, 256);
+  dbias_reduce_tc<<<(int)(blocks < 4096 ? blocks : 4096), 256, 0, stream>>>(P, outs);
+  CG_LAUNCHED("edge_attn_tc dbias reduction");
   return kOk;
+}
+
+int launch_fp32(int which, const Params& P, int dp, cudaStream_t stream) {
+  return launch_prec<true>(which, P, dp, stream);
 }
 
 int launch(int which, const cg_edge_attn_args& a, int dbias_mode, int ki, int kj, int vec_ok, int dp,
@@ -57,14 +48,7 @@ int launch(int which, const cg_edge_attn_args& a, int dbias_mode, int ki, int kj
   P.kj = kj;
   // 16-byte operand loads need rows of exactly the padded width
   P.vec_ok = vec_ok && a.d == dp;
-  switch (dp) {
-    case 8: return launch_dp<8>(which, P, stream);
-    case 16: return launch_dp<16>(which, P, stream);
-    case 32: return launch_dp<32>(which, P, stream);
-    case 64: return launch_dp<64>(which, P, stream);
-  }
-  set_error("edge_attn: no tensor-core variant for padded head dim %d", dp);
-  return kUnsupported;
+  return a.precision == CG_ATTN_TF32 ? launch_tf32(which, P, dp, stream) : launch_fp32(which, P, dp, stream);
 }
 
 }  // namespace attn_tc

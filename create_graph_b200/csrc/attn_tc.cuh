@@ -1,10 +1,15 @@
 // Masked edge attention (float32) on the tensor cores.
 //
 // Same arithmetic as the CUDA-core kernels in edge_attn.cuh (the reference's
-// kernels/edge_attn/ops.py:26-104), organised for mma.sync m16n8k8 tf32 with
-// a three-term split of every operand (x = hi + lo, hi = x truncated to tf32,
-// lo = tf32(x - hi); a*b ~ hi*hi + hi*lo + lo*hi), which keeps fp32-level
-// accuracy (~1e-6 relative) while the products run on the tensor pipe.
+// kernels/edge_attn/ops.py:26-104), organised for mma.sync m16n8k8 tf32 in
+// one of two precisions (cg_edge_attn_args.precision):
+// - CG_ATTN_FP32: a three-term split of every operand (x = hi + lo, hi = x
+//   truncated to tf32, lo = tf32(x - hi); a*b ~ hi*hi + hi*lo + lo*hi), which
+//   keeps fp32-level accuracy (~1e-6 relative) at three products per tile;
+// - CG_ATTN_TF32: one product of round-to-nearest tf32 operands per tile
+//   (operand rounding 2^-11 relative, fp32 accumulation), the precision of the
+//   tcgen05 projections.
+// Softmax, row reductions and all elementwise work are fp32 in both.
 //
 // One CTA of two warps owns one slice (n, h) of k <= 32 tokens: warp w holds
 // query rows [16w, 16w + 16) of every k x k matrix as mma accumulator
@@ -35,19 +40,26 @@ struct Params {
   int vec_ok;
 };
 
+// per-slice dbias partials -> dbias, when the bias broadcasts over n or h
+int reduce_dbias(const Params& P, cudaStream_t stream);
+
 // ---- mma.sync tf32 with a 3-term split ---------------------------------------
 
 struct Split {
   uint32_t hi, lo;
 };
 
-// hi: x truncated to tf32 (mantissa bits below the 10 kept ones cleared);
-// lo: the exact remainder x - hi rounded to tf32 by adding half an ulp to its
-// bit pattern before clearing. Integer and FADD work only: no conversions.
+// The tensor cores read a tf32 operand from the top 19 bits of its register
+// and ignore the low 13. Single-term products (tf32 mode) pass x with half an
+// ulp added to its bit pattern, which rounds it to nearest. The three-term
+// split (fp32 mode): hi = x truncated to tf32 (low bits cleared, so that the
+// remainder x - hi is exact), lo = the remainder rounded the same way.
+// Integer and FADD work only: no conversions.
+__device__ inline uint32_t tf32_rn(float x) { return __float_as_uint(x) + 0x1000u; }
+
 __device__ inline Split split(float x) {
   const uint32_t hi = __float_as_uint(x) & 0xffffe000u;
-  const float rem = x - __uint_as_float(hi);
-  return {hi, (__float_as_uint(rem) + 0x1000u) & 0xffffe000u};
+  return {hi, tf32_rn(x - __uint_as_float(hi))};
 }
 
 __device__ inline void mma(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
@@ -62,23 +74,34 @@ __device__ inline void mma(float (&d)[4], const uint32_t (&a)[4], const uint32_t
 // la(m, k): A element (m < 16); lb(k, n): B element. Fragment layout of
 // m16n8k8: A a0 (g, t) a1 (g+8, t) a2 (g, t+4) a3 (g+8, t+4); B b0 (t, g)
 // b1 (t+4, g); C c0 (g, 2t) c1 (g, 2t+1) c2 (g+8, 2t) c3 (g+8, 2t+1).
-template <int NT, int KT, class LA, class LB>
+// X3: three-term split products (fp32 accuracy); else one rounded tf32 term.
+template <bool X3, int NT, int KT, class LA, class LB>
 __device__ inline void band_mma(float (&acc)[NT][4], LA la, LB lb, int g, int t) {
 #pragma unroll 1
   for (int kt = 0; kt < KT; ++kt) {
     const int k0 = kt * 8;
-    const Split a0 = split(la(g, k0 + t)), a1 = split(la(g + 8, k0 + t));
-    const Split a2 = split(la(g, k0 + t + 4)), a3 = split(la(g + 8, k0 + t + 4));
-    const uint32_t ahi[4] = {a0.hi, a1.hi, a2.hi, a3.hi};
-    const uint32_t alo[4] = {a0.lo, a1.lo, a2.lo, a3.lo};
+    if constexpr (X3) {
+      const Split a0 = split(la(g, k0 + t)), a1 = split(la(g + 8, k0 + t));
+      const Split a2 = split(la(g, k0 + t + 4)), a3 = split(la(g + 8, k0 + t + 4));
+      const uint32_t ahi[4] = {a0.hi, a1.hi, a2.hi, a3.hi};
+      const uint32_t alo[4] = {a0.lo, a1.lo, a2.lo, a3.lo};
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const Split b0 = split(lb(k0 + t, nt * 8 + g)), b1 = split(lb(k0 + t + 4, nt * 8 + g));
-      const uint32_t bhi[2] = {b0.hi, b1.hi};
-      const uint32_t blo[2] = {b0.lo, b1.lo};
-      mma(acc[nt], alo, bhi);
-      mma(acc[nt], ahi, blo);
-      mma(acc[nt], ahi, bhi);
+      for (int nt = 0; nt < NT; ++nt) {
+        const Split b0 = split(lb(k0 + t, nt * 8 + g)), b1 = split(lb(k0 + t + 4, nt * 8 + g));
+        const uint32_t bhi[2] = {b0.hi, b1.hi};
+        const uint32_t blo[2] = {b0.lo, b1.lo};
+        mma(acc[nt], alo, bhi);
+        mma(acc[nt], ahi, blo);
+        mma(acc[nt], ahi, bhi);
+      }
+    } else {
+      const uint32_t a[4] = {tf32_rn(la(g, k0 + t)), tf32_rn(la(g + 8, k0 + t)), tf32_rn(la(g, k0 + t + 4)),
+                             tf32_rn(la(g + 8, k0 + t + 4))};
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const uint32_t b[2] = {tf32_rn(lb(k0 + t, nt * 8 + g)), tf32_rn(lb(k0 + t + 4, nt * 8 + g))};
+        mma(acc[nt], a, b);
+      }
     }
   }
 }
@@ -326,7 +349,7 @@ struct Layout {
   static constexpr int KK = KP * LDP;    // floats per k x k matrix
 };
 
-template <int DP>
+template <int DP, bool X3>
 __global__ void __launch_bounds__(kThreads) fwd1_tc(const Params P) {
   using L = Layout<DP>;
   extern __shared__ __align__(16) float smem[];
@@ -355,7 +378,7 @@ __global__ void __launch_bounds__(kThreads) fwd1_tc(const Params P) {
     const int band = warp;
     float S[4][4], p[4][4], lse[2];
     zero(S);
-    band_mma<4, DP / 8>(S, [&](int m, int kk) { return sQ[(band * 16 + m) * L::LD + kk]; },
+    band_mma<X3, 4, DP / 8>(S, [&](int m, int kk) { return sQ[(band * 16 + m) * L::LD + kk]; },
                         [&](int kk, int j) { return sK[j * L::LD + kk]; }, g, t);
     band_softmax(p, S, sP, band, g, t, scale, kc, nullptr, lse);
     cp_async_wait<0>();
@@ -365,7 +388,7 @@ __global__ void __launch_bounds__(kThreads) fwd1_tc(const Params P) {
     __syncwarp();
     float O[DP / 8][4];
     zero(O);
-    band_mma<DP / 8, 4>(O, [&](int m, int j) { return sP[(band * 16 + m) * LDP + j]; },
+    band_mma<X3, DP / 8, 4>(O, [&](int m, int j) { return sP[(band * 16 + m) * LDP + j]; },
                         [&](int j, int c) { return sV[j * L::LD + c]; }, g, t);
     store_band<DP / 8>(a.out, n, h, band, k, d, O, g, t, 1.0f);
     if (t == 0) {
@@ -378,7 +401,7 @@ __global__ void __launch_bounds__(kThreads) fwd1_tc(const Params P) {
   }
 }
 
-template <int DP>
+template <int DP, bool X3>
 __global__ void __launch_bounds__(kThreads) bwd1_tc(const Params P) {
   using L = Layout<DP>;
   extern __shared__ __align__(16) float smem[];
@@ -413,14 +436,14 @@ __global__ void __launch_bounds__(kThreads) bwd1_tc(const Params P) {
     {
       float S[4][4], p[4][4], lse[2];
       zero(S);
-      band_mma<4, DP / 8>(S, [&](int m, int kk) { return sQ[(band * 16 + m) * L::LD + kk]; },
+      band_mma<X3, 4, DP / 8>(S, [&](int m, int kk) { return sQ[(band * 16 + m) * L::LD + kk]; },
                           [&](int kk, int j) { return sK[j * L::LD + kk]; }, g, t);
       band_softmax(p, S, sGL, band, g, t, scale, kc, sLse, lse);
       cp_async_wait<0>();
       __syncthreads();
       float GP[4][4];
       zero(GP);
-      band_mma<4, DP / 8>(GP, [&](int m, int kk) { return sG[(band * 16 + m) * L::LD + kk]; },
+      band_mma<X3, 4, DP / 8>(GP, [&](int m, int kk) { return sG[(band * 16 + m) * L::LD + kk]; },
                           [&](int kk, int j) { return sV[j * L::LD + kk]; }, g, t);
       float rs[2];
       row_dot(rs, p, GP);
@@ -436,7 +459,7 @@ __global__ void __launch_bounds__(kThreads) bwd1_tc(const Params P) {
     {
       float O[DP / 8][4];
       zero(O);  // grad_q = scale * grad_logits k
-      band_mma<DP / 8, 4>(O, [&](int m, int j) { return sGL[(band * 16 + m) * LDP + j]; },
+      band_mma<X3, DP / 8, 4>(O, [&](int m, int j) { return sGL[(band * 16 + m) * LDP + j]; },
                           [&](int j, int c) { return sK[j * L::LD + c]; }, g, t);
       store_band<DP / 8>(a.dq, n, h, band, k, d, O, g, t, scale);
     }
@@ -444,11 +467,11 @@ __global__ void __launch_bounds__(kThreads) bwd1_tc(const Params P) {
     {
       float O[DP / 8][4];
       zero(O);  // grad_v = probs^T grad_out (rows: keys of this band)
-      band_mma<DP / 8, 4>(O, [&](int m, int i) { return sP[i * LDP + band * 16 + m]; },
+      band_mma<X3, DP / 8, 4>(O, [&](int m, int i) { return sP[i * LDP + band * 16 + m]; },
                           [&](int i, int c) { return sG[i * L::LD + c]; }, g, t);
       store_band<DP / 8>(a.dv, n, h, band, k, d, O, g, t, 1.0f);
       zero(O);  // grad_k = scale * grad_logits^T q
-      band_mma<DP / 8, 4>(O, [&](int m, int i) { return sGL[i * LDP + band * 16 + m]; },
+      band_mma<X3, DP / 8, 4>(O, [&](int m, int i) { return sGL[i * LDP + band * 16 + m]; },
                           [&](int i, int c) { return sQ[i * L::LD + c]; }, g, t);
       store_band<DP / 8>(a.dk, n, h, band, k, d, O, g, t, scale);
     }
@@ -456,7 +479,7 @@ __global__ void __launch_bounds__(kThreads) bwd1_tc(const Params P) {
   }
 }
 
-template <int DP>
+template <int DP, bool X3>
 __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
   using L = Layout<DP>;
   extern __shared__ __align__(16) float smem[];
@@ -503,13 +526,13 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
     {
       float p[4][4], lse[2], A[4][4], B[4][4];
       zero(A);  // scores
-      band_mma<4, DP / 8>(A, [&](int m, int kk) { return sQ[(band * 16 + m) * L::LD + kk]; },
+      band_mma<X3, 4, DP / 8>(A, [&](int m, int kk) { return sQ[(band * 16 + m) * L::LD + kk]; },
                           [&](int kk, int j) { return sK[j * L::LD + kk]; }, g, t);
       band_softmax(p, A, sGL, band, g, t, scale, kc, sLse, lse);
       cp_async_wait<2>();
       __syncthreads();
       zero(B);  // grad_probs = grad_out v^T
-      band_mma<4, DP / 8>(B, [&](int m, int kk) { return sG[(band * 16 + m) * L::LD + kk]; },
+      band_mma<X3, 4, DP / 8>(B, [&](int m, int kk) { return sG[(band * 16 + m) * L::LD + kk]; },
                           [&](int kk, int j) { return sV[j * L::LD + kk]; }, g, t);
       float rs[2];
       row_dot(rs, p, B);
@@ -521,9 +544,9 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
       cp_async_wait<1>();
       __syncthreads();
       zero(A);  // d_logits = scale * (hq k^T + q hk^T) + hb
-      band_mma<4, DP / 8>(A, [&](int m, int kk) { return sHQ[(band * 16 + m) * L::LD + kk]; },
+      band_mma<X3, 4, DP / 8>(A, [&](int m, int kk) { return sHQ[(band * 16 + m) * L::LD + kk]; },
                           [&](int kk, int j) { return sK[j * L::LD + kk]; }, g, t);
-      band_mma<4, DP / 8>(A, [&](int m, int kk) { return sQ[(band * 16 + m) * L::LD + kk]; },
+      band_mma<X3, 4, DP / 8>(A, [&](int m, int kk) { return sQ[(band * 16 + m) * L::LD + kk]; },
                           [&](int kk, int j) { return sHK[j * L::LD + kk]; }, g, t);
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt)
@@ -535,7 +558,7 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
       cp_async_wait<0>();
       __syncthreads();
       zero(B);  // grad_out hv^T
-      band_mma<4, DP / 8>(B, [&](int m, int kk) { return sG[(band * 16 + m) * L::LD + kk]; },
+      band_mma<X3, 4, DP / 8>(B, [&](int m, int kk) { return sG[(band * 16 + m) * L::LD + kk]; },
                           [&](int kk, int j) { return sHV[j * L::LD + kk]; }, g, t);
       float dg[4][4];
 #pragma unroll
@@ -566,15 +589,15 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
     {
       float O[DP / 8][4];
       zero(O);  // grad_q = scale * (grad_logits hk + d_scores k)
-      band_mma<DP / 8, 4>(O, [&](int m, int j) { return sGL[(band * 16 + m) * LDP + j]; },
+      band_mma<X3, DP / 8, 4>(O, [&](int m, int j) { return sGL[(band * 16 + m) * LDP + j]; },
                           [&](int j, int c) { return sHK[j * L::LD + c]; }, g, t);
-      band_mma<DP / 8, 4>(O, [&](int m, int j) { return sDS[(band * 16 + m) * LDP + j]; },
+      band_mma<X3, DP / 8, 4>(O, [&](int m, int j) { return sDS[(band * 16 + m) * LDP + j]; },
                           [&](int j, int c) { return sK[j * L::LD + c]; }, g, t);
       store_band<DP / 8>(a.dq, n, h, band, k, d, O, g, t, scale);
       zero(O);  // grad_out cotangent = d_grad_probs v + probs hv
-      band_mma<DP / 8, 4>(O, [&](int m, int j) { return sDG[(band * 16 + m) * LDP + j]; },
+      band_mma<X3, DP / 8, 4>(O, [&](int m, int j) { return sDG[(band * 16 + m) * LDP + j]; },
                           [&](int j, int c) { return sV[j * L::LD + c]; }, g, t);
-      band_mma<DP / 8, 4>(O, [&](int m, int j) { return sP[(band * 16 + m) * LDP + j]; },
+      band_mma<X3, DP / 8, 4>(O, [&](int m, int j) { return sP[(band * 16 + m) * LDP + j]; },
                           [&](int j, int c) { return sHV[j * L::LD + c]; }, g, t);
       store_band<DP / 8>(a.dgrad_out, n, h, band, k, d, O, g, t, 1.0f);
     }
@@ -582,13 +605,13 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
     {
       float O[DP / 8][4];
       zero(O);  // grad_k = scale * (grad_logits^T hq + d_scores^T q)
-      band_mma<DP / 8, 4>(O, [&](int m, int i) { return sGL[i * LDP + band * 16 + m]; },
+      band_mma<X3, DP / 8, 4>(O, [&](int m, int i) { return sGL[i * LDP + band * 16 + m]; },
                           [&](int i, int c) { return sHQ[i * L::LD + c]; }, g, t);
-      band_mma<DP / 8, 4>(O, [&](int m, int i) { return sDS[i * LDP + band * 16 + m]; },
+      band_mma<X3, DP / 8, 4>(O, [&](int m, int i) { return sDS[i * LDP + band * 16 + m]; },
                           [&](int i, int c) { return sQ[i * L::LD + c]; }, g, t);
       store_band<DP / 8>(a.dk, n, h, band, k, d, O, g, t, scale);
       zero(O);  // grad_v = d_grad_probs^T grad_out
-      band_mma<DP / 8, 4>(O, [&](int m, int i) { return sDG[i * LDP + band * 16 + m]; },
+      band_mma<X3, DP / 8, 4>(O, [&](int m, int i) { return sDG[i * LDP + band * 16 + m]; },
                           [&](int i, int c) { return sG[i * L::LD + c]; }, g, t);
       store_band<DP / 8>(a.dv, n, h, band, k, d, O, g, t, 1.0f);
     }
@@ -606,6 +629,41 @@ inline int smem_bytes(int which) {
     default: return (7 * L::OP + 4 * L::KK + 2 * KP) * 4;
   }
 }
+
+// One launch of kernel `which` (0 fwd1, 1 bwd1, 2 bwd2): a persistent grid of
+// as many CTAs as fit per SM (shared memory bound), slices strided over it.
+template <int DP, bool X3>
+int launch_dp(int which, const Params& P, cudaStream_t stream) {
+  const int smem = smem_bytes<DP>(which);
+  void (*kernel)(const Params) = which == 0 ? fwd1_tc<DP, X3> : which == 1 ? bwd1_tc<DP, X3> : bwd2_tc<DP, X3>;
+  CG_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int64_t slices = P.a.n * P.a.h;
+  int per_sm = (220 * 1024) / smem;
+  if (per_sm < 1) per_sm = 1;
+  if (per_sm > 16) per_sm = 16;
+  const int64_t cap = (int64_t)sm_count() * per_sm;
+  const int grid = (int)(slices < cap ? slices : cap);
+  kernel<<<grid, kThreads, smem, stream>>>(P);
+  CG_LAUNCHED("edge_attn_tc");
+  if (which != 0 && P.dbias_mode == 2) return reduce_dbias(P, stream);
+  return kOk;
+}
+
+template <bool X3>
+int launch_prec(int which, const Params& P, int dp, cudaStream_t stream) {
+  switch (dp) {
+    case 8: return launch_dp<8, X3>(which, P, stream);
+    case 16: return launch_dp<16, X3>(which, P, stream);
+    case 32: return launch_dp<32, X3>(which, P, stream);
+    case 64: return launch_dp<64, X3>(which, P, stream);
+  }
+  set_error("edge_attn: no tensor-core variant for padded head dim %d", dp);
+  return kUnsupported;
+}
+
+// the two precisions live in separate translation units (parallel builds)
+int launch_fp32(int which, const Params& P, int dp, cudaStream_t stream);  // attn_tc.cu
+int launch_tf32(int which, const Params& P, int dp, cudaStream_t stream);  // attn_tc_tf32.cu
 
 }  // namespace attn_tc
 }  // namespace cg

@@ -38,6 +38,8 @@ static int run(Which w, const cg_edge_attn_args* args, void* stream) {
       return rc;
   }
   CG_REQUIRE(a.token_index == nullptr || a.dtype == CG_F32, "edge_attn: token_index needs float32");
+  CG_REQUIRE(a.precision == CG_ATTN_FP32 || a.precision == CG_ATTN_TF32,
+             "edge_attn: precision = %d is neither CG_ATTN_FP32 nor CG_ATTN_TF32", a.precision);
   Params P;
   P.a = a;
   const int es = a.dtype == CG_F32 ? 4 : 8;

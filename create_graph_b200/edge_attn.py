@@ -13,6 +13,13 @@ q, k, v are (..., S, D) with S <= 32 tokens and D <= 64; the bias broadcasts to
 the scores (..., S, S). Rows whose keys are all -inf get zero probabilities.
 ``key_counts`` (model path, ``edge_attention_masked``) masks keys
 j >= key_counts[n] without a -inf bias.
+
+``precision`` selects how float32 products run on the tensor cores: "fp32"
+(three-term tf32 split, ~1e-6 relative, the reference's float32 results) or
+"tf32" (one tf32 product per tile, operands rounded to 2^-11 relative, fp32
+accumulation and softmax; the precision of the tcgen05 projections).
+``cg_b200::edge_attn`` is the fp32 op, ``cg_b200::edge_attn_tf32`` the tf32
+one; float64 inputs always compute in float64.
 """
 
 from __future__ import annotations
@@ -82,7 +89,8 @@ def _reduce_to(grad: Tensor, like: Tensor) -> Tensor:
 class _Call:
     """Argument block of one kernel call plus the tensors it points into."""
 
-    def __init__(self, q: Tensor, k: Tensor, v: Tensor, bias: Tensor | None, scale: float, key_counts=None):
+    def __init__(self, q: Tensor, k: Tensor, v: Tensor, bias: Tensor | None, scale: float, key_counts=None,
+                 precision: str = "fp32"):
         native.require_cuda(q, k, v, bias)
         if not (q.dtype == k.dtype == v.dtype and (bias is None or bias.dtype == q.dtype)):
             raise NativeError("edge_attn: q, k, v and bias must share one dtype")
@@ -103,6 +111,7 @@ class _Call:
         a = self.args
         a.n, a.h, a.k, a.d = self.n, self.h, self.s, self.d
         a.dtype = native.dtype_code(q)
+        a.precision = native.attn_precision(precision)
         a.scale = float(scale)
         a.key_count = None if key_counts is None else key_counts.data_ptr()
         a.q, a.k_, a.v = _mat(self.q), _mat(self.k), _mat(self.v)
@@ -156,8 +165,8 @@ class _Call:
         return view
 
 
-def attn_forward1(q, k, v, bias, scale, key_counts=None) -> tuple[Tensor, Tensor]:
-    c = _Call(q, k, v, bias, scale, key_counts)
+def attn_forward1(q, k, v, bias, scale, key_counts=None, precision="fp32") -> tuple[Tensor, Tensor]:
+    c = _Call(q, k, v, bias, scale, key_counts, precision)
     out = c.new(c.n, c.h, c.s, c.d)
     lse = c.new(c.n, c.h, c.s)
     c.args.out = _mat(out)
@@ -166,8 +175,8 @@ def attn_forward1(q, k, v, bias, scale, key_counts=None) -> tuple[Tensor, Tensor
     return out.view(*c.lead, c.s, c.d), lse.view(*c.lead, c.s)
 
 
-def attn_backward1(q, k, v, bias, lse, grad_out, scale, key_counts=None):
-    c = _Call(q, k, v, bias, scale, key_counts)
+def attn_backward1(q, k, v, bias, lse, grad_out, scale, key_counts=None, precision="fp32"):
+    c = _Call(q, k, v, bias, scale, key_counts, precision)
     lse_c = lse.reshape(c.n, c.h, c.s).contiguous()
     c.keep.append(lse_c)
     c.args.lse = lse_c.data_ptr()
@@ -180,8 +189,8 @@ def attn_backward1(q, k, v, bias, lse, grad_out, scale, key_counts=None):
     return dq.view(shape), dk.view(shape), dv.view(shape), c.finish_dbias(dbias)
 
 
-def attn_backward2(q, k, v, bias, lse, grad_out, scale, hq, hk, hv, hb, key_counts=None):
-    c = _Call(q, k, v, bias, scale, key_counts)
+def attn_backward2(q, k, v, bias, lse, grad_out, scale, hq, hk, hv, hb, key_counts=None, precision="fp32"):
+    c = _Call(q, k, v, bias, scale, key_counts, precision)
     lse_c = lse.reshape(c.n, c.h, c.s).contiguous()
     c.keep.append(lse_c)
     c.args.lse = lse_c.data_ptr()
@@ -198,35 +207,43 @@ def attn_backward2(q, k, v, bias, lse, grad_out, scale, hq, hk, hv, hb, key_coun
     return dq.view(shape), dk.view(shape), dv.view(shape), c.finish_dbias(dbias), dg.view(shape)
 
 
-@custom_op("cg_b200::edge_attn")
-class EdgeAttention:
+def _edge_attention_op(name: str, precision: str):
     """The reference's EdgeAttention (kernels/edge_attn/ops.py:57-104) with
-    sm_100a kernel bodies."""
+    sm_100a kernel bodies, registered as ``name`` for one precision."""
 
-    outputs = ("out", "lse")
-    save = ("q", "k", "v", "bias", "lse")
-    nondiff = ("lse",)
+    class EdgeAttention:
+        outputs = ("out", "lse")
+        save = ("q", "k", "v", "bias", "lse")
+        nondiff = ("lse",)
 
-    @staticmethod
-    def forward1(q: Tensor, k: Tensor, v: Tensor, bias: Tensor, scale: float) -> tuple[Tensor, Tensor]:
-        return attn_forward1(q, k, v, bias, scale)
+        @staticmethod
+        def forward1(q: Tensor, k: Tensor, v: Tensor, bias: Tensor, scale: float) -> tuple[Tensor, Tensor]:
+            return attn_forward1(q, k, v, bias, scale, precision=precision)
 
-    @staticmethod
-    def fake(q, k, v, bias, scale):
-        return q.new_empty((*q.shape[:-1], v.shape[-1])), q.new_empty(q.shape[:-1])
+        @staticmethod
+        def fake(q, k, v, bias, scale):
+            return q.new_empty((*q.shape[:-1], v.shape[-1])), q.new_empty(q.shape[:-1])
 
-    @staticmethod
-    def backward1(q, k, v, bias, lse, grad_out, scale):
-        return attn_backward1(q, k, v, bias, lse, grad_out, scale)
+        @staticmethod
+        def backward1(q, k, v, bias, lse, grad_out, scale):
+            return attn_backward1(q, k, v, bias, lse, grad_out, scale, precision=precision)
 
-    @staticmethod
-    def backward2(q, k, v, bias, lse, grad_out, scale, hq, hk, hv, hb):
-        return attn_backward2(q, k, v, bias, lse, grad_out, scale, hq, hk, hv, hb)
+        @staticmethod
+        def backward2(q, k, v, bias, lse, grad_out, scale, hq, hk, hv, hb):
+            return attn_backward2(q, k, v, bias, lse, grad_out, scale, hq, hk, hv, hb, precision=precision)
+
+    return custom_op(name)(EdgeAttention)
 
 
-def edge_attention(q, k, v, bias, scale: float) -> Tensor:
+EdgeAttention = _edge_attention_op("cg_b200::edge_attn", "fp32")
+EdgeAttentionTF32 = _edge_attention_op("cg_b200::edge_attn_tf32", "tf32")
+_OPS = {"fp32": EdgeAttention, "tf32": EdgeAttentionTF32}
+
+
+def edge_attention(q, k, v, bias, scale: float, precision: str = "fp32") -> Tensor:
     """``softmax(q k^T * scale + bias) v`` through the fused op."""
-    return EdgeAttention(q, k, v, bias, scale)[0]
+    native.attn_precision(precision)
+    return _OPS[precision](q, k, v, bias, scale)[0]
 
 
 # ---------------------------------------------------------------------------
@@ -260,7 +277,8 @@ def _token_bias(t: Tensor | None, k: int, heads: int) -> native.Bias:
     return native.Bias(t.data_ptr(), k * heads, 1, 0, heads)
 
 
-def _gathered_args(qkv: Tensor, bias: Tensor, index: Tensor, counts: Tensor, k: int, heads: int, scale: float):
+def _gathered_args(qkv: Tensor, bias: Tensor, index: Tensor, counts: Tensor, k: int, heads: int, scale: float,
+                   precision: str):
     native.require_cuda(qkv, bias, counts, index)
     if qkv.dtype != torch.float32 or bias.dtype != torch.float32:
         raise NativeError("token attention: qkv and bias must be float32")
@@ -275,6 +293,7 @@ def _gathered_args(qkv: Tensor, bias: Tensor, index: Tensor, counts: Tensor, k: 
     a = native.EdgeAttnArgs()
     a.n, a.h, a.k, a.d = n, heads, k, d
     a.dtype = native.F32
+    a.precision = native.attn_precision(precision)
     a.scale = float(scale)
     a.key_count = counts.data_ptr()
     a.token_index = index.data_ptr()
@@ -291,10 +310,10 @@ def _run(fn: str, a, device) -> None:
     native.invoke(fn, ctypes.byref(a), native.stream_ptr(device), info=_info(a))
 
 
-def token_attention_forward1(qkv, bias, index, counts, k, heads, scale):
+def token_attention_forward1(qkv, bias, index, counts, k, heads, scale, precision="fp32"):
     """(out (n, k, h*d), lse (n, h, k)) of the gathered tokens."""
     qkv, bias = qkv.contiguous(), bias.contiguous()
-    a, n, d = _gathered_args(qkv, bias, index, counts, k, heads, scale)
+    a, n, d = _gathered_args(qkv, bias, index, counts, k, heads, scale, precision)
     out = torch.empty(n, k, heads * d, device=qkv.device)
     lse = torch.empty(n, heads, k, device=qkv.device)
     (a.out,) = _token_mats(out, n, k, heads, d, 1)
@@ -303,10 +322,10 @@ def token_attention_forward1(qkv, bias, index, counts, k, heads, scale):
     return out, lse
 
 
-def token_attention_backward1(qkv, bias, lse, g, index, counts, k, heads, scale):
+def token_attention_backward1(qkv, bias, lse, g, index, counts, k, heads, scale, precision="fp32"):
     """(dtok (n*k, 3*h*d) per-token q/k/v gradients, dbias (n*k, h))."""
     qkv, bias, g = qkv.contiguous(), bias.contiguous(), g.contiguous()
-    a, n, d = _gathered_args(qkv, bias, index, counts, k, heads, scale)
+    a, n, d = _gathered_args(qkv, bias, index, counts, k, heads, scale, precision)
     a.lse = lse.data_ptr()
     (a.grad_out,) = _token_mats(g, n, k, heads, d, 1)
     dtok = torch.empty(n * k, qkv.shape[1], device=qkv.device)
@@ -317,12 +336,12 @@ def token_attention_backward1(qkv, bias, lse, g, index, counts, k, heads, scale)
     return dtok, dbias
 
 
-def token_attention_backward2(qkv, bias, lse, g, h_qkv, h_bias, index, counts, k, heads, scale):
+def token_attention_backward2(qkv, bias, lse, g, h_qkv, h_bias, index, counts, k, heads, scale, precision="fp32"):
     """Second derivative: per-token (dtok, dbias, dg) for the per-atom
     cotangent h_qkv of the q/k/v gradient (read through the same index) and
     the cotangent h_bias of dbias."""
     qkv, bias, g, h_qkv = qkv.contiguous(), bias.contiguous(), g.contiguous(), h_qkv.contiguous()
-    a, n, d = _gathered_args(qkv, bias, index, counts, k, heads, scale)
+    a, n, d = _gathered_args(qkv, bias, index, counts, k, heads, scale, precision)
     a.lse = lse.data_ptr()
     (a.grad_out,) = _token_mats(g, n, k, heads, d, 1)
     a.hq, a.hk, a.hv = _atom_mats(h_qkv, heads, d)

@@ -1,13 +1,14 @@
 """
 Microbenchmarks of the hot kernels, timed with CUDA events.
 
-    python -m create_graph_b200.microbench attn [--n 4096] [--iters 10]
+    python -m create_graph_b200.microbench attn [--n 4096] [--iters 10] [--precision fp32|tf32]
     python -m create_graph_b200.microbench gemm M N K [--silu]
 
 ``attn``: the masked edge-attention microbenchmark: n atoms x 8 heads x 32
 tokens x 32 dims, fp32, q/k/v ~ N(0, 1), bias ~ N(0, 0.1) per (n, h, i, j),
 keys j >= c_n masked with c_n ~ U{8..32}; forward1, backward1 and backward2,
-each against its algorithmic bytes (every operand read or written once).
+each against its algorithmic bytes (every operand read or written once), in
+the fp32 (three-term tf32 split) or tf32 (one tf32 product) precision.
 ``gemm``: one tcgen05 tf32 GEMM shape (bias, optionally the SiLU epilogue).
 """
 
@@ -56,14 +57,16 @@ def _time(fn, iters: int) -> float:
     return sorted(times)[len(times) // 2]
 
 
-def attn(n: int = 4096, iters: int = 10, hbm_gbs: float | None = None, which=("fwd1", "bwd1", "bwd2")) -> dict:
+def attn(n: int = 4096, iters: int = 10, hbm_gbs: float | None = None, which=("fwd1", "bwd1", "bwd2"),
+         precision: str = "fp32") -> dict:
     """Median launch time and achieved GB/s of each kernel at (n, 8, 32, 32)."""
     q, k, v, bias, counts, g, hq, hk, hv, hb, scale = attn_inputs(n)
-    _, lse = attn_forward1(q, k, v, bias, scale, counts)
+    kw = {"precision": precision}
+    _, lse = attn_forward1(q, k, v, bias, scale, counts, **kw)
     fns = {
-        "fwd1": lambda: attn_forward1(q, k, v, bias, scale, counts),
-        "bwd1": lambda: attn_backward1(q, k, v, bias, lse, g, scale, counts),
-        "bwd2": lambda: attn_backward2(q, k, v, bias, lse, g, scale, hq, hk, hv, hb, counts),
+        "fwd1": lambda: attn_forward1(q, k, v, bias, scale, counts, **kw),
+        "bwd1": lambda: attn_backward1(q, k, v, bias, lse, g, scale, counts, **kw),
+        "bwd2": lambda: attn_backward2(q, k, v, bias, lse, g, scale, hq, hk, hv, hb, counts, **kw),
     }
     nbytes = attn_algorithmic_bytes(n)
     out = {}
@@ -93,12 +96,13 @@ def main() -> None:
     p_attn = sub.add_parser("attn")
     p_attn.add_argument("--n", type=int, default=4096)
     p_attn.add_argument("--iters", type=int, default=10)
+    p_attn.add_argument("--precision", choices=("fp32", "tf32"), default="fp32")
     p_gemm = sub.add_parser("gemm")
     p_gemm.add_argument("shape", type=int, nargs=3)
     p_gemm.add_argument("--silu", action="store_true")
     args = parser.parse_args()
     if args.what == "attn":
-        print(json.dumps(attn(args.n, args.iters)))
+        print(json.dumps(attn(args.n, args.iters, precision=args.precision)))
     else:
         print(json.dumps(gemm_bench(*args.shape, silu=args.silu)))
 

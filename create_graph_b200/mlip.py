@@ -49,6 +49,9 @@ class ModelSpec:
     n_rbf: int
     cutoff: float
     k: int
+    # tensor-core product precision of the edge attention: "fp32" (three-term
+    # tf32 split) or "tf32" (one product, the precision of the projections)
+    attn_precision: str = "fp32"
 
     @property
     def head_dim(self) -> int:
@@ -61,7 +64,8 @@ class ModelSpec:
 
 
 SMALL_MLIP = ModelSpec(n_species=10, hidden=128, heads=4, blocks=4, ffn=512, n_rbf=64, cutoff=6.0, k=32)
-ALLSCAIP_85M = ModelSpec(n_species=50, hidden=768, heads=12, blocks=12, ffn=3072, n_rbf=128, cutoff=6.0, k=30)
+ALLSCAIP_85M = ModelSpec(n_species=50, hidden=768, heads=12, blocks=12, ffn=3072, n_rbf=128, cutoff=6.0, k=30,
+                         attn_precision="tf32")
 SPECS = {"small_mlip": SMALL_MLIP, "allscaip_85m": ALLSCAIP_85M}
 
 
@@ -71,6 +75,7 @@ class Block(nn.Module):
         c = s.hidden
         self.heads = s.heads
         self.scale = 1.0 / math.sqrt(s.head_dim)
+        self.precision = s.attn_precision
         self.norm1 = cgnn.LayerNorm(c)
         self.qkv = cgnn.Linear(c, 3 * c)
         self.rbf_bias = cgnn.Linear(s.n_rbf, s.heads)
@@ -82,7 +87,8 @@ class Block(nn.Module):
     def forward(self, h: Tensor, rbf: Tensor, env: Tensor, graph: cgnn.NeighborGraph) -> Tensor:
         n = h.shape[0]
         bias = self.rbf_bias(rbf)
-        o = cgnn.TokenAttention.apply(self.qkv(self.norm1(h)), bias, graph, self.heads, self.scale)
+        o = cgnn.TokenAttention.apply(self.qkv(self.norm1(h)), bias, graph, self.heads, self.scale,
+                                      self.precision)
         m = cgnn.Pool.apply(o, env.view(n, graph.k))
         h = h + self.out(m)
         return h + self.ffn2(self.ffn1(self.norm2(h)))

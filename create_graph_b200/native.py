@@ -21,6 +21,15 @@ from create_graph_b200.errors import NativeError
 LIB_PATH = pathlib.Path(__file__).resolve().parent / "_lib" / "libcg_b200.so"
 ABI_VERSION = 1
 F32, F64 = 0, 1
+ATTN_PRECISIONS = {"fp32": 0, "tf32": 1}  # CG_ATTN_FP32, CG_ATTN_TF32
+
+
+def attn_precision(name: str) -> int:
+    try:
+        return ATTN_PRECISIONS[name]
+    except KeyError:
+        raise ValueError(f"attention precision must be one of {sorted(ATTN_PRECISIONS)}, got {name!r}") from None
+
 _DTYPES = {torch.float32: F32, torch.float64: F64}
 
 i64 = ctypes.c_int64
@@ -43,7 +52,7 @@ class EdgeAttnArgs(ctypes.Structure):
         ("k", i32),
         ("d", i32),
         ("dtype", i32),
-        ("pad0", i32),
+        ("precision", i32),
         ("scale", ctypes.c_double),
         ("key_count", vp),
         ("q", Mat),

@@ -536,13 +536,15 @@ class TokenAttention(_Fused):
     (n*k, h) is the per-key additive bias and keys past graph.counts[n] are
     masked. Returns the token outputs (n, k, h*d), heads concatenated. The
     per-token q/k/v gradients are reduced to atoms by the deterministic CSR
-    segment sum (the transpose of the gather).
+    segment sum (the transpose of the gather). ``precision`` ("fp32" or
+    "tf32") selects the kernels' tensor-core product precision.
     """
 
     @staticmethod
-    def forward(ctx, qkv, bias, graph, heads, scale):
-        meta = (graph, heads, scale)
-        out, lse = token_attention_forward1(qkv, bias, graph.tokens.index, graph.counts, graph.k, heads, scale)
+    def forward(ctx, qkv, bias, graph, heads, scale, precision="fp32"):
+        meta = (graph, heads, scale, precision)
+        out, lse = token_attention_forward1(qkv, bias, graph.tokens.index, graph.counts, graph.k, heads, scale,
+                                            precision)
         ctx.save_for_backward(qkv, bias, lse)
         ctx.meta = meta
         return out
@@ -551,7 +553,7 @@ class TokenAttention(_Fused):
     def backward(ctx, g):
         qkv, bias, lse = ctx.saved_tensors
         d_qkv, dbias = TokenAttentionGrad.apply(qkv, bias, lse, g, ctx.meta)
-        return d_qkv, dbias, None, None, None
+        return d_qkv, dbias, None, None, None, None
 
 
 class TokenAttentionGrad(_Fused):
@@ -560,9 +562,9 @@ class TokenAttentionGrad(_Fused):
 
     @staticmethod
     def forward(ctx, qkv, bias, lse, g, meta):
-        graph, heads, scale = meta
+        graph, heads, scale, precision = meta
         dtok, dbias = token_attention_backward1(qkv, bias, lse, g, graph.tokens.index, graph.counts, graph.k,
-                                                heads, scale)
+                                                heads, scale, precision)
         ctx.save_for_backward(qkv, bias, lse, g)
         ctx.meta = meta
         return segment_sum_raw(dtok, graph.tokens), dbias
@@ -570,11 +572,11 @@ class TokenAttentionGrad(_Fused):
     @staticmethod
     def backward(ctx, h_qkv, h_bias):
         qkv, bias, lse, g = ctx.saved_tensors
-        graph, heads, scale = ctx.meta
+        graph, heads, scale, precision = ctx.meta
         if h_qkv is None:
             h_qkv = torch.zeros_like(qkv)
         dtok, dbias, dg = token_attention_backward2(qkv, bias, lse, g, h_qkv, h_bias, graph.tokens.index,
-                                                    graph.counts, graph.k, heads, scale)
+                                                    graph.counts, graph.k, heads, scale, precision)
         return segment_sum_raw(dtok, graph.tokens), dbias, None, dg, None
 
 

@@ -58,11 +58,19 @@ typedef struct cg_bias {
   int64_t sn, sh, si, sj;
 } cg_bias;
 
+/* Precision of the float32 attention products (the float64 kernels ignore it):
+ * CG_ATTN_FP32 three-term tf32 split on the tensor cores, fp32-level accuracy
+ * (~1e-6 relative); CG_ATTN_TF32 one tf32 product (operands rounded to
+ * nearest tf32, 2^-11 relative; fp32 accumulation), the precision of the
+ * projections. Softmax and elementwise work are fp32 in both. */
+#define CG_ATTN_FP32 0
+#define CG_ATTN_TF32 1
+
 typedef struct cg_edge_attn_args {
   int64_t n, h;           /* slice grid */
   int32_t k, d;           /* tokens per slice, head dim */
   int32_t dtype;          /* CG_F32 or CG_F64 */
-  int32_t pad0;
+  int32_t precision;      /* float32 products: CG_ATTN_FP32 (0) or CG_ATTN_TF32 */
   double scale;
   const int32_t* key_count; /* optional (n,): valid keys per n; NULL = all k */
   /* inputs */

@@ -1,12 +1,15 @@
 """
 Data parallelism on CPU ranks (gloo, 2 processes, float64): each rank runs
 cg.create_graph on its own systems, gradients live in one flat buffer
-(create_graph_b200.ddp.FlatGradients) and one all-reduce averages them. The
-reduced gradients must be identical on both ranks and equal the mean of the
-per-rank eager create_graph gradients -- the property the reference's DDP
-test asserts (tests/test_ddp.py there). A second case has one rank raise
-before the collective and checks the other fails with an error instead of
-waiting forever.
+(create_graph_b200.ddp.FlatGradients) whose buckets are averaged by
+all-reduces launched from inside loss.backward() as their gradients complete.
+The reduced gradients must be identical on both ranks and equal the mean of
+the per-rank eager create_graph gradients -- the property the reference's DDP
+test asserts (tests/test_ddp.py there) -- for one bucket and for buckets of a
+single parameter, and with small buckets some all-reduces must have started
+before backward returned. A second case has one rank raise before its first
+collective and checks the other fails with an error instead of waiting
+forever.
 """
 
 from __future__ import annotations
@@ -57,29 +60,32 @@ def rank_data(rank):
     }
 
 
-def step(model, data, exact=False):
+def step(model, data, exact=False, fail=False):
     out, grads = cg.create_graph(model, data, exact=exact)
+    if fail:
+        raise RuntimeError("injected failure before the all-reduce")
     (out["energy"].sum() + grads["pos"].square().sum()).backward()
 
 
-def worker(rank, world, port, path, fail_rank):
+def worker(rank, world, port, path, fail_rank, bucket_bytes):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
     torch.set_default_dtype(torch.float64)
     torch.manual_seed(0)
     model = Net()
-    grads = FlatGradients(model.parameters(), world)
+    grads = FlatGradients(model.parameters(), world, bucket_bytes=bucket_bytes)
     try:
-        grads.zero()
-        step(model, rank_data(rank))
-        if rank == fail_rank:
-            raise RuntimeError("injected failure before the all-reduce")
-        grads.allreduce()
+        for _ in range(2):  # a second step reuses the hooks and buckets
+            grads.zero()
+            step(model, rank_data(rank), fail=rank == fail_rank)
+            in_backward = grads.launched_in_backward
+            grads.allreduce()
         flat = grads.flat.clone()
         gathered = [torch.empty_like(flat) for _ in range(world)]
         dist.all_gather(gathered, flat)
         if rank == 0:
-            torch.save({"flat": flat, "identical": all(torch.equal(gathered[0], g) for g in gathered[1:])}, path)
+            torch.save({"flat": flat, "identical": all(torch.equal(gathered[0], g) for g in gathered[1:]),
+                        "buckets": len(grads.buckets), "in_backward": in_backward}, path)
     except RuntimeError as error:
         torch.save({"error": str(error)}, f"{path}.{rank}")
     finally:
@@ -111,20 +117,24 @@ def expected_flat():
         torch.set_default_dtype(torch.float32)
 
 
-def test_averaged_gradients_match_eager_mean():
+@pytest.mark.parametrize("bucket_bytes", [1 << 30, 1])
+def test_averaged_gradients_match_eager_mean(bucket_bytes):
     want = expected_flat()
     with tempfile.TemporaryDirectory() as tmp:
         path = os.path.join(tmp, "out.pt")
-        mp.spawn(worker, args=(2, free_port(), path, -1), nprocs=2, join=True)
+        mp.spawn(worker, args=(2, free_port(), path, -1, bucket_bytes), nprocs=2, join=True)
         got = torch.load(path)
     assert got["identical"]
     assert ((got["flat"] - want).norm() / want.norm()).item() < 1e-10
+    if bucket_bytes == 1:  # one bucket per parameter: most start inside backward
+        assert got["buckets"] == 10
+        assert got["in_backward"] >= 5
 
 
 def test_failing_rank_ends_the_other_with_an_error():
     with tempfile.TemporaryDirectory() as tmp:
         path = os.path.join(tmp, "out.pt")
-        mp.spawn(worker, args=(2, free_port(), path, 1), nprocs=2, join=True)
+        mp.spawn(worker, args=(2, free_port(), path, 1, 1), nprocs=2, join=True)
         assert "injected failure" in torch.load(f"{path}.1")["error"]
         # rank 0 is left alone in the collective: gloo ends it with an error, not a hang
         assert os.path.exists(f"{path}.0")

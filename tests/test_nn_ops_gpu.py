@@ -138,14 +138,16 @@ def ref_token_attention(qkv, bias, index, counts, heads, scale):
     return (p @ v).permute(0, 2, 1, 3).reshape(n, k, heads * d)
 
 
-def test_token_attention():
+@pytest.mark.parametrize("precision,tol", [("fp32", F32_TOL), ("tf32", 5e-3)])
+def test_token_attention(precision, tol):
     """Tokens gathered from per-atom qkv rows through the neighbour index (padded
-    slots read zeros); per-token gradients reduced back to atoms."""
+    slots read zeros); per-token gradients reduced back to atoms. tf32: one
+    tf32 product per tile, checked at the stated TF32 bound."""
     pos, graph = neighbor_case(n=40, k=12)
     heads, d = 4, 16
     g = torch.Generator().manual_seed(15)
     qkv = torch.randn(40, 3 * heads * d, generator=g).cuda()
     bias = torch.randn(40 * 12, heads, generator=g).cuda()
-    mine = lambda q, b: cgnn.TokenAttention.apply(q, b, graph, heads, 0.25)  # noqa: E731
+    mine = lambda q, b: cgnn.TokenAttention.apply(q, b, graph, heads, 0.25, precision)  # noqa: E731
     ref = lambda q, b: ref_token_attention(q, b, graph.tokens.index, graph.counts, heads, 0.25)  # noqa: E731
-    check(twice_errors(mine, ref, [qkv, bias]), F32_TOL)
+    check(twice_errors(mine, ref, [qkv, bias]), tol)
