@@ -39,6 +39,17 @@ int launch_fp32(int which, const Params& P, int dp, cudaStream_t stream) {
   return launch_prec<true>(which, P, dp, stream);
 }
 
+// How a bias tile is staged: one key row when it broadcasts over queries
+// (si == 0); 16-byte copies when its rows are contiguous, 16-byte aligned and
+// k is a multiple of 4 (a copy never crosses the row's end); else scalars.
+static int bias_mode(const cg_bias& b, int k) {
+  if (b.ptr == nullptr) return kBiasNone;
+  if (b.si == 0) return kBiasKeyRow;
+  const bool vec = b.sj == 1 && k % 4 == 0 && (reinterpret_cast<uintptr_t>(b.ptr) & 15) == 0 && b.si % 4 == 0 &&
+                   b.sh % 4 == 0 && b.sn % 4 == 0;
+  return vec ? kBiasVec : kBiasScalar;
+}
+
 int launch(int which, const cg_edge_attn_args& a, int dbias_mode, int ki, int kj, int vec_ok, int dp,
            cudaStream_t stream) {
   Params P;
@@ -48,6 +59,8 @@ int launch(int which, const cg_edge_attn_args& a, int dbias_mode, int ki, int kj
   P.kj = kj;
   // 16-byte operand loads need rows of exactly the padded width
   P.vec_ok = vec_ok && a.d == dp;
+  P.bias_mode = bias_mode(a.bias, a.k);
+  P.hb_mode = bias_mode(a.hb, a.k);
   return a.precision == CG_ATTN_TF32 ? launch_tf32(which, P, dp, stream) : launch_fp32(which, P, dp, stream);
 }
 

@@ -14,14 +14,24 @@
 // One CTA of two warps owns one slice (n, h) of k <= 32 tokens: warp w holds
 // query rows [16w, 16w + 16) of every k x k matrix as mma accumulator
 // fragments, so row reductions of the softmax are quad shuffles. The k x d
-// operands sit in shared memory with a 4-float row pad; k x k intermediates
-// (probs, grad_logits, d_scores, d_grad_probs) are written to shared memory
-// once, then read back as A fragments, straight for the row products
-// (dq, grad_out) and transposed for the key products (dk, dv) after a CTA
-// barrier. Rows past k and columns past d are zero in shared memory.
+// operands sit in shared memory; k x k intermediates (probs, grad_logits,
+// d_scores, d_grad_probs) are written there once, then read back as A
+// fragments, straight for the row products (dq, grad_out) and transposed for
+// the key products (dk, dv) after a CTA barrier. Rows past k and columns past
+// d are zero in shared memory.
+//
+// Fragment loads. The mma's k-slot t holds logical k0 + 2t and slot t + 4
+// holds k0 + 2t + 1 (a reduction does not care which slot carries which k, as
+// long as A and B agree), so a lane's two k values of one row are adjacent
+// and come in one 64-bit shared load. Rows of 32 floats are XOR-swizzled in
+// 8-float groups, element (r, c) at column c ^ 8 f(r), f(r) = (r & 3) ^
+// ((r >> 2) & 1): the row-by-g 64-bit loads (rows g of a band, columns 2t)
+// and the transposed row-by-t 32-bit loads (rows k0 + 2t (+1), columns g) of
+// one warp then both hit 32 distinct banks, with no padding.
 #pragma once
 
 #include <math.h>
+#include <stdint.h>
 
 #include "common.cuh"
 #include "../../include/cg_b200.h"
@@ -29,21 +39,43 @@
 namespace cg {
 namespace attn_tc {
 
-constexpr int KP = 32;    // padded tokens per slice
-constexpr int LDP = 36;   // pitch of k x k matrices
+constexpr int KP = 32;  // padded tokens per slice
 constexpr int kThreads = 64;
+
+// shared-memory bias tiles: none, one key row broadcast over queries, a full
+// k x k tile by 16-byte copies, a full tile by scalar loads
+enum BiasMode { kBiasNone = 0, kBiasKeyRow = 1, kBiasVec = 2, kBiasScalar = 3 };
 
 struct Params {
   cg_edge_attn_args a;
   int dbias_mode;  // 0 none, 1 direct, 2 per-slice partials into scratch
   int ki, kj;
   int vec_ok;
+  int bias_mode, hb_mode;
 };
 
 // per-slice dbias partials -> dbias, when the bias broadcasts over n or h
 int reduce_dbias(const Params& P, cudaStream_t stream);
 
-// ---- mma.sync tf32 with a 3-term split ---------------------------------------
+// ---- shared layout ------------------------------------------------------------
+
+__device__ __forceinline__ int swz(int r) { return ((r & 3) ^ ((r >> 2) & 1)) << 3; }
+// element (r, c) of a k x k matrix
+__device__ __forceinline__ int kk(int r, int c) { return r * KP + (c ^ swz(r)); }
+
+template <int DP>
+struct Layout {
+  // widths of 32 and 64 are swizzled in place; narrower ones padded by 4
+  static constexpr bool kSwz = DP >= 32;
+  static constexpr int LD = kSwz ? DP : DP + 4;
+  static constexpr int OP = KP * LD;  // floats per k x d operand
+  static constexpr int KK = KP * KP;  // floats per k x k matrix
+  __device__ static __forceinline__ int op(int r, int c) { return r * LD + (kSwz ? (c ^ swz(r)) : c); }
+};
+
+__device__ __forceinline__ float2 ld2(const float* s, int i) { return *reinterpret_cast<const float2*>(s + i); }
+
+// ---- mma.sync tf32 ---------------------------------------------------------------
 
 struct Split {
   uint32_t hi, lo;
@@ -55,14 +87,14 @@ struct Split {
 // split (fp32 mode): hi = x truncated to tf32 (low bits cleared, so that the
 // remainder x - hi is exact), lo = the remainder rounded the same way.
 // Integer and FADD work only: no conversions.
-__device__ inline uint32_t tf32_rn(float x) { return __float_as_uint(x) + 0x1000u; }
+__device__ __forceinline__ uint32_t tf32_rn(float x) { return __float_as_uint(x) + 0x1000u; }
 
-__device__ inline Split split(float x) {
+__device__ __forceinline__ Split split(float x) {
   const uint32_t hi = __float_as_uint(x) & 0xffffe000u;
   return {hi, tf32_rn(x - __uint_as_float(hi))};
 }
 
-__device__ inline void mma(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+__device__ __forceinline__ void mma(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
   asm volatile(
       "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
       "{%0, %1, %2, %3};"
@@ -70,72 +102,88 @@ __device__ inline void mma(float (&d)[4], const uint32_t (&a)[4], const uint32_t
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
-// acc[nt] += A(16 x 8*KT) * B(8*KT x 8*NT) for one 16-row band.
-// la(m, k): A element (m < 16); lb(k, n): B element. Fragment layout of
-// m16n8k8: A a0 (g, t) a1 (g+8, t) a2 (g, t+4) a3 (g+8, t+4); B b0 (t, g)
-// b1 (t+4, g); C c0 (g, 2t) c1 (g, 2t+1) c2 (g+8, 2t) c3 (g+8, 2t+1).
-// X3: three-term split products (fp32 accuracy); else one rounded tf32 term.
-template <bool X3, int NT, int KT, class LA, class LB>
-__device__ inline void band_mma(float (&acc)[NT][4], LA la, LB lb, int g, int t) {
-#pragma unroll 1
-  for (int kt = 0; kt < KT; ++kt) {
-    const int k0 = kt * 8;
-    if constexpr (X3) {
-      const Split a0 = split(la(g, k0 + t)), a1 = split(la(g + 8, k0 + t));
-      const Split a2 = split(la(g, k0 + t + 4)), a3 = split(la(g + 8, k0 + t + 4));
-      const uint32_t ahi[4] = {a0.hi, a1.hi, a2.hi, a3.hi};
-      const uint32_t alo[4] = {a0.lo, a1.lo, a2.lo, a3.lo};
+// One 8-deep k step of acc[nt] += A(16 x 8) * B(8 x 8*NT) for one 16-row
+// band, k = k0 .. k0 + 7. la(m, k) returns {A(m, k), A(m, k + 1)} and
+// lb(k, n) returns {B(k, n), B(k + 1, n)} for even k. m16n8k8 fragments: A a0
+// (g, slot t) a1 (g+8, t) a2 (g, t+4) a3 (g+8, t+4); B b0 (t, g) b1 (t+4, g);
+// C c0 (g, 2t) c1 (g, 2t+1) c2 (g+8, 2t) c3 (g+8, 2t+1).
+template <bool X3, int NT, class LA, class LB>
+__device__ __forceinline__ void kstep(float (&acc)[NT][4], LA la, LB lb, int k0, int g, int t) {
+  const float2 r0 = la(g, k0 + 2 * t), r1 = la(g + 8, k0 + 2 * t);
+  if constexpr (X3) {
+    const Split a0 = split(r0.x), a1 = split(r1.x), a2 = split(r0.y), a3 = split(r1.y);
+    const uint32_t ahi[4] = {a0.hi, a1.hi, a2.hi, a3.hi};
+    const uint32_t alo[4] = {a0.lo, a1.lo, a2.lo, a3.lo};
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const Split b0 = split(lb(k0 + t, nt * 8 + g)), b1 = split(lb(k0 + t + 4, nt * 8 + g));
-        const uint32_t bhi[2] = {b0.hi, b1.hi};
-        const uint32_t blo[2] = {b0.lo, b1.lo};
-        mma(acc[nt], alo, bhi);
-        mma(acc[nt], ahi, blo);
-        mma(acc[nt], ahi, bhi);
-      }
-    } else {
-      const uint32_t a[4] = {tf32_rn(la(g, k0 + t)), tf32_rn(la(g + 8, k0 + t)), tf32_rn(la(g, k0 + t + 4)),
-                             tf32_rn(la(g + 8, k0 + t + 4))};
+    for (int nt = 0; nt < NT; ++nt) {
+      const float2 b = lb(k0 + 2 * t, nt * 8 + g);
+      const Split b0 = split(b.x), b1 = split(b.y);
+      const uint32_t bhi[2] = {b0.hi, b1.hi};
+      const uint32_t blo[2] = {b0.lo, b1.lo};
+      mma(acc[nt], alo, bhi);
+      mma(acc[nt], ahi, blo);
+      mma(acc[nt], ahi, bhi);
+    }
+  } else {
+    const uint32_t a[4] = {tf32_rn(r0.x), tf32_rn(r1.x), tf32_rn(r0.y), tf32_rn(r1.y)};
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const uint32_t b[2] = {tf32_rn(lb(k0 + t, nt * 8 + g)), tf32_rn(lb(k0 + t + 4, nt * 8 + g))};
-        mma(acc[nt], a, b);
-      }
+    for (int nt = 0; nt < NT; ++nt) {
+      const float2 b = lb(k0 + 2 * t, nt * 8 + g);
+      const uint32_t bb[2] = {tf32_rn(b.x), tf32_rn(b.y)};
+      mma(acc[nt], a, bb);
     }
   }
 }
 
+// acc += A(16 x 8*KT) * B(8*KT x 8*NT); the tf32 loop is unrolled, the
+// three-term one (three times the code per step) is not.
+template <bool X3, int NT, int KT, class LA, class LB>
+__device__ __forceinline__ void band_mma(float (&acc)[NT][4], LA la, LB lb, int g, int t) {
+  constexpr int U = X3 ? 1 : KT;
+#pragma unroll U
+  for (int kt = 0; kt < KT; ++kt) kstep<X3>(acc, la, lb, kt * 8, g, t);
+}
+
+// Two independent products in one k loop: twice the accumulator chains in
+// flight per warp.
+template <bool X3, int NT, int KT, class LA1, class LB1, class LA2, class LB2>
+__device__ __forceinline__ void band_mma2(float (&acc1)[NT][4], LA1 la1, LB1 lb1, float (&acc2)[NT][4], LA2 la2,
+                                          LB2 lb2, int g, int t) {
+  constexpr int U = X3 ? 1 : KT;
+#pragma unroll U
+  for (int kt = 0; kt < KT; ++kt) {
+    kstep<X3>(acc1, la1, lb1, kt * 8, g, t);
+    kstep<X3>(acc2, la2, lb2, kt * 8, g, t);
+  }
+}
+
 template <int NT>
-__device__ inline void zero(float (&acc)[NT][4]) {
+__device__ __forceinline__ void zero(float (&acc)[NT][4]) {
 #pragma unroll
   for (int i = 0; i < NT; ++i)
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[i][e] = 0.0f;
 }
 
-// C-fragment element e of tile nt: row (within the band) and column.
-__device__ inline int frag_row(int g, int e) { return g + 8 * (e >> 1); }
-__device__ inline int frag_col(int nt, int t, int e) { return nt * 8 + 2 * t + (e & 1); }
-
 // Sum over the quad (the four lanes sharing g): a full row of a k x k band.
-__device__ inline float quad_sum(float v) {
+__device__ __forceinline__ float quad_sum(float v) {
   v += __shfl_xor_sync(0xffffffffu, v, 1);
   v += __shfl_xor_sync(0xffffffffu, v, 2);
   return v;
 }
-__device__ inline float quad_max(float v) {
+__device__ __forceinline__ float quad_max(float v) {
   v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
   v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
   return v;
 }
 
-// ---- shared-memory staging -------------------------------------------------------
+// ---- operand staging -------------------------------------------------------------
 // Row r of a slice operand, or null for a zero row: plain rows
 // ptr + n*sn + h*sh + r*sr, or, with the slice's token index staged in shared
 // memory (sidx[r] = token_index[n*k + r]), the gathered row
 // ptr + sidx[r]*sr + h*sh (negative index: zero row).
-__device__ inline const float* op_row(const cg_mat& m, const int32_t* sidx, int64_t n, int64_t h, int r, int k) {
+__device__ __forceinline__ const float* op_row(const cg_mat& m, const int32_t* sidx, int64_t n, int64_t h, int r,
+                                               int k) {
   if (r >= k) return nullptr;
   const float* base = reinterpret_cast<const float*>(m.ptr) + h * m.sh;
   if (sidx == nullptr) return base + n * m.sn + (int64_t)r * m.sr;
@@ -145,82 +193,87 @@ __device__ inline const float* op_row(const cg_mat& m, const int32_t* sidx, int6
 
 // Stage the slice's token index in shared memory (all threads; a barrier
 // follows before use). Returns the pointer the loads take, or null.
-__device__ inline const int32_t* stage_index(int32_t* sidx, const int32_t* token_index, int64_t n, int k) {
+__device__ __forceinline__ const int32_t* stage_index(int32_t* sidx, const int32_t* token_index, int64_t n, int k) {
   if (token_index == nullptr) return nullptr;
   if (threadIdx.x < KP) sidx[threadIdx.x] = threadIdx.x < k ? token_index[n * k + threadIdx.x] : -1;
   __syncthreads();
   return sidx;
 }
 
-template <int DP>
-__device__ inline void load_op(float* s, const cg_mat& m, int64_t n, int64_t h, int k, int d, bool vec,
-                               const int32_t* idx = nullptr) {
-  constexpr int LD = DP + 4;
-  if (vec) {
-    constexpr int VPR = DP / 4;
-    for (int f = threadIdx.x; f < KP * VPR; f += kThreads) {
-      const int r = f / VPR, c = (f % VPR) * 4;
-      const float* row = op_row(m, idx, n, h, r, k);
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (row) v = __ldg(reinterpret_cast<const float4*>(row + c));
-      *reinterpret_cast<float4*>(s + r * LD + c) = v;
-    }
-  } else {
-    for (int f = threadIdx.x; f < KP * DP; f += kThreads) {
-      const int r = f / DP, c = f % DP;
-      const float* row = op_row(m, idx, n, h, r, k);
-      s[r * LD + c] = (row && c < d) ? row[c] : 0.0f;
-    }
-  }
-}
-
-// Asynchronous version of load_op for the aligned layout: 16-byte cp.async
-// copies (rows past k zero-filled by a source size of 0), completed by
-// cp_async_wait<N>() + __syncthreads() before use. Unaligned layouts fall back
-// to load_op.
-__device__ inline void cp_async16(void* dst, const void* src, int src_bytes) {
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
                    static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
                "l"(src), "r"(src_bytes)
                : "memory");
 }
-__device__ inline void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
-__device__ inline void cp_async_wait() {
+__device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// k x d operand into shared memory. Aligned layouts (vec): 16-byte cp.async
+// copies (rows past k zero-filled by a source size of 0), completed by
+// cp_async_wait<N>() + __syncthreads() before use; otherwise scalar loads
+// (zeros past k and d).
 template <int DP>
-__device__ inline void load_op_async(float* s, const cg_mat& m, int64_t n, int64_t h, int k, int d, bool vec,
-                                     const int32_t* idx = nullptr) {
-  if (!vec) {
-    load_op<DP>(s, m, n, h, k, d, false, idx);
-    return;
-  }
-  constexpr int LD = DP + 4;
-  constexpr int VPR = DP / 4;
-  for (int f = threadIdx.x; f < KP * VPR; f += kThreads) {
-    const int r = f / VPR, c = (f % VPR) * 4;
-    const float* row = op_row(m, idx, n, h, r, k);
-    cp_async16(s + r * LD + c, row ? row + c : reinterpret_cast<const float*>(m.ptr), row ? 16 : 0);
-  }
-}
-
-// k x k tile of a broadcastable bias (zeros outside [0,k)^2 or without bias).
-__device__ inline void load_bias(float* s, const cg_bias& b, int64_t n, int64_t h, int k) {
-  for (int f = threadIdx.x; f < KP * KP; f += kThreads) {
-    const int i = f / KP, j = f % KP;
-    float v = 0.0f;
-    if (b.ptr != nullptr && i < k && j < k)
-      v = reinterpret_cast<const float*>(b.ptr)[n * b.sn + h * b.sh + (int64_t)i * b.si + (int64_t)j * b.sj];
-    s[i * LDP + j] = v;
+__device__ __forceinline__ void load_op_async(float* s, const cg_mat& m, int64_t n, int64_t h, int k, int d,
+                                              bool vec, const int32_t* idx = nullptr) {
+  using L = Layout<DP>;
+  if (vec) {
+    constexpr int VPR = DP / 4;
+    for (int f = threadIdx.x; f < KP * VPR; f += kThreads) {
+      const int r = f / VPR, c = (f % VPR) * 4;
+      const float* row = op_row(m, idx, n, h, r, k);
+      cp_async16(s + L::op(r, c), row ? row + c : reinterpret_cast<const float*>(m.ptr), row ? 16 : 0);
+    }
+  } else {
+    for (int f = threadIdx.x; f < KP * DP; f += kThreads) {
+      const int r = f / DP, c = f % DP;
+      const float* row = op_row(m, idx, n, h, r, k);
+      s[L::op(r, c)] = (row && c < d) ? row[c] : 0.0f;
+    }
   }
 }
 
-// Store a 16 x 8*NT band (rows 16*band + ...) of a k x d output.
+// Bias tile of the slice into shared memory (zeros outside [0,k)^2; the
+// 16-byte copies join the caller's next cp.async group). Returns the row mask
+// its readers apply to the query row (0: one key row broadcast over queries).
+__device__ __forceinline__ int load_bias(float* s, const cg_bias& b, int mode, int64_t n, int64_t h, int k) {
+  const float* base = reinterpret_cast<const float*>(b.ptr);
+  switch (mode) {
+    case kBiasNone:
+      if (threadIdx.x < KP) s[threadIdx.x] = 0.0f;
+      return 0;
+    case kBiasKeyRow:
+      if (threadIdx.x < KP) {
+        const int j = threadIdx.x;
+        s[j] = j < k ? base[n * b.sn + h * b.sh + (int64_t)j * b.sj] : 0.0f;
+      }
+      return 0;
+    case kBiasVec:
+      for (int f = threadIdx.x; f < KP * (KP / 4); f += kThreads) {
+        const int i = f / (KP / 4), j = (f % (KP / 4)) * 4;
+        const bool ok = i < k && j < k;
+        const float* src = ok ? base + n * b.sn + h * b.sh + (int64_t)i * b.si + j : base;
+        cp_async16(s + kk(i, j), src, ok ? 16 : 0);
+      }
+      return ~0;
+    default:
+      for (int f = threadIdx.x; f < KP * KP; f += kThreads) {
+        const int i = f / KP, j = f % KP;
+        float v = 0.0f;
+        if (i < k && j < k) v = base[n * b.sn + h * b.sh + (int64_t)i * b.si + (int64_t)j * b.sj];
+        s[kk(i, j)] = v;
+      }
+      return ~0;
+  }
+}
+
+// Store a 16 x 8*NT band (rows 16*band + ...) of a k x d output, times scale.
 template <int NT>
-__device__ inline void store_band(const cg_mat& m, int64_t n, int64_t h, int band, int k, int d,
-                                  const float (&acc)[NT][4], int g, int t, float scale) {
+__device__ __forceinline__ void store_band(const cg_mat& m, int64_t n, int64_t h, int band, int k, int d,
+                                           const float (&acc)[NT][4], int g, int t, float scale, bool vec) {
   float* base = reinterpret_cast<float*>(m.ptr) + n * m.sn + h * m.sh;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
@@ -230,41 +283,44 @@ __device__ inline void store_band(const cg_mat& m, int64_t n, int64_t h, int ban
       const int c = nt * 8 + 2 * t;
       if (r < k) {
         float* dst = base + (int64_t)r * m.sr + c;
-        if (c + 1 < d) {
-          dst[0] = acc[nt][2 * half] * scale;
-          dst[1] = acc[nt][2 * half + 1] * scale;
+        const float x = acc[nt][2 * half] * scale, y = acc[nt][2 * half + 1] * scale;
+        if (vec) {
+          *reinterpret_cast<float2*>(dst) = make_float2(x, y);
+        } else if (c + 1 < d) {
+          dst[0] = x;
+          dst[1] = y;
         } else if (c < d) {
-          dst[0] = acc[nt][2 * half] * scale;
+          dst[0] = x;
         }
       }
     }
   }
 }
 
-__device__ inline int valid_keys(const Params& P, int64_t n) {
+__device__ __forceinline__ int valid_keys(const Params& P, int64_t n) {
   const int k = P.a.k;
   if (P.a.key_count == nullptr) return k;
   const int c = P.a.key_count[n];
   return c < 0 ? 0 : (c > k ? k : c);
 }
 
-// Per-slice dbias from a k x k matrix M in shared memory (pitch LDP), reduced
-// over i and/or j when the bias broadcasts them; to dbias or scratch.
-__device__ inline void write_dbias(const Params& P, const float* M, int64_t n, int64_t h, int64_t slice) {
+// Per-slice dbias from a k x k matrix M in shared memory, reduced over i
+// and/or j when the bias broadcasts them; to dbias or scratch.
+__device__ __forceinline__ void write_dbias(const Params& P, const float* M, int64_t n, int64_t h, int64_t slice) {
   if (P.dbias_mode == 0) return;
   const int k = P.a.k, ki = P.ki, kj = P.kj;
   for (int f = threadIdx.x; f < ki * kj; f += kThreads) {
     const int i = f / kj, j = f % kj;
     float v = 0.0f;
     if (ki == k && kj == k) {
-      v = M[i * LDP + j];
+      v = M[kk(i, j)];
     } else if (ki == 1 && kj == k) {
-      for (int r = 0; r < k; ++r) v += M[r * LDP + j];
+      for (int r = 0; r < k; ++r) v += M[kk(r, j)];
     } else if (ki == k && kj == 1) {
-      for (int c = 0; c < k; ++c) v += M[i * LDP + c];
+      for (int c = 0; c < k; ++c) v += M[kk(i, c)];
     } else {
       for (int r = 0; r < k; ++r)
-        for (int c = 0; c < k; ++c) v += M[r * LDP + c];
+        for (int c = 0; c < k; ++c) v += M[kk(r, c)];
     }
     if (P.dbias_mode == 1) {
       const cg_bias& db = P.a.dbias;
@@ -275,21 +331,27 @@ __device__ inline void write_dbias(const Params& P, const float* M, int64_t n, i
   }
 }
 
-// Logits of the band from the S accumulator: scale * S + bias, masked to -inf
-// for keys past kc and non-finite values. Returns probabilities in `p`
-// (exp(l - lse)) and, when lse_in is null, computes the row lse.
-__device__ inline void band_softmax(float (&p)[4][4], const float (&s)[4][4], const float* sbias, int band,
-                                    int g, int t, float scale, int kc, const float* lse_in, float (&lse)[2]) {
+// Logits of the band from the S accumulator: scale * S + bias (bias row
+// r & brow), masked to -inf for keys past kc and non-finite values. Returns
+// probabilities in `p` (exp(l - lse)) and, when lse_in is null, computes the
+// row lse.
+__device__ __forceinline__ void band_softmax(float (&p)[4][4], const float (&s)[4][4], const float* sbias,
+                                             int brow, int band, int g, int t, float scale, int kc,
+                                             const float* lse_in, float (&lse)[2]) {
   float l[4][4];
   bool ok[4][4];
 #pragma unroll
   for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int r = band * 16 + frag_row(g, e), c = frag_col(nt, t, e);
-      const float v = s[nt][e] * scale + sbias[r * LDP + c];
-      l[nt][e] = v;
-      ok[nt][e] = c < kc && isfinite(v);
+    for (int half = 0; half < 2; ++half) {
+      const int r = band * 16 + g + 8 * half, c = nt * 8 + 2 * t;
+      const float2 b = ld2(sbias, kk(r & brow, c));
+#pragma unroll
+      for (int e2 = 0; e2 < 2; ++e2) {
+        const float v = s[nt][2 * half + e2] * scale + (e2 ? b.y : b.x);
+        l[nt][2 * half + e2] = v;
+        ok[nt][2 * half + e2] = c + e2 < kc && isfinite(v);
+      }
     }
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
@@ -322,16 +384,18 @@ __device__ inline void band_softmax(float (&p)[4][4], const float (&s)[4][4], co
     }
 }
 
-// Write a band of a k x k fragment matrix to shared memory.
-__device__ inline void put_band(float* M, const float (&v)[4][4], int band, int g, int t) {
+// Write a band of a k x k fragment matrix to shared memory (64-bit stores).
+__device__ __forceinline__ void put_band(float* M, const float (&v)[4][4], int band, int g, int t) {
 #pragma unroll
   for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) M[(band * 16 + frag_row(g, e)) * LDP + frag_col(nt, t, e)] = v[nt][e];
+    for (int half = 0; half < 2; ++half)
+      *reinterpret_cast<float2*>(M + kk(band * 16 + g + 8 * half, nt * 8 + 2 * t)) =
+          make_float2(v[nt][2 * half], v[nt][2 * half + 1]);
 }
 
 // row sums of a band (both halves) of a product of two fragment matrices
-__device__ inline void row_dot(float (&out)[2], const float (&a)[4][4], const float (&b)[4][4]) {
+__device__ __forceinline__ void row_dot(float (&out)[2], const float (&a)[4][4], const float (&b)[4][4]) {
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     float s = 0.0f;
@@ -341,13 +405,18 @@ __device__ inline void row_dot(float (&out)[2], const float (&a)[4][4], const fl
   }
 }
 
+// ---- fragment loaders ---------------------------------------------------------------
+// k x d operand X as A, rows from the band (reduction over d).
+#define CG_A_ROWS(X) [&](int m, int c) { return ld2(X, L::op(band * 16 + m, c)); }
+// X as the B of X^T (n = token row, reduction over d).
+#define CG_B_ROWS(X) [&](int c, int j) { return ld2(X, L::op(j, c)); }
+// X as B with the reduction over tokens (k = token row, n = column).
+#define CG_B_COLS(X) [&](int j, int c) { return make_float2(X[L::op(j, c)], X[L::op(j + 1, c)]); }
+// k x k matrix M as A, straight (rows from the band) or transposed.
+#define CG_A_KK(M) [&](int m, int j) { return ld2(M, kk(band * 16 + m, j)); }
+#define CG_A_KKT(M) [&](int m, int i) { return make_float2(M[kk(i, band * 16 + m)], M[kk(i + 1, band * 16 + m)]); }
+
 // ---------------------------------------------------------------------------
-template <int DP>
-struct Layout {
-  static constexpr int LD = DP + 4;
-  static constexpr int OP = KP * LD;     // floats per k x d operand
-  static constexpr int KK = KP * LDP;    // floats per k x k matrix
-};
 
 template <int DP, bool X3>
 __global__ void __launch_bounds__(kThreads) fwd1_tc(const Params P) {
@@ -361,36 +430,34 @@ __global__ void __launch_bounds__(kThreads) fwd1_tc(const Params P) {
   const cg_edge_attn_args& a = P.a;
   const int k = a.k, d = a.d;
   const float scale = (float)a.scale;
+  const bool vec = P.vec_ok;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int band = warp;
   for (int64_t s = blockIdx.x; s < a.n * a.h; s += gridDim.x) {
     const int64_t n = s / a.h, h = s % a.h;
     __syncthreads();
     const int32_t* tix = stage_index(sIdx, a.token_index, n, k);
-    load_op_async<DP>(sQ, a.q, n, h, k, d, P.vec_ok, tix);
-    load_op_async<DP>(sK, a.k_, n, h, k, d, P.vec_ok, tix);
+    load_op_async<DP>(sQ, a.q, n, h, k, d, vec, tix);
+    load_op_async<DP>(sK, a.k_, n, h, k, d, vec, tix);
+    const int brow = load_bias(sP, a.bias, P.bias_mode, n, h, k);
     cp_async_commit();
-    load_op_async<DP>(sV, a.v, n, h, k, d, P.vec_ok, tix);
+    load_op_async<DP>(sV, a.v, n, h, k, d, vec, tix);
     cp_async_commit();
-    load_bias(sP, a.bias, n, h, k);
     cp_async_wait<1>();
     __syncthreads();
     const int kc = valid_keys(P, n);
-    const int band = warp;
     float S[4][4], p[4][4], lse[2];
     zero(S);
-    band_mma<X3, 4, DP / 8>(S, [&](int m, int kk) { return sQ[(band * 16 + m) * L::LD + kk]; },
-                        [&](int kk, int j) { return sK[j * L::LD + kk]; }, g, t);
-    band_softmax(p, S, sP, band, g, t, scale, kc, nullptr, lse);
+    band_mma<X3, 4, DP / 8>(S, CG_A_ROWS(sQ), CG_B_ROWS(sK), g, t);
+    band_softmax(p, S, sP, brow, band, g, t, scale, kc, nullptr, lse);
     cp_async_wait<0>();
-    __syncthreads();
-    __syncwarp();
+    __syncthreads();  // V landed; every warp is done with the bias tile
     put_band(sP, p, band, g, t);
     __syncwarp();
     float O[DP / 8][4];
     zero(O);
-    band_mma<X3, DP / 8, 4>(O, [&](int m, int j) { return sP[(band * 16 + m) * LDP + j]; },
-                        [&](int j, int c) { return sV[j * L::LD + c]; }, g, t);
-    store_band<DP / 8>(a.out, n, h, band, k, d, O, g, t, 1.0f);
+    band_mma<X3, DP / 8, 4>(O, CG_A_KK(sP), CG_B_COLS(sV), g, t);
+    store_band<DP / 8>(a.out, n, h, band, k, d, O, g, t, 1.0f, vec);
     if (t == 0) {
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
@@ -416,42 +483,37 @@ __global__ void __launch_bounds__(kThreads) bwd1_tc(const Params P) {
   const cg_edge_attn_args& a = P.a;
   const int k = a.k, d = a.d;
   const float scale = (float)a.scale;
+  const bool vec = P.vec_ok;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int band = warp;
   for (int64_t s = blockIdx.x; s < a.n * a.h; s += gridDim.x) {
     const int64_t n = s / a.h, h = s % a.h;
     __syncthreads();
     const int32_t* tix = stage_index(sIdx, a.token_index, n, k);
-    load_op_async<DP>(sQ, a.q, n, h, k, d, P.vec_ok, tix);
-    load_op_async<DP>(sK, a.k_, n, h, k, d, P.vec_ok, tix);
+    load_op_async<DP>(sQ, a.q, n, h, k, d, vec, tix);
+    load_op_async<DP>(sK, a.k_, n, h, k, d, vec, tix);
+    load_op_async<DP>(sV, a.v, n, h, k, d, vec, tix);
+    load_op_async<DP>(sG, a.grad_out, n, h, k, d, vec);
+    const int brow = load_bias(sGL, a.bias, P.bias_mode, n, h, k);
     cp_async_commit();
-    load_op_async<DP>(sV, a.v, n, h, k, d, P.vec_ok, tix);
-    load_op_async<DP>(sG, a.grad_out, n, h, k, d, P.vec_ok);
-    cp_async_commit();
-    load_bias(sGL, a.bias, n, h, k);
-    if (threadIdx.x < KP) sLse[threadIdx.x] = threadIdx.x < k ? reinterpret_cast<const float*>(a.lse)[s * k + threadIdx.x] : 0.0f;
-    cp_async_wait<1>();
+    if (threadIdx.x < KP)
+      sLse[threadIdx.x] = threadIdx.x < k ? reinterpret_cast<const float*>(a.lse)[s * k + threadIdx.x] : 0.0f;
+    cp_async_wait<0>();
     __syncthreads();
     const int kc = valid_keys(P, n);
-    const int band = warp;
     {
-      float S[4][4], p[4][4], lse[2];
-      zero(S);
-      band_mma<X3, 4, DP / 8>(S, [&](int m, int kk) { return sQ[(band * 16 + m) * L::LD + kk]; },
-                          [&](int kk, int j) { return sK[j * L::LD + kk]; }, g, t);
-      band_softmax(p, S, sGL, band, g, t, scale, kc, sLse, lse);
-      cp_async_wait<0>();
-      __syncthreads();
-      float GP[4][4];
-      zero(GP);
-      band_mma<X3, 4, DP / 8>(GP, [&](int m, int kk) { return sG[(band * 16 + m) * L::LD + kk]; },
-                          [&](int kk, int j) { return sV[j * L::LD + kk]; }, g, t);
+      float S[4][4], GP[4][4], p[4][4], lse[2];
+      zero(S);   // scores
+      zero(GP);  // grad_probs = grad_out v^T
+      band_mma2<X3, 4, DP / 8>(S, CG_A_ROWS(sQ), CG_B_ROWS(sK), GP, CG_A_ROWS(sG), CG_B_ROWS(sV), g, t);
+      band_softmax(p, S, sGL, brow, band, g, t, scale, kc, sLse, lse);
       float rs[2];
       row_dot(rs, p, GP);
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) GP[nt][e] = p[nt][e] * (GP[nt][e] - rs[e >> 1]);  // grad_logits
-      __syncwarp();
+      __syncthreads();  // every warp is done with the bias tile
       put_band(sP, p, band, g, t);
       put_band(sGL, GP, band, g, t);
       __syncwarp();
@@ -459,21 +521,17 @@ __global__ void __launch_bounds__(kThreads) bwd1_tc(const Params P) {
     {
       float O[DP / 8][4];
       zero(O);  // grad_q = scale * grad_logits k
-      band_mma<X3, DP / 8, 4>(O, [&](int m, int j) { return sGL[(band * 16 + m) * LDP + j]; },
-                          [&](int j, int c) { return sK[j * L::LD + c]; }, g, t);
-      store_band<DP / 8>(a.dq, n, h, band, k, d, O, g, t, scale);
+      band_mma<X3, DP / 8, 4>(O, CG_A_KK(sGL), CG_B_COLS(sK), g, t);
+      store_band<DP / 8>(a.dq, n, h, band, k, d, O, g, t, scale, vec);
     }
     __syncthreads();
     {
-      float O[DP / 8][4];
-      zero(O);  // grad_v = probs^T grad_out (rows: keys of this band)
-      band_mma<X3, DP / 8, 4>(O, [&](int m, int i) { return sP[i * LDP + band * 16 + m]; },
-                          [&](int i, int c) { return sG[i * L::LD + c]; }, g, t);
-      store_band<DP / 8>(a.dv, n, h, band, k, d, O, g, t, 1.0f);
-      zero(O);  // grad_k = scale * grad_logits^T q
-      band_mma<X3, DP / 8, 4>(O, [&](int m, int i) { return sGL[i * LDP + band * 16 + m]; },
-                          [&](int i, int c) { return sQ[i * L::LD + c]; }, g, t);
-      store_band<DP / 8>(a.dk, n, h, band, k, d, O, g, t, scale);
+      float DV[DP / 8][4], DK[DP / 8][4];
+      zero(DV);  // grad_v = probs^T grad_out (rows: keys of this band)
+      zero(DK);  // grad_k = scale * grad_logits^T q
+      band_mma2<X3, DP / 8, 4>(DV, CG_A_KKT(sP), CG_B_COLS(sG), DK, CG_A_KKT(sGL), CG_B_COLS(sQ), g, t);
+      store_band<DP / 8>(a.dv, n, h, band, k, d, DV, g, t, 1.0f, vec);
+      store_band<DP / 8>(a.dk, n, h, band, k, d, DK, g, t, scale, vec);
     }
     write_dbias(P, sGL, n, h, s);
   }
@@ -499,41 +557,36 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
   const cg_edge_attn_args& a = P.a;
   const int k = a.k, d = a.d;
   const float scale = (float)a.scale;
+  const bool vec = P.vec_ok;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int band = warp;
   for (int64_t s = blockIdx.x; s < a.n * a.h; s += gridDim.x) {
     const int64_t n = s / a.h, h = s % a.h;
     __syncthreads();
     const int32_t* tix = stage_index(sIdx, a.token_index, n, k);
-    // operands in the order the products need them, four cp.async groups
-    load_op_async<DP>(sQ, a.q, n, h, k, d, P.vec_ok, tix);
-    load_op_async<DP>(sK, a.k_, n, h, k, d, P.vec_ok, tix);
+    // operands in the order the products need them, two cp.async groups
+    load_op_async<DP>(sQ, a.q, n, h, k, d, vec, tix);
+    load_op_async<DP>(sK, a.k_, n, h, k, d, vec, tix);
+    load_op_async<DP>(sG, a.grad_out, n, h, k, d, vec);
+    load_op_async<DP>(sV, a.v, n, h, k, d, vec, tix);
+    const int brow = load_bias(sGL, a.bias, P.bias_mode, n, h, k);
     cp_async_commit();
-    load_op_async<DP>(sG, a.grad_out, n, h, k, d, P.vec_ok);
-    load_op_async<DP>(sV, a.v, n, h, k, d, P.vec_ok, tix);
+    load_op_async<DP>(sHQ, a.hq, n, h, k, d, vec, tix);
+    load_op_async<DP>(sHK, a.hk, n, h, k, d, vec, tix);
+    load_op_async<DP>(sHV, a.hv, n, h, k, d, vec, tix);
+    const int hrow = load_bias(sDS, a.hb, P.hb_mode, n, h, k);
     cp_async_commit();
-    load_op_async<DP>(sHQ, a.hq, n, h, k, d, P.vec_ok, tix);
-    load_op_async<DP>(sHK, a.hk, n, h, k, d, P.vec_ok, tix);
-    cp_async_commit();
-    load_op_async<DP>(sHV, a.hv, n, h, k, d, P.vec_ok, tix);
-    cp_async_commit();
-    load_bias(sGL, a.bias, n, h, k);
-    load_bias(sDS, a.hb, n, h, k);
-    if (threadIdx.x < KP) sLse[threadIdx.x] = threadIdx.x < k ? reinterpret_cast<const float*>(a.lse)[s * k + threadIdx.x] : 0.0f;
-    cp_async_wait<3>();
+    if (threadIdx.x < KP)
+      sLse[threadIdx.x] = threadIdx.x < k ? reinterpret_cast<const float*>(a.lse)[s * k + threadIdx.x] : 0.0f;
+    cp_async_wait<1>();
     __syncthreads();
     const int kc = valid_keys(P, n);
-    const int band = warp;
     {
       float p[4][4], lse[2], A[4][4], B[4][4];
       zero(A);  // scores
-      band_mma<X3, 4, DP / 8>(A, [&](int m, int kk) { return sQ[(band * 16 + m) * L::LD + kk]; },
-                          [&](int kk, int j) { return sK[j * L::LD + kk]; }, g, t);
-      band_softmax(p, A, sGL, band, g, t, scale, kc, sLse, lse);
-      cp_async_wait<2>();
-      __syncthreads();
       zero(B);  // grad_probs = grad_out v^T
-      band_mma<X3, 4, DP / 8>(B, [&](int m, int kk) { return sG[(band * 16 + m) * L::LD + kk]; },
-                          [&](int kk, int j) { return sV[j * L::LD + kk]; }, g, t);
+      band_mma2<X3, 4, DP / 8>(A, CG_A_ROWS(sQ), CG_B_ROWS(sK), B, CG_A_ROWS(sG), CG_B_ROWS(sV), g, t);
+      band_softmax(p, A, sGL, brow, band, g, t, scale, kc, sLse, lse);
       float rs[2];
       row_dot(rs, p, B);
       float cen[4][4];
@@ -541,25 +594,22 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
       for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) cen[nt][e] = B[nt][e] - rs[e >> 1];
-      cp_async_wait<1>();
+      cp_async_wait<0>();
       __syncthreads();
       zero(A);  // d_logits = scale * (hq k^T + q hk^T) + hb
-      band_mma<X3, 4, DP / 8>(A, [&](int m, int kk) { return sHQ[(band * 16 + m) * L::LD + kk]; },
-                          [&](int kk, int j) { return sK[j * L::LD + kk]; }, g, t);
-      band_mma<X3, 4, DP / 8>(A, [&](int m, int kk) { return sQ[(band * 16 + m) * L::LD + kk]; },
-                          [&](int kk, int j) { return sHK[j * L::LD + kk]; }, g, t);
+      zero(B);  // grad_out hv^T
+      band_mma2<X3, 4, DP / 8>(A, CG_A_ROWS(sHQ), CG_B_ROWS(sK), B, CG_A_ROWS(sG), CG_B_ROWS(sHV), g, t);
+      band_mma<X3, 4, DP / 8>(A, CG_A_ROWS(sQ), CG_B_ROWS(sHK), g, t);
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-          A[nt][e] = scale * A[nt][e] + sDS[(band * 16 + frag_row(g, e)) * LDP + frag_col(nt, t, e)];
+        for (int half = 0; half < 2; ++half) {
+          const float2 hb = ld2(sDS, kk((band * 16 + g + 8 * half) & hrow, nt * 8 + 2 * t));
+          A[nt][2 * half] = scale * A[nt][2 * half] + hb.x;
+          A[nt][2 * half + 1] = scale * A[nt][2 * half + 1] + hb.y;
+        }
       float drs[2];
       row_dot(drs, A, p);
-      cp_async_wait<0>();
-      __syncthreads();
-      zero(B);  // grad_out hv^T
-      band_mma<X3, 4, DP / 8>(B, [&](int m, int kk) { return sG[(band * 16 + m) * L::LD + kk]; },
-                          [&](int kk, int j) { return sHV[j * L::LD + kk]; }, g, t);
       float dg[4][4];
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt)
@@ -579,7 +629,7 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
           A[nt][e] = p[nt][e] * (B[nt][e] - rs2[e >> 1]);  // d_scores
           cen[nt][e] = p[nt][e] * cen[nt][e];              // grad_logits
         }
-      __syncwarp();
+      __syncthreads();  // every warp is done with the bias and hb tiles
       put_band(sP, p, band, g, t);
       put_band(sDG, dg, band, g, t);
       put_band(sGL, cen, band, g, t);
@@ -587,37 +637,33 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
       __syncwarp();
     }
     {
-      float O[DP / 8][4];
-      zero(O);  // grad_q = scale * (grad_logits hk + d_scores k)
-      band_mma<X3, DP / 8, 4>(O, [&](int m, int j) { return sGL[(band * 16 + m) * LDP + j]; },
-                          [&](int j, int c) { return sHK[j * L::LD + c]; }, g, t);
-      band_mma<X3, DP / 8, 4>(O, [&](int m, int j) { return sDS[(band * 16 + m) * LDP + j]; },
-                          [&](int j, int c) { return sK[j * L::LD + c]; }, g, t);
-      store_band<DP / 8>(a.dq, n, h, band, k, d, O, g, t, scale);
-      zero(O);  // grad_out cotangent = d_grad_probs v + probs hv
-      band_mma<X3, DP / 8, 4>(O, [&](int m, int j) { return sDG[(band * 16 + m) * LDP + j]; },
-                          [&](int j, int c) { return sV[j * L::LD + c]; }, g, t);
-      band_mma<X3, DP / 8, 4>(O, [&](int m, int j) { return sP[(band * 16 + m) * LDP + j]; },
-                          [&](int j, int c) { return sHV[j * L::LD + c]; }, g, t);
-      store_band<DP / 8>(a.dgrad_out, n, h, band, k, d, O, g, t, 1.0f);
+      float DQ[DP / 8][4], DGO[DP / 8][4];
+      zero(DQ);   // grad_q = scale * (grad_logits hk + d_scores k)
+      zero(DGO);  // grad_out cotangent = d_grad_probs v + probs hv
+      band_mma2<X3, DP / 8, 4>(DQ, CG_A_KK(sGL), CG_B_COLS(sHK), DGO, CG_A_KK(sDG), CG_B_COLS(sV), g, t);
+      band_mma2<X3, DP / 8, 4>(DQ, CG_A_KK(sDS), CG_B_COLS(sK), DGO, CG_A_KK(sP), CG_B_COLS(sHV), g, t);
+      store_band<DP / 8>(a.dq, n, h, band, k, d, DQ, g, t, scale, vec);
+      store_band<DP / 8>(a.dgrad_out, n, h, band, k, d, DGO, g, t, 1.0f, vec);
     }
     __syncthreads();
     {
-      float O[DP / 8][4];
-      zero(O);  // grad_k = scale * (grad_logits^T hq + d_scores^T q)
-      band_mma<X3, DP / 8, 4>(O, [&](int m, int i) { return sGL[i * LDP + band * 16 + m]; },
-                          [&](int i, int c) { return sHQ[i * L::LD + c]; }, g, t);
-      band_mma<X3, DP / 8, 4>(O, [&](int m, int i) { return sDS[i * LDP + band * 16 + m]; },
-                          [&](int i, int c) { return sQ[i * L::LD + c]; }, g, t);
-      store_band<DP / 8>(a.dk, n, h, band, k, d, O, g, t, scale);
-      zero(O);  // grad_v = d_grad_probs^T grad_out
-      band_mma<X3, DP / 8, 4>(O, [&](int m, int i) { return sDG[i * LDP + band * 16 + m]; },
-                          [&](int i, int c) { return sG[i * L::LD + c]; }, g, t);
-      store_band<DP / 8>(a.dv, n, h, band, k, d, O, g, t, 1.0f);
+      float DK[DP / 8][4], DV[DP / 8][4];
+      zero(DK);  // grad_k = scale * (grad_logits^T hq + d_scores^T q)
+      zero(DV);  // grad_v = d_grad_probs^T grad_out
+      band_mma2<X3, DP / 8, 4>(DK, CG_A_KKT(sGL), CG_B_COLS(sHQ), DV, CG_A_KKT(sDG), CG_B_COLS(sG), g, t);
+      band_mma<X3, DP / 8, 4>(DK, CG_A_KKT(sDS), CG_B_COLS(sQ), g, t);
+      store_band<DP / 8>(a.dk, n, h, band, k, d, DK, g, t, scale, vec);
+      store_band<DP / 8>(a.dv, n, h, band, k, d, DV, g, t, 1.0f, vec);
     }
     write_dbias(P, sDS, n, h, s);
   }
 }
+
+#undef CG_A_ROWS
+#undef CG_B_ROWS
+#undef CG_B_COLS
+#undef CG_A_KK
+#undef CG_A_KKT
 
 // shared memory per CTA (bytes)
 template <int DP>
@@ -638,7 +684,8 @@ int launch_dp(int which, const Params& P, cudaStream_t stream) {
   void (*kernel)(const Params) = which == 0 ? fwd1_tc<DP, X3> : which == 1 ? bwd1_tc<DP, X3> : bwd2_tc<DP, X3>;
   CG_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   const int64_t slices = P.a.n * P.a.h;
-  int per_sm = (220 * 1024) / smem;
+  // 228 KB of shared memory per SM, 1 KB of it reserved per resident CTA
+  int per_sm = (228 * 1024) / (smem + 1024);
   if (per_sm < 1) per_sm = 1;
   if (per_sm > 16) per_sm = 16;
   const int64_t cap = (int64_t)sm_count() * per_sm;
