@@ -61,6 +61,13 @@ int launch(int which, const cg_edge_attn_args& a, int dbias_mode, int ki, int kj
   P.vec_ok = vec_ok && a.d == dp;
   P.bias_mode = bias_mode(a.bias, a.k);
   P.hb_mode = bias_mode(a.hb, a.k);
+  // full-tile dbias in 16-byte stores: contiguous aligned rows (dbias, or the
+  // scratch partials of k x k per slice), k a multiple of 4
+  const bool db_rows = dbias_mode == 1
+                           ? a.dbias.sj == 1 && a.dbias.si % 4 == 0 && a.dbias.sh % 4 == 0 && a.dbias.sn % 4 == 0 &&
+                                 (reinterpret_cast<uintptr_t>(a.dbias.ptr) & 15) == 0
+                           : (reinterpret_cast<uintptr_t>(a.scratch) & 15) == 0;
+  P.dbias_vec = dbias_mode != 0 && ki == a.k && kj == a.k && a.k % 4 == 0 && db_rows;
   return a.precision == CG_ATTN_TF32 ? launch_tf32(which, P, dp, stream) : launch_fp32(which, P, dp, stream);
 }
 

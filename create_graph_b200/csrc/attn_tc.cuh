@@ -14,11 +14,12 @@
 // One CTA of two warps owns one slice (n, h) of k <= 32 tokens: warp w holds
 // query rows [16w, 16w + 16) of every k x k matrix as mma accumulator
 // fragments, so row reductions of the softmax are quad shuffles. The k x d
-// operands sit in shared memory; k x k intermediates (probs, grad_logits,
-// d_scores, d_grad_probs) are written there once, then read back as A
-// fragments, straight for the row products (dq, grad_out) and transposed for
-// the key products (dk, dv) after a CTA barrier. Rows past k and columns past
-// d are zero in shared memory.
+// operands sit in shared memory. The k x k intermediates (probs,
+// grad_logits, d_scores, d_grad_probs) feed the row products (out, dq,
+// grad_out) straight from their accumulator fragments, and are written to
+// shared memory once for the key products (dk, dv), which read them
+// transposed after a CTA barrier. Rows past k and columns past d are zero in
+// shared memory.
 //
 // Fragment loads. The mma's k-slot t holds logical k0 + 2t and slot t + 4
 // holds k0 + 2t + 1 (a reduction does not care which slot carries which k, as
@@ -52,6 +53,7 @@ struct Params {
   int ki, kj;
   int vec_ok;
   int bias_mode, hb_mode;
+  int dbias_vec;  // full-tile dbias rows leave in 16-byte stores
 };
 
 // per-slice dbias partials -> dbias, when the bias broadcasts over n or h
@@ -107,11 +109,11 @@ __device__ __forceinline__ void mma(float (&d)[4], const uint32_t (&a)[4], const
 // lb(k, n) returns {B(k, n), B(k + 1, n)} for even k. m16n8k8 fragments: A a0
 // (g, slot t) a1 (g+8, t) a2 (g, t+4) a3 (g+8, t+4); B b0 (t, g) b1 (t+4, g);
 // C c0 (g, 2t) c1 (g, 2t+1) c2 (g+8, 2t) c3 (g+8, 2t+1).
-template <bool X3, int NT, class LA, class LB>
-__device__ __forceinline__ void kstep(float (&acc)[NT][4], LA la, LB lb, int k0, int g, int t) {
-  const float2 r0 = la(g, k0 + 2 * t), r1 = la(g + 8, k0 + 2 * t);
+template <bool X3, int NT, class LB>
+__device__ __forceinline__ void kstep_a(float (&acc)[NT][4], float x0, float x1, float x2, float x3, LB lb, int k0,
+                                        int g, int t) {
   if constexpr (X3) {
-    const Split a0 = split(r0.x), a1 = split(r1.x), a2 = split(r0.y), a3 = split(r1.y);
+    const Split a0 = split(x0), a1 = split(x1), a2 = split(x2), a3 = split(x3);
     const uint32_t ahi[4] = {a0.hi, a1.hi, a2.hi, a3.hi};
     const uint32_t alo[4] = {a0.lo, a1.lo, a2.lo, a3.lo};
 #pragma unroll
@@ -125,7 +127,7 @@ __device__ __forceinline__ void kstep(float (&acc)[NT][4], LA la, LB lb, int k0,
       mma(acc[nt], ahi, bhi);
     }
   } else {
-    const uint32_t a[4] = {tf32_rn(r0.x), tf32_rn(r1.x), tf32_rn(r0.y), tf32_rn(r1.y)};
+    const uint32_t a[4] = {tf32_rn(x0), tf32_rn(x1), tf32_rn(x2), tf32_rn(x3)};
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const float2 b = lb(k0 + 2 * t, nt * 8 + g);
@@ -133,6 +135,12 @@ __device__ __forceinline__ void kstep(float (&acc)[NT][4], LA la, LB lb, int k0,
       mma(acc[nt], a, bb);
     }
   }
+}
+
+template <bool X3, int NT, class LA, class LB>
+__device__ __forceinline__ void kstep(float (&acc)[NT][4], LA la, LB lb, int k0, int g, int t) {
+  const float2 r0 = la(g, k0 + 2 * t), r1 = la(g + 8, k0 + 2 * t);
+  kstep_a<X3>(acc, r0.x, r1.x, r0.y, r1.y, lb, k0, g, t);
 }
 
 // acc += A(16 x 8*KT) * B(8*KT x 8*NT); the tf32 loop is unrolled, the
@@ -154,6 +162,28 @@ __device__ __forceinline__ void band_mma2(float (&acc1)[NT][4], LA1 la1, LB1 lb1
   for (int kt = 0; kt < KT; ++kt) {
     kstep<X3>(acc1, la1, lb1, kt * 8, g, t);
     kstep<X3>(acc2, la2, lb2, kt * 8, g, t);
+  }
+}
+
+// acc += A(16 x 32) * B(32 x 8*NT) with A a 16 x 32 band held as C fragments
+// of four m16n8 tiles (c[kt] covers columns 8kt .. 8kt + 7). With the k-slot
+// mapping above, tile kt's C fragment {c0, c1, c2, c3} = {(g, 2t), (g, 2t+1),
+// (g+8, 2t), (g+8, 2t+1)} is the A fragment of k step kt in the order
+// {a0, a2, a1, a3}: no shared-memory round trip. Always unrolled (register
+// arrays take constant indices only).
+template <bool X3, int NT, class LB>
+__device__ __forceinline__ void band_mma_reg(float (&acc)[NT][4], const float (&c)[4][4], LB lb, int g, int t) {
+#pragma unroll
+  for (int kt = 0; kt < 4; ++kt) kstep_a<X3>(acc, c[kt][0], c[kt][2], c[kt][1], c[kt][3], lb, kt * 8, g, t);
+}
+
+template <bool X3, int NT, class LB1, class LB2>
+__device__ __forceinline__ void band_mma_reg2(float (&acc1)[NT][4], const float (&c1)[4][4], LB1 lb1,
+                                              float (&acc2)[NT][4], const float (&c2)[4][4], LB2 lb2, int g, int t) {
+#pragma unroll
+  for (int kt = 0; kt < 4; ++kt) {
+    kstep_a<X3>(acc1, c1[kt][0], c1[kt][2], c1[kt][1], c1[kt][3], lb1, kt * 8, g, t);
+    kstep_a<X3>(acc2, c2[kt][0], c2[kt][2], c2[kt][1], c2[kt][3], lb2, kt * 8, g, t);
   }
 }
 
@@ -220,12 +250,13 @@ template <int DP>
 __device__ __forceinline__ void load_op_async(float* s, const cg_mat& m, int64_t n, int64_t h, int k, int d,
                                               bool vec, const int32_t* idx = nullptr) {
   using L = Layout<DP>;
+  const float* ptr = reinterpret_cast<const float*>(m.ptr);
   if (vec) {
     constexpr int VPR = DP / 4;
     for (int f = threadIdx.x; f < KP * VPR; f += kThreads) {
       const int r = f / VPR, c = (f % VPR) * 4;
       const float* row = op_row(m, idx, n, h, r, k);
-      cp_async16(s + L::op(r, c), row ? row + c : reinterpret_cast<const float*>(m.ptr), row ? 16 : 0);
+      cp_async16(s + L::op(r, c), row ? row + c : ptr, row ? 16 : 0);
     }
   } else {
     for (int f = threadIdx.x; f < KP * DP; f += kThreads) {
@@ -305,28 +336,59 @@ __device__ __forceinline__ int valid_keys(const Params& P, int64_t n) {
 }
 
 // Per-slice dbias from a k x k matrix M in shared memory, reduced over i
-// and/or j when the bias broadcasts them; to dbias or scratch.
+// and/or j when the bias broadcasts them; to dbias (mode 1) or to the slice's
+// ki x kj partial in scratch (mode 2). Reductions run in a fixed order.
 __device__ __forceinline__ void write_dbias(const Params& P, const float* M, int64_t n, int64_t h, int64_t slice) {
   if (P.dbias_mode == 0) return;
   const int k = P.a.k, ki = P.ki, kj = P.kj;
-  for (int f = threadIdx.x; f < ki * kj; f += kThreads) {
-    const int i = f / kj, j = f % kj;
-    float v = 0.0f;
-    if (ki == k && kj == k) {
-      v = M[kk(i, j)];
-    } else if (ki == 1 && kj == k) {
-      for (int r = 0; r < k; ++r) v += M[kk(r, j)];
-    } else if (ki == k && kj == 1) {
-      for (int c = 0; c < k; ++c) v += M[kk(i, c)];
+  float* dst;
+  int64_t si, sj;
+  if (P.dbias_mode == 1) {
+    const cg_bias& db = P.a.dbias;
+    dst = reinterpret_cast<float*>(db.ptr) + n * db.sn + h * db.sh;
+    si = db.si;
+    sj = db.sj;
+  } else {
+    dst = reinterpret_cast<float*>(P.a.scratch) + slice * (int64_t)(ki * kj);
+    si = kj;
+    sj = 1;
+  }
+  if (ki == k && kj == k) {
+    if (P.dbias_vec) {
+      for (int f = threadIdx.x; f < KP * (KP / 4); f += kThreads) {
+        const int i = f >> 3, j = (f & 7) * 4;
+        if (i < k && j < k)
+          *reinterpret_cast<float4*>(dst + i * si + j) = *reinterpret_cast<const float4*>(M + kk(i, j));
+      }
     } else {
-      for (int r = 0; r < k; ++r)
-        for (int c = 0; c < k; ++c) v += M[kk(r, c)];
+      for (int f = threadIdx.x; f < KP * KP; f += kThreads) {
+        const int i = f >> 5, j = f & 31;
+        if (i < k && j < k) dst[i * si + j * sj] = M[kk(i, j)];
+      }
     }
-    if (P.dbias_mode == 1) {
-      const cg_bias& db = P.a.dbias;
-      reinterpret_cast<float*>(db.ptr)[n * db.sn + h * db.sh + (int64_t)i * db.si + (int64_t)j * db.sj] = v;
-    } else {
-      reinterpret_cast<float*>(P.a.scratch)[slice * (ki * kj) + f] = v;
+  } else if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    if (ki == 1 && kj == k) {  // column sums: lane j, four partial sums over rows
+      float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 2
+      for (int r = 0; r < KP; r += 4)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) v[q] += r + q < k ? M[kk(r + q, lane)] : 0.0f;
+      if (lane < k) dst[lane * sj] = (v[0] + v[1]) + (v[2] + v[3]);
+    } else {  // row sums (ki == k), or the total (ki == 1): lane i
+      float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 2
+      for (int c = 0; c < KP; c += 4)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) v[q] += c + q < k && lane < k ? M[kk(lane, c + q)] : 0.0f;
+      float row = (v[0] + v[1]) + (v[2] + v[3]);
+      if (ki == k) {
+        if (lane < k) dst[lane * si] = row;
+      } else {
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) row += __shfl_xor_sync(0xffffffffu, row, off);
+        if (lane == 0) dst[0] = row;
+      }
     }
   }
 }
@@ -412,8 +474,7 @@ __device__ __forceinline__ void row_dot(float (&out)[2], const float (&a)[4][4],
 #define CG_B_ROWS(X) [&](int c, int j) { return ld2(X, L::op(j, c)); }
 // X as B with the reduction over tokens (k = token row, n = column).
 #define CG_B_COLS(X) [&](int j, int c) { return make_float2(X[L::op(j, c)], X[L::op(j + 1, c)]); }
-// k x k matrix M as A, straight (rows from the band) or transposed.
-#define CG_A_KK(M) [&](int m, int j) { return ld2(M, kk(band * 16 + m, j)); }
+// k x k matrix M as A, transposed (rows of A = columns of M from the band).
 #define CG_A_KKT(M) [&](int m, int i) { return make_float2(M[kk(i, band * 16 + m)], M[kk(i + 1, band * 16 + m)]); }
 
 // ---------------------------------------------------------------------------
@@ -425,7 +486,7 @@ __global__ void __launch_bounds__(kThreads) fwd1_tc(const Params P) {
   float* sQ = smem;
   float* sK = sQ + L::OP;
   float* sV = sK + L::OP;
-  float* sP = sV + L::OP;  // bias tile, then probabilities
+  float* sP = sV + L::OP;  // bias tile
   int32_t* sIdx = reinterpret_cast<int32_t*>(sP + L::KK);
   const cg_edge_attn_args& a = P.a;
   const int k = a.k, d = a.d;
@@ -451,12 +512,10 @@ __global__ void __launch_bounds__(kThreads) fwd1_tc(const Params P) {
     band_mma<X3, 4, DP / 8>(S, CG_A_ROWS(sQ), CG_B_ROWS(sK), g, t);
     band_softmax(p, S, sP, brow, band, g, t, scale, kc, nullptr, lse);
     cp_async_wait<0>();
-    __syncthreads();  // V landed; every warp is done with the bias tile
-    put_band(sP, p, band, g, t);
-    __syncwarp();
+    __syncthreads();  // V landed
     float O[DP / 8][4];
-    zero(O);
-    band_mma<X3, DP / 8, 4>(O, CG_A_KK(sP), CG_B_COLS(sV), g, t);
+    zero(O);  // out = probs v, probs straight from the fragments
+    band_mma_reg<X3, DP / 8>(O, p, CG_B_COLS(sV), g, t);
     store_band<DP / 8>(a.out, n, h, band, k, d, O, g, t, 1.0f, vec);
     if (t == 0) {
 #pragma unroll
@@ -513,16 +572,13 @@ __global__ void __launch_bounds__(kThreads) bwd1_tc(const Params P) {
       for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) GP[nt][e] = p[nt][e] * (GP[nt][e] - rs[e >> 1]);  // grad_logits
+      float O[DP / 8][4];
+      zero(O);  // grad_q = scale * grad_logits k, grad_logits straight from the fragments
+      band_mma_reg<X3, DP / 8>(O, GP, CG_B_COLS(sK), g, t);
+      store_band<DP / 8>(a.dq, n, h, band, k, d, O, g, t, scale, vec);
       __syncthreads();  // every warp is done with the bias tile
       put_band(sP, p, band, g, t);
       put_band(sGL, GP, band, g, t);
-      __syncwarp();
-    }
-    {
-      float O[DP / 8][4];
-      zero(O);  // grad_q = scale * grad_logits k
-      band_mma<X3, DP / 8, 4>(O, CG_A_KK(sGL), CG_B_COLS(sK), g, t);
-      store_band<DP / 8>(a.dq, n, h, band, k, d, O, g, t, scale, vec);
     }
     __syncthreads();
     {
@@ -634,14 +690,12 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
       put_band(sDG, dg, band, g, t);
       put_band(sGL, cen, band, g, t);
       put_band(sDS, A, band, g, t);
-      __syncwarp();
-    }
-    {
+      // row products with A straight from the fragments
       float DQ[DP / 8][4], DGO[DP / 8][4];
       zero(DQ);   // grad_q = scale * (grad_logits hk + d_scores k)
       zero(DGO);  // grad_out cotangent = d_grad_probs v + probs hv
-      band_mma2<X3, DP / 8, 4>(DQ, CG_A_KK(sGL), CG_B_COLS(sHK), DGO, CG_A_KK(sDG), CG_B_COLS(sV), g, t);
-      band_mma2<X3, DP / 8, 4>(DQ, CG_A_KK(sDS), CG_B_COLS(sK), DGO, CG_A_KK(sP), CG_B_COLS(sHV), g, t);
+      band_mma_reg2<X3, DP / 8>(DQ, cen, CG_B_COLS(sHK), DGO, dg, CG_B_COLS(sV), g, t);
+      band_mma_reg2<X3, DP / 8>(DQ, A, CG_B_COLS(sK), DGO, p, CG_B_COLS(sHV), g, t);
       store_band<DP / 8>(a.dq, n, h, band, k, d, DQ, g, t, scale, vec);
       store_band<DP / 8>(a.dgrad_out, n, h, band, k, d, DGO, g, t, 1.0f, vec);
     }
@@ -662,7 +716,6 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
 #undef CG_A_ROWS
 #undef CG_B_ROWS
 #undef CG_B_COLS
-#undef CG_A_KK
 #undef CG_A_KKT
 
 // shared memory per CTA (bytes)
