@@ -303,6 +303,22 @@ def attn_bytes(info, name):
     return 3 * t + b + lse + t + 3 * t + b + 3 * t + b + t
 
 
+def pooled_attn_bytes(info, name):
+    """Algorithmic bytes of one pooled-attention launch: every per-atom operand
+    once (the gathered token rows are re-reads of the atom rows), plus the
+    per-token [dq | dk] rows the backward kernels must write."""
+    n, h, k, d = info
+    C = h * d
+    atom, key, tok = n * C * 4, n * k * h * 4, n * k * 4   # one (n, C), (n*k, h), (n*k) tensor
+    stats = 2 * n * h * k * 4                              # lse and w
+    if name == "cg_pooled_attn_fwd":
+        return 3 * atom + key + tok + atom + stats
+    dqk = 2 * n * k * C * 4
+    if name == "cg_pooled_attn_bwd1":
+        return 3 * atom + key + tok + stats + atom + dqk + 2 * key + tok
+    return 6 * atom + 2 * key + 2 * tok + stats + atom + dqk + 2 * key + tok + atom
+
+
 def roofline_of(kernels, hbm, bf16, bf16_sus, src):
     """Roofline of the dominant kernel family: HBM-bound edge attention, or the
     tf32 GEMM against the tf32 tensor peak (half the measured bf16 figure)."""
@@ -318,8 +334,9 @@ def roofline_of(kernels, hbm, bf16, bf16_sus, src):
         return {"kernel": name, "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak, "traffic": None,
                 "peak_source": f"{src} bf16 sustained / 2 (dense tf32)"}
-    if name.startswith("cg_edge_attn"):
-        nbytes = sum(attn_bytes(info, name) for _, _, info in rec)
+    if name.startswith("cg_edge_attn") or name.startswith("cg_pooled_attn"):
+        count = attn_bytes if name.startswith("cg_edge_attn") else pooled_attn_bytes
+        nbytes = sum(count(info, name) for _, _, info in rec)
         secs = sum(a.elapsed_time(b) for a, b, _ in rec) / 1e3
         achieved = nbytes / secs / 1e9
         return {"kernel": name, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",

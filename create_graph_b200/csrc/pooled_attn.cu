@@ -1,0 +1,58 @@
+// Envelope-pooled token attention: argument checks, the C entry points and
+// the fp32-precision instantiations (pooled_attn.cuh).
+#include "pooled_attn.cuh"
+
+namespace cg {
+namespace pooled {
+
+int launch_fp32(int which, const PParams& P, int dp, cudaStream_t stream) {
+  return launch_prec<true>(which, P, dp, stream);
+}
+
+static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+static int run(int which, const cg_pooled_attn_args* args, void* stream) {
+  CG_REQUIRE(args != nullptr, "pooled_attn: args is NULL");
+  const cg_pooled_attn_args& a = *args;
+  CG_REQUIRE(a.n >= 0, "pooled_attn: negative atom count");
+  CG_REQUIRE(a.h >= 1, "pooled_attn: h = %d must be positive", a.h);
+  CG_REQUIRE(a.k >= 1 && a.k <= attn_tc::KP, "pooled_attn: k = %d outside [1, %d]", a.k, attn_tc::KP);
+  CG_REQUIRE(a.d >= 1 && a.d <= 64, "pooled_attn: d = %d outside [1, 64]", a.d);
+  CG_REQUIRE(a.precision == CG_ATTN_FP32 || a.precision == CG_ATTN_TF32,
+             "pooled_attn: precision = %d is neither CG_ATTN_FP32 nor CG_ATTN_TF32", a.precision);
+  if (a.n == 0) return kOk;
+  const int64_t C = (int64_t)a.h * a.d;
+  CG_REQUIRE(a.token_index && a.key_count && a.qkv && a.env && a.lse && a.w,
+             "pooled_attn: token_index, key_count, qkv, env, lse and w are required");
+  CG_REQUIRE(a.ld_qkv >= 3 * C, "pooled_attn: ld_qkv = %lld below 3*h*d = %lld", (long long)a.ld_qkv,
+             (long long)(3 * C));
+  if (which == 0) {
+    CG_REQUIRE(a.out != nullptr, "pooled_attn: out is NULL");
+  } else {
+    CG_REQUIRE(a.dout && a.dqk && a.wv, "pooled_attn: dout, dqk and wv are required");
+    CG_REQUIRE(a.ld_dqk >= 2 * C, "pooled_attn: ld_dqk = %lld below 2*h*d", (long long)a.ld_dqk);
+  }
+  if (which == 2) CG_REQUIRE(a.hqkv && a.ddout, "pooled_attn: hqkv and ddout are required");
+  const int dp = a.d <= 16 ? 16 : a.d <= 32 ? 32 : 64;
+  PParams P;
+  P.a = a;
+  bool vec = a.d == dp && a.ld_qkv % 4 == 0 && al16(a.qkv);
+  if (which == 2) vec = vec && al16(a.hqkv);
+  if (which != 0) vec = vec && a.ld_dqk % 4 == 0 && al16(a.dqk);
+  P.vec = vec ? 1 : 0;
+  const cudaStream_t s = as_stream(stream);
+  return a.precision == CG_ATTN_TF32 ? launch_tf32(which, P, dp, s) : launch_fp32(which, P, dp, s);
+}
+
+}  // namespace pooled
+}  // namespace cg
+
+extern "C" {
+
+int cg_pooled_attn_fwd(const cg_pooled_attn_args* a, void* stream) { return cg::pooled::run(0, a, stream); }
+
+int cg_pooled_attn_bwd1(const cg_pooled_attn_args* a, void* stream) { return cg::pooled::run(1, a, stream); }
+
+int cg_pooled_attn_bwd2(const cg_pooled_attn_args* a, void* stream) { return cg::pooled::run(2, a, stream); }
+
+}  // extern "C"

@@ -1,0 +1,532 @@
+// Envelope-pooled token attention (cg_pooled_attn_fwd / bwd1 / bwd2) on the
+// tensor cores: the energy network's attention among the k <= 32 edge tokens
+// of an atom followed by the envelope-weighted sum over tokens, fused so that
+// neither the (n, k, h*d) token outputs nor their cotangents exist.
+//
+// One CTA of two warps owns an atom and walks its heads; per head the slice
+// machinery of attn_tc.cuh applies (warp w holds query rows [16w, 16w + 16)
+// as mma fragments, operands gathered through the staged token index into
+// swizzled shared memory, tf32 or three-term products). What pooling changes:
+// - forward: w_j = sum_i env_i P_ij is a column sum of the fragments (quad
+//   shuffles over g, then the two bands in a fixed order) and
+//   out = sum_j w_j v_j a per-column FMA loop; the P v product disappears;
+// - backward1: the token cotangent is env_i dm, so grad_probs = env_i u_j
+//   with u = V dm (an N = 1 mma), dv_j = w_j dm is rank one (left to
+//   cg_segment_sum_scaled as the weight w) and only S, dq and dk are
+//   products;
+// - backward2: 7 products instead of 11 (S, the two halves of d_logits, dq
+//   and dk twice), u = V dm and t = HV dm as N = 1 mmas, the rest row or
+//   column sums and a per-column FMA loop for d(dm).
+// The envelope gradient, a sum over heads, accumulates in registers across
+// the head loop and leaves once per atom.
+//
+// Padded query rows (past k) get lse = +inf in the backward kernels, hence
+// zero probabilities; their envelope weights and cotangents are zero as well.
+#pragma once
+
+#include "attn_tc.cuh"
+
+namespace cg {
+namespace pooled {
+
+using attn_tc::band_mma;
+using attn_tc::band_mma2;
+using attn_tc::band_mma_reg;
+using attn_tc::band_softmax;
+using attn_tc::cp_async_commit;
+using attn_tc::cp_async_wait;
+using attn_tc::kk;
+using attn_tc::KP;
+using attn_tc::kThreads;
+using attn_tc::ld2;
+using attn_tc::Layout;
+using attn_tc::load_op_async;
+using attn_tc::put_band;
+using attn_tc::quad_sum;
+using attn_tc::stage_index;
+using attn_tc::store_band;
+using attn_tc::zero;
+
+struct PParams {
+  cg_pooled_attn_args a;
+  int vec;  // 16-byte operand rows and 8-byte output pairs (d equal to the padded width)
+};
+
+// q, k or v part (part 0, 1, 2) of per-atom rows, read through the token index
+__device__ __forceinline__ cg_mat part_mat(const float* rows, int part, int64_t C, int d, int64_t ld) {
+  cg_mat m;
+  m.ptr = const_cast<float*>(rows) + part * C;
+  m.sn = 0;
+  m.sh = d;
+  m.sr = ld;
+  return m;
+}
+
+// per-token [dq | dk] rows (n*k, ld): part 0 dq, part 1 dk
+__device__ __forceinline__ cg_mat token_mat(float* dqk, int part, int64_t C, int k, int d, int64_t ld) {
+  cg_mat m;
+  m.ptr = dqk + part * C;
+  m.sn = (int64_t)k * ld;
+  m.sh = d;
+  m.sr = ld;
+  return m;
+}
+
+// Column sums over the band's 16 rows of a k x k fragment matrix (rows g
+// and g + 8 first, then a butterfly over g): lanes 0..3 write the 32
+// column sums of the band to dst.
+__device__ __forceinline__ void band_colsum(float* dst, const float (&v)[4][4], int g, int t) {
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+    for (int e1 = 0; e1 < 2; ++e1) {
+      float x = v[nt][e1] + v[nt][2 + e1];
+      x += __shfl_xor_sync(0xffffffffu, x, 4);
+      x += __shfl_xor_sync(0xffffffffu, x, 8);
+      x += __shfl_xor_sync(0xffffffffu, x, 16);
+      if (g == 0) dst[nt * 8 + 2 * t + e1] = x;
+    }
+}
+
+// Sum over rows of one column of a k x k matrix in shared memory (fixed order).
+__device__ __forceinline__ float smem_colsum(const float* M, int j) {
+  float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+  for (int i = 0; i < KP; i += 4)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) v[q] += M[kk(i + q, j)];
+  return (v[0] + v[1]) + (v[2] + v[3]);
+}
+
+__device__ __forceinline__ int key_count(const cg_pooled_attn_args& a, int64_t n) {
+  const int c = a.key_count[n];
+  return c < 0 ? 0 : (c > a.k ? a.k : c);
+}
+
+// per-token vector of the atom (env, henv) into shared memory, zeros past k
+__device__ __forceinline__ void load_tokens(float* s, const float* src, int64_t n, int k) {
+  if (threadIdx.x < KP) s[threadIdx.x] = (src != nullptr && (int)threadIdx.x < k) ? src[n * k + threadIdx.x] : 0.0f;
+}
+
+// key row of a per-key (n*k, h) matrix for head hh, zeros past k (or all zeros)
+__device__ __forceinline__ void load_key_row(float* s, const float* src, int64_t n, int hh, int k, int H) {
+  if (threadIdx.x < KP)
+    s[threadIdx.x] = (src != nullptr && (int)threadIdx.x < k) ? src[(n * k + threadIdx.x) * H + hh] : 0.0f;
+}
+
+// dm = dout[n, hh*d : hh*d + d] into shared memory, zeros to the padded width
+template <int DP>
+__device__ __forceinline__ void load_dm(float* s, const float* dout, int64_t n, int hh, int d, int64_t C) {
+  for (int c = threadIdx.x; c < DP; c += kThreads) s[c] = c < d ? dout[n * C + (int64_t)hh * d + c] : 0.0f;
+}
+
+// B operand of a matrix-vector product as an N = 1 mma: column 0 is dm
+#define CG_B_VEC(V) [&](int c, int nn) { return nn == 0 ? ld2(V, c) : make_float2(0.0f, 0.0f); }
+#define CG_A_ROWS(X) [&](int m, int c) { return ld2(X, L::op(band * 16 + m, c)); }
+#define CG_B_ROWS(X) [&](int c, int j) { return ld2(X, L::op(j, c)); }
+#define CG_B_COLS(X) [&](int j, int c) { return make_float2(X[L::op(j, c)], X[L::op(j + 1, c)]); }
+#define CG_A_KKT(M) [&](int m, int i) { return make_float2(M[kk(i, band * 16 + m)], M[kk(i + 1, band * 16 + m)]); }
+
+// ---------------------------------------------------------------------------
+
+template <int DP, bool X3>
+__global__ void __launch_bounds__(kThreads) pooled_fwd(const PParams P) {
+  using L = Layout<DP>;
+  extern __shared__ __align__(16) float smem[];
+  float* sQ = smem;
+  float* sK = sQ + L::OP;
+  float* sV = sK + L::OP;
+  float* sB = sV + L::OP;  // key bias row
+  float* sE = sB + KP;     // env of the atom's tokens
+  float* sW = sE + KP;     // band partials of w: [2][KP]
+  int32_t* sIdx = reinterpret_cast<int32_t*>(sW + 2 * KP);
+  const cg_pooled_attn_args& a = P.a;
+  const int k = a.k, d = a.d, H = a.h;
+  const int64_t C = (int64_t)H * d;
+  const float scale = (float)a.scale;
+  const bool vec = P.vec;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int band = warp;
+  const cg_mat mq = part_mat(a.qkv, 0, C, d, a.ld_qkv), mk = part_mat(a.qkv, 1, C, d, a.ld_qkv),
+               mv = part_mat(a.qkv, 2, C, d, a.ld_qkv);
+  for (int64_t n = blockIdx.x; n < a.n; n += gridDim.x) {
+    __syncthreads();
+    const int32_t* tix = stage_index(sIdx, a.token_index, n, k);
+    load_tokens(sE, a.env, n, k);
+    const int kc = key_count(a, n);
+    for (int hh = 0; hh < H; ++hh) {
+      if (hh > 0) __syncthreads();  // the previous head is done with shared memory
+      load_op_async<DP>(sQ, mq, n, hh, k, d, vec, tix);
+      load_op_async<DP>(sK, mk, n, hh, k, d, vec, tix);
+      load_key_row(sB, a.bias, n, hh, k, H);
+      cp_async_commit();
+      load_op_async<DP>(sV, mv, n, hh, k, d, vec, tix);
+      cp_async_commit();
+      cp_async_wait<1>();
+      __syncthreads();
+      float S[4][4], p[4][4], lse[2];
+      zero(S);
+      band_mma<X3, 4, DP / 8>(S, CG_A_ROWS(sQ), CG_B_ROWS(sK), g, t);
+      band_softmax(p, S, sB, 0, band, g, t, scale, kc, nullptr, lse);
+      const float e0 = sE[band * 16 + g], e1 = sE[band * 16 + g + 8];
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) S[nt][e] = p[nt][e] * (e < 2 ? e0 : e1);  // env_i P_ij
+      band_colsum(sW + band * KP, S, g, t);
+      if (t == 0) {
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int r = band * 16 + g + 8 * half;
+          if (r < k) a.lse[(n * H + hh) * k + r] = lse[half];
+        }
+      }
+      cp_async_wait<0>();
+      __syncthreads();  // V landed, both bands' partials of w visible
+      if (threadIdx.x < k) a.w[(n * H + hh) * k + threadIdx.x] = sW[threadIdx.x] + sW[KP + threadIdx.x];
+      for (int c = threadIdx.x; c < d; c += kThreads) {
+        float acc = 0.0f;
+#pragma unroll 8
+        for (int j = 0; j < KP; ++j) acc += (sW[j] + sW[KP + j]) * sV[L::op(j, c)];
+        a.out[n * C + (int64_t)hh * d + c] = acc;
+      }
+    }
+  }
+}
+
+template <int DP, bool X3>
+__global__ void __launch_bounds__(kThreads) pooled_bwd1(const PParams P) {
+  using L = Layout<DP>;
+  extern __shared__ __align__(16) float smem[];
+  float* sQ = smem;
+  float* sK = sQ + L::OP;
+  float* sV = sK + L::OP;
+  float* sGL = sV + L::OP;   // grad_logits
+  float* sB = sGL + L::KK;   // key bias row
+  float* sE = sB + KP;       // env
+  float* sU = sE + KP;       // u = V dm
+  float* sW = sU + KP;       // w
+  float* sLse = sW + KP;     // lse (+inf past k)
+  float* sDm = sLse + KP;    // dm (64)
+  int32_t* sIdx = reinterpret_cast<int32_t*>(sDm + 64);
+  const cg_pooled_attn_args& a = P.a;
+  const int k = a.k, d = a.d, H = a.h;
+  const int64_t C = (int64_t)H * d;
+  const float scale = (float)a.scale;
+  const bool vec = P.vec;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int band = warp;
+  const cg_mat mq = part_mat(a.qkv, 0, C, d, a.ld_qkv), mk = part_mat(a.qkv, 1, C, d, a.ld_qkv),
+               mv = part_mat(a.qkv, 2, C, d, a.ld_qkv);
+  const cg_mat tq = token_mat(a.dqk, 0, C, k, d, a.ld_dqk), tk = token_mat(a.dqk, 1, C, k, d, a.ld_dqk);
+  for (int64_t n = blockIdx.x; n < a.n; n += gridDim.x) {
+    __syncthreads();
+    const int32_t* tix = stage_index(sIdx, a.token_index, n, k);
+    load_tokens(sE, a.env, n, k);
+    const int kc = key_count(a, n);
+    float denv[2] = {0.0f, 0.0f};
+    for (int hh = 0; hh < H; ++hh) {
+      if (hh > 0) __syncthreads();
+      load_op_async<DP>(sQ, mq, n, hh, k, d, vec, tix);
+      load_op_async<DP>(sK, mk, n, hh, k, d, vec, tix);
+      load_op_async<DP>(sV, mv, n, hh, k, d, vec, tix);
+      cp_async_commit();
+      load_key_row(sB, a.bias, n, hh, k, H);
+      if (threadIdx.x < KP) {
+        const int i = threadIdx.x;
+        sLse[i] = i < k ? a.lse[(n * H + hh) * k + i] : INFINITY;
+        sW[i] = i < k ? a.w[(n * H + hh) * k + i] : 0.0f;
+      }
+      load_dm<DP>(sDm, a.dout, n, hh, d, C);
+      cp_async_wait<0>();
+      __syncthreads();
+      float S[4][4], p[4][4], lse[2], U[1][4];
+      zero(S);
+      zero(U);
+      band_mma<X3, 4, DP / 8>(S, CG_A_ROWS(sQ), CG_B_ROWS(sK), g, t);
+      band_mma<X3, 1, DP / 8>(U, CG_A_ROWS(sV), CG_B_VEC(sDm), g, t);
+      band_softmax(p, S, sB, 0, band, g, t, scale, kc, sLse, lse);
+      if (t == 0) {
+        sU[band * 16 + g] = U[0][0];
+        sU[band * 16 + g + 8] = U[0][2];
+      }
+      __syncthreads();  // u of every key visible
+      float uc[4][2];
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const float2 u2 = ld2(sU, nt * 8 + 2 * t);
+        uc[nt][0] = u2.x;
+        uc[nt][1] = u2.y;
+      }
+      const float er[2] = {sE[band * 16 + g], sE[band * 16 + g + 8]};
+      float ubar[2];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float s = 0.0f;
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) s += p[nt][2 * half] * uc[nt][0] + p[nt][2 * half + 1] * uc[nt][1];
+        ubar[half] = quad_sum(s);
+        denv[half] += ubar[half];
+      }
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) S[nt][e] = er[e >> 1] * p[nt][e] * (uc[nt][e & 1] - ubar[e >> 1]);  // dL
+      float O[DP / 8][4];
+      zero(O);  // dq = scale dL k
+      band_mma_reg<X3, DP / 8>(O, S, CG_B_COLS(sK), g, t);
+      store_band<DP / 8>(tq, n, hh, band, k, d, O, g, t, scale, vec);
+      put_band(sGL, S, band, g, t);
+      __syncthreads();
+      zero(O);  // dk = scale dL^T q
+      band_mma<X3, DP / 8, 4>(O, CG_A_KKT(sGL), CG_B_COLS(sQ), g, t);
+      store_band<DP / 8>(tk, n, hh, band, k, d, O, g, t, scale, vec);
+      if (warp == 0) {
+        if (a.dbias != nullptr) {
+          const float db = smem_colsum(sGL, lane);
+          if (lane < k) a.dbias[(n * k + lane) * H + hh] = db;
+        }
+      } else if (lane < k) {
+        a.wv[(n * k + lane) * H + hh] = sW[lane];
+      }
+    }
+    if (t == 0 && a.denv != nullptr) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int r = band * 16 + g + 8 * half;
+        if (r < k) a.denv[n * k + r] = denv[half];
+      }
+    }
+  }
+}
+
+template <int DP, bool X3>
+__global__ void __launch_bounds__(kThreads) pooled_bwd2(const PParams P) {
+  using L = Layout<DP>;
+  extern __shared__ __align__(16) float smem[];
+  float* sQ = smem;
+  float* sK = sQ + L::OP;
+  float* sV = sK + L::OP;
+  float* sHQ = sV + L::OP;
+  float* sHK = sHQ + L::OP;
+  float* sHV = sHK + L::OP;
+  float* sGL = sHV + L::OP;  // grad_logits dL
+  float* sDS = sGL + L::KK;  // d_scores
+  float* sB = sDS + L::KK;   // key bias row
+  float* sHB = sB + KP;      // key row of the dbias cotangent
+  float* sE = sHB + KP;      // env
+  float* sHE = sE + KP;      // denv cotangent
+  float* sU = sHE + KP;      // u = V dm
+  float* sT = sU + KP;       // t = HV dm
+  float* sW = sT + KP;       // w
+  float* sLse = sW + KP;     // lse (+inf past k)
+  float* sDu = sLse + KP;    // band partials of du: [2][KP]
+  float* sDm = sDu + 2 * KP; // dm (64)
+  int32_t* sIdx = reinterpret_cast<int32_t*>(sDm + 64);
+  const cg_pooled_attn_args& a = P.a;
+  const int k = a.k, d = a.d, H = a.h;
+  const int64_t C = (int64_t)H * d;
+  const float scale = (float)a.scale;
+  const bool vec = P.vec;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int band = warp;
+  const cg_mat mq = part_mat(a.qkv, 0, C, d, a.ld_qkv), mk = part_mat(a.qkv, 1, C, d, a.ld_qkv),
+               mv = part_mat(a.qkv, 2, C, d, a.ld_qkv);
+  const cg_mat nq = part_mat(a.hqkv, 0, C, d, a.ld_qkv), nk = part_mat(a.hqkv, 1, C, d, a.ld_qkv),
+               nv = part_mat(a.hqkv, 2, C, d, a.ld_qkv);
+  const cg_mat tq = token_mat(a.dqk, 0, C, k, d, a.ld_dqk), tk = token_mat(a.dqk, 1, C, k, d, a.ld_dqk);
+  for (int64_t n = blockIdx.x; n < a.n; n += gridDim.x) {
+    __syncthreads();
+    const int32_t* tix = stage_index(sIdx, a.token_index, n, k);
+    load_tokens(sE, a.env, n, k);
+    load_tokens(sHE, a.henv, n, k);
+    const int kc = key_count(a, n);
+    float denv[2] = {0.0f, 0.0f};
+    for (int hh = 0; hh < H; ++hh) {
+      if (hh > 0) __syncthreads();
+      load_op_async<DP>(sQ, mq, n, hh, k, d, vec, tix);
+      load_op_async<DP>(sK, mk, n, hh, k, d, vec, tix);
+      load_op_async<DP>(sHQ, nq, n, hh, k, d, vec, tix);
+      load_op_async<DP>(sHK, nk, n, hh, k, d, vec, tix);
+      cp_async_commit();
+      load_op_async<DP>(sV, mv, n, hh, k, d, vec, tix);
+      load_op_async<DP>(sHV, nv, n, hh, k, d, vec, tix);
+      cp_async_commit();
+      load_key_row(sB, a.bias, n, hh, k, H);
+      load_key_row(sHB, a.hbias, n, hh, k, H);
+      if (threadIdx.x < KP) {
+        const int i = threadIdx.x;
+        sLse[i] = i < k ? a.lse[(n * H + hh) * k + i] : INFINITY;
+        sW[i] = i < k ? a.w[(n * H + hh) * k + i] : 0.0f;
+      }
+      load_dm<DP>(sDm, a.dout, n, hh, d, C);
+      cp_async_wait<1>();
+      __syncthreads();
+      float S[4][4], A[4][4], p[4][4], lse[2];
+      zero(S);  // scores
+      zero(A);  // d_logits = scale (hq k^T + q hk^T) + hb
+      band_mma2<X3, 4, DP / 8>(S, CG_A_ROWS(sQ), CG_B_ROWS(sK), A, CG_A_ROWS(sHQ), CG_B_ROWS(sK), g, t);
+      band_mma<X3, 4, DP / 8>(A, CG_A_ROWS(sQ), CG_B_ROWS(sHK), g, t);
+      band_softmax(p, S, sB, 0, band, g, t, scale, kc, sLse, lse);
+      cp_async_wait<0>();
+      __syncthreads();  // V and HV landed
+      float U[1][4], T[1][4];
+      zero(U);
+      zero(T);
+      band_mma2<X3, 1, DP / 8>(U, CG_A_ROWS(sV), CG_B_VEC(sDm), T, CG_A_ROWS(sHV), CG_B_VEC(sDm), g, t);
+      if (t == 0) {
+        sU[band * 16 + g] = U[0][0];
+        sU[band * 16 + g + 8] = U[0][2];
+        sT[band * 16 + g] = T[0][0];
+        sT[band * 16 + g + 8] = T[0][2];
+      }
+      __syncthreads();  // u and t of every key visible
+      float uc[4][2], tc[4][2];
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const float2 u2 = ld2(sU, nt * 8 + 2 * t), t2 = ld2(sT, nt * 8 + 2 * t), b2 = ld2(sHB, nt * 8 + 2 * t);
+        uc[nt][0] = u2.x;
+        uc[nt][1] = u2.y;
+        tc[nt][0] = t2.x;
+        tc[nt][1] = t2.y;
+        A[nt][0] = scale * A[nt][0] + b2.x;
+        A[nt][1] = scale * A[nt][1] + b2.y;
+        A[nt][2] = scale * A[nt][2] + b2.x;
+        A[nt][3] = scale * A[nt][3] + b2.y;
+      }
+      const float er[2] = {sE[band * 16 + g], sE[band * 16 + g + 8]};
+      const float hr[2] = {sHE[band * 16 + g], sHE[band * 16 + g + 8]};
+      float ubar[2], abar[2];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float su = 0.0f, sa = 0.0f;
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+          for (int e1 = 0; e1 < 2; ++e1) {
+            su += p[nt][2 * half + e1] * uc[nt][e1];
+            sa += p[nt][2 * half + e1] * A[nt][2 * half + e1];
+          }
+        ubar[half] = quad_sum(su);
+        abar[half] = quad_sum(sa);
+      }
+      // dL (into S), X = P (env (A - abar) + henv), G_P (into A), and the
+      // envelope row sums de_i = sum_j P ((u - ubar) A + t)
+      float X[4][4], dep[2] = {0.0f, 0.0f};
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = e >> 1;
+          const float u = uc[nt][e & 1], tt = tc[nt][e & 1], pv = p[nt][e], av = A[nt][e];
+          const float du = u - ubar[r];
+          S[nt][e] = er[r] * pv * du;
+          X[nt][e] = pv * (er[r] * (av - abar[r]) + hr[r]);
+          dep[r] += pv * (du * av + tt);
+          A[nt][e] = er[r] * (du * av + tt - abar[r] * u) + hr[r] * u;
+        }
+      float gbar[2];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float sg = 0.0f;
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+          for (int e1 = 0; e1 < 2; ++e1) sg += p[nt][2 * half + e1] * A[nt][2 * half + e1];
+        gbar[half] = quad_sum(sg);
+        denv[half] += quad_sum(dep[half]);
+      }
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) A[nt][e] = p[nt][e] * (A[nt][e] - gbar[e >> 1]);  // d_scores
+      band_colsum(sDu + band * KP, X, g, t);
+      float O[DP / 8][4];
+      zero(O);  // dq = scale (dL hk + d_scores k)
+      band_mma_reg<X3, DP / 8>(O, S, CG_B_COLS(sHK), g, t);
+      band_mma_reg<X3, DP / 8>(O, A, CG_B_COLS(sK), g, t);
+      store_band<DP / 8>(tq, n, hh, band, k, d, O, g, t, scale, vec);
+      put_band(sGL, S, band, g, t);
+      put_band(sDS, A, band, g, t);
+      __syncthreads();
+      zero(O);  // dk = scale (dL^T hq + d_scores^T q)
+      band_mma<X3, DP / 8, 4>(O, CG_A_KKT(sGL), CG_B_COLS(sHQ), g, t);
+      band_mma<X3, DP / 8, 4>(O, CG_A_KKT(sDS), CG_B_COLS(sQ), g, t);
+      store_band<DP / 8>(tk, n, hh, band, k, d, O, g, t, scale, vec);
+      if (warp == 0) {
+        if (a.dbias != nullptr) {
+          const float db = smem_colsum(sDS, lane);
+          if (lane < k) a.dbias[(n * k + lane) * H + hh] = db;
+        }
+      } else if (lane < k) {
+        a.wv[(n * k + lane) * H + hh] = sDu[lane] + sDu[KP + lane];
+      }
+      // d(dm)_c = sum_j du_j v_jc + w_j hv_jc
+      for (int c = threadIdx.x; c < d; c += kThreads) {
+        float acc = 0.0f;
+#pragma unroll 8
+        for (int j = 0; j < KP; ++j)
+          acc += (sDu[j] + sDu[KP + j]) * sV[L::op(j, c)] + sW[j] * sHV[L::op(j, c)];
+        a.ddout[n * C + (int64_t)hh * d + c] = acc;
+      }
+    }
+    if (t == 0 && a.denv != nullptr) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int r = band * 16 + g + 8 * half;
+        if (r < k) a.denv[n * k + r] = denv[half];
+      }
+    }
+  }
+}
+
+#undef CG_B_VEC
+#undef CG_A_ROWS
+#undef CG_B_ROWS
+#undef CG_B_COLS
+#undef CG_A_KKT
+
+// shared memory per CTA (bytes); which: 0 fwd, 1 bwd1, 2 bwd2
+template <int DP>
+inline int smem_bytes(int which) {
+  using L = Layout<DP>;
+  switch (which) {
+    case 0: return (3 * L::OP + 4 * KP + KP) * 4;
+    case 1: return (3 * L::OP + L::KK + 5 * KP + 64 + KP) * 4;
+    default: return (6 * L::OP + 2 * L::KK + 10 * KP + 64 + KP) * 4;
+  }
+}
+
+// A persistent grid of as many CTAs as fit per SM, atoms strided over it.
+template <int DP, bool X3>
+int launch_dp(int which, const PParams& P, cudaStream_t stream) {
+  const int smem = smem_bytes<DP>(which);
+  void (*kernel)(const PParams) =
+      which == 0 ? pooled_fwd<DP, X3> : which == 1 ? pooled_bwd1<DP, X3> : pooled_bwd2<DP, X3>;
+  CG_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  int per_sm = (228 * 1024) / (smem + 1024);
+  if (per_sm < 1) per_sm = 1;
+  if (per_sm > 16) per_sm = 16;
+  const int64_t cap = (int64_t)sm_count() * per_sm;
+  const int grid = (int)(P.a.n < cap ? P.a.n : cap);
+  kernel<<<grid, kThreads, smem, stream>>>(P);
+  CG_LAUNCHED("pooled_attn");
+  return kOk;
+}
+
+template <bool X3>
+int launch_prec(int which, const PParams& P, int dp, cudaStream_t stream) {
+  switch (dp) {
+    case 16: return launch_dp<16, X3>(which, P, stream);
+    case 32: return launch_dp<32, X3>(which, P, stream);
+    case 64: return launch_dp<64, X3>(which, P, stream);
+  }
+  set_error("pooled_attn: no variant for padded head dim %d", dp);
+  return kUnsupported;
+}
+
+int launch_fp32(int which, const PParams& P, int dp, cudaStream_t stream);  // pooled_attn.cu
+int launch_tf32(int which, const PParams& P, int dp, cudaStream_t stream);  // pooled_attn_tf32.cu
+
+}  // namespace pooled
+}  // namespace cg

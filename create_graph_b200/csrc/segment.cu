@@ -69,6 +69,49 @@ __global__ void segment_sum_kernel(const float* __restrict__ src, int64_t ld_src
   }
 }
 
+// out[r, h*d + c] (+)= sum over e in [row_ptr[r], row_ptr[r+1]) of
+// w[s*heads + h] * src[(s / group)*ld_src + h*d + c], s = perm ? perm[e] : e,
+// in increasing e: one warp per output row, lanes over 4-column chunks (vec:
+// d a multiple of 4, so a chunk never straddles two heads).
+__global__ void segment_sum_scaled_kernel(const float* __restrict__ w, const float* __restrict__ src,
+                                          int64_t ld_src, int group, int heads, int d,
+                                          const int32_t* __restrict__ row_ptr,
+                                          const int32_t* __restrict__ perm, int64_t n_rows,
+                                          float* __restrict__ out, int64_t ld_out, bool accumulate,
+                                          bool vec) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int cols = heads * d;
+  for (int64_t r = warp; r < n_rows; r += warps) {
+    const int32_t e0 = row_ptr[r], e1 = row_ptr[r + 1];
+    float* dst = out + r * ld_out;
+    if (vec) {
+      for (int c = lane * 4; c < cols; c += 128) {
+        const int hh = c / d;
+        float4 acc = accumulate ? *reinterpret_cast<const float4*>(dst + c) : make_float4(0, 0, 0, 0);
+        for (int32_t e = e0; e < e1; ++e) {
+          const int32_t s = perm ? perm[e] : e;
+          const float wt = __ldg(w + (int64_t)s * heads + hh);
+          const float4 v = __ldg(reinterpret_cast<const float4*>(src + (int64_t)(s / group) * ld_src + c));
+          acc.x += wt * v.x; acc.y += wt * v.y; acc.z += wt * v.z; acc.w += wt * v.w;
+        }
+        *reinterpret_cast<float4*>(dst + c) = acc;
+      }
+    } else {
+      for (int c = lane; c < cols; c += 32) {
+        const int hh = c / d;
+        float acc = accumulate ? dst[c] : 0.0f;
+        for (int32_t e = e0; e < e1; ++e) {
+          const int32_t s = perm ? perm[e] : e;
+          acc += w[(int64_t)s * heads + hh] * src[(int64_t)(s / group) * ld_src + c];
+        }
+        dst[c] = acc;
+      }
+    }
+  }
+}
+
 // Column sums in two fixed-order passes: block (cb, chunk) sums rows
 // [chunk*rows_per, (chunk+1)*rows_per) of 32 columns into partial[chunk, :];
 // then one thread per column adds the partials in chunk order.
@@ -166,6 +209,22 @@ int cg_segment_sum(const float* src, int64_t ld_src, const int32_t* row_ptr, con
   seg::segment_sum_kernel<<<seg::grid_for_warps(n_rows), 256, 0, as_stream(stream)>>>(
       src, ld_src, row_ptr, perm, n_rows, cols, out, ld_out, accumulate != 0, vec);
   CG_LAUNCHED("segment_sum");
+  return kOk;
+}
+
+int cg_segment_sum_scaled(const float* w, const float* src, int64_t ld_src, int64_t group, int32_t heads,
+                          int32_t d, const int32_t* row_ptr, const int32_t* perm, int64_t n_rows, float* out,
+                          int64_t ld_out, int accumulate, void* stream) {
+  using namespace cg;
+  CG_REQUIRE(n_rows >= 0 && heads >= 0 && d >= 0, "segment_sum_scaled: negative size");
+  if (n_rows == 0 || heads == 0 || d == 0) return kOk;
+  CG_REQUIRE(w && src && row_ptr && out, "segment_sum_scaled: null pointer");
+  CG_REQUIRE(group >= 1 && group <= (1 << 30), "segment_sum_scaled: group = %lld outside [1, 2^30]",
+             (long long)group);
+  const bool vec = d % 4 == 0 && ld_src % 4 == 0 && ld_out % 4 == 0 && seg::aligned16(src) && seg::aligned16(out);
+  seg::segment_sum_scaled_kernel<<<seg::grid_for_warps(n_rows), 256, 0, as_stream(stream)>>>(
+      w, src, ld_src, (int)group, heads, d, row_ptr, perm, n_rows, out, ld_out, accumulate != 0, vec);
+  CG_LAUNCHED("segment_sum_scaled");
   return kOk;
 }
 

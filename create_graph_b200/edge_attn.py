@@ -356,3 +356,95 @@ def token_attention_backward2(qkv, bias, lse, g, h_qkv, h_bias, index, counts, k
     (a.dgrad_out,) = _token_mats(dg, n, k, heads, d, 1)
     _run("cg_edge_attn_bwd2", a, qkv.device)
     return dtok, dbias, dg
+
+
+# ---------------------------------------------------------------------------
+# Envelope-pooled token attention: token attention followed by the
+# envelope-weighted sum over each atom's tokens, as one op
+# (cg_pooled_attn_fwd / bwd1 / bwd2). The v gradient of token (n, j) is rank
+# one, wv[n*k + j, h] * dout[n, h]; callers reduce it with
+# cg_segment_sum_scaled.
+# ---------------------------------------------------------------------------
+
+
+def _pooled_args(qkv, bias, env, index, counts, k, heads, scale, precision):
+    native.require_cuda(qkv, bias, env, counts, index)
+    if qkv.dtype != torch.float32 or bias.dtype != torch.float32 or env.dtype != torch.float32:
+        raise NativeError("pooled attention: qkv, bias and env must be float32")
+    if counts.dtype != torch.int32 or index.dtype != torch.int32:
+        raise NativeError("pooled attention: counts and index must be int32")
+    n = counts.shape[0]
+    d = qkv.shape[1] // (3 * heads)
+    if (qkv.shape[1] != 3 * heads * d or index.numel() != n * k or tuple(bias.shape) != (n * k, heads)
+            or env.numel() != n * k or qkv.stride(1) != 1):
+        raise NativeError(
+            f"pooled attention: qkv {tuple(qkv.shape)}, bias {tuple(bias.shape)}, env {tuple(env.shape)}, "
+            f"index {index.numel()}, n {n}, k {k}, heads {heads}"
+        )
+    a = native.PooledAttnArgs()
+    a.n, a.h, a.k, a.d = n, heads, k, d
+    a.precision = native.attn_precision(precision)
+    a.scale = float(scale)
+    a.token_index = index.data_ptr()
+    a.key_count = counts.data_ptr()
+    a.qkv = qkv.data_ptr()
+    a.ld_qkv = qkv.stride(0)
+    a.bias = bias.data_ptr()
+    a.env = env.data_ptr()
+    return a, n, d
+
+
+def pooled_attention_forward(qkv, bias, env, index, counts, k, heads, scale, precision="fp32"):
+    """(out (n, h*d), lse (n, h, k), w (n, h, k)) with w_j = sum_i env_i P_ij."""
+    qkv, bias, env = qkv.contiguous(), bias.contiguous(), env.contiguous()
+    a, n, d = _pooled_args(qkv, bias, env, index, counts, k, heads, scale, precision)
+    out = torch.empty(n, heads * d, device=qkv.device)
+    lse = torch.empty(n, heads, k, device=qkv.device)
+    w = torch.empty(n, heads, k, device=qkv.device)
+    a.out, a.lse, a.w = out.data_ptr(), lse.data_ptr(), w.data_ptr()
+    _run("cg_pooled_attn_fwd", a, qkv.device)
+    return out, lse, w
+
+
+def pooled_attention_backward1(qkv, bias, env, lse, w, dout, index, counts, k, heads, scale, precision="fp32"):
+    """(dqk (n*k, 2*h*d) per-token [dq | dk], wv (n*k, h), dbias (n*k, h), denv (n, k))."""
+    qkv, bias, env, dout = qkv.contiguous(), bias.contiguous(), env.contiguous(), dout.contiguous()
+    a, n, d = _pooled_args(qkv, bias, env, index, counts, k, heads, scale, precision)
+    dqk = torch.empty(n * k, 2 * heads * d, device=qkv.device)
+    wv = torch.empty(n * k, heads, device=qkv.device)
+    dbias = torch.empty(n * k, heads, device=qkv.device)
+    denv = torch.empty(n, k, device=qkv.device)
+    a.lse, a.w, a.dout = lse.data_ptr(), w.data_ptr(), dout.data_ptr()
+    a.dqk, a.ld_dqk, a.wv = dqk.data_ptr(), dqk.stride(0), wv.data_ptr()
+    a.dbias, a.denv = dbias.data_ptr(), denv.data_ptr()
+    _run("cg_pooled_attn_bwd1", a, qkv.device)
+    return dqk, wv, dbias, denv
+
+
+def pooled_attention_backward2(qkv, bias, env, lse, w, dout, h_qkv, h_bias, h_env, index, counts, k, heads, scale,
+                               precision="fp32"):
+    """Second derivative: (dqk, wv, dbias, denv, ddout) of <h_qkv, d_qkv> +
+    <h_bias, dbias> + <h_env, denv> (h_bias, h_env may be None: zero)."""
+    qkv, bias, env, dout, h_qkv = (t.contiguous() for t in (qkv, bias, env, dout, h_qkv))
+    a, n, d = _pooled_args(qkv, bias, env, index, counts, k, heads, scale, precision)
+    if h_qkv.shape != qkv.shape or h_qkv.stride(0) != qkv.stride(0):
+        raise NativeError(f"pooled attention: h_qkv {tuple(h_qkv.shape)} must match qkv {tuple(qkv.shape)}")
+    keep = []
+    if h_bias is not None:
+        h_bias = h_bias.contiguous()
+        keep.append(h_bias)
+        a.hbias = h_bias.data_ptr()
+    if h_env is not None:
+        h_env = h_env.contiguous()
+        keep.append(h_env)
+        a.henv = h_env.data_ptr()
+    dqk = torch.empty(n * k, 2 * heads * d, device=qkv.device)
+    wv = torch.empty(n * k, heads, device=qkv.device)
+    dbias = torch.empty(n * k, heads, device=qkv.device)
+    denv = torch.empty(n, k, device=qkv.device)
+    ddout = torch.empty(n, heads * d, device=qkv.device)
+    a.lse, a.w, a.dout, a.hqkv = lse.data_ptr(), w.data_ptr(), dout.data_ptr(), h_qkv.data_ptr()
+    a.dqk, a.ld_dqk, a.wv = dqk.data_ptr(), dqk.stride(0), wv.data_ptr()
+    a.dbias, a.denv, a.ddout = dbias.data_ptr(), denv.data_ptr(), ddout.data_ptr()
+    _run("cg_pooled_attn_bwd2", a, qkv.device)
+    return dqk, wv, dbias, denv, ddout

@@ -85,11 +85,10 @@ class Block(nn.Module):
         self.ffn2 = cgnn.Linear(s.ffn, c)
 
     def forward(self, h: Tensor, rbf: Tensor, env: Tensor, graph: cgnn.NeighborGraph) -> Tensor:
-        n = h.shape[0]
         bias = self.rbf_bias(rbf)
-        o = cgnn.TokenAttention.apply(self.qkv(self.norm1(h)), bias, graph, self.heads, self.scale,
-                                      self.precision)
-        m = cgnn.Pool.apply(o, env.view(n, graph.k))
+        # attention among the atom's edge tokens, pooled by the envelope, one fused op
+        m = cgnn.PooledTokenAttention.apply(self.qkv(self.norm1(h)), bias, env, graph, self.heads, self.scale,
+                                            self.precision)
         h = h + self.out(m)
         return h + self.ffn2(self.ffn1(self.norm2(h)))
 

@@ -102,6 +102,36 @@ class GemmArgs(ctypes.Structure):
     ]
 
 
+class PooledAttnArgs(ctypes.Structure):
+    _fields_ = [
+        ("n", i64),
+        ("h", i32),
+        ("k", i32),
+        ("d", i32),
+        ("precision", i32),
+        ("scale", ctypes.c_double),
+        ("token_index", vp),
+        ("key_count", vp),
+        ("qkv", vp),
+        ("hqkv", vp),
+        ("ld_qkv", i64),
+        ("bias", vp),
+        ("env", vp),
+        ("lse", vp),
+        ("w", vp),
+        ("out", vp),
+        ("dout", vp),
+        ("hbias", vp),
+        ("henv", vp),
+        ("dqk", vp),
+        ("ld_dqk", i64),
+        ("wv", vp),
+        ("dbias", vp),
+        ("denv", vp),
+        ("ddout", vp),
+    ]
+
+
 class GeomArgs(ctypes.Structure):
     _fields_ = [
         ("pos", vp),
@@ -135,6 +165,10 @@ _SIGNATURES = {
     "cg_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
     "cg_gather_rows": (_I, [vp, i64, vp, i64, i64, vp, i64, vp]),
     "cg_segment_sum": (_I, [vp, i64, vp, vp, i64, i64, vp, i64, _I, vp]),
+    "cg_segment_sum_scaled": (_I, [vp, vp, i64, i64, i32, i32, vp, vp, i64, vp, i64, _I, vp]),
+    "cg_pooled_attn_fwd": (_I, [ctypes.POINTER(PooledAttnArgs), vp]),
+    "cg_pooled_attn_bwd1": (_I, [ctypes.POINTER(PooledAttnArgs), vp]),
+    "cg_pooled_attn_bwd2": (_I, [ctypes.POINTER(PooledAttnArgs), vp]),
     "cg_colsum_scratch_bytes": (i64, [i64, i64]),
     "cg_colsum": (_I, [vp, i64, i64, i64, vp, _I, vp, vp]),
     "cg_coldot_scratch_bytes": (i64, [i64, i64]),

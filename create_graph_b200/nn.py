@@ -34,7 +34,14 @@ from torch import Tensor, nn
 
 from create_graph_b200 import native
 from create_graph_b200.compile_config import engine_will_execute, gradient_edge
-from create_graph_b200.edge_attn import token_attention_backward1, token_attention_backward2, token_attention_forward1
+from create_graph_b200.edge_attn import (
+    pooled_attention_backward1,
+    pooled_attention_backward2,
+    pooled_attention_forward,
+    token_attention_backward1,
+    token_attention_backward2,
+    token_attention_forward1,
+)
 from create_graph_b200.errors import NativeError
 from create_graph_b200.gemm import ACT_SILU, gemm
 
@@ -578,6 +585,71 @@ class TokenAttentionGrad(_Fused):
         dtok, dbias, dg = token_attention_backward2(qkv, bias, lse, g, h_qkv, h_bias, graph.tokens.index,
                                                     graph.counts, graph.k, heads, scale, precision)
         return segment_sum_raw(dtok, graph.tokens), dbias, None, dg, None
+
+
+def _pooled_qkv_grad(dqk: Tensor, wv: Tensor, dm: Tensor, graph, heads: int) -> Tensor:
+    """Per-atom q/k/v gradient (n_atoms, 3C) of the pooled attention: the
+    per-token [dq | dk] rows and the rank-one v rows wv[token, h] * dm[atom of
+    token, h], each reduced to atoms in a fixed order."""
+    csr = graph.tokens
+    C = dm.shape[1]
+    d = C // heads
+    out = torch.empty(csr.rows, 3 * C, device=dm.device)
+    native.call("cg_segment_sum", dqk.data_ptr(), dqk.stride(0), csr.row_ptr.data_ptr(), csr.perm.data_ptr(),
+                csr.rows, 2 * C, out.data_ptr(), out.stride(0), 0, _stream())
+    dm = _f32(dm, "segment_sum_scaled")
+    native.call("cg_segment_sum_scaled", wv.data_ptr(), dm.data_ptr(), dm.stride(0), graph.k, heads, d,
+                csr.row_ptr.data_ptr(), csr.perm.data_ptr(), csr.rows, out.data_ptr() + 2 * C * out.element_size(),
+                out.stride(0), 0, _stream())
+    return out
+
+
+class PooledTokenAttention(_Fused):
+    """m[n] = sum_i env[n*k + i] * (attention output of token (n, i)): the
+    TokenAttention above followed by Pool, as one fused op whose kernels never
+    form the (n, k, h*d) token outputs. Returns (n, h*d), heads concatenated.
+    ``precision`` ("fp32" or "tf32") selects the product precision."""
+
+    @staticmethod
+    def forward(ctx, qkv, bias, env, graph, heads, scale, precision="fp32"):
+        meta = (graph, heads, scale, precision)
+        out, lse, w = pooled_attention_forward(qkv, bias, env, graph.tokens.index, graph.counts, graph.k, heads,
+                                               scale, precision)
+        ctx.save_for_backward(qkv, bias, env, lse, w)
+        ctx.meta = meta
+        return out
+
+    @staticmethod
+    def backward(ctx, dm):
+        qkv, bias, env, lse, w = ctx.saved_tensors
+        d_qkv, dbias, denv = PooledTokenAttentionGrad.apply(qkv, bias, env, lse, w, dm, ctx.meta)
+        return d_qkv, dbias, denv, None, None, None, None
+
+
+class PooledTokenAttentionGrad(_Fused):
+    """backward1 of PooledTokenAttention (per-atom q/k/v, bias and envelope
+    gradients); its backward is the backward2 kernel (lse and w are
+    statistics, not differentiated)."""
+
+    @staticmethod
+    def forward(ctx, qkv, bias, env, lse, w, dm, meta):
+        graph, heads, scale, precision = meta
+        dqk, wv, dbias, denv = pooled_attention_backward1(qkv, bias, env, lse, w, dm, graph.tokens.index,
+                                                          graph.counts, graph.k, heads, scale, precision)
+        ctx.save_for_backward(qkv, bias, env, lse, w, dm)
+        ctx.meta = meta
+        return _pooled_qkv_grad(dqk, wv, dm, graph, heads), dbias, denv.view_as(env)
+
+    @staticmethod
+    def backward(ctx, h_qkv, h_bias, h_env):
+        qkv, bias, env, lse, w, dm = ctx.saved_tensors
+        graph, heads, scale, precision = ctx.meta
+        if h_qkv is None:
+            h_qkv = torch.zeros_like(qkv)
+        dqk, wv, dbias, denv, ddm = pooled_attention_backward2(
+            qkv, bias, env, lse, w, dm, h_qkv, h_bias, h_env, graph.tokens.index, graph.counts, graph.k, heads,
+            scale, precision)
+        return _pooled_qkv_grad(dqk, wv, dm, graph, heads), dbias, denv.view_as(env), None, None, ddm, None
 
 
 # ---------------------------------------------------------------------------

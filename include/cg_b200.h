@@ -113,6 +113,58 @@ int cg_edge_attn_bwd2(const cg_edge_attn_args* a, void* stream);
 int64_t cg_edge_attn_scratch_bytes(const cg_edge_attn_args* a);
 
 /* ------------------------------------------------------------------------
+ * Envelope-pooled token attention of the energy network: for atom n and
+ * head h, over the atom's k <= 32 edge tokens (token (n, r) reads row
+ * token_index[n*k + r] of qkv; < 0 reads zeros),
+ *   L_ij = scale q_i.k_j + bias[n*k + j, h]   (keys j >= key_count[n] masked)
+ *   P    = softmax_j(L)                        (rows without a key: zeros)
+ *   w_j  = sum_i env[n, i] P_ij,   out[n, h] = sum_j w_j v_j.
+ * This is the reference model's attention over neighbour tokens followed by
+ * the envelope-weighted sum over tokens (the masked edge attention of
+ * kernels/edge_attn/ops.py:26-34, 64-68, then a pooling), fused so that the
+ * (n, k, h*d) token outputs and their cotangents never exist. No counterpart
+ * entry point in the reference (its model composes the two ops).
+ * Backward1 (given dout = dm): u_j = v_j.dm, ubar_i = sum_j P_ij u_j,
+ *   dL_ij = env_i P_ij (u_j - ubar_i), dq_i = scale sum_j dL_ij k_j,
+ *   dk_j = scale sum_i dL_ij q_i, dbias_j = sum_i dL_ij, dv_j = w_j dm,
+ *   denv_i = sum_h ubar_i.
+ * Backward2: the gradients of <hq,dq> + <hk,dk> + <hv,dv> + <hb,dbias> +
+ * <he,denv> w.r.t. qkv, bias, env and dm (cotangents hq, hk, hv read through
+ * token_index from hqkv). dv of a token is rank one, wv[n*k + j, h] * dm[n, h]:
+ * the kernels write the weight wv and cg_segment_sum_scaled reduces it to
+ * atoms; dq and dk leave per token in dqk for cg_segment_sum.
+ * ---------------------------------------------------------------------- */
+typedef struct cg_pooled_attn_args {
+  int64_t n;                  /* atoms */
+  int32_t h, k, d;            /* heads, tokens per atom (<= 32), head dim (<= 64) */
+  int32_t precision;          /* CG_ATTN_FP32 or CG_ATTN_TF32 */
+  double scale;
+  const int32_t* token_index; /* (n*k,) row of qkv / hqkv of token (n, r), < 0: zero row */
+  const int32_t* key_count;   /* (n,) keys j >= key_count[n] are masked */
+  const float* qkv;           /* (rows, ld_qkv): [q | k | v], heads contiguous, h*d each */
+  const float* hqkv;          /* bwd2: cotangent of the q/k/v gradient, same layout */
+  int64_t ld_qkv;
+  const float* bias;          /* (n*k, h) additive bias of key (n, j); NULL = none */
+  const float* env;           /* (n, k) pooling weight of query token (n, i) */
+  float* lse;                 /* (n, h, k): written by fwd, read by bwd1 / bwd2 */
+  float* w;                   /* (n, h, k): w_j, written by fwd, read by bwd1 / bwd2 */
+  float* out;                 /* fwd: (n, h*d) */
+  const float* dout;          /* bwd1 / bwd2: (n, h*d) cotangent of out */
+  const float* hbias;         /* bwd2: (n*k, h) cotangent of dbias; NULL = 0 */
+  const float* henv;          /* bwd2: (n, k) cotangent of denv; NULL = 0 */
+  float* dqk;                 /* bwd1 / bwd2: (n*k, ld_dqk) per-token [dq | dk], 2*h*d columns */
+  int64_t ld_dqk;
+  float* wv;                  /* bwd1 / bwd2: (n*k, h) v gradient of token j is wv[j, h] * dout[n, h] */
+  float* dbias;               /* bwd1 / bwd2: (n*k, h); NULL = skip */
+  float* denv;                /* bwd1 / bwd2: (n, k), summed over heads; NULL = skip */
+  float* ddout;               /* bwd2: (n, h*d) gradient w.r.t. dout */
+} cg_pooled_attn_args;
+
+int cg_pooled_attn_fwd(const cg_pooled_attn_args* a, void* stream);
+int cg_pooled_attn_bwd1(const cg_pooled_attn_args* a, void* stream);
+int cg_pooled_attn_bwd2(const cg_pooled_attn_args* a, void* stream);
+
+/* ------------------------------------------------------------------------
  * Dense projections on the tcgen05 tensor cores (kind::tf32: fp32 operands
  * rounded to tf32, fp32 accumulation in TMEM):
  *   C[m, n] = epi( alpha * sum_k A(m, k) B(n, k) )
@@ -186,6 +238,14 @@ int cg_gather_rows(const float* src, int64_t ld_src, const int32_t* index, int64
 int cg_segment_sum(const float* src, int64_t ld_src, const int32_t* row_ptr, const int32_t* perm,
                    int64_t n_rows, int64_t cols, float* out, int64_t ld_out, int accumulate,
                    void* stream);
+/* The segment sum of rank-one rows: for s = perm ? perm[e] : e,
+ * out[r, h*d + c] (+)= sum_{e in [row_ptr[r], row_ptr[r+1])} w[s*heads + h] * src[(s / group)*ld_src + h*d + c],
+ * in increasing e (c < d, h < heads). Reduces the per-token v gradient
+ * w[token, h] * dm[atom of token, h] of the pooled attention to atoms without
+ * materialising it; no reference counterpart. */
+int cg_segment_sum_scaled(const float* w, const float* src, int64_t ld_src, int64_t group, int32_t heads,
+                          int32_t d, const int32_t* row_ptr, const int32_t* perm, int64_t n_rows, float* out,
+                          int64_t ld_out, int accumulate, void* stream);
 /* out[c] (+)= sum_r src[r*ld + c], two fixed-order passes through `scratch`
  * (cg_colsum_scratch_bytes bytes); the bias gradients of nn.Linear. */
 int64_t cg_colsum_scratch_bytes(int64_t rows, int64_t cols);

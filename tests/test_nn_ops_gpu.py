@@ -16,6 +16,7 @@ import pytest
 import torch
 import torch.nn.functional as F
 
+from create_graph_b200 import native
 from create_graph_b200 import nn as cgnn
 from tests.twice import twice_errors
 
@@ -151,3 +152,65 @@ def test_token_attention(precision, tol):
     mine = lambda q, b: cgnn.TokenAttention.apply(q, b, graph, heads, 0.25, precision)  # noqa: E731
     ref = lambda q, b: ref_token_attention(q, b, graph.tokens.index, graph.counts, heads, 0.25)  # noqa: E731
     check(twice_errors(mine, ref, [qkv, bias]), tol)
+
+
+@pytest.mark.parametrize("precision,tol", [("fp32", F32_TOL), ("tf32", 5e-3)])
+@pytest.mark.parametrize("heads,d", [(4, 16), (2, 64), (3, 20)])
+def test_pooled_token_attention(precision, tol, heads, d):
+    """Attention among each atom's tokens followed by the envelope-weighted sum
+    over tokens, fused (cg_pooled_attn_*), against the torch composition of the
+    two: output, first and second derivatives w.r.t. qkv, bias and env; atoms
+    with no neighbour, padded token slots and a head dim below the padded
+    width included."""
+    n, k = 40, 12
+    pos, graph = neighbor_case(n=n, k=k)
+    g = torch.Generator().manual_seed(16)
+    qkv = torch.randn(n, 3 * heads * d, generator=g).cuda()
+    bias = torch.randn(n * k, heads, generator=g).cuda()
+    env = torch.rand(n * k, generator=g).cuda()
+    mine = lambda q, b, e: cgnn.PooledTokenAttention.apply(q, b, e, graph, heads, 0.25, precision)  # noqa: E731
+
+    def ref(q, b, e):
+        o = ref_token_attention(q, b, graph.tokens.index, graph.counts, heads, 0.25)
+        return (e.view(n, k, 1) * o).sum(1)
+
+    check(twice_errors(mine, ref, [qkv, bias, env]), tol)
+
+
+def test_pooled_token_attention_deterministic():
+    n, k, heads, d = 40, 12, 2, 64
+    pos, graph = neighbor_case(n=n, k=k)
+    g = torch.Generator().manual_seed(17)
+    qkv = torch.randn(n, 3 * heads * d, generator=g).cuda().requires_grad_(True)
+    bias = torch.randn(n * k, heads, generator=g).cuda().requires_grad_(True)
+    env = torch.rand(n * k, generator=g).cuda().requires_grad_(True)
+
+    def run():
+        out = cgnn.PooledTokenAttention.apply(qkv, bias, env, graph, heads, 0.125, "tf32")
+        gq, gb, ge = torch.autograd.grad(out.square().sum(), [qkv, bias, env], create_graph=True)
+        return [out, gq, gb, ge, *torch.autograd.grad(gq.sum() + gb.square().sum() + ge.sum(), [qkv, bias, env])]
+
+    first, second = run(), run()
+    assert all(torch.equal(a, b) for a, b in zip(first, second))
+
+
+def test_segment_sum_scaled():
+    """out[a, h*d + c] = sum over tokens t of atom a of w[t, h] * src[t // k, h*d + c]."""
+    n, k, heads, d = 30, 7, 3, 12
+    pos, graph = neighbor_case(n=n, k=k)
+    g = torch.Generator().manual_seed(18)
+    w = torch.randn(n * k, heads, generator=g).cuda()
+    src = torch.randn(n, heads * d, generator=g).cuda()
+    csr = graph.tokens
+    out = torch.full((n, heads * d + 5), 7.0, device="cuda")
+    native.call("cg_segment_sum_scaled", w.data_ptr(), src.data_ptr(), src.stride(0), k, heads, d,
+                csr.row_ptr.data_ptr(), csr.perm.data_ptr(), n, out.data_ptr(), out.stride(0), 0,
+                native.stream_ptr())
+    idx = csr.index.long().cpu()
+    want = torch.zeros(n, heads, d, dtype=torch.float64)
+    rows = (w.double().cpu()[:, :, None] * src.double().cpu().view(n, 1, heads, d).repeat_interleave(k, 0)[:, 0])
+    for t in range(n * k):
+        if idx[t] >= 0:
+            want[idx[t]] += rows[t]
+    assert torch.allclose(out[:, : heads * d].double().cpu(), want.view(n, -1), rtol=1e-5, atol=1e-5)
+    assert torch.all(out[:, heads * d :] == 7.0)
