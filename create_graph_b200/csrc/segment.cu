@@ -69,6 +69,65 @@ __global__ void segment_sum_kernel(const float* __restrict__ src, int64_t ld_src
   }
 }
 
+// 16-byte variant of segment_sum_kernel with one warp per (row, block of 128
+// columns): a lane owns one float4 column chunk and walks the segment in
+// increasing e, loads unrolled ahead of the ordered adds; rows x blocks warps
+// keep enough loads in flight for HBM.
+__global__ void segment_sum_blocks_kernel(const float* __restrict__ src, int64_t ld_src,
+                                          const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ perm,
+                                          int64_t n_rows, int cols4, float* __restrict__ out, int64_t ld_out,
+                                          bool accumulate) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int nblk = (cols4 + 31) / 32;
+  for (int64_t task = warp; task < n_rows * nblk; task += warps) {
+    const int64_t r = task / nblk;
+    const int c = (int)(task % nblk) * 32 + lane;
+    if (c >= cols4) continue;
+    const int32_t e0 = row_ptr[r], e1 = row_ptr[r + 1];
+    float4* dst = reinterpret_cast<float4*>(out + r * ld_out) + c;
+    float4 acc = accumulate ? *dst : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll 8
+    for (int32_t e = e0; e < e1; ++e) {
+      const int64_t s = perm ? perm[e] : e;
+      const float4 v = __ldg(reinterpret_cast<const float4*>(src + s * ld_src) + c);
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    *dst = acc;
+  }
+}
+
+// The rank-one version, the same way (d a multiple of 4).
+__global__ void segment_sum_scaled_blocks_kernel(const float* __restrict__ w, const float* __restrict__ src,
+                                                 int64_t ld_src, int group, int heads, int d,
+                                                 const int32_t* __restrict__ row_ptr,
+                                                 const int32_t* __restrict__ perm, int64_t n_rows,
+                                                 float* __restrict__ out, int64_t ld_out, bool accumulate) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int cols4 = heads * d / 4;
+  const int nblk = (cols4 + 31) / 32;
+  for (int64_t task = warp; task < n_rows * nblk; task += warps) {
+    const int64_t r = task / nblk;
+    const int c = (int)(task % nblk) * 32 + lane;
+    if (c >= cols4) continue;
+    const int hh = 4 * c / d;
+    const int32_t e0 = row_ptr[r], e1 = row_ptr[r + 1];
+    float4* dst = reinterpret_cast<float4*>(out + r * ld_out) + c;
+    float4 acc = accumulate ? *dst : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll 8
+    for (int32_t e = e0; e < e1; ++e) {
+      const int32_t s = perm ? perm[e] : e;
+      const float wt = __ldg(w + (int64_t)s * heads + hh);
+      const float4 v = __ldg(reinterpret_cast<const float4*>(src + (int64_t)(s / group) * ld_src) + c);
+      acc.x += wt * v.x; acc.y += wt * v.y; acc.z += wt * v.z; acc.w += wt * v.w;
+    }
+    *dst = acc;
+  }
+}
+
 // out[r, h*d + c] (+)= sum over e in [row_ptr[r], row_ptr[r+1]) of
 // w[s*heads + h] * src[(s / group)*ld_src + h*d + c], s = perm ? perm[e] : e,
 // in increasing e: one warp per output row, lanes over 4-column chunks (vec:
@@ -206,8 +265,14 @@ int cg_segment_sum(const float* src, int64_t ld_src, const int32_t* row_ptr, con
   CG_REQUIRE(src && row_ptr && out, "segment_sum: null pointer");
   const bool vec = cols % 4 == 0 && ld_src % 4 == 0 && ld_out % 4 == 0 && seg::aligned16(src) &&
                    seg::aligned16(out);
-  seg::segment_sum_kernel<<<seg::grid_for_warps(n_rows), 256, 0, as_stream(stream)>>>(
-      src, ld_src, row_ptr, perm, n_rows, cols, out, ld_out, accumulate != 0, vec);
+  if (vec) {
+    const int64_t tasks = n_rows * ceil_div<int64_t>(cols / 4, 32);
+    seg::segment_sum_blocks_kernel<<<seg::grid_for_warps(tasks), 256, 0, as_stream(stream)>>>(
+        src, ld_src, row_ptr, perm, n_rows, (int)(cols / 4), out, ld_out, accumulate != 0);
+  } else {
+    seg::segment_sum_kernel<<<seg::grid_for_warps(n_rows), 256, 0, as_stream(stream)>>>(
+        src, ld_src, row_ptr, perm, n_rows, cols, out, ld_out, accumulate != 0, vec);
+  }
   CG_LAUNCHED("segment_sum");
   return kOk;
 }
@@ -222,8 +287,14 @@ int cg_segment_sum_scaled(const float* w, const float* src, int64_t ld_src, int6
   CG_REQUIRE(group >= 1 && group <= (1 << 30), "segment_sum_scaled: group = %lld outside [1, 2^30]",
              (long long)group);
   const bool vec = d % 4 == 0 && ld_src % 4 == 0 && ld_out % 4 == 0 && seg::aligned16(src) && seg::aligned16(out);
-  seg::segment_sum_scaled_kernel<<<seg::grid_for_warps(n_rows), 256, 0, as_stream(stream)>>>(
-      w, src, ld_src, (int)group, heads, d, row_ptr, perm, n_rows, out, ld_out, accumulate != 0, vec);
+  if (vec) {
+    const int64_t tasks = n_rows * ceil_div<int64_t>((int64_t)heads * d / 4, 32);
+    seg::segment_sum_scaled_blocks_kernel<<<seg::grid_for_warps(tasks), 256, 0, as_stream(stream)>>>(
+        w, src, ld_src, (int)group, heads, d, row_ptr, perm, n_rows, out, ld_out, accumulate != 0);
+  } else {
+    seg::segment_sum_scaled_kernel<<<seg::grid_for_warps(n_rows), 256, 0, as_stream(stream)>>>(
+        w, src, ld_src, (int)group, heads, d, row_ptr, perm, n_rows, out, ld_out, accumulate != 0, vec);
+  }
   CG_LAUNCHED("segment_sum_scaled");
   return kOk;
 }

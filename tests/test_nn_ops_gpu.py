@@ -214,3 +214,28 @@ def test_segment_sum_scaled():
             want[idx[t]] += rows[t]
     assert torch.allclose(out[:, : heads * d].double().cpu(), want.view(n, -1), rtol=1e-5, atol=1e-5)
     assert torch.all(out[:, heads * d :] == 7.0)
+
+
+@pytest.mark.parametrize("cols", [20, 132, 1536])
+def test_segment_sum_long_segments(cols):
+    """Segments longer than the 32 rows the kernel prefetches, and column
+    counts that leave the last 128-column chunk partial."""
+    n, e = 5, 400
+    g = torch.Generator().manual_seed(19)
+    index = torch.randint(-1, n, (e,), generator=g).cuda()
+    csr = cgnn.Csr.from_index(index, n)
+    rows = randn(e, cols, seed=20)
+    keep = index >= 0
+    want = torch.zeros(n, cols, dtype=torch.float64, device="cuda").index_add(0, index[keep].long(),
+                                                                             rows[keep].double())
+    got = cgnn.segment_sum_raw(rows, csr)
+    assert torch.allclose(got.double(), want, rtol=1e-5, atol=1e-4)
+    assert torch.equal(got, cgnn.segment_sum_raw(rows, csr))
+    w = randn(e, 4, seed=21)
+    src = randn(e // 8, 4 * 8, seed=22)
+    out = torch.empty(n, 32, device="cuda")
+    native.call("cg_segment_sum_scaled", w.data_ptr(), src.data_ptr(), src.stride(0), 8, 4, 8, csr.row_ptr.data_ptr(),
+                csr.perm.data_ptr(), n, out.data_ptr(), out.stride(0), 0, native.stream_ptr())
+    terms = (w.double()[:, :, None] * src.double().repeat_interleave(8, 0).view(e, 4, 8)).view(e, 32)
+    want2 = torch.zeros(n, 32, dtype=torch.float64, device="cuda").index_add(0, index[keep].long(), terms[keep])
+    assert torch.allclose(out.double(), want2, rtol=1e-5, atol=1e-4)
