@@ -393,10 +393,20 @@ __device__ __forceinline__ void write_dbias(const Params& P, const float* M, int
   }
 }
 
+// exp for the softmax: the accurate expf, or (FAST, tf32 precision) the
+// hardware-approximated __expf, whose relative error (~1e-6 over the range
+// used) is far below the tf32 operand rounding.
+template <bool FAST>
+__device__ __forceinline__ float sm_exp(float x) {
+  if constexpr (FAST) return __expf(x);
+  else return expf(x);
+}
+
 // Logits of the band from the S accumulator: scale * S + bias (bias row
 // r & brow), masked to -inf for keys past kc and non-finite values. Returns
 // probabilities in `p` (exp(l - lse)) and, when lse_in is null, computes the
 // row lse.
+template <bool FAST>
 __device__ __forceinline__ void band_softmax(float (&p)[4][4], const float (&s)[4][4], const float* sbias,
                                              int brow, int band, int g, int t, float scale, int kc,
                                              const float* lse_in, float (&lse)[2]) {
@@ -432,7 +442,7 @@ __device__ __forceinline__ void band_softmax(float (&p)[4][4], const float (&s)[
       for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
         for (int e2 = 0; e2 < 2; ++e2)
-          if (ok[nt][2 * half + e2]) sum += expf(l[nt][2 * half + e2] - m);
+          if (ok[nt][2 * half + e2]) sum += sm_exp<FAST>(l[nt][2 * half + e2] - m);
       sum = quad_sum(sum);
       lse[half] = m == -INFINITY ? -INFINITY : m + logf(sum);
     }
@@ -442,7 +452,7 @@ __device__ __forceinline__ void band_softmax(float (&p)[4][4], const float (&s)[
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const float ls = lse[e >> 1];
-      p[nt][e] = (ok[nt][e] && isfinite(ls)) ? expf(l[nt][e] - ls) : 0.0f;
+      p[nt][e] = (ok[nt][e] && isfinite(ls)) ? sm_exp<FAST>(l[nt][e] - ls) : 0.0f;
     }
 }
 
@@ -510,7 +520,7 @@ __global__ void __launch_bounds__(kThreads) fwd1_tc(const Params P) {
     float S[4][4], p[4][4], lse[2];
     zero(S);
     band_mma<X3, 4, DP / 8>(S, CG_A_ROWS(sQ), CG_B_ROWS(sK), g, t);
-    band_softmax(p, S, sP, brow, band, g, t, scale, kc, nullptr, lse);
+    band_softmax<!X3>(p, S, sP, brow, band, g, t, scale, kc, nullptr, lse);
     cp_async_wait<0>();
     __syncthreads();  // V landed
     float O[DP / 8][4];
@@ -565,7 +575,7 @@ __global__ void __launch_bounds__(kThreads) bwd1_tc(const Params P) {
       zero(S);   // scores
       zero(GP);  // grad_probs = grad_out v^T
       band_mma2<X3, 4, DP / 8>(S, CG_A_ROWS(sQ), CG_B_ROWS(sK), GP, CG_A_ROWS(sG), CG_B_ROWS(sV), g, t);
-      band_softmax(p, S, sGL, brow, band, g, t, scale, kc, sLse, lse);
+      band_softmax<!X3>(p, S, sGL, brow, band, g, t, scale, kc, sLse, lse);
       float rs[2];
       row_dot(rs, p, GP);
 #pragma unroll
@@ -642,7 +652,7 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
       zero(A);  // scores
       zero(B);  // grad_probs = grad_out v^T
       band_mma2<X3, 4, DP / 8>(A, CG_A_ROWS(sQ), CG_B_ROWS(sK), B, CG_A_ROWS(sG), CG_B_ROWS(sV), g, t);
-      band_softmax(p, A, sGL, brow, band, g, t, scale, kc, sLse, lse);
+      band_softmax<!X3>(p, A, sGL, brow, band, g, t, scale, kc, sLse, lse);
       float rs[2];
       row_dot(rs, p, B);
       float cen[4][4];

@@ -9,7 +9,8 @@
 // swizzled shared memory, tf32 or three-term products). What pooling changes:
 // - forward: w_j = sum_i env_i P_ij is a column sum of the fragments (quad
 //   shuffles over g, then the two bands in a fixed order) and
-//   out = sum_j w_j v_j a per-column FMA loop; the P v product disappears;
+//   out = sum_j w_j v_j a per-column FMA loop reading v straight from the
+//   atom rows; the P v product and the staging of v disappear;
 // - backward1: the token cotangent is env_i dm, so grad_probs = env_i u_j
 //   with u = V dm (an N = 1 mma), dv_j = w_j dm is rank one (left to
 //   cg_segment_sum_scaled as the weight w) and only S, dq and dk are
@@ -40,10 +41,8 @@ using attn_tc::KP;
 using attn_tc::kThreads;
 using attn_tc::ld2;
 using attn_tc::Layout;
-using attn_tc::load_op_async;
 using attn_tc::put_band;
 using attn_tc::quad_sum;
-using attn_tc::stage_index;
 using attn_tc::store_band;
 using attn_tc::zero;
 
@@ -51,16 +50,6 @@ struct PParams {
   cg_pooled_attn_args a;
   int vec;  // 16-byte operand rows and 8-byte output pairs (d equal to the padded width)
 };
-
-// q, k or v part (part 0, 1, 2) of per-atom rows, read through the token index
-__device__ __forceinline__ cg_mat part_mat(const float* rows, int part, int64_t C, int d, int64_t ld) {
-  cg_mat m;
-  m.ptr = const_cast<float*>(rows) + part * C;
-  m.sn = 0;
-  m.sh = d;
-  m.sr = ld;
-  return m;
-}
 
 // per-token [dq | dk] rows (n*k, ld): part 0 dq, part 1 dk
 __device__ __forceinline__ cg_mat token_mat(float* dqk, int part, int64_t C, int k, int d, int64_t ld) {
@@ -120,6 +109,38 @@ __device__ __forceinline__ void load_dm(float* s, const float* dout, int64_t n, 
   for (int c = threadIdx.x; c < DP; c += kThreads) s[c] = c < d ? dout[n * C + (int64_t)hh * d + c] : 0.0f;
 }
 
+// Float offsets of the atom's token rows in the per-atom row matrices
+// (token_index * ld, -1 for padding and past k), staged once per atom and
+// shared by every operand and head.
+__device__ __forceinline__ void stage_rows(int64_t* srow, const int32_t* token_index, int64_t n, int k, int64_t ld) {
+  if (threadIdx.x < KP) {
+    const int32_t j = (int)threadIdx.x < k ? token_index[n * k + threadIdx.x] : -1;
+    srow[threadIdx.x] = j < 0 ? -1 : (int64_t)j * ld;
+  }
+}
+
+// k x d operand gathered from base + srow[r] (base = rows + part*C + h*d) into
+// shared memory: 16-byte cp.async copies (vec) or scalar loads; zero rows and
+// columns past d.
+template <int DP>
+__device__ __forceinline__ void load_rows_async(float* s, const float* base, const int64_t* srow, int d, bool vec) {
+  using L = Layout<DP>;
+  if (vec) {
+    constexpr int VPR = DP / 4;
+    for (int f = threadIdx.x; f < KP * VPR; f += kThreads) {
+      const int r = f / VPR, c = (f % VPR) * 4;
+      const int64_t off = srow[r];
+      attn_tc::cp_async16(s + L::op(r, c), off >= 0 ? base + off + c : base, off >= 0 ? 16 : 0);
+    }
+  } else {
+    for (int f = threadIdx.x; f < KP * DP; f += kThreads) {
+      const int r = f / DP, c = f % DP;
+      const int64_t off = srow[r];
+      s[L::op(r, c)] = (off >= 0 && c < d) ? base[off + c] : 0.0f;
+    }
+  }
+}
+
 // B operand of a matrix-vector product as an N = 1 mma: column 0 is dm
 #define CG_B_VEC(V) [&](int c, int nn) { return nn == 0 ? ld2(V, c) : make_float2(0.0f, 0.0f); }
 #define CG_A_ROWS(X) [&](int m, int c) { return ld2(X, L::op(band * 16 + m, c)); }
@@ -135,11 +156,10 @@ __global__ void __launch_bounds__(kThreads) pooled_fwd(const PParams P) {
   extern __shared__ __align__(16) float smem[];
   float* sQ = smem;
   float* sK = sQ + L::OP;
-  float* sV = sK + L::OP;
-  float* sB = sV + L::OP;  // key bias row
+  float* sB = sK + L::OP;  // key bias row
   float* sE = sB + KP;     // env of the atom's tokens
-  float* sW = sE + KP;     // band partials of w: [2][KP]
-  int32_t* sIdx = reinterpret_cast<int32_t*>(sW + 2 * KP);
+  float* sW = sE + KP;     // band partials of w: [2][KP], then w in the first row
+  int64_t* sRow = reinterpret_cast<int64_t*>(sW + 2 * KP);
   const cg_pooled_attn_args& a = P.a;
   const int k = a.k, d = a.d, H = a.h;
   const int64_t C = (int64_t)H * d;
@@ -147,27 +167,24 @@ __global__ void __launch_bounds__(kThreads) pooled_fwd(const PParams P) {
   const bool vec = P.vec;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int band = warp;
-  const cg_mat mq = part_mat(a.qkv, 0, C, d, a.ld_qkv), mk = part_mat(a.qkv, 1, C, d, a.ld_qkv),
-               mv = part_mat(a.qkv, 2, C, d, a.ld_qkv);
   for (int64_t n = blockIdx.x; n < a.n; n += gridDim.x) {
     __syncthreads();
-    const int32_t* tix = stage_index(sIdx, a.token_index, n, k);
+    stage_rows(sRow, a.token_index, n, k, a.ld_qkv);
     load_tokens(sE, a.env, n, k);
+    __syncthreads();
     const int kc = key_count(a, n);
     for (int hh = 0; hh < H; ++hh) {
       if (hh > 0) __syncthreads();  // the previous head is done with shared memory
-      load_op_async<DP>(sQ, mq, n, hh, k, d, vec, tix);
-      load_op_async<DP>(sK, mk, n, hh, k, d, vec, tix);
+      load_rows_async<DP>(sQ, a.qkv + (int64_t)hh * d, sRow, d, vec);
+      load_rows_async<DP>(sK, a.qkv + C + (int64_t)hh * d, sRow, d, vec);
       load_key_row(sB, a.bias, n, hh, k, H);
       cp_async_commit();
-      load_op_async<DP>(sV, mv, n, hh, k, d, vec, tix);
-      cp_async_commit();
-      cp_async_wait<1>();
+      cp_async_wait<0>();
       __syncthreads();
       float S[4][4], p[4][4], lse[2];
       zero(S);
       band_mma<X3, 4, DP / 8>(S, CG_A_ROWS(sQ), CG_B_ROWS(sK), g, t);
-      band_softmax(p, S, sB, 0, band, g, t, scale, kc, nullptr, lse);
+      band_softmax<!X3>(p, S, sB, 0, band, g, t, scale, kc, nullptr, lse);
       const float e0 = sE[band * 16 + g], e1 = sE[band * 16 + g + 8];
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt)
@@ -181,13 +198,23 @@ __global__ void __launch_bounds__(kThreads) pooled_fwd(const PParams P) {
           if (r < k) a.lse[(n * H + hh) * k + r] = lse[half];
         }
       }
-      cp_async_wait<0>();
-      __syncthreads();  // V landed, both bands' partials of w visible
-      if (threadIdx.x < k) a.w[(n * H + hh) * k + threadIdx.x] = sW[threadIdx.x] + sW[KP + threadIdx.x];
+      __syncthreads();  // both bands' partials of w visible
+      if (threadIdx.x < KP) {
+        const float wj = sW[threadIdx.x] + sW[KP + threadIdx.x];
+        if ((int)threadIdx.x < k) a.w[(n * H + hh) * k + threadIdx.x] = wj;
+        sW[threadIdx.x] = wj;  // each thread rewrites only the entry it read
+      }
+      __syncthreads();
+      // out = sum_j w_j v_j over the valid keys (w_j = 0 past kc), v read
+      // straight from the atom rows (coalesced over c)
+      const float* vbase = a.qkv + 2 * C + (int64_t)hh * d;
       for (int c = threadIdx.x; c < d; c += kThreads) {
         float acc = 0.0f;
 #pragma unroll 8
-        for (int j = 0; j < KP; ++j) acc += (sW[j] + sW[KP + j]) * sV[L::op(j, c)];
+        for (int j = 0; j < kc; ++j) {
+          const int64_t off = sRow[j];
+          if (off >= 0) acc += sW[j] * __ldg(vbase + off + c);
+        }
         a.out[n * C + (int64_t)hh * d + c] = acc;
       }
     }
@@ -208,7 +235,7 @@ __global__ void __launch_bounds__(kThreads) pooled_bwd1(const PParams P) {
   float* sW = sU + KP;       // w
   float* sLse = sW + KP;     // lse (+inf past k)
   float* sDm = sLse + KP;    // dm (64)
-  int32_t* sIdx = reinterpret_cast<int32_t*>(sDm + 64);
+  int64_t* sRow = reinterpret_cast<int64_t*>(sDm + 64);
   const cg_pooled_attn_args& a = P.a;
   const int k = a.k, d = a.d, H = a.h;
   const int64_t C = (int64_t)H * d;
@@ -216,20 +243,20 @@ __global__ void __launch_bounds__(kThreads) pooled_bwd1(const PParams P) {
   const bool vec = P.vec;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int band = warp;
-  const cg_mat mq = part_mat(a.qkv, 0, C, d, a.ld_qkv), mk = part_mat(a.qkv, 1, C, d, a.ld_qkv),
-               mv = part_mat(a.qkv, 2, C, d, a.ld_qkv);
   const cg_mat tq = token_mat(a.dqk, 0, C, k, d, a.ld_dqk), tk = token_mat(a.dqk, 1, C, k, d, a.ld_dqk);
   for (int64_t n = blockIdx.x; n < a.n; n += gridDim.x) {
     __syncthreads();
-    const int32_t* tix = stage_index(sIdx, a.token_index, n, k);
+    stage_rows(sRow, a.token_index, n, k, a.ld_qkv);
     load_tokens(sE, a.env, n, k);
+    __syncthreads();
     const int kc = key_count(a, n);
     float denv[2] = {0.0f, 0.0f};
     for (int hh = 0; hh < H; ++hh) {
       if (hh > 0) __syncthreads();
-      load_op_async<DP>(sQ, mq, n, hh, k, d, vec, tix);
-      load_op_async<DP>(sK, mk, n, hh, k, d, vec, tix);
-      load_op_async<DP>(sV, mv, n, hh, k, d, vec, tix);
+      const float* hq = a.qkv + (int64_t)hh * d;
+      load_rows_async<DP>(sQ, hq, sRow, d, vec);
+      load_rows_async<DP>(sK, hq + C, sRow, d, vec);
+      load_rows_async<DP>(sV, hq + 2 * C, sRow, d, vec);
       cp_async_commit();
       load_key_row(sB, a.bias, n, hh, k, H);
       if (threadIdx.x < KP) {
@@ -245,7 +272,7 @@ __global__ void __launch_bounds__(kThreads) pooled_bwd1(const PParams P) {
       zero(U);
       band_mma<X3, 4, DP / 8>(S, CG_A_ROWS(sQ), CG_B_ROWS(sK), g, t);
       band_mma<X3, 1, DP / 8>(U, CG_A_ROWS(sV), CG_B_VEC(sDm), g, t);
-      band_softmax(p, S, sB, 0, band, g, t, scale, kc, sLse, lse);
+      band_softmax<!X3>(p, S, sB, 0, band, g, t, scale, kc, sLse, lse);
       if (t == 0) {
         sU[band * 16 + g] = U[0][0];
         sU[band * 16 + g + 8] = U[0][2];
@@ -322,7 +349,7 @@ __global__ void __launch_bounds__(kThreads) pooled_bwd2(const PParams P) {
   float* sLse = sW + KP;     // lse (+inf past k)
   float* sDu = sLse + KP;    // band partials of du: [2][KP]
   float* sDm = sDu + 2 * KP; // dm (64)
-  int32_t* sIdx = reinterpret_cast<int32_t*>(sDm + 64);
+  int64_t* sRow = reinterpret_cast<int64_t*>(sDm + 64);
   const cg_pooled_attn_args& a = P.a;
   const int k = a.k, d = a.d, H = a.h;
   const int64_t C = (int64_t)H * d;
@@ -330,27 +357,26 @@ __global__ void __launch_bounds__(kThreads) pooled_bwd2(const PParams P) {
   const bool vec = P.vec;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int band = warp;
-  const cg_mat mq = part_mat(a.qkv, 0, C, d, a.ld_qkv), mk = part_mat(a.qkv, 1, C, d, a.ld_qkv),
-               mv = part_mat(a.qkv, 2, C, d, a.ld_qkv);
-  const cg_mat nq = part_mat(a.hqkv, 0, C, d, a.ld_qkv), nk = part_mat(a.hqkv, 1, C, d, a.ld_qkv),
-               nv = part_mat(a.hqkv, 2, C, d, a.ld_qkv);
   const cg_mat tq = token_mat(a.dqk, 0, C, k, d, a.ld_dqk), tk = token_mat(a.dqk, 1, C, k, d, a.ld_dqk);
   for (int64_t n = blockIdx.x; n < a.n; n += gridDim.x) {
     __syncthreads();
-    const int32_t* tix = stage_index(sIdx, a.token_index, n, k);
+    stage_rows(sRow, a.token_index, n, k, a.ld_qkv);
     load_tokens(sE, a.env, n, k);
     load_tokens(sHE, a.henv, n, k);
+    __syncthreads();
     const int kc = key_count(a, n);
     float denv[2] = {0.0f, 0.0f};
     for (int hh = 0; hh < H; ++hh) {
       if (hh > 0) __syncthreads();
-      load_op_async<DP>(sQ, mq, n, hh, k, d, vec, tix);
-      load_op_async<DP>(sK, mk, n, hh, k, d, vec, tix);
-      load_op_async<DP>(sHQ, nq, n, hh, k, d, vec, tix);
-      load_op_async<DP>(sHK, nk, n, hh, k, d, vec, tix);
+      const float* hq = a.qkv + (int64_t)hh * d;
+      const float* nq = a.hqkv + (int64_t)hh * d;
+      load_rows_async<DP>(sQ, hq, sRow, d, vec);
+      load_rows_async<DP>(sK, hq + C, sRow, d, vec);
+      load_rows_async<DP>(sHQ, nq, sRow, d, vec);
+      load_rows_async<DP>(sHK, nq + C, sRow, d, vec);
       cp_async_commit();
-      load_op_async<DP>(sV, mv, n, hh, k, d, vec, tix);
-      load_op_async<DP>(sHV, nv, n, hh, k, d, vec, tix);
+      load_rows_async<DP>(sV, hq + 2 * C, sRow, d, vec);
+      load_rows_async<DP>(sHV, nq + 2 * C, sRow, d, vec);
       cp_async_commit();
       load_key_row(sB, a.bias, n, hh, k, H);
       load_key_row(sHB, a.hbias, n, hh, k, H);
@@ -367,7 +393,7 @@ __global__ void __launch_bounds__(kThreads) pooled_bwd2(const PParams P) {
       zero(A);  // d_logits = scale (hq k^T + q hk^T) + hb
       band_mma2<X3, 4, DP / 8>(S, CG_A_ROWS(sQ), CG_B_ROWS(sK), A, CG_A_ROWS(sHQ), CG_B_ROWS(sK), g, t);
       band_mma<X3, 4, DP / 8>(A, CG_A_ROWS(sQ), CG_B_ROWS(sHK), g, t);
-      band_softmax(p, S, sB, 0, band, g, t, scale, kc, sLse, lse);
+      band_softmax<!X3>(p, S, sB, 0, band, g, t, scale, kc, sLse, lse);
       cp_async_wait<0>();
       __syncthreads();  // V and HV landed
       float U[1][4], T[1][4];
@@ -491,9 +517,9 @@ template <int DP>
 inline int smem_bytes(int which) {
   using L = Layout<DP>;
   switch (which) {
-    case 0: return (3 * L::OP + 4 * KP + KP) * 4;
-    case 1: return (3 * L::OP + L::KK + 5 * KP + 64 + KP) * 4;
-    default: return (6 * L::OP + 2 * L::KK + 10 * KP + 64 + KP) * 4;
+    case 0: return (2 * L::OP + 4 * KP + 2 * KP) * 4;
+    case 1: return (3 * L::OP + L::KK + 5 * KP + 64 + 2 * KP) * 4;
+    default: return (6 * L::OP + 2 * L::KK + 10 * KP + 64 + 2 * KP) * 4;
   }
 }
 
