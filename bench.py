@@ -253,8 +253,9 @@ def run_mine(args):
         line["edge_attn_bwd2"] = {"shape": "(4096, 8, 32, 32) fp32, keys masked past U{8..32}"}
         for prec in ("tf32", "fp32"):
             mb = microbench.attn(4096, iters=10, hbm_gbs=hbm, which=("bwd2",), precision=prec)["bwd2"]
+            traffic = EDGE_BWD2_TRAFFIC_PER_ATOM * 4096 if prec == "tf32" else None
             entry = {"bound": "hbm", "achieved": mb["gb_s"], "peak": hbm, "unit": "GB/s",
-                     "frac": mb["gb_s"] / hbm, "traffic": None, "algorithmic_bytes": mb["bytes"],
+                     "frac": mb["gb_s"] / hbm, "traffic": traffic, "algorithmic_bytes": mb["bytes"],
                      "us_per_launch": mb["us"], "peak_source": f"{src} hbm_gbs", "precision": prec}
             line["edge_attn_bwd2"]["roofline" if prec == "tf32" else "roofline_fp32"] = entry
         if not args.no_cpu_baseline:
@@ -303,6 +304,16 @@ def attn_bytes(info, name):
     return 3 * t + b + lse + t + 3 * t + b + 3 * t + b + t
 
 
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per atom of one ncu
+# capture of each kernel at a smaller size; traffic grows with the atoms a launch
+# processes, so a launch's traffic is this figure times its atoms.
+TRAFFIC_PER_ATOM = {
+    "cg_pooled_attn_bwd1": (66.736896e6 + 333.938688e6) / 2048,  # 12 heads x 30 tokens x 64 dims, tf32
+}
+# the edge-attention backward2 microbenchmark kernel, 8 heads x 32 tokens x 32 dims, tf32
+EDGE_BWD2_TRAFFIC_PER_ATOM = (303.151360e6 + 134.537728e6) / 1024
+
+
 def pooled_attn_bytes(info, name):
     """Algorithmic bytes of one pooled-attention launch: every per-atom operand
     once (the gathered token rows are re-reads of the atom rows), plus the
@@ -339,8 +350,12 @@ def roofline_of(kernels, hbm, bf16, bf16_sus, src):
         nbytes = sum(count(info, name) for _, _, info in rec)
         secs = sum(a.elapsed_time(b) for a, b, _ in rec) / 1e3
         achieved = nbytes / secs / 1e9
+        traffic = None
+        if name in TRAFFIC_PER_ATOM:
+            traffic = TRAFFIC_PER_ATOM[name] * sum(info[0] for _, _, info in rec) / len(rec)
         return {"kernel": name, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                "frac": achieved / hbm, "traffic": None, "peak_source": f"{src} hbm_gbs"}
+                "frac": achieved / hbm, "traffic": traffic, "algorithmic_bytes": nbytes / len(rec),
+                "peak_source": f"{src} hbm_gbs", "traffic_source": "ncu capture at 2048 atoms, scaled by atoms"}
     return {"kernel": name, "bound": "hbm", "achieved": None, "peak": hbm, "unit": "GB/s", "frac": None,
             "traffic": None}
 

@@ -2,6 +2,7 @@
 Microbenchmarks of the hot kernels, timed with CUDA events.
 
     python -m create_graph_b200.microbench attn [--n 4096] [--iters 10] [--precision fp32|tf32]
+    python -m create_graph_b200.microbench pooled [--n 8280] [--iters 10] [--precision tf32|fp32]
     python -m create_graph_b200.microbench gemm M N K [--silu]
 
 ``attn``: the masked edge-attention microbenchmark: n atoms x 8 heads x 32
@@ -9,6 +10,9 @@ tokens x 32 dims, fp32, q/k/v ~ N(0, 1), bias ~ N(0, 0.1) per (n, h, i, j),
 keys j >= c_n masked with c_n ~ U{8..32}; forward1, backward1 and backward2,
 each against its algorithmic bytes (every operand read or written once), in
 the fp32 (three-term tf32 split) or tf32 (one tf32 product) precision.
+``pooled``: the envelope-pooled token attention of the 85M model's blocks:
+n atoms x 12 heads x k = 30 tokens x 64 dims gathered from per-atom rows,
+keys masked past c_n ~ U{8..30}, forward / backward1 / backward2.
 ``gemm``: one tcgen05 tf32 GEMM shape (bias, optionally the SiLU epilogue).
 """
 
@@ -19,7 +23,14 @@ import json
 
 import torch
 
-from create_graph_b200.edge_attn import attn_backward1, attn_backward2, attn_forward1
+from create_graph_b200.edge_attn import (
+    attn_backward1,
+    attn_backward2,
+    attn_forward1,
+    pooled_attention_backward1,
+    pooled_attention_backward2,
+    pooled_attention_forward,
+)
 from create_graph_b200.gemm import ACT_SILU, gemm
 
 
@@ -79,6 +90,33 @@ def attn(n: int = 4096, iters: int = 10, hbm_gbs: float | None = None, which=("f
     return out
 
 
+def pooled_inputs(n: int, h: int = 12, k: int = 30, d: int = 64, seed: int = 0):
+    gen = torch.Generator().manual_seed(seed)
+    qkv = torch.randn(n, 3 * h * d, generator=gen)
+    bias = 0.1 * torch.randn(n * k, h, generator=gen)
+    env = torch.rand(n * k, generator=gen)
+    counts = torch.randint(8, k + 1, (n,), generator=gen, dtype=torch.int32)
+    index = torch.randint(0, n, (n, k), generator=gen, dtype=torch.int32)
+    index[torch.arange(k)[None, :] >= counts[:, None]] = -1
+    dm, hqkv = torch.randn(n, h * d, generator=gen), torch.randn(n, 3 * h * d, generator=gen)
+    hb, he = torch.randn(n * k, h, generator=gen), torch.randn(n * k, generator=gen)
+    cuda = [t.cuda() for t in (qkv, bias, env, index.view(-1), counts, dm, hqkv, hb, he)]
+    return cuda, k, h
+
+
+def pooled(n: int = 8280, iters: int = 10, precision: str = "tf32") -> dict:
+    """Median launch time of the pooled attention kernels at the model shape."""
+    (qkv, bias, env, index, counts, dm, hqkv, hb, he), k, h = pooled_inputs(n)
+    args = (index, counts, k, h, 0.125, precision)
+    _, lse, w = pooled_attention_forward(qkv, bias, env, *args)
+    fns = {
+        "fwd": lambda: pooled_attention_forward(qkv, bias, env, *args),
+        "bwd1": lambda: pooled_attention_backward1(qkv, bias, env, lse, w, dm, *args),
+        "bwd2": lambda: pooled_attention_backward2(qkv, bias, env, lse, w, dm, hqkv, hb, he, *args),
+    }
+    return {name: {"us": _time(fn, iters) * 1e3} for name, fn in fns.items()}
+
+
 def gemm_bench(m: int, n: int, k: int, silu: bool = False, iters: int = 20) -> dict:
     a = torch.randn(m, k, device="cuda")
     b = torch.randn(n, k, device="cuda")
@@ -97,12 +135,18 @@ def main() -> None:
     p_attn.add_argument("--n", type=int, default=4096)
     p_attn.add_argument("--iters", type=int, default=10)
     p_attn.add_argument("--precision", choices=("fp32", "tf32"), default="fp32")
+    p_pool = sub.add_parser("pooled")
+    p_pool.add_argument("--n", type=int, default=8280)
+    p_pool.add_argument("--iters", type=int, default=10)
+    p_pool.add_argument("--precision", choices=("fp32", "tf32"), default="tf32")
     p_gemm = sub.add_parser("gemm")
     p_gemm.add_argument("shape", type=int, nargs=3)
     p_gemm.add_argument("--silu", action="store_true")
     args = parser.parse_args()
     if args.what == "attn":
         print(json.dumps(attn(args.n, args.iters, precision=args.precision)))
+    elif args.what == "pooled":
+        print(json.dumps(pooled(args.n, args.iters, args.precision)))
     else:
         print(json.dumps(gemm_bench(*args.shape, silu=args.silu)))
 
