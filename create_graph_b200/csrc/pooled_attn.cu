@@ -38,7 +38,7 @@ static int run(int which, const cg_pooled_attn_args* args, void* stream) {
   P.a = a;
   bool vec = a.d == dp && a.ld_qkv % 4 == 0 && al16(a.qkv);
   if (which == 2) vec = vec && al16(a.hqkv);
-  if (which != 0) vec = vec && a.ld_dqk % 4 == 0 && al16(a.dqk);
+  if (which != 0) vec = vec && a.ld_dqk % 4 == 0 && al16(a.dqk) && al16(a.dout);
   P.vec = vec ? 1 : 0;
   const cudaStream_t s = as_stream(stream);
   return a.precision == CG_ATTN_TF32 ? launch_tf32(which, P, dp, s) : launch_fp32(which, P, dp, s);

@@ -12,12 +12,15 @@
 //   out = sum_j w_j v_j a per-column FMA loop reading v straight from the
 //   atom rows; the P v product and the staging of v disappear;
 // - backward1: the token cotangent is env_i dm, so grad_probs = env_i u_j
-//   with u = V dm (an N = 1 mma), dv_j = w_j dm is rank one (left to
-//   cg_segment_sum_scaled as the weight w) and only S, dq and dk are
-//   products;
+//   with u = V dm, dv_j = w_j dm is rank one (left to cg_segment_sum_scaled
+//   as the weight w) and only S, dq and dk are products;
 // - backward2: 7 products instead of 11 (S, the two halves of d_logits, dq
-//   and dk twice), u = V dm and t = HV dm as N = 1 mmas, the rest row or
-//   column sums and a per-column FMA loop for d(dm).
+//   and dk twice), the rest row or column sums and a per-column FMA loop for
+//   d(dm).
+// v and hv enter only through matrix-vector products (u = V dm, t = HV dm,
+// d(dm) = V^T du + HV^T w): fp32 FMA loops read them straight from the
+// per-atom rows (L2) while the q / k copies are in flight, so they are never
+// staged in shared memory.
 // The envelope gradient, a sum over heads, accumulates in registers across
 // the head loop and leaves once per atom.
 //
@@ -103,12 +106,6 @@ __device__ __forceinline__ void load_key_row(float* s, const float* src, int64_t
     s[threadIdx.x] = (src != nullptr && (int)threadIdx.x < k) ? src[(n * k + threadIdx.x) * H + hh] : 0.0f;
 }
 
-// dm = dout[n, hh*d : hh*d + d] into shared memory, zeros to the padded width
-template <int DP>
-__device__ __forceinline__ void load_dm(float* s, const float* dout, int64_t n, int hh, int d, int64_t C) {
-  for (int c = threadIdx.x; c < DP; c += kThreads) s[c] = c < d ? dout[n * C + (int64_t)hh * d + c] : 0.0f;
-}
-
 // Float offsets of the atom's token rows in the per-atom row matrices
 // (token_index * ld, -1 for padding and past k), staged once per atom and
 // shared by every operand and head.
@@ -141,8 +138,31 @@ __device__ __forceinline__ void load_rows_async(float* s, const float* base, con
   }
 }
 
-// B operand of a matrix-vector product as an N = 1 mma: column 0 is dm
-#define CG_B_VEC(V) [&](int c, int nn) { return nn == 0 ? ld2(V, c) : make_float2(0.0f, 0.0f); }
+// u_j = row_j . x for the atom's tokens, read straight from the per-atom rows
+// (L2) while the operand copies are in flight: two threads per token j =
+// tid / 2 (alternate 4-column chunks, then one shuffle), zero for padding
+// and past k. vec: 16-byte rows and x.
+__device__ __forceinline__ void token_dots(float* out, const float* base, const int64_t* srow, const float* x, int d,
+                                           bool vec) {
+  const int j = threadIdx.x >> 1, half = threadIdx.x & 1;
+  const int64_t off = srow[j];
+  float acc = 0.0f;
+  if (off >= 0) {
+    const float* row = base + off;
+    if (vec) {
+      for (int q = half; q < d / 4; q += 2) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(row) + q);
+        const float4 m = __ldg(reinterpret_cast<const float4*>(x) + q);
+        acc += v.x * m.x + v.y * m.y + v.z * m.z + v.w * m.w;
+      }
+    } else {
+      for (int c = half; c < d; c += 2) acc += __ldg(row + c) * __ldg(x + c);
+    }
+  }
+  acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+  if (half == 0) out[j] = acc;
+}
+
 #define CG_A_ROWS(X) [&](int m, int c) { return ld2(X, L::op(band * 16 + m, c)); }
 #define CG_B_ROWS(X) [&](int c, int j) { return ld2(X, L::op(j, c)); }
 #define CG_B_COLS(X) [&](int j, int c) { return make_float2(X[L::op(j, c)], X[L::op(j + 1, c)]); }
@@ -227,15 +247,13 @@ __global__ void __launch_bounds__(kThreads) pooled_bwd1(const PParams P) {
   extern __shared__ __align__(16) float smem[];
   float* sQ = smem;
   float* sK = sQ + L::OP;
-  float* sV = sK + L::OP;
-  float* sGL = sV + L::OP;   // grad_logits
+  float* sGL = sK + L::OP;   // grad_logits
   float* sB = sGL + L::KK;   // key bias row
   float* sE = sB + KP;       // env
   float* sU = sE + KP;       // u = V dm
   float* sW = sU + KP;       // w
   float* sLse = sW + KP;     // lse (+inf past k)
-  float* sDm = sLse + KP;    // dm (64)
-  int64_t* sRow = reinterpret_cast<int64_t*>(sDm + 64);
+  int64_t* sRow = reinterpret_cast<int64_t*>(sLse + KP);
   const cg_pooled_attn_args& a = P.a;
   const int k = a.k, d = a.d, H = a.h;
   const int64_t C = (int64_t)H * d;
@@ -256,7 +274,6 @@ __global__ void __launch_bounds__(kThreads) pooled_bwd1(const PParams P) {
       const float* hq = a.qkv + (int64_t)hh * d;
       load_rows_async<DP>(sQ, hq, sRow, d, vec);
       load_rows_async<DP>(sK, hq + C, sRow, d, vec);
-      load_rows_async<DP>(sV, hq + 2 * C, sRow, d, vec);
       cp_async_commit();
       load_key_row(sB, a.bias, n, hh, k, H);
       if (threadIdx.x < KP) {
@@ -264,20 +281,13 @@ __global__ void __launch_bounds__(kThreads) pooled_bwd1(const PParams P) {
         sLse[i] = i < k ? a.lse[(n * H + hh) * k + i] : INFINITY;
         sW[i] = i < k ? a.w[(n * H + hh) * k + i] : 0.0f;
       }
-      load_dm<DP>(sDm, a.dout, n, hh, d, C);
+      token_dots(sU, hq + 2 * C, sRow, a.dout + n * C + (int64_t)hh * d, d, vec);  // u = V dm
       cp_async_wait<0>();
       __syncthreads();
-      float S[4][4], p[4][4], lse[2], U[1][4];
+      float S[4][4], p[4][4], lse[2];
       zero(S);
-      zero(U);
       band_mma<X3, 4, DP / 8>(S, CG_A_ROWS(sQ), CG_B_ROWS(sK), g, t);
-      band_mma<X3, 1, DP / 8>(U, CG_A_ROWS(sV), CG_B_VEC(sDm), g, t);
       band_softmax<!X3>(p, S, sB, 0, band, g, t, scale, kc, sLse, lse);
-      if (t == 0) {
-        sU[band * 16 + g] = U[0][0];
-        sU[band * 16 + g + 8] = U[0][2];
-      }
-      __syncthreads();  // u of every key visible
       float uc[4][2];
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt) {
@@ -333,11 +343,9 @@ __global__ void __launch_bounds__(kThreads) pooled_bwd2(const PParams P) {
   extern __shared__ __align__(16) float smem[];
   float* sQ = smem;
   float* sK = sQ + L::OP;
-  float* sV = sK + L::OP;
-  float* sHQ = sV + L::OP;
+  float* sHQ = sK + L::OP;
   float* sHK = sHQ + L::OP;
-  float* sHV = sHK + L::OP;
-  float* sGL = sHV + L::OP;  // grad_logits dL
+  float* sGL = sHK + L::OP;  // grad_logits dL
   float* sDS = sGL + L::KK;  // d_scores
   float* sB = sDS + L::KK;   // key bias row
   float* sHB = sB + KP;      // key row of the dbias cotangent
@@ -348,8 +356,7 @@ __global__ void __launch_bounds__(kThreads) pooled_bwd2(const PParams P) {
   float* sW = sT + KP;       // w
   float* sLse = sW + KP;     // lse (+inf past k)
   float* sDu = sLse + KP;    // band partials of du: [2][KP]
-  float* sDm = sDu + 2 * KP; // dm (64)
-  int64_t* sRow = reinterpret_cast<int64_t*>(sDm + 64);
+  int64_t* sRow = reinterpret_cast<int64_t*>(sDu + 2 * KP);
   const cg_pooled_attn_args& a = P.a;
   const int k = a.k, d = a.d, H = a.h;
   const int64_t C = (int64_t)H * d;
@@ -375,9 +382,6 @@ __global__ void __launch_bounds__(kThreads) pooled_bwd2(const PParams P) {
       load_rows_async<DP>(sHQ, nq, sRow, d, vec);
       load_rows_async<DP>(sHK, nq + C, sRow, d, vec);
       cp_async_commit();
-      load_rows_async<DP>(sV, hq + 2 * C, sRow, d, vec);
-      load_rows_async<DP>(sHV, nq + 2 * C, sRow, d, vec);
-      cp_async_commit();
       load_key_row(sB, a.bias, n, hh, k, H);
       load_key_row(sHB, a.hbias, n, hh, k, H);
       if (threadIdx.x < KP) {
@@ -385,8 +389,10 @@ __global__ void __launch_bounds__(kThreads) pooled_bwd2(const PParams P) {
         sLse[i] = i < k ? a.lse[(n * H + hh) * k + i] : INFINITY;
         sW[i] = i < k ? a.w[(n * H + hh) * k + i] : 0.0f;
       }
-      load_dm<DP>(sDm, a.dout, n, hh, d, C);
-      cp_async_wait<1>();
+      const float* dm = a.dout + n * C + (int64_t)hh * d;
+      token_dots(sU, hq + 2 * C, sRow, dm, d, vec);  // u = V dm
+      token_dots(sT, nq + 2 * C, sRow, dm, d, vec);  // t = HV dm
+      cp_async_wait<0>();
       __syncthreads();
       float S[4][4], A[4][4], p[4][4], lse[2];
       zero(S);  // scores
@@ -394,19 +400,6 @@ __global__ void __launch_bounds__(kThreads) pooled_bwd2(const PParams P) {
       band_mma2<X3, 4, DP / 8>(S, CG_A_ROWS(sQ), CG_B_ROWS(sK), A, CG_A_ROWS(sHQ), CG_B_ROWS(sK), g, t);
       band_mma<X3, 4, DP / 8>(A, CG_A_ROWS(sQ), CG_B_ROWS(sHK), g, t);
       band_softmax<!X3>(p, S, sB, 0, band, g, t, scale, kc, sLse, lse);
-      cp_async_wait<0>();
-      __syncthreads();  // V and HV landed
-      float U[1][4], T[1][4];
-      zero(U);
-      zero(T);
-      band_mma2<X3, 1, DP / 8>(U, CG_A_ROWS(sV), CG_B_VEC(sDm), T, CG_A_ROWS(sHV), CG_B_VEC(sDm), g, t);
-      if (t == 0) {
-        sU[band * 16 + g] = U[0][0];
-        sU[band * 16 + g + 8] = U[0][2];
-        sT[band * 16 + g] = T[0][0];
-        sT[band * 16 + g + 8] = T[0][2];
-      }
-      __syncthreads();  // u and t of every key visible
       float uc[4][2], tc[4][2];
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt) {
@@ -487,12 +480,17 @@ __global__ void __launch_bounds__(kThreads) pooled_bwd2(const PParams P) {
       } else if (lane < k) {
         a.wv[(n * k + lane) * H + hh] = sDu[lane] + sDu[KP + lane];
       }
-      // d(dm)_c = sum_j du_j v_jc + w_j hv_jc
+      // d(dm)_c = sum_j du_j v_jc + w_j hv_jc over the valid keys (du_j = w_j = 0
+      // past kc), v and hv read straight from the atom rows (coalesced over c)
+      const float* vb = hq + 2 * C;
+      const float* hvb = nq + 2 * C;
       for (int c = threadIdx.x; c < d; c += kThreads) {
         float acc = 0.0f;
-#pragma unroll 8
-        for (int j = 0; j < KP; ++j)
-          acc += (sDu[j] + sDu[KP + j]) * sV[L::op(j, c)] + sW[j] * sHV[L::op(j, c)];
+#pragma unroll 4
+        for (int j = 0; j < kc; ++j) {
+          const int64_t off = sRow[j];
+          if (off >= 0) acc += (sDu[j] + sDu[KP + j]) * __ldg(vb + off + c) + sW[j] * __ldg(hvb + off + c);
+        }
         a.ddout[n * C + (int64_t)hh * d + c] = acc;
       }
     }
@@ -506,7 +504,6 @@ __global__ void __launch_bounds__(kThreads) pooled_bwd2(const PParams P) {
   }
 }
 
-#undef CG_B_VEC
 #undef CG_A_ROWS
 #undef CG_B_ROWS
 #undef CG_B_COLS
@@ -518,8 +515,8 @@ inline int smem_bytes(int which) {
   using L = Layout<DP>;
   switch (which) {
     case 0: return (2 * L::OP + 4 * KP + 2 * KP) * 4;
-    case 1: return (3 * L::OP + L::KK + 5 * KP + 64 + 2 * KP) * 4;
-    default: return (6 * L::OP + 2 * L::KK + 10 * KP + 64 + 2 * KP) * 4;
+    case 1: return (2 * L::OP + L::KK + 5 * KP + 2 * KP) * 4;
+    default: return (4 * L::OP + 2 * L::KK + 10 * KP + 2 * KP) * 4;
   }
 }
 
