@@ -50,9 +50,14 @@ struct Epilogue {
   int vec;              // 16-byte column groups: N, ldc, ld_aux multiples of 4, pointers aligned
 };
 
-__device__ inline float silu(float z) { return z / (1.0f + expf(-z)); }
+// SiLU and its derivative in the epilogue, with the hardware-approximated
+// exp and division (relative error ~1e-6, far below the tf32 rounding of the
+// products): the epilogue warps apply them to every output element, and with
+// the accurate expf and IEEE division they, not the tensor cores, bound the
+// SiLU GEMMs. exp(-z) overflowing to inf gives silu = 0 and silu' = 0.
+__device__ inline float silu(float z) { return __fdividef(z, 1.0f + __expf(-z)); }
 __device__ inline float silu_grad(float z) {
-  const float s = 1.0f / (1.0f + expf(-z));
+  const float s = __fdividef(1.0f, 1.0f + __expf(-z));
   return s * (1.0f + z * (1.0f - s));
 }
 
