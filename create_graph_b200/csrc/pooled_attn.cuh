@@ -242,7 +242,8 @@ __global__ void __launch_bounds__(kThreads) pooled_fwd(const PParams P) {
 }
 
 template <int DP, bool X3>
-__global__ void __launch_bounds__(kThreads) pooled_bwd1(const PParams P) {
+// 10 CTAs per SM: registers capped at 96 (no spills), shared memory 21 KB per CTA
+__global__ void __launch_bounds__(kThreads, 10) pooled_bwd1(const PParams P) {
   using L = Layout<DP>;
   extern __shared__ __align__(16) float smem[];
   float* sQ = smem;
