@@ -362,22 +362,26 @@ struct Plan {
   int kt_per;
 };
 
-// Tile width and split-K factor of a problem: tiles as wide as N allows; when
-// the output tiles cannot fill the SMs and K is long, split K so that about
-// one wave of CTAs runs, each with at least 4 k-tiles.
+// Tile width and split-K factor of a problem. Wide (128 x 256) tiles halve
+// the operand bytes per flop against 128 x 128 ones, which L2 cannot feed at
+// the tensor-core rate: they are used whenever N allows and either fill the
+// SMs by themselves or K is long enough to split. Short-output, long-K
+// problems split K into as many parts as fit one wave (floor(SMs / tiles)),
+// each of at least 4 k-tiles.
 static Plan plan_of(const cg_gemm_args& g) {
   Plan p;
   const int64_t mt = ceil_div<int64_t>(g.m, BM);
+  const int64_t ktiles = ceil_div<int64_t>(g.k, BK);
+  const int64_t sms = sm_count();
   if (g.n <= 16 && !g.b_mn_major) p.bn = 16;
   else if (g.n <= 32) p.bn = 32;
   else if (g.n <= 64) p.bn = 64;
-  else if (g.n >= 256 && mt * ceil_div<int64_t>(g.n, 256) >= sm_count()) p.bn = 256;
+  else if (g.n >= 256 && (mt * ceil_div<int64_t>(g.n, 256) >= sms || ktiles >= 32)) p.bn = 256;
   else p.bn = 128;
   const int64_t tiles = mt * ceil_div<int64_t>(g.n, p.bn);
-  const int64_t ktiles = ceil_div<int64_t>(g.k, BK);
   int64_t splits = 1;
-  if (tiles < sm_count() && ktiles >= 8) {
-    splits = ceil_div<int64_t>(sm_count(), tiles);
+  if (tiles < sms && ktiles >= 8) {
+    splits = sms / tiles;
     const int64_t cap = ktiles / 4;
     if (splits > cap) splits = cap;
     if (splits < 1) splits = 1;

@@ -117,15 +117,18 @@ def pooled(n: int = 8280, iters: int = 10, precision: str = "tf32") -> dict:
     return {name: {"us": _time(fn, iters) * 1e3} for name, fn in fns.items()}
 
 
-def gemm_bench(m: int, n: int, k: int, silu: bool = False, iters: int = 20) -> dict:
-    a = torch.randn(m, k, device="cuda")
-    b = torch.randn(n, k, device="cuda")
+def gemm_bench(m: int, n: int, k: int, silu: bool = False, iters: int = 20, a_mn: bool = False,
+               b_mn: bool = False) -> dict:
+    """One shape; a_mn / b_mn store A as (k, m) / B as (k, n) (the weight-gradient layouts)."""
+    a = torch.randn(k, m, device="cuda") if a_mn else torch.randn(m, k, device="cuda")
+    b = torch.randn(k, n, device="cuda") if b_mn else torch.randn(n, k, device="cuda")
     bias = torch.randn(n, device="cuda")
-    kw = {"bias": bias}
+    kw = {"bias": bias, "a_t": a_mn, "b_t": b_mn}
     if silu:
         kw.update(act=ACT_SILU, aux_out=torch.empty(m, n, device="cuda"))
     ms = _time(lambda: gemm(a, b, **kw), iters)
-    return {"shape": [m, n, k], "silu": silu, "us": ms * 1e3, "tflops": 2 * m * n * k / (ms / 1e3) / 1e12}
+    return {"shape": [m, n, k], "silu": silu, "a_mn": a_mn, "b_mn": b_mn, "us": ms * 1e3,
+            "tflops": 2 * m * n * k / (ms / 1e3) / 1e12}
 
 
 def main() -> None:
@@ -142,13 +145,15 @@ def main() -> None:
     p_gemm = sub.add_parser("gemm")
     p_gemm.add_argument("shape", type=int, nargs=3)
     p_gemm.add_argument("--silu", action="store_true")
+    p_gemm.add_argument("--a-mn", action="store_true", help="A stored (k, m)")
+    p_gemm.add_argument("--b-mn", action="store_true", help="B stored (k, n)")
     args = parser.parse_args()
     if args.what == "attn":
         print(json.dumps(attn(args.n, args.iters, precision=args.precision)))
     elif args.what == "pooled":
         print(json.dumps(pooled(args.n, args.iters, args.precision)))
     else:
-        print(json.dumps(gemm_bench(*args.shape, silu=args.silu)))
+        print(json.dumps(gemm_bench(*args.shape, silu=args.silu, a_mn=args.a_mn, b_mn=args.b_mn)))
 
 
 if __name__ == "__main__":
