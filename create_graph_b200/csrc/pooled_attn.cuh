@@ -342,13 +342,16 @@ template <int DP, bool X3>
 __global__ void __launch_bounds__(kThreads) pooled_bwd2(const PParams P) {
   using L = Layout<DP>;
   extern __shared__ __align__(16) float smem[];
+  // grad_logits and d_scores take the places of k and hk, dead once dq is
+  // done; those two slots hold the larger of a k x d operand and a k x k matrix
+  constexpr int SLOT = L::OP > L::KK ? L::OP : L::KK;
   float* sQ = smem;
   float* sK = sQ + L::OP;
-  float* sHQ = sK + L::OP;
+  float* sHQ = sK + SLOT;
   float* sHK = sHQ + L::OP;
-  float* sGL = sHK + L::OP;  // grad_logits dL
-  float* sDS = sGL + L::KK;  // d_scores
-  float* sB = sDS + L::KK;   // key bias row
+  float* sGL = sK;           // grad_logits dL
+  float* sDS = sHK;          // d_scores
+  float* sB = sHK + SLOT;    // key bias row
   float* sHB = sB + KP;      // key row of the dbias cotangent
   float* sE = sHB + KP;      // env
   float* sHE = sE + KP;      // denv cotangent
@@ -466,6 +469,7 @@ __global__ void __launch_bounds__(kThreads) pooled_bwd2(const PParams P) {
       band_mma_reg<X3, DP / 8>(O, S, CG_B_COLS(sHK), g, t);
       band_mma_reg<X3, DP / 8>(O, A, CG_B_COLS(sK), g, t);
       store_band<DP / 8>(tq, n, hh, band, k, d, O, g, t, scale, vec);
+      __syncthreads();  // both warps are done with k and hk
       put_band(sGL, S, band, g, t);
       put_band(sDS, A, band, g, t);
       __syncthreads();
@@ -517,7 +521,7 @@ inline int smem_bytes(int which) {
   switch (which) {
     case 0: return (2 * L::OP + 4 * KP + 2 * KP) * 4;
     case 1: return (2 * L::OP + L::KK + 5 * KP + 2 * KP) * 4;
-    default: return (4 * L::OP + 2 * L::KK + 10 * KP + 2 * KP) * 4;
+    default: return (2 * L::OP + 2 * (L::OP > L::KK ? L::OP : L::KK) + 10 * KP + 2 * KP) * 4;
   }
 }
 
