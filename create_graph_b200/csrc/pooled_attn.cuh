@@ -138,6 +138,29 @@ __device__ __forceinline__ void load_rows_async(float* s, const float* base, con
   }
 }
 
+// Two operands with the same rows (q and k, or hq and hk) in one pass: the
+// row offset, the swizzled destination and the predicate of a 16-byte chunk
+// serve both copies.
+template <int DP>
+__device__ __forceinline__ void load_rows2_async(float* s1, const float* b1, float* s2, const float* b2,
+                                                 const int64_t* srow, int d, bool vec) {
+  using L = Layout<DP>;
+  if (!vec) {
+    load_rows_async<DP>(s1, b1, srow, d, false);
+    load_rows_async<DP>(s2, b2, srow, d, false);
+    return;
+  }
+  constexpr int VPR = DP / 4;
+  for (int f = threadIdx.x; f < KP * VPR; f += kThreads) {
+    const int r = f / VPR, c = (f % VPR) * 4;
+    const int64_t off = srow[r];
+    const int so = L::op(r, c);
+    const bool ok = off >= 0;
+    attn_tc::cp_async16(s1 + so, ok ? b1 + off + c : b1, ok ? 16 : 0);
+    attn_tc::cp_async16(s2 + so, ok ? b2 + off + c : b2, ok ? 16 : 0);
+  }
+}
+
 // u_j = row_j . x for the atom's tokens, read straight from the per-atom rows
 // (L2) while the operand copies are in flight: two threads per token j =
 // tid / 2 (alternate 4-column chunks, then one shuffle), zero for padding
@@ -195,8 +218,7 @@ __global__ void __launch_bounds__(kThreads) pooled_fwd(const PParams P) {
     const int kc = key_count(a, n);
     for (int hh = 0; hh < H; ++hh) {
       if (hh > 0) __syncthreads();  // the previous head is done with shared memory
-      load_rows_async<DP>(sQ, a.qkv + (int64_t)hh * d, sRow, d, vec);
-      load_rows_async<DP>(sK, a.qkv + C + (int64_t)hh * d, sRow, d, vec);
+      load_rows2_async<DP>(sQ, a.qkv + (int64_t)hh * d, sK, a.qkv + C + (int64_t)hh * d, sRow, d, vec);
       load_key_row(sB, a.bias, n, hh, k, H);
       cp_async_commit();
       cp_async_wait<0>();
@@ -273,8 +295,7 @@ __global__ void __launch_bounds__(kThreads, 10) pooled_bwd1(const PParams P) {
     for (int hh = 0; hh < H; ++hh) {
       if (hh > 0) __syncthreads();
       const float* hq = a.qkv + (int64_t)hh * d;
-      load_rows_async<DP>(sQ, hq, sRow, d, vec);
-      load_rows_async<DP>(sK, hq + C, sRow, d, vec);
+      load_rows2_async<DP>(sQ, hq, sK, hq + C, sRow, d, vec);
       cp_async_commit();
       load_key_row(sB, a.bias, n, hh, k, H);
       if (threadIdx.x < KP) {
@@ -381,10 +402,8 @@ __global__ void __launch_bounds__(kThreads) pooled_bwd2(const PParams P) {
       if (hh > 0) __syncthreads();
       const float* hq = a.qkv + (int64_t)hh * d;
       const float* nq = a.hqkv + (int64_t)hh * d;
-      load_rows_async<DP>(sQ, hq, sRow, d, vec);
-      load_rows_async<DP>(sK, hq + C, sRow, d, vec);
-      load_rows_async<DP>(sHQ, nq, sRow, d, vec);
-      load_rows_async<DP>(sHK, nq + C, sRow, d, vec);
+      load_rows2_async<DP>(sQ, hq, sK, hq + C, sRow, d, vec);
+      load_rows2_async<DP>(sHQ, nq, sHK, nq + C, sRow, d, vec);
       cp_async_commit();
       load_key_row(sB, a.bias, n, hh, k, H);
       load_key_row(sHB, a.hbias, n, hh, k, H);
