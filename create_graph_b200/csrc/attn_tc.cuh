@@ -607,19 +607,24 @@ template <int DP, bool X3>
 __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
   using L = Layout<DP>;
   extern __shared__ __align__(16) float smem[];
+  // grad_logits, d_grad_probs and d_scores, which only the key products
+  // need, take the slots of k, v and hk, dead after the row products; those
+  // slots hold the larger of a k x d operand and a k x k matrix
+  constexpr int SLOT = L::OP > L::KK ? L::OP : L::KK;
   float* sQ = smem;
   float* sK = sQ + L::OP;
-  float* sV = sK + L::OP;
-  float* sG = sV + L::OP;
+  float* sV = sK + SLOT;
+  float* sG = sV + SLOT;
   float* sHQ = sG + L::OP;
   float* sHK = sHQ + L::OP;
-  float* sHV = sHK + L::OP;
-  float* sP = sHV + L::OP;
-  float* sDG = sP + L::KK;
-  float* sGL = sDG + L::KK;  // bias tile, then grad_logits
-  float* sDS = sGL + L::KK;  // hb tile, then d_scores
-  float* sLse = sDS + L::KK;
+  float* sHV = sHK + SLOT;
+  float* sBias = sHV + L::OP;  // bias tile
+  float* sHb = sBias + L::KK;  // hb tile
+  float* sLse = sHb + L::KK;
   int32_t* sIdx = reinterpret_cast<int32_t*>(sLse + KP);
+  float* sGL = sK;
+  float* sDG = sV;
+  float* sDS = sHK;
   const cg_edge_attn_args& a = P.a;
   const int k = a.k, d = a.d;
   const float scale = (float)a.scale;
@@ -635,12 +640,12 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
     load_op_async<DP>(sK, a.k_, n, h, k, d, vec, tix);
     load_op_async<DP>(sG, a.grad_out, n, h, k, d, vec);
     load_op_async<DP>(sV, a.v, n, h, k, d, vec, tix);
-    const int brow = load_bias(sGL, a.bias, P.bias_mode, n, h, k);
+    const int brow = load_bias(sBias, a.bias, P.bias_mode, n, h, k);
     cp_async_commit();
     load_op_async<DP>(sHQ, a.hq, n, h, k, d, vec, tix);
     load_op_async<DP>(sHK, a.hk, n, h, k, d, vec, tix);
     load_op_async<DP>(sHV, a.hv, n, h, k, d, vec, tix);
-    const int hrow = load_bias(sDS, a.hb, P.hb_mode, n, h, k);
+    const int hrow = load_bias(sHb, a.hb, P.hb_mode, n, h, k);
     cp_async_commit();
     if (threadIdx.x < KP)
       sLse[threadIdx.x] = threadIdx.x < k ? reinterpret_cast<const float*>(a.lse)[s * k + threadIdx.x] : 0.0f;
@@ -652,7 +657,7 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
       zero(A);  // scores
       zero(B);  // grad_probs = grad_out v^T
       band_mma2<X3, 4, DP / 8>(A, CG_A_ROWS(sQ), CG_B_ROWS(sK), B, CG_A_ROWS(sG), CG_B_ROWS(sV), g, t);
-      band_softmax<!X3>(p, A, sGL, brow, band, g, t, scale, kc, sLse, lse);
+      band_softmax<!X3>(p, A, sBias, brow, band, g, t, scale, kc, sLse, lse);
       float rs[2];
       row_dot(rs, p, B);
       float cen[4][4];
@@ -670,7 +675,7 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
       for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
-          const float2 hb = ld2(sDS, kk((band * 16 + g + 8 * half) & hrow, nt * 8 + 2 * t));
+          const float2 hb = ld2(sHb, kk((band * 16 + g + 8 * half) & hrow, nt * 8 + 2 * t));
           A[nt][2 * half] = scale * A[nt][2 * half] + hb.x;
           A[nt][2 * half + 1] = scale * A[nt][2 * half + 1] + hb.y;
         }
@@ -695,11 +700,6 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
           A[nt][e] = p[nt][e] * (B[nt][e] - rs2[e >> 1]);  // d_scores
           cen[nt][e] = p[nt][e] * cen[nt][e];              // grad_logits
         }
-      __syncthreads();  // every warp is done with the bias and hb tiles
-      put_band(sP, p, band, g, t);
-      put_band(sDG, dg, band, g, t);
-      put_band(sGL, cen, band, g, t);
-      put_band(sDS, A, band, g, t);
       // row products with A straight from the fragments
       float DQ[DP / 8][4], DGO[DP / 8][4];
       zero(DQ);   // grad_q = scale * (grad_logits hk + d_scores k)
@@ -708,6 +708,10 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
       band_mma_reg2<X3, DP / 8>(DQ, A, CG_B_COLS(sK), DGO, p, CG_B_COLS(sHV), g, t);
       store_band<DP / 8>(a.dq, n, h, band, k, d, DQ, g, t, scale, vec);
       store_band<DP / 8>(a.dgrad_out, n, h, band, k, d, DGO, g, t, 1.0f, vec);
+      __syncthreads();  // both warps are done with k, v and hk
+      put_band(sDG, dg, band, g, t);
+      put_band(sGL, cen, band, g, t);
+      put_band(sDS, A, band, g, t);
     }
     __syncthreads();
     {
@@ -735,7 +739,7 @@ inline int smem_bytes(int which) {
   switch (which) {
     case 0: return (3 * L::OP + L::KK + KP) * 4;
     case 1: return (4 * L::OP + 2 * L::KK + 2 * KP) * 4;
-    default: return (7 * L::OP + 4 * L::KK + 2 * KP) * 4;
+    default: return (4 * L::OP + 3 * (L::OP > L::KK ? L::OP : L::KK) + 2 * L::KK + 2 * KP) * 4;
   }
 }
 
