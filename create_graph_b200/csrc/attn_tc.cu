@@ -59,6 +59,15 @@ int launch(int which, const cg_edge_attn_args& a, int dbias_mode, int ki, int kj
   P.kj = kj;
   // 16-byte operand loads need rows of exactly the padded width
   P.vec_ok = vec_ok && a.d == dp;
+  {
+    // the operands this kernel reads (null ones excepted) share their strides
+    const cg_mat* mats[7] = {&a.q, &a.k_, &a.v, &a.grad_out, &a.hq, &a.hk, &a.hv};
+    const int used = which == 0 ? 3 : which == 1 ? 4 : 7;
+    bool same = P.vec_ok && a.token_index == nullptr;
+    for (int i = 1; i < used && same; ++i)
+      same = mats[i]->ptr != nullptr && mats[i]->sn == a.q.sn && mats[i]->sh == a.q.sh && mats[i]->sr == a.q.sr;
+    P.same = same ? 1 : 0;
+  }
   P.bias_mode = bias_mode(a.bias, a.k);
   P.hb_mode = bias_mode(a.hb, a.k);
   // full-tile dbias in 16-byte stores: contiguous aligned rows (dbias, or the

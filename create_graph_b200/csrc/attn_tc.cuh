@@ -54,6 +54,7 @@ struct Params {
   int vec_ok;
   int bias_mode, hb_mode;
   int dbias_vec;  // full-tile dbias rows leave in 16-byte stores
+  int same;       // 16-byte rows, no token index, and every k x d operand with the same strides
 };
 
 // per-slice dbias partials -> dbias, when the bias broadcasts over n or h
@@ -263,6 +264,28 @@ __device__ __forceinline__ void load_op_async(float* s, const cg_mat& m, int64_t
       const int r = f / DP, c = f % DP;
       const float* row = op_row(m, idx, n, h, r, k);
       s[L::op(r, c)] = (row && c < d) ? row[c] : 0.0f;
+    }
+  }
+}
+
+// Several k x d operands with the same strides (and no token index) in one
+// pass: the row offset, destination and predicate of a 16-byte chunk are
+// computed once for all of them.
+template <int DP, int NOPS>
+__device__ __forceinline__ void load_same_async(float* const (&s)[NOPS], const cg_mat (&m)[NOPS], int64_t n,
+                                                int64_t h, int k) {
+  using L = Layout<DP>;
+  constexpr int VPR = DP / 4;
+  const int64_t slice = n * m[0].sn + h * m[0].sh;
+  for (int f = threadIdx.x; f < KP * VPR; f += kThreads) {
+    const int r = f / VPR, c = (f % VPR) * 4;
+    const bool ok = r < k;
+    const int64_t off = slice + (int64_t)r * m[0].sr + c;
+    const int so = L::op(r, c);
+#pragma unroll
+    for (int i = 0; i < NOPS; ++i) {
+      const float* base = reinterpret_cast<const float*>(m[i].ptr);
+      cp_async16(s[i] + so, ok ? base + off : base, ok ? 16 : 0);
     }
   }
 }
@@ -508,8 +531,12 @@ __global__ void __launch_bounds__(kThreads) fwd1_tc(const Params P) {
     const int64_t n = s / a.h, h = s % a.h;
     __syncthreads();
     const int32_t* tix = stage_index(sIdx, a.token_index, n, k);
-    load_op_async<DP>(sQ, a.q, n, h, k, d, vec, tix);
-    load_op_async<DP>(sK, a.k_, n, h, k, d, vec, tix);
+    if (P.same) {
+      load_same_async<DP, 2>({sQ, sK}, {a.q, a.k_}, n, h, k);
+    } else {
+      load_op_async<DP>(sQ, a.q, n, h, k, d, vec, tix);
+      load_op_async<DP>(sK, a.k_, n, h, k, d, vec, tix);
+    }
     const int brow = load_bias(sP, a.bias, P.bias_mode, n, h, k);
     cp_async_commit();
     load_op_async<DP>(sV, a.v, n, h, k, d, vec, tix);
@@ -559,10 +586,14 @@ __global__ void __launch_bounds__(kThreads) bwd1_tc(const Params P) {
     const int64_t n = s / a.h, h = s % a.h;
     __syncthreads();
     const int32_t* tix = stage_index(sIdx, a.token_index, n, k);
-    load_op_async<DP>(sQ, a.q, n, h, k, d, vec, tix);
-    load_op_async<DP>(sK, a.k_, n, h, k, d, vec, tix);
-    load_op_async<DP>(sV, a.v, n, h, k, d, vec, tix);
-    load_op_async<DP>(sG, a.grad_out, n, h, k, d, vec);
+    if (P.same) {
+      load_same_async<DP, 4>({sQ, sK, sV, sG}, {a.q, a.k_, a.v, a.grad_out}, n, h, k);
+    } else {
+      load_op_async<DP>(sQ, a.q, n, h, k, d, vec, tix);
+      load_op_async<DP>(sK, a.k_, n, h, k, d, vec, tix);
+      load_op_async<DP>(sV, a.v, n, h, k, d, vec, tix);
+      load_op_async<DP>(sG, a.grad_out, n, h, k, d, vec);
+    }
     const int brow = load_bias(sGL, a.bias, P.bias_mode, n, h, k);
     cp_async_commit();
     if (threadIdx.x < KP)
@@ -636,15 +667,23 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
     __syncthreads();
     const int32_t* tix = stage_index(sIdx, a.token_index, n, k);
     // operands in the order the products need them, two cp.async groups
-    load_op_async<DP>(sQ, a.q, n, h, k, d, vec, tix);
-    load_op_async<DP>(sK, a.k_, n, h, k, d, vec, tix);
-    load_op_async<DP>(sG, a.grad_out, n, h, k, d, vec);
-    load_op_async<DP>(sV, a.v, n, h, k, d, vec, tix);
+    if (P.same) {
+      load_same_async<DP, 4>({sQ, sK, sG, sV}, {a.q, a.k_, a.grad_out, a.v}, n, h, k);
+    } else {
+      load_op_async<DP>(sQ, a.q, n, h, k, d, vec, tix);
+      load_op_async<DP>(sK, a.k_, n, h, k, d, vec, tix);
+      load_op_async<DP>(sG, a.grad_out, n, h, k, d, vec);
+      load_op_async<DP>(sV, a.v, n, h, k, d, vec, tix);
+    }
     const int brow = load_bias(sBias, a.bias, P.bias_mode, n, h, k);
     cp_async_commit();
-    load_op_async<DP>(sHQ, a.hq, n, h, k, d, vec, tix);
-    load_op_async<DP>(sHK, a.hk, n, h, k, d, vec, tix);
-    load_op_async<DP>(sHV, a.hv, n, h, k, d, vec, tix);
+    if (P.same) {
+      load_same_async<DP, 3>({sHQ, sHK, sHV}, {a.hq, a.hk, a.hv}, n, h, k);
+    } else {
+      load_op_async<DP>(sHQ, a.hq, n, h, k, d, vec, tix);
+      load_op_async<DP>(sHK, a.hk, n, h, k, d, vec, tix);
+      load_op_async<DP>(sHV, a.hv, n, h, k, d, vec, tix);
+    }
     const int hrow = load_bias(sHb, a.hb, P.hb_mode, n, h, k);
     cp_async_commit();
     if (threadIdx.x < KP)
