@@ -308,10 +308,10 @@ def attn_bytes(info, name):
 # capture of each kernel at a smaller size; traffic grows with the atoms a launch
 # processes, so a launch's traffic is this figure times its atoms.
 TRAFFIC_PER_ATOM = {
-    "cg_pooled_attn_bwd1": (66.736896e6 + 333.938688e6) / 2048,  # 12 heads x 30 tokens x 64 dims, tf32
+    "cg_pooled_attn_bwd1": (53.767680e6 + 329.964032e6) / 2048,  # 12 heads x 30 tokens x 64 dims, tf32
 }
 # the edge-attention backward2 microbenchmark kernel, 8 heads x 32 tokens x 32 dims, tf32
-EDGE_BWD2_TRAFFIC_PER_ATOM = (303.151360e6 + 134.537728e6) / 1024
+EDGE_BWD2_TRAFFIC_PER_ATOM = (303.211264e6 + 133.112064e6) / 1024
 
 
 def pooled_attn_bytes(info, name):
