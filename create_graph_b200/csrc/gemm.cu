@@ -2,7 +2,7 @@
 // with kind::tf32 UMMA (fp32 in, fp32 accumulate in TMEM).
 //
 // Persistent: one CTA per SM walks the BM x BN output tiles (BM = 128,
-// BN in {16, 32, 64, 128, 256}) and k-splits:
+// BN in {16, 32, 64, 128, 192, 256}) and k-splits:
 //   warp 0        TMA producer: A and B k-slices of 32 fp32 (128 B, 128B
 //                 swizzle) into a ring of STAGES shared-memory stages;
 //   warp 1        allocates TMEM (two accumulators); one thread issues 4 UMMAs
@@ -138,7 +138,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + BN - 1) / BN;
   const int ktiles_all = (K + BK - 1) / BK;
   const int items = m_tiles * n_tiles * splits;
-  constexpr uint32_t kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+  // tcgen05.alloc takes a power of two of at least 32 columns
+  constexpr uint32_t kTmemCols = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -376,8 +377,23 @@ static Plan plan_of(const cg_gemm_args& g) {
   if (g.n <= 16 && !g.b_mn_major) p.bn = 16;
   else if (g.n <= 32) p.bn = 32;
   else if (g.n <= 64) p.bn = 64;
-  else if (g.n >= 256 && (mt * ceil_div<int64_t>(g.n, 256) >= sms || ktiles >= 32)) p.bn = 256;
-  else p.bn = 128;
+  else if (g.n >= 256 && mt * ceil_div<int64_t>(g.n, 256) < sms && ktiles >= 32) p.bn = 256;  // split K below
+  else if (g.n >= 192) {
+    // the width whose waves of tiles take the least time: waves x width,
+    // narrower tiles weighted for their lower flops per operand byte
+    const int widths[3] = {256, 192, 128};
+    const double weight[3] = {1.0, 1.05, 1.15};
+    double best = 0.0;
+    for (int i = 0; i < 3; ++i) {
+      if (g.n < widths[i]) continue;
+      const int64_t waves = ceil_div<int64_t>(mt * ceil_div<int64_t>(g.n, widths[i]), sms);
+      const double cost = (double)waves * widths[i] * weight[i];
+      if (best == 0.0 || cost < best) {
+        best = cost;
+        p.bn = widths[i];
+      }
+    }
+  } else p.bn = 128;
   const int64_t tiles = mt * ceil_div<int64_t>(g.n, p.bn);
   int64_t splits = 1;
   if (tiles < sms && ktiles >= 8) {
@@ -480,6 +496,7 @@ static int run(const cg_gemm_args* args, void* stream) {
     case 32: return launch_majors<32, 9>(g, p, s);
     case 64: return launch_majors<64, 8>(g, p, s);
     case 128: return launch_majors<128, 6>(g, p, s);
+    case 192: return launch_majors<192, 5>(g, p, s);
     default: return launch_majors<256, 4>(g, p, s);
   }
 }

@@ -39,7 +39,7 @@ def operands(m, n, k, a_t, b_t, seed=0):
 @pytest.mark.parametrize(
     "mnk",
     [(128, 64, 32), (300, 200, 100), (1000, 2304, 768), (768, 768, 4100), (77, 3072, 768), (12, 128, 20000),
-     (128, 12, 20000), (5000, 12, 128), (5000, 128, 12), (40, 24, 300)],
+     (128, 12, 20000), (5000, 12, 128), (5000, 128, 12), (40, 24, 300), (8280, 768, 768)],
 )
 def test_layouts_and_sizes(a_t, b_t, mnk):
     m, n, k = mnk
