@@ -63,6 +63,10 @@ namespace seg {
 // Row chunking of the two-pass column reductions (segment.cu): `chunks`
 // partial rows of `cols` floats each.
 void colsum_plan(int64_t rows, int64_t cols, int64_t* chunks, int64_t* rows_per);
+// 16-byte column sums (b null) or column dot products of contiguous (rows, cols)
+// matrices into partial[chunk, c]; false (nothing launched) when not 16-byte aligned
+bool colsum4_launch(const float* a, const float* b, int64_t rows, int64_t cols, int64_t chunks, int64_t rows_per,
+                    float* partial, cudaStream_t s);
 }  // namespace seg
 
 }  // namespace cg

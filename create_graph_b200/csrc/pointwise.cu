@@ -305,8 +305,10 @@ int cg_coldot(const float* a, const float* b, int64_t rows, int64_t cols, float*
   CG_REQUIRE(a && b && out && scratch, "coldot: null pointer");
   int64_t chunks, per;
   cg::seg::colsum_plan(rows, cols, &chunks, &per);
-  dim3 grid((unsigned)ceil_div<int64_t>(cols, 32), (unsigned)chunks);
-  pw::coldot_partial_kernel<<<grid, 256, 0, as_stream(stream)>>>(a, b, rows, cols, per, scratch);
+  if (!cg::seg::colsum4_launch(a, b, rows, cols, chunks, per, scratch, as_stream(stream))) {
+    dim3 grid((unsigned)ceil_div<int64_t>(cols, 32), (unsigned)chunks);
+    pw::coldot_partial_kernel<<<grid, 256, 0, as_stream(stream)>>>(a, b, rows, cols, per, scratch);
+  }
   CG_LAUNCHED("coldot_partial");
   pw::partial_final_kernel<<<(unsigned)ceil_div<int64_t>(cols, 256), 256, 0, as_stream(stream)>>>(
       scratch, chunks, cols, out, accumulate != 0);

@@ -197,13 +197,82 @@ __global__ void colsum_partial_kernel(const float* __restrict__ src, int64_t ld,
   }
 }
 
+// Column sums (b == null) or column dot products (sum_r a[r, c] b[r, c]) of
+// 16-byte rows over one chunk of rows: partial[chunk, c]. A lane owns four
+// columns; the 8 warps of a block take interleaved rows, four rows in flight
+// per thread; matrices narrower than 128 columns pack 32 / (cols / 4) rows into
+// one warp step. The block's lanes are then summed in a fixed order (warp,
+// packed row), so results are reproducible.
+__global__ void colsum4_partial_kernel(const float* __restrict__ a, const float* __restrict__ b, int64_t lda,
+                                       int64_t ldb, int64_t rows, int cols4, int64_t rows_per,
+                                       float* __restrict__ partial) {
+  __shared__ float4 red[8][32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int span = cols4 < 32 ? cols4 : 32;  // float4 columns a warp covers per row
+  const int pack = 32 / span;                // rows per warp step
+  const int rr = lane / span, c4 = blockIdx.x * 32 + lane % span;
+  const bool active = rr < pack && c4 < cols4;
+  const int64_t r0 = blockIdx.y * rows_per;
+  const int64_t r1 = r0 + rows_per < rows ? r0 + rows_per : rows;
+  const int64_t step = 8 * (int64_t)pack;
+  float4 acc[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) acc[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  if (active) {
+    int64_t r = r0 + w * pack + rr;
+    for (; r + 3 * step < r1; r += 4 * step) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        float4 x = __ldg(reinterpret_cast<const float4*>(a + (r + u * step) * lda) + c4);
+        if (b != nullptr) {
+          const float4 y = __ldg(reinterpret_cast<const float4*>(b + (r + u * step) * ldb) + c4);
+          x.x *= y.x; x.y *= y.y; x.z *= y.z; x.w *= y.w;
+        }
+        acc[u].x += x.x; acc[u].y += x.y; acc[u].z += x.z; acc[u].w += x.w;
+      }
+    }
+    for (; r < r1; r += step) {
+      float4 x = __ldg(reinterpret_cast<const float4*>(a + r * lda) + c4);
+      if (b != nullptr) {
+        const float4 y = __ldg(reinterpret_cast<const float4*>(b + r * ldb) + c4);
+        x.x *= y.x; x.y *= y.y; x.z *= y.z; x.w *= y.w;
+      }
+      acc[0].x += x.x; acc[0].y += x.y; acc[0].z += x.z; acc[0].w += x.w;
+    }
+  }
+  float4 tot;
+  tot.x = (acc[0].x + acc[1].x) + (acc[2].x + acc[3].x);
+  tot.y = (acc[0].y + acc[1].y) + (acc[2].y + acc[3].y);
+  tot.z = (acc[0].z + acc[1].z) + (acc[2].z + acc[3].z);
+  tot.w = (acc[0].w + acc[1].w) + (acc[2].w + acc[3].w);
+  red[w][lane] = tot;
+  __syncthreads();
+  if ((int)threadIdx.x < span) {
+    const int cc = blockIdx.x * 32 + threadIdx.x;
+    if (cc < cols4) {
+      float4 sum = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      for (int ww = 0; ww < 8; ++ww)
+        for (int q = 0; q < pack; ++q) {
+          const float4 v = red[ww][q * span + threadIdx.x];
+          sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+        }
+      reinterpret_cast<float4*>(partial + blockIdx.y * (int64_t)cols4 * 4)[cc] = sum;
+    }
+  }
+}
+
 __global__ void colsum_final_kernel(const float* __restrict__ partial, int64_t chunks, int64_t cols,
                                     float* __restrict__ out, bool accumulate) {
   const int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (c >= cols) return;
-  float s = 0.0f;
-  for (int64_t k = 0; k < chunks; ++k) s += partial[k * cols + c];
-  out[c] = accumulate ? out[c] + s : s;
+  float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  int64_t k = 0;
+  for (; k + 3 < chunks; k += 4)
+#pragma unroll
+    for (int u = 0; u < 4; ++u) s[u] += partial[(k + u) * cols + c];
+  for (; k < chunks; ++k) s[0] += partial[k * cols + c];
+  const float t = (s[0] + s[1]) + (s[2] + s[3]);
+  out[c] = accumulate ? out[c] + t : t;
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -215,21 +284,38 @@ static int grid_for_warps(int64_t items) {
 }
 
 void colsum_plan(int64_t rows, int64_t cols, int64_t* chunks, int64_t* rows_per) {
-  // enough row chunks to fill the GPU, each at least 64 rows
-  const int64_t col_blocks = ceil_div<int64_t>(cols, kColTile);
-  int64_t want = ceil_div<int64_t>((int64_t)sm_count() * 8, col_blocks);
+  // enough row chunks of 128-column blocks for ~16 blocks per SM, each chunk
+  // at least 64 rows, at most 512 chunks (the final pass reads them all)
+  const int64_t col_blocks = ceil_div<int64_t>(cols, 128);
+  int64_t want = ceil_div<int64_t>((int64_t)sm_count() * 16, col_blocks);
+  if (want > 512) want = 512;
   int64_t per = ceil_div<int64_t>(rows, want < 1 ? 1 : want);
   if (per < 64) per = 64;
   *rows_per = per;
   *chunks = ceil_div<int64_t>(rows, per);
 }
 
+bool colsum4_launch(const float* a, const float* b, int64_t rows, int64_t cols, int64_t chunks, int64_t rows_per,
+                    float* partial, cudaStream_t s) {
+  if (cols % 4 != 0 || !aligned16(a) || (b != nullptr && !aligned16(b)) || !aligned16(partial)) return false;
+  const int cols4 = (int)(cols / 4);
+  dim3 grid((unsigned)(cols4 < 32 ? 1 : ceil_div<int64_t>(cols4, 32)), (unsigned)chunks);
+  colsum4_partial_kernel<<<grid, 256, 0, s>>>(a, b, cols, cols, rows, cols4, rows_per, partial);
+  return true;
+}
+
 int colsum_launch(const float* src, int64_t ld, int64_t rows, int64_t cols, float* out, int accumulate,
                   float* partial, cudaStream_t s) {
   int64_t chunks, per;
   colsum_plan(rows, cols, &chunks, &per);
-  dim3 grid((unsigned)ceil_div<int64_t>(cols, kColTile), (unsigned)chunks);
-  colsum_partial_kernel<<<grid, 256, 0, s>>>(src, ld, rows, cols, per, partial);
+  if (cols % 4 == 0 && ld % 4 == 0 && aligned16(src) && aligned16(partial)) {
+    const int cols4 = (int)(cols / 4);
+    dim3 grid((unsigned)(cols4 < 32 ? 1 : ceil_div<int64_t>(cols4, 32)), (unsigned)chunks);
+    colsum4_partial_kernel<<<grid, 256, 0, s>>>(src, nullptr, ld, 0, rows, cols4, per, partial);
+  } else {
+    dim3 grid((unsigned)ceil_div<int64_t>(cols, kColTile), (unsigned)chunks);
+    colsum_partial_kernel<<<grid, 256, 0, s>>>(src, ld, rows, cols, per, partial);
+  }
   CG_LAUNCHED("colsum_partial");
   colsum_final_kernel<<<(unsigned)ceil_div<int64_t>(cols, 256), 256, 0, s>>>(partial, chunks, cols, out,
                                                                                accumulate != 0);

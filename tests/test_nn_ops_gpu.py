@@ -239,3 +239,19 @@ def test_segment_sum_long_segments(cols):
     terms = (w.double()[:, :, None] * src.double().repeat_interleave(8, 0).view(e, 4, 8)).view(e, 32)
     want2 = torch.zeros(n, 32, dtype=torch.float64, device="cuda").index_add(0, index[keep].long(), terms[keep])
     assert torch.allclose(out.double(), want2, rtol=1e-5, atol=1e-4)
+
+
+@pytest.mark.parametrize("rows,cols", [(248400, 12), (8280, 768), (3001, 132), (777, 130), (5, 3072)])
+def test_colsum_coldot_shapes(rows, cols):
+    """Column sums and column dot products: packed narrow rows, full 128-column
+    blocks, a partial block, the scalar path (columns not a multiple of 4) and
+    fewer rows than warps; bitwise repeatable."""
+    a, b = randn(rows, cols, seed=23), randn(rows, cols, seed=24)
+    s1, s2 = cgnn.ColSum.apply(a), cgnn.ColSum.apply(a)
+    d1, d2 = cgnn.ColDot.apply(a, b), cgnn.ColDot.apply(a, b)
+    assert torch.equal(s1, s2) and torch.equal(d1, d2)
+    want_s = a.double().sum(0)
+    want_d = (a.double() * b.double()).sum(0)
+    scale = rows ** 0.5
+    assert (s1.double() - want_s).abs().max().item() < 1e-5 * scale
+    assert (d1.double() - want_d).abs().max().item() < 1e-5 * scale
