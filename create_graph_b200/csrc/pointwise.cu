@@ -13,7 +13,9 @@
 namespace cg {
 namespace pw {
 
-__device__ inline float sigm(float z) { return 1.0f / (1.0f + expf(-z)); }
+// logistic sigmoid with the hardware-approximated exp and division (relative
+// error ~1e-6), as in the GEMM's SiLU epilogue; exp(-z) = inf gives 0
+__device__ inline float sigm(float z) { return __fdividef(1.0f, 1.0f + __expf(-z)); }
 // silu(z) = z s, silu' = s (1 + z (1 - s)), silu'' = s (1 - s) (2 + z (1 - 2 s))
 __device__ inline float silu_d1(float z) {
   const float s = sigm(z);
@@ -35,6 +37,8 @@ inline bool vec_ok(const float* a, const float* b, int64_t cols) {
   return (cols & 3) == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0 && (reinterpret_cast<uintptr_t>(b) & 15) == 0;
 }
 
+inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 inline int blocks_for(int64_t n, int threads) {
   const int64_t b = ceil_div<int64_t>(n, threads);
   const int64_t cap = (int64_t)sm_count() * 32;
@@ -49,6 +53,43 @@ __global__ void silu_grad_kernel(const float* __restrict__ a, const float* __res
        i += (int64_t)gridDim.x * blockDim.x) {
     out[i] = mode == 0 ? a[i] * silu_d1(z[i]) : a[i] * b[i] * silu_d2(z[i]);
   }
+}
+
+// float4 version of silu_grad_kernel (n4 = n / 4 groups, 16-byte aligned)
+__global__ void silu_grad4_kernel(const float4* __restrict__ a, const float4* __restrict__ b,
+                                  const float4* __restrict__ z, float4* __restrict__ out, int64_t n4, int mode) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 x = __ldg(a + i), zz = __ldg(z + i);
+    float4 y;
+    if (mode == 0) {
+      y = make_float4(x.x * silu_d1(zz.x), x.y * silu_d1(zz.y), x.z * silu_d1(zz.z), x.w * silu_d1(zz.w));
+    } else {
+      const float4 bb = __ldg(b + i);
+      y = make_float4(x.x * bb.x * silu_d2(zz.x), x.y * bb.y * silu_d2(zz.y), x.z * bb.z * silu_d2(zz.z),
+                      x.w * bb.w * silu_d2(zz.w));
+    }
+    out[i] = y;
+  }
+}
+
+// float4 version of scale_shift_kernel: blocks walk rows, threads the row's
+// 16-byte column groups (no per-element index division)
+__global__ void scale_shift4_kernel(const float4* __restrict__ x, const float4* __restrict__ gamma,
+                                    const float4* __restrict__ beta, float4* __restrict__ out, int64_t rows,
+                                    int cols4) {
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x)
+    for (int c = threadIdx.x; c < cols4; c += blockDim.x) {
+      float4 v = __ldg(x + r * cols4 + c);
+      if (gamma) {
+        const float4 g = __ldg(gamma + c);
+        v.x *= g.x; v.y *= g.y; v.z *= g.z; v.w *= g.w;
+      }
+      if (beta) {
+        const float4 b = __ldg(beta + c);
+        v.x += b.x; v.y += b.y; v.z += b.z; v.w += b.w;
+      }
+      out[r * cols4 + c] = v;
+    }
 }
 
 // out[r, c] = x[r, c] * (gamma ? gamma[c] : 1) + (beta ? beta[c] : 0)
@@ -269,7 +310,12 @@ using namespace cg;
 int cg_silu_grad(const float* a, const float* z, float* out, int64_t n, void* stream) {
   CG_REQUIRE(n >= 0, "silu_grad: negative size");
   if (n == 0) return kOk;
-  pw::silu_grad_kernel<<<pw::blocks_for(n, 256), 256, 0, as_stream(stream)>>>(a, nullptr, z, out, n, 0);
+  if (n % 4 == 0 && pw::al16(a) && pw::al16(z) && pw::al16(out))
+    pw::silu_grad4_kernel<<<pw::blocks_for(n / 4, 256), 256, 0, as_stream(stream)>>>(
+        reinterpret_cast<const float4*>(a), nullptr, reinterpret_cast<const float4*>(z),
+        reinterpret_cast<float4*>(out), n / 4, 0);
+  else
+    pw::silu_grad_kernel<<<pw::blocks_for(n, 256), 256, 0, as_stream(stream)>>>(a, nullptr, z, out, n, 0);
   CG_LAUNCHED("silu_grad");
   return kOk;
 }
@@ -277,7 +323,12 @@ int cg_silu_grad(const float* a, const float* z, float* out, int64_t n, void* st
 int cg_silu_grad2(const float* a, const float* b, const float* z, float* out, int64_t n, void* stream) {
   CG_REQUIRE(n >= 0, "silu_grad2: negative size");
   if (n == 0) return kOk;
-  pw::silu_grad_kernel<<<pw::blocks_for(n, 256), 256, 0, as_stream(stream)>>>(a, b, z, out, n, 1);
+  if (n % 4 == 0 && pw::al16(a) && pw::al16(b) && pw::al16(z) && pw::al16(out))
+    pw::silu_grad4_kernel<<<pw::blocks_for(n / 4, 256), 256, 0, as_stream(stream)>>>(
+        reinterpret_cast<const float4*>(a), reinterpret_cast<const float4*>(b), reinterpret_cast<const float4*>(z),
+        reinterpret_cast<float4*>(out), n / 4, 1);
+  else
+    pw::silu_grad_kernel<<<pw::blocks_for(n, 256), 256, 0, as_stream(stream)>>>(a, b, z, out, n, 1);
   CG_LAUNCHED("silu_grad2");
   return kOk;
 }
@@ -286,8 +337,16 @@ int cg_scale_shift(const float* x, const float* gamma, const float* beta, float*
                    int64_t cols, void* stream) {
   CG_REQUIRE(rows >= 0 && cols >= 0, "scale_shift: negative size");
   if (rows * cols == 0) return kOk;
-  pw::scale_shift_kernel<<<pw::blocks_for(rows * cols, 256), 256, 0, as_stream(stream)>>>(x, gamma, beta,
-                                                                                          out, rows, cols);
+  if (cols % 4 == 0 && pw::al16(x) && pw::al16(out) && (gamma == nullptr || pw::al16(gamma)) &&
+      (beta == nullptr || pw::al16(beta))) {
+    const int64_t blocks = rows < (int64_t)sm_count() * 16 ? rows : (int64_t)sm_count() * 16;
+    pw::scale_shift4_kernel<<<(unsigned)blocks, 128, 0, as_stream(stream)>>>(
+        reinterpret_cast<const float4*>(x), reinterpret_cast<const float4*>(gamma),
+        reinterpret_cast<const float4*>(beta), reinterpret_cast<float4*>(out), rows, (int)(cols / 4));
+  } else {
+    pw::scale_shift_kernel<<<pw::blocks_for(rows * cols, 256), 256, 0, as_stream(stream)>>>(x, gamma, beta, out,
+                                                                                            rows, cols);
+  }
   CG_LAUNCHED("scale_shift");
   return kOk;
 }
