@@ -316,6 +316,24 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ partial, int spli
   }
 }
 
+// The same on 16-byte column groups (ep.vec): blocks walk rows, threads the
+// row's groups, splits added in z order.
+__global__ void splitk_reduce4_kernel(const float* __restrict__ partial, int splits, int M, int N, Epilogue ep) {
+  const int64_t mn = (int64_t)M * N;
+  const int n4 = N / 4;
+  for (int64_t r = blockIdx.x; r < M; r += gridDim.x)
+    for (int c4 = threadIdx.x; c4 < n4; c4 += blockDim.x) {
+      float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      for (int z = 0; z < splits; ++z) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(partial + z * mn + r * N) + c4);
+        x.x += v.x; x.y += v.y; x.z += v.z; x.w += v.w;
+      }
+      const float4 bias =
+          ep.bias ? __ldg(reinterpret_cast<const float4*>(ep.bias) + c4) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      epilogue_store4(ep, r, 4 * c4, x, bias);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
@@ -456,10 +474,15 @@ static int launch(const cg_gemm_args& g, const Plan& p, cudaStream_t stream) {
                                                 ep);
   CG_LAUNCHED("gemm_tf32");
   if (p.splits > 1) {
-    const int64_t mn = g.m * g.n;
-    const int64_t blocks = ceil_div<int64_t>(mn, 256);
-    splitk_reduce_kernel<<<(unsigned)(blocks < 8192 ? blocks : 8192), 256, 0, stream>>>(partial, p.splits, (int)g.m,
-                                                                                        (int)g.n, ep);
+    if (ep.vec) {
+      const int64_t blocks = g.m < (int64_t)sm_count() * 16 ? g.m : (int64_t)sm_count() * 16;
+      splitk_reduce4_kernel<<<(unsigned)blocks, 128, 0, stream>>>(partial, p.splits, (int)g.m, (int)g.n, ep);
+    } else {
+      const int64_t mn = g.m * g.n;
+      const int64_t blocks = ceil_div<int64_t>(mn, 256);
+      splitk_reduce_kernel<<<(unsigned)(blocks < 8192 ? blocks : 8192), 256, 0, stream>>>(partial, p.splits,
+                                                                                          (int)g.m, (int)g.n, ep);
+    }
     CG_LAUNCHED("gemm_tf32 split-K reduction");
   }
   return kOk;

@@ -130,12 +130,23 @@ __global__ void coldot_partial_kernel(const float* __restrict__ a, const float* 
 }
 
 __global__ void partial_final_kernel(const float* __restrict__ partial, int64_t chunks, int64_t cols,
-                                     float* __restrict__ out, bool accumulate) {
-  const int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (c >= cols) return;
+                                    float* __restrict__ out, bool accumulate) {
+  // block: 32 columns x 8 warps; warp w adds chunks w, w + 8, ... of its
+  // column, then the 8 warp sums are added in warp order (fixed order)
+  __shared__ float red[8][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t c = blockIdx.x * 32ll + tx;
   float s = 0.0f;
-  for (int64_t k = 0; k < chunks; ++k) s += partial[k * cols + c];
-  out[c] = accumulate ? out[c] + s : s;
+  if (c < cols)
+    for (int64_t k = ty; k < chunks; k += 8) s += partial[k * cols + c];
+  red[ty][tx] = s;
+  __syncthreads();
+  if (ty == 0 && c < cols) {
+    float t = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += red[w][tx];
+    out[c] = accumulate ? out[c] + t : t;
+  }
 }
 
 // ---- row normalisation: xhat = (x - mean) / sqrt(var + eps) -----------------
@@ -369,7 +380,7 @@ int cg_coldot(const float* a, const float* b, int64_t rows, int64_t cols, float*
     pw::coldot_partial_kernel<<<grid, 256, 0, as_stream(stream)>>>(a, b, rows, cols, per, scratch);
   }
   CG_LAUNCHED("coldot_partial");
-  pw::partial_final_kernel<<<(unsigned)ceil_div<int64_t>(cols, 256), 256, 0, as_stream(stream)>>>(
+  pw::partial_final_kernel<<<(unsigned)ceil_div<int64_t>(cols, 32), 256, 0, as_stream(stream)>>>(
       scratch, chunks, cols, out, accumulate != 0);
   CG_LAUNCHED("coldot_final");
   return kOk;

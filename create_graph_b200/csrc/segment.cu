@@ -263,16 +263,22 @@ __global__ void colsum4_partial_kernel(const float* __restrict__ a, const float*
 
 __global__ void colsum_final_kernel(const float* __restrict__ partial, int64_t chunks, int64_t cols,
                                     float* __restrict__ out, bool accumulate) {
-  const int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (c >= cols) return;
-  float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-  int64_t k = 0;
-  for (; k + 3 < chunks; k += 4)
+  // block: 32 columns x 8 warps; warp w adds chunks w, w + 8, ... of its
+  // column, then the 8 warp sums are added in warp order (fixed order)
+  __shared__ float red[8][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t c = blockIdx.x * 32ll + tx;
+  float s = 0.0f;
+  if (c < cols)
+    for (int64_t k = ty; k < chunks; k += 8) s += partial[k * cols + c];
+  red[ty][tx] = s;
+  __syncthreads();
+  if (ty == 0 && c < cols) {
+    float t = 0.0f;
 #pragma unroll
-    for (int u = 0; u < 4; ++u) s[u] += partial[(k + u) * cols + c];
-  for (; k < chunks; ++k) s[0] += partial[k * cols + c];
-  const float t = (s[0] + s[1]) + (s[2] + s[3]);
-  out[c] = accumulate ? out[c] + t : t;
+    for (int w = 0; w < 8; ++w) t += red[w][tx];
+    out[c] = accumulate ? out[c] + t : t;
+  }
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -317,7 +323,7 @@ int colsum_launch(const float* src, int64_t ld, int64_t rows, int64_t cols, floa
     colsum_partial_kernel<<<grid, 256, 0, s>>>(src, ld, rows, cols, per, partial);
   }
   CG_LAUNCHED("colsum_partial");
-  colsum_final_kernel<<<(unsigned)ceil_div<int64_t>(cols, 256), 256, 0, s>>>(partial, chunks, cols, out,
+  colsum_final_kernel<<<(unsigned)ceil_div<int64_t>(cols, 32), 256, 0, s>>>(partial, chunks, cols, out,
                                                                                accumulate != 0);
   CG_LAUNCHED("colsum_final");
   return kOk;
