@@ -33,9 +33,13 @@ static int run(int which, const cg_pooled_attn_args* args, void* stream) {
     CG_REQUIRE(a.ld_dqk >= 2 * C, "pooled_attn: ld_dqk = %lld below 2*h*d", (long long)a.ld_dqk);
   }
   if (which == 2) CG_REQUIRE(a.hqkv && a.ddout, "pooled_attn: hqkv and ddout are required");
+  CG_REQUIRE(a.ld_bias == 0 || a.ld_bias >= a.h, "pooled_attn: ld_bias = %lld below h", (long long)a.ld_bias);
+  CG_REQUIRE(a.ld_hbias == 0 || a.ld_hbias >= a.h, "pooled_attn: ld_hbias = %lld below h", (long long)a.ld_hbias);
   const int dp = a.d <= 16 ? 16 : a.d <= 32 ? 32 : 64;
   PParams P;
   P.a = a;
+  if (P.a.ld_bias == 0) P.a.ld_bias = a.h;
+  if (P.a.ld_hbias == 0) P.a.ld_hbias = a.h;
   bool vec = a.d == dp && a.ld_qkv % 4 == 0 && al16(a.qkv);
   if (which == 2) vec = vec && al16(a.hqkv);
   if (which != 0) vec = vec && a.ld_dqk % 4 == 0 && al16(a.dqk) && al16(a.dout);

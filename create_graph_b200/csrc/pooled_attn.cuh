@@ -100,10 +100,11 @@ __device__ __forceinline__ void load_tokens(float* s, const float* src, int64_t 
   if (threadIdx.x < KP) s[threadIdx.x] = (src != nullptr && (int)threadIdx.x < k) ? src[n * k + threadIdx.x] : 0.0f;
 }
 
-// key row of a per-key (n*k, h) matrix for head hh, zeros past k (or all zeros)
-__device__ __forceinline__ void load_key_row(float* s, const float* src, int64_t n, int hh, int k, int H) {
+// key row of a per-key (n*k, h) matrix (row pitch ld) for head hh, zeros past
+// k (or all zeros)
+__device__ __forceinline__ void load_key_row(float* s, const float* src, int64_t n, int hh, int k, int64_t ld) {
   if (threadIdx.x < KP)
-    s[threadIdx.x] = (src != nullptr && (int)threadIdx.x < k) ? src[(n * k + threadIdx.x) * H + hh] : 0.0f;
+    s[threadIdx.x] = (src != nullptr && (int)threadIdx.x < k) ? src[(n * k + threadIdx.x) * ld + hh] : 0.0f;
 }
 
 // Float offsets of the atom's token rows in the per-atom row matrices
@@ -219,7 +220,7 @@ __global__ void __launch_bounds__(kThreads) pooled_fwd(const PParams P) {
     for (int hh = 0; hh < H; ++hh) {
       if (hh > 0) __syncthreads();  // the previous head is done with shared memory
       load_rows2_async<DP>(sQ, a.qkv + (int64_t)hh * d, sK, a.qkv + C + (int64_t)hh * d, sRow, d, vec);
-      load_key_row(sB, a.bias, n, hh, k, H);
+      load_key_row(sB, a.bias, n, hh, k, a.ld_bias);
       cp_async_commit();
       cp_async_wait<0>();
       __syncthreads();
@@ -297,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 10) pooled_bwd1(const PParams P) {
       const float* hq = a.qkv + (int64_t)hh * d;
       load_rows2_async<DP>(sQ, hq, sK, hq + C, sRow, d, vec);
       cp_async_commit();
-      load_key_row(sB, a.bias, n, hh, k, H);
+      load_key_row(sB, a.bias, n, hh, k, a.ld_bias);
       if (threadIdx.x < KP) {
         const int i = threadIdx.x;
         sLse[i] = i < k ? a.lse[(n * H + hh) * k + i] : INFINITY;
@@ -405,8 +406,8 @@ __global__ void __launch_bounds__(kThreads) pooled_bwd2(const PParams P) {
       load_rows2_async<DP>(sQ, hq, sK, hq + C, sRow, d, vec);
       load_rows2_async<DP>(sHQ, nq, sHK, nq + C, sRow, d, vec);
       cp_async_commit();
-      load_key_row(sB, a.bias, n, hh, k, H);
-      load_key_row(sHB, a.hbias, n, hh, k, H);
+      load_key_row(sB, a.bias, n, hh, k, a.ld_bias);
+      load_key_row(sHB, a.hbias, n, hh, k, a.ld_hbias);
       if (threadIdx.x < KP) {
         const int i = threadIdx.x;
         sLse[i] = i < k ? a.lse[(n * H + hh) * k + i] : INFINITY;

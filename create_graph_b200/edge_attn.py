@@ -367,6 +367,11 @@ def token_attention_backward2(qkv, bias, lse, g, h_qkv, h_bias, index, counts, k
 # ---------------------------------------------------------------------------
 
 
+def _rows(t: Tensor) -> Tensor:
+    """t itself when its columns are contiguous (rows may be strided), else a copy."""
+    return t if t.stride(-1) == 1 and t.stride(0) >= t.shape[-1] else t.contiguous()
+
+
 def _pooled_args(qkv, bias, env, index, counts, k, heads, scale, precision):
     native.require_cuda(qkv, bias, env, counts, index)
     if qkv.dtype != torch.float32 or bias.dtype != torch.float32 or env.dtype != torch.float32:
@@ -376,7 +381,7 @@ def _pooled_args(qkv, bias, env, index, counts, k, heads, scale, precision):
     n = counts.shape[0]
     d = qkv.shape[1] // (3 * heads)
     if (qkv.shape[1] != 3 * heads * d or index.numel() != n * k or tuple(bias.shape) != (n * k, heads)
-            or env.numel() != n * k or qkv.stride(1) != 1):
+            or bias.stride(1) != 1 or env.numel() != n * k or qkv.stride(1) != 1):
         raise NativeError(
             f"pooled attention: qkv {tuple(qkv.shape)}, bias {tuple(bias.shape)}, env {tuple(env.shape)}, "
             f"index {index.numel()}, n {n}, k {k}, heads {heads}"
@@ -390,13 +395,15 @@ def _pooled_args(qkv, bias, env, index, counts, k, heads, scale, precision):
     a.qkv = qkv.data_ptr()
     a.ld_qkv = qkv.stride(0)
     a.bias = bias.data_ptr()
+    a.ld_bias = bias.stride(0)
     a.env = env.data_ptr()
     return a, n, d
 
 
 def pooled_attention_forward(qkv, bias, env, index, counts, k, heads, scale, precision="fp32"):
-    """(out (n, h*d), lse (n, h, k), w (n, h, k)) with w_j = sum_i env_i P_ij."""
-    qkv, bias, env = qkv.contiguous(), bias.contiguous(), env.contiguous()
+    """(out (n, h*d), lse (n, h, k), w (n, h, k)) with w_j = sum_i env_i P_ij. bias
+    may be a column block of a wider matrix (unit column stride)."""
+    qkv, bias, env = qkv.contiguous(), _rows(bias), env.contiguous()
     a, n, d = _pooled_args(qkv, bias, env, index, counts, k, heads, scale, precision)
     out = torch.empty(n, heads * d, device=qkv.device)
     lse = torch.empty(n, heads, k, device=qkv.device)
@@ -408,7 +415,7 @@ def pooled_attention_forward(qkv, bias, env, index, counts, k, heads, scale, pre
 
 def pooled_attention_backward1(qkv, bias, env, lse, w, dout, index, counts, k, heads, scale, precision="fp32"):
     """(dqk (n*k, 2*h*d) per-token [dq | dk], wv (n*k, h), dbias (n*k, h), denv (n, k))."""
-    qkv, bias, env, dout = qkv.contiguous(), bias.contiguous(), env.contiguous(), dout.contiguous()
+    qkv, bias, env, dout = qkv.contiguous(), _rows(bias), env.contiguous(), dout.contiguous()
     a, n, d = _pooled_args(qkv, bias, env, index, counts, k, heads, scale, precision)
     dqk = torch.empty(n * k, 2 * heads * d, device=qkv.device)
     wv = torch.empty(n * k, heads, device=qkv.device)
@@ -425,15 +432,17 @@ def pooled_attention_backward2(qkv, bias, env, lse, w, dout, h_qkv, h_bias, h_en
                                precision="fp32"):
     """Second derivative: (dqk, wv, dbias, denv, ddout) of <h_qkv, d_qkv> +
     <h_bias, dbias> + <h_env, denv> (h_bias, h_env may be None: zero)."""
-    qkv, bias, env, dout, h_qkv = (t.contiguous() for t in (qkv, bias, env, dout, h_qkv))
+    qkv, env, dout, h_qkv = (t.contiguous() for t in (qkv, env, dout, h_qkv))
+    bias = _rows(bias)
     a, n, d = _pooled_args(qkv, bias, env, index, counts, k, heads, scale, precision)
     if h_qkv.shape != qkv.shape or h_qkv.stride(0) != qkv.stride(0):
         raise NativeError(f"pooled attention: h_qkv {tuple(h_qkv.shape)} must match qkv {tuple(qkv.shape)}")
     keep = []
     if h_bias is not None:
-        h_bias = h_bias.contiguous()
+        h_bias = _rows(h_bias)
         keep.append(h_bias)
         a.hbias = h_bias.data_ptr()
+        a.ld_hbias = h_bias.stride(0)
     if h_env is not None:
         h_env = h_env.contiguous()
         keep.append(h_env)

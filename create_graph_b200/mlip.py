@@ -78,14 +78,15 @@ class Block(nn.Module):
         self.precision = s.attn_precision
         self.norm1 = cgnn.LayerNorm(c)
         self.qkv = cgnn.Linear(c, 3 * c)
+        # per-key attention bias from the RBF features; applied for all blocks at
+        # once by EnergyNetwork (one GEMM over the shared RBF tensor)
         self.rbf_bias = cgnn.Linear(s.n_rbf, s.heads)
         self.out = cgnn.Linear(c, c)
         self.norm2 = cgnn.LayerNorm(c)
         self.ffn1 = cgnn.Linear(c, s.ffn, silu=True)
         self.ffn2 = cgnn.Linear(s.ffn, c)
 
-    def forward(self, h: Tensor, rbf: Tensor, env: Tensor, graph: cgnn.NeighborGraph) -> Tensor:
-        bias = self.rbf_bias(rbf)
+    def forward(self, h: Tensor, bias: Tensor, env: Tensor, graph: cgnn.NeighborGraph) -> Tensor:
         # attention among the atom's edge tokens, pooled by the envelope, one fused op
         m = cgnn.PooledTokenAttention.apply(self.qkv(self.norm1(h)), bias, env, graph, self.heads, self.scale,
                                             self.precision)
@@ -108,8 +109,13 @@ class EnergyNetwork(nn.Module):
         s = self.spec
         rbf, env = cgnn.EdgeGeometry.apply(pos, graph, s.n_rbf, s.cutoff, s.rbf_gamma)
         h = cgnn.Gather.apply(self.embed, species_csr)
-        for block in self.blocks:
-            h = block(h, rbf, env, graph)
+        # every block's rbf_bias projection in one GEMM over the RBF tensor, each
+        # block then reading its column block (bias = rbf W_b^T + b_b, as per block)
+        w = torch.cat([block.rbf_bias.weight for block in self.blocks])
+        b = torch.cat([block.rbf_bias.bias for block in self.blocks])
+        biases = cgnn.SplitCols.apply(cgnn.LinearFn.apply(rbf, w, b), s.heads)
+        for block, bias in zip(self.blocks, biases):
+            h = block(h, bias, env, graph)
         e_atom = self.readout(self.norm(h))
         return cgnn.SegmentSum.apply(e_atom, system_csr).view(-1)
 

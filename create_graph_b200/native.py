@@ -129,6 +129,8 @@ class PooledAttnArgs(ctypes.Structure):
         ("dbias", vp),
         ("denv", vp),
         ("ddout", vp),
+        ("ld_bias", i64),
+        ("ld_hbias", i64),
     ]
 
 

@@ -257,6 +257,24 @@ class LinearSiluFn(_Fused):
         return _linear_backward(ctx, g, x, w, ctx.has_bias)
 
 
+class SplitCols(_Fused):
+    """The column blocks x[:, i*width:(i+1)*width] of x as views (no copy);
+    backward: the blocks' gradients side by side (one concatenation instead of
+    a zero-filled full-width gradient per block summed by the engine)."""
+
+    @staticmethod
+    def forward(ctx, x, width):
+        ctx.width = width
+        ctx.shape = x.shape
+        return tuple(x[:, i * width:(i + 1) * width] for i in range(x.shape[1] // width))
+
+    @staticmethod
+    def backward(ctx, *grads):
+        parts = [g if g is not None else torch.zeros(ctx.shape[0], ctx.width, device=grads[0].device)
+                 for g in grads]
+        return torch.cat(parts, dim=1), None
+
+
 # ---------------------------------------------------------------------------
 # Row normalisation (LayerNorm without its affine part)
 # ---------------------------------------------------------------------------

@@ -144,13 +144,13 @@ typedef struct cg_pooled_attn_args {
   const float* qkv;           /* (rows, ld_qkv): [q | k | v], heads contiguous, h*d each */
   const float* hqkv;          /* bwd2: cotangent of the q/k/v gradient, same layout */
   int64_t ld_qkv;
-  const float* bias;          /* (n*k, h) additive bias of key (n, j); NULL = none */
+  const float* bias;          /* (n*k, h) additive bias of key (n, j), row pitch ld_bias; NULL = none */
   const float* env;           /* (n, k) pooling weight of query token (n, i) */
   float* lse;                 /* (n, h, k): written by fwd, read by bwd1 / bwd2 */
   float* w;                   /* (n, h, k): w_j, written by fwd, read by bwd1 / bwd2 */
   float* out;                 /* fwd: (n, h*d) */
   const float* dout;          /* bwd1 / bwd2: (n, h*d) cotangent of out */
-  const float* hbias;         /* bwd2: (n*k, h) cotangent of dbias; NULL = 0 */
+  const float* hbias;         /* bwd2: (n*k, h) cotangent of dbias, row pitch ld_hbias; NULL = 0 */
   const float* henv;          /* bwd2: (n, k) cotangent of denv; NULL = 0 */
   float* dqk;                 /* bwd1 / bwd2: (n*k, ld_dqk) per-token [dq | dk], 2*h*d columns */
   int64_t ld_dqk;
@@ -158,6 +158,7 @@ typedef struct cg_pooled_attn_args {
   float* dbias;               /* bwd1 / bwd2: (n*k, h); NULL = skip */
   float* denv;                /* bwd1 / bwd2: (n, k), summed over heads; NULL = skip */
   float* ddout;               /* bwd2: (n, h*d) gradient w.r.t. dout */
+  int64_t ld_bias, ld_hbias;  /* row pitch (floats, >= h) of bias and hbias; 0 = h */
 } cg_pooled_attn_args;
 
 int cg_pooled_attn_fwd(const cg_pooled_attn_args* a, void* stream);

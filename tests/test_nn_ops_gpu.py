@@ -255,3 +255,31 @@ def test_colsum_coldot_shapes(rows, cols):
     scale = rows ** 0.5
     assert (s1.double() - want_s).abs().max().item() < 1e-5 * scale
     assert (d1.double() - want_d).abs().max().item() < 1e-5 * scale
+
+
+@pytest.mark.parametrize("precision,tol", [("fp32", F32_TOL), ("tf32", 5e-3)])
+def test_pooled_token_attention_strided_bias(precision, tol):
+    """The per-key bias as a column block of a wider matrix (the model's one
+    GEMM for every block's bias), read in place through its row pitch, in the
+    forward and both derivatives (the dbias cotangent arrives strided too)."""
+    n, k, heads, d = 40, 12, 4, 16
+    pos, graph = neighbor_case(n=n, k=k)
+    g = torch.Generator().manual_seed(25)
+    qkv = torch.randn(n, 3 * heads * d, generator=g).cuda()
+    bias = torch.randn(n * k, heads, generator=g).cuda()
+    env = torch.rand(n * k, generator=g).cuda()
+
+    def widen(b):
+        z = torch.zeros(b.shape[0], heads, dtype=b.dtype, device=b.device)
+        return cgnn.SplitCols.apply(torch.cat([z, b, z], dim=1), heads)[1]
+
+    def mine(q, b, e):
+        view = widen(b)
+        assert view.stride(0) == 3 * heads and view.stride(1) == 1
+        return cgnn.PooledTokenAttention.apply(q, view, e, graph, heads, 0.25, precision)
+
+    def ref(q, b, e):
+        o = ref_token_attention(q, b, graph.tokens.index, graph.counts, heads, 0.25)
+        return (e.view(n, k, 1) * o).sum(1)
+
+    check(twice_errors(mine, ref, [qkv, bias, env]), tol)
