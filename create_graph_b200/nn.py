@@ -242,6 +242,9 @@ class LinearSiluFn(_Fused):
         ctx.save_for_backward(x, w, z)
         ctx.edges = _edges(x, w, b)
         ctx.has_bias = b is not None
+        # z is usually unused: its gradient arrives as None, not as a zero-filled
+        # (rows, out) tensor added to the SiLU gradient
+        ctx.set_materialize_grads(False)
         return y, z
 
     @staticmethod
@@ -266,11 +269,15 @@ class SplitCols(_Fused):
     def forward(ctx, x, width):
         ctx.width = width
         ctx.shape = x.shape
+        ctx.set_materialize_grads(False)
         return tuple(x[:, i * width:(i + 1) * width] for i in range(x.shape[1] // width))
 
     @staticmethod
     def backward(ctx, *grads):
-        parts = [g if g is not None else torch.zeros(ctx.shape[0], ctx.width, device=grads[0].device)
+        some = next((g for g in grads if g is not None), None)
+        if some is None:
+            return None, None
+        parts = [g if g is not None else torch.zeros(ctx.shape[0], ctx.width, device=some.device, dtype=some.dtype)
                  for g in grads]
         return torch.cat(parts, dim=1), None
 
