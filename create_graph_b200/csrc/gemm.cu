@@ -41,7 +41,7 @@ struct Epilogue {
   float* c;
   int64_t ldc;
   const float* bias;    // (N,) or null
-  const float* aux_in;  // (M, N) pre-activation for the SiLU derivative, ld = ld_aux
+  const float* aux_in;  // (M, N) SiLU pre-activation (SILU_GRAD) or residual (ADD), ld = ld_aux
   float* aux_out;       // (M, N) pre-activation written by the SiLU forward, ld = ld_aux
   int64_t ld_aux;
   int act;              // CG_ACT_*
@@ -81,25 +81,39 @@ __device__ inline void epilogue_store(const Epilogue& ep, int64_t row, int col, 
     x = silu(x);
   } else if (ep.act == CG_ACT_SILU_GRAD) {
     x *= silu_grad(ep.aux_in[row * ep.ld_aux + col]);
+  } else if (ep.act == CG_ACT_ADD) {
+    x += ep.aux_in[row * ep.ld_aux + col];
   }
   float* c = ep.c + row * ep.ldc + col;
   if (ep.accumulate) x += *c;
   *c = x;
 }
 
-// Epilogue of four consecutive columns (col % 4 == 0, all in range).
-__device__ inline void epilogue_store4(const Epilogue& ep, int64_t row, int col, float4 x, float4 bias) {
+// Whether the epilogue reads aux_in (the SiLU pre-activation or the residual).
+__device__ inline bool reads_aux(const Epilogue& ep) { return ep.act == CG_ACT_SILU_GRAD || ep.act == CG_ACT_ADD; }
+
+__device__ inline float4 load_aux4(const Epilogue& ep, int64_t row, int col) {
+  return *reinterpret_cast<const float4*>(ep.aux_in + row * ep.ld_aux + col);
+}
+
+// Epilogue of four consecutive columns (col % 4 == 0, all in range); aux =
+// aux_in[row, col .. col + 3] when reads_aux(ep), loaded ahead by the caller.
+__device__ inline void epilogue_store4(const Epilogue& ep, int64_t row, int col, float4 x, float4 bias, float4 aux) {
   float v[4] = {x.x * ep.alpha + bias.x, x.y * ep.alpha + bias.y, x.z * ep.alpha + bias.z, x.w * ep.alpha + bias.w};
   if (ep.act == CG_ACT_SILU) {
     if (ep.aux_out) *reinterpret_cast<float4*>(ep.aux_out + row * ep.ld_aux + col) = make_float4(v[0], v[1], v[2], v[3]);
 #pragma unroll
     for (int e = 0; e < 4; ++e) v[e] = silu(v[e]);
   } else if (ep.act == CG_ACT_SILU_GRAD) {
-    const float4 z = *reinterpret_cast<const float4*>(ep.aux_in + row * ep.ld_aux + col);
-    v[0] *= silu_grad(z.x);
-    v[1] *= silu_grad(z.y);
-    v[2] *= silu_grad(z.z);
-    v[3] *= silu_grad(z.w);
+    v[0] *= silu_grad(aux.x);
+    v[1] *= silu_grad(aux.y);
+    v[2] *= silu_grad(aux.z);
+    v[3] *= silu_grad(aux.w);
+  } else if (ep.act == CG_ACT_ADD) {
+    v[0] += aux.x;
+    v[1] += aux.y;
+    v[2] += aux.z;
+    v[3] += aux.w;
   }
   float4* c = reinterpret_cast<float4*>(ep.c + row * ep.ldc + col);
   if (ep.accumulate) {
@@ -247,6 +261,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       item_coords(w, m0, n0, kt0, kt1);
       const int z = w / (m_tiles * n_tiles);
       const int b = j & 1, use = j >> 1;
+      // aux_in rows of a 32-column chunk (SiLU gradient, residual), loaded a
+      // chunk ahead so that their latency hides behind the accumulator wait
+      // and the previous chunk's stores; lane (l & 7) holds columns
+      // 4 (l & 7) .. +3 of rows (l >> 3) + 4 i
+      const int cl = (lane & 7) * 4;
+      const bool prefetch = ep.vec && partial == nullptr && reads_aux(ep);
+      auto fetch_aux = [&](float4 (&dst)[8], int c0) {
+        const int col = n0 + c0 + cl;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int row = m0 + quarter * 32 + (lane >> 3) + 4 * i;
+          dst[i] = (prefetch && c0 < BN && c0 + cl < BN && col < N && row < M) ? load_aux4(ep, row, col)
+                                                                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      };
+      float4 aux[8];
+      if (prefetch) fetch_aux(aux, 0);
       if (!mbar_wait(&acc_full[b], use & 1, &g_gemm_error)) break;
       tc_fence_after();
 #pragma unroll 1
@@ -259,20 +290,33 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<float4*>(stage + lane * kStagePitch + 4 * q) =
               make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
         __syncwarp();
+        float4 aux_next[8];
+        if (prefetch) fetch_aux(aux_next, c0 + 32);
         // each store instruction writes 4 full rows of 32 columns (8 lanes x 16 B per row)
-        const int cl = (lane & 7) * 4;
         const int col = n0 + c0 + cl;
         if (ep.vec && c0 + cl < BN && col < N) {
           const float4 bias = ep.bias ? *reinterpret_cast<const float4*>(ep.bias + col) : make_float4(0, 0, 0, 0);
+          if (prefetch) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int r = (lane >> 3) + 4 * i;
+              const int row = m0 + quarter * 32 + r;
+              if (row >= M) break;
+              const float4 x = *reinterpret_cast<const float4*>(stage + r * kStagePitch + cl);
+              epilogue_store4(ep, row, col, x, bias, aux[i]);
+            }
+          } else {
+            const float4 none = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 2
-          for (int r = lane >> 3; r < 32; r += 4) {
-            const int row = m0 + quarter * 32 + r;
-            if (row >= M) break;
-            const float4 x = *reinterpret_cast<const float4*>(stage + r * kStagePitch + cl);
-            if (partial) {
-              *reinterpret_cast<float4*>(partial + z * mn + (int64_t)row * N + col) = x;
-            } else {
-              epilogue_store4(ep, row, col, x, bias);
+            for (int r = lane >> 3; r < 32; r += 4) {
+              const int row = m0 + quarter * 32 + r;
+              if (row >= M) break;
+              const float4 x = *reinterpret_cast<const float4*>(stage + r * kStagePitch + cl);
+              if (partial) {
+                *reinterpret_cast<float4*>(partial + z * mn + (int64_t)row * N + col) = x;
+              } else {
+                epilogue_store4(ep, row, col, x, bias, none);
+              }
             }
           }
         } else if (!ep.vec) {
@@ -291,6 +335,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         __syncwarp();
+        if (prefetch) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) aux[i] = aux_next[i];
+        }
       }
       // the accumulator may be overwritten once every epilogue warp has read it
       tc_fence_before();
@@ -330,7 +378,8 @@ __global__ void splitk_reduce4_kernel(const float* __restrict__ partial, int spl
       }
       const float4 bias =
           ep.bias ? __ldg(reinterpret_cast<const float4*>(ep.bias) + c4) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      epilogue_store4(ep, r, 4 * c4, x, bias);
+      const float4 aux = reads_aux(ep) ? load_aux4(ep, r, 4 * c4) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      epilogue_store4(ep, r, 4 * c4, x, bias, aux);
     }
 }
 
@@ -510,8 +559,10 @@ static int run(const cg_gemm_args* args, void* stream) {
   CG_REQUIRE(g.lda % 4 == 0 && g.ldb % 4 == 0, "gemm: lda and ldb must be multiples of 4 floats");
   CG_REQUIRE(g.lda >= (g.a_mn_major ? g.m : g.k) && g.ldb >= (g.b_mn_major ? g.n : g.k),
              "gemm: leading dimension smaller than the contiguous extent");
-  CG_REQUIRE(g.act == CG_ACT_NONE || g.act == CG_ACT_SILU || g.act == CG_ACT_SILU_GRAD, "gemm: bad act");
-  CG_REQUIRE(g.act != CG_ACT_SILU_GRAD || g.aux_in != nullptr, "gemm: SiLU gradient needs aux_in");
+  CG_REQUIRE(g.act == CG_ACT_NONE || g.act == CG_ACT_SILU || g.act == CG_ACT_SILU_GRAD || g.act == CG_ACT_ADD,
+             "gemm: bad act");
+  CG_REQUIRE((g.act != CG_ACT_SILU_GRAD && g.act != CG_ACT_ADD) || g.aux_in != nullptr,
+             "gemm: the SiLU gradient and the residual add need aux_in");
   cudaStream_t s = as_stream(stream);
   const Plan p = plan_of(g);
   switch (p.bn) {

@@ -7,6 +7,8 @@
 // reduction is a fixed-order warp tree: deterministic.
 #include <math.h>
 
+#include <initializer_list>
+
 #include "common.cuh"
 #include "../../include/cg_b200.h"
 
@@ -178,8 +180,8 @@ __global__ void rownorm_fwd_kernel(const float* __restrict__ x, int64_t rows, in
 // where b = mean(g xhat), c = mean(h xhat), gx' = rstd (g - mean g - xhat b),
 // hx' = rstd (h - mean h - xhat c).
 __global__ void rownorm_bwd_kernel(const float* __restrict__ x, const float* __restrict__ g,
-                                   const float* __restrict__ h, int64_t rows, int cols, float eps,
-                                   float* __restrict__ out_a, float* __restrict__ out_b) {
+                                   const float* __restrict__ h, const float* __restrict__ add, int64_t rows,
+                                   int cols, float eps, float* __restrict__ out_a, float* __restrict__ out_b) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -205,7 +207,7 @@ __global__ void rownorm_bwd_kernel(const float* __restrict__ x, const float* __r
     if (h == nullptr) {
       for (int c = lane; c < cols; c += 32) {
         const float xh = (xr[c] - mean) * rstd;
-        out_a[r * cols + c] = rstd * (gr[c] - a - xh * b);
+        out_a[r * cols + c] = rstd * (gr[c] - a - xh * b) + (add != nullptr ? add[r * cols + c] : 0.0f);
       }
       continue;
     }
@@ -228,6 +230,137 @@ __global__ void rownorm_bwd_kernel(const float* __restrict__ x, const float* __r
     }
   }
 }
+
+// Row-resident variants for cols = 128 V (V <= 8, 16-byte aligned rows): the
+// lanes hold the row in registers as V float4 (column 4 (lane + 32 v)), so x,
+// g and h are read from memory once and every statistic is a sum over the
+// registers followed by one warp tree. `add` (bwd1 only, may be null) is
+// added to gx: the gradient of a residual branch point x -> (x, rownorm(x))
+// in the same pass.
+template <int V>
+__device__ __forceinline__ void load_row(float (&v)[4 * V], const float* row, int lane) {
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const float4 t = reinterpret_cast<const float4*>(row)[lane + 32 * i];
+    v[4 * i] = t.x;
+    v[4 * i + 1] = t.y;
+    v[4 * i + 2] = t.z;
+    v[4 * i + 3] = t.w;
+  }
+}
+
+template <int V>
+__device__ __forceinline__ void store_row(float* row, const float (&v)[4 * V], int lane) {
+#pragma unroll
+  for (int i = 0; i < V; ++i)
+    reinterpret_cast<float4*>(row)[lane + 32 * i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+
+template <int V>
+__device__ __forceinline__ void row_stats(const float (&x)[4 * V], int cols, float eps, float& mean, float& rstd) {
+  float s = 0.0f;
+#pragma unroll
+  for (int e = 0; e < 4 * V; ++e) s += x[e];
+  mean = warp_sum(s) / cols;
+  float q = 0.0f;
+#pragma unroll
+  for (int e = 0; e < 4 * V; ++e) q += (x[e] - mean) * (x[e] - mean);
+  rstd = rsqrtf(warp_sum(q) / cols + eps);
+}
+
+template <int V>
+__global__ void rownorm_fwd_rows_kernel(const float* __restrict__ x, int64_t rows, int cols, float eps,
+                                        float* __restrict__ xhat, float* __restrict__ rstd_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp; r < rows; r += warps) {
+    float v[4 * V];
+    load_row<V>(v, x + r * cols, lane);
+    float mean, rstd;
+    row_stats<V>(v, cols, eps, mean, rstd);
+#pragma unroll
+    for (int e = 0; e < 4 * V; ++e) v[e] = (v[e] - mean) * rstd;
+    store_row<V>(xhat + r * cols, v, lane);
+    if (lane == 0 && rstd_out) rstd_out[r] = rstd;
+  }
+}
+
+template <int V>
+__global__ void rownorm_bwd_rows_kernel(const float* __restrict__ x, const float* __restrict__ g,
+                                        const float* __restrict__ h, const float* __restrict__ add, int64_t rows,
+                                        int cols, float eps, float* __restrict__ out_a, float* __restrict__ out_b) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp; r < rows; r += warps) {
+    float xh[4 * V], gv[4 * V];
+    load_row<V>(xh, x + r * cols, lane);
+    load_row<V>(gv, g + r * cols, lane);
+    float mean, rstd;
+    row_stats<V>(xh, cols, eps, mean, rstd);
+    float sg = 0.0f, sgx = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 4 * V; ++e) {
+      xh[e] = (xh[e] - mean) * rstd;
+      sg += gv[e];
+      sgx += gv[e] * xh[e];
+    }
+    const float a = warp_sum(sg) / cols, b = warp_sum(sgx) / cols;
+    if (h == nullptr) {
+      float out[4 * V];
+      if (add != nullptr) load_row<V>(out, add + r * cols, lane);
+#pragma unroll
+      for (int e = 0; e < 4 * V; ++e) {
+        const float gx = rstd * (gv[e] - a - xh[e] * b);
+        out[e] = add != nullptr ? out[e] + gx : gx;
+      }
+      store_row<V>(out_a + r * cols, out, lane);
+      continue;
+    }
+    float hv[4 * V];
+    load_row<V>(hv, h + r * cols, lane);
+    float sh = 0.0f, shx = 0.0f, shg = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 4 * V; ++e) {
+      sh += hv[e];
+      shx += hv[e] * xh[e];
+      shg += hv[e] * gv[e];
+    }
+    const float mh = warp_sum(sh) / cols, cc = warp_sum(shx) / cols, mhg = warp_sum(shg) / cols;
+    const float r2 = rstd * rstd;
+#pragma unroll
+    for (int e = 0; e < 4 * V; ++e) {
+      const float gx = rstd * (gv[e] - a - xh[e] * b);
+      const float hx = rstd * (hv[e] - mh - xh[e] * cc);
+      hv[e] = hx;  // d_g
+      gv[e] = -xh[e] * (mhg - a * mh) * r2 - (cc * gx + b * hx) * rstd + b * cc * xh[e] * r2;  // d_x
+    }
+    store_row<V>(out_b + r * cols, hv, lane);
+    store_row<V>(out_a + r * cols, gv, lane);
+  }
+}
+
+// V = cols / 128 when the row-resident kernels apply (every pointer 16-byte
+// aligned), else 0
+inline int rows_v(int64_t cols, std::initializer_list<const void*> ptrs) {
+  if (cols % 128 != 0 || cols > 1024) return 0;
+  for (const void* p : ptrs)
+    if (p != nullptr && !al16(p)) return 0;
+  return (int)(cols / 128);
+}
+
+#define CG_ROWS_SWITCH(V, KERNEL, GRID, ...)                  \
+  switch (V) {                                                 \
+    case 1: KERNEL<1><<<GRID, 256, 0, s>>>(__VA_ARGS__); break; \
+    case 2: KERNEL<2><<<GRID, 256, 0, s>>>(__VA_ARGS__); break; \
+    case 3: KERNEL<3><<<GRID, 256, 0, s>>>(__VA_ARGS__); break; \
+    case 4: KERNEL<4><<<GRID, 256, 0, s>>>(__VA_ARGS__); break; \
+    case 5: KERNEL<5><<<GRID, 256, 0, s>>>(__VA_ARGS__); break; \
+    case 6: KERNEL<6><<<GRID, 256, 0, s>>>(__VA_ARGS__); break; \
+    case 7: KERNEL<7><<<GRID, 256, 0, s>>>(__VA_ARGS__); break; \
+    default: KERNEL<8><<<GRID, 256, 0, s>>>(__VA_ARGS__); break; \
+  }
 
 // ---- envelope pooling over the k tokens of each n ------------------------------
 // pool:  out[n, c]    = sum_s w[n, s] x[n, s, c]
@@ -390,20 +523,35 @@ int cg_rownorm_fwd(const float* x, int64_t rows, int64_t cols, float eps, float*
                    void* stream) {
   CG_REQUIRE(rows >= 0 && cols >= 1 && cols < (1 << 30), "rownorm: bad size");
   if (rows == 0) return kOk;
-  pw::rownorm_fwd_kernel<<<pw::blocks_for(rows * 32, 256), 256, 0, as_stream(stream)>>>(x, rows, (int)cols,
-                                                                                        eps, xhat, rstd);
+  const cudaStream_t s = as_stream(stream);
+  const int grid = pw::blocks_for(rows * 32, 256);
+  if (const int v = pw::rows_v(cols, {x, xhat})) {
+    CG_ROWS_SWITCH(v, pw::rownorm_fwd_rows_kernel, grid, x, rows, (int)cols, eps, xhat, rstd)
+  } else {
+    pw::rownorm_fwd_kernel<<<grid, 256, 0, s>>>(x, rows, (int)cols, eps, xhat, rstd);
+  }
   CG_LAUNCHED("rownorm_fwd");
+  return kOk;
+}
+
+int cg_rownorm_bwd1_add(const float* x, const float* g, const float* add, int64_t rows, int64_t cols, float eps,
+                        float* gx, void* stream) {
+  CG_REQUIRE(rows >= 0 && cols >= 1 && cols < (1 << 30), "rownorm: bad size");
+  if (rows == 0) return kOk;
+  const cudaStream_t s = as_stream(stream);
+  const int grid = pw::blocks_for(rows * 32, 256);
+  if (const int v = pw::rows_v(cols, {x, g, add, gx})) {
+    CG_ROWS_SWITCH(v, pw::rownorm_bwd_rows_kernel, grid, x, g, nullptr, add, rows, (int)cols, eps, gx, nullptr)
+  } else {
+    pw::rownorm_bwd_kernel<<<grid, 256, 0, s>>>(x, g, nullptr, add, rows, (int)cols, eps, gx, nullptr);
+  }
+  CG_LAUNCHED("rownorm_bwd1");
   return kOk;
 }
 
 int cg_rownorm_bwd1(const float* x, const float* g, int64_t rows, int64_t cols, float eps, float* gx,
                     void* stream) {
-  CG_REQUIRE(rows >= 0 && cols >= 1 && cols < (1 << 30), "rownorm: bad size");
-  if (rows == 0) return kOk;
-  pw::rownorm_bwd_kernel<<<pw::blocks_for(rows * 32, 256), 256, 0, as_stream(stream)>>>(
-      x, g, nullptr, rows, (int)cols, eps, gx, nullptr);
-  CG_LAUNCHED("rownorm_bwd1");
-  return kOk;
+  return cg_rownorm_bwd1_add(x, g, nullptr, rows, cols, eps, gx, stream);
 }
 
 int cg_rownorm_bwd2(const float* x, const float* g, const float* h, int64_t rows, int64_t cols, float eps,
@@ -411,8 +559,13 @@ int cg_rownorm_bwd2(const float* x, const float* g, const float* h, int64_t rows
   CG_REQUIRE(rows >= 0 && cols >= 1 && cols < (1 << 30), "rownorm: bad size");
   if (rows == 0) return kOk;
   CG_REQUIRE(h != nullptr, "rownorm_bwd2: h is NULL");
-  pw::rownorm_bwd_kernel<<<pw::blocks_for(rows * 32, 256), 256, 0, as_stream(stream)>>>(
-      x, g, h, rows, (int)cols, eps, d_x, d_g);
+  const cudaStream_t s = as_stream(stream);
+  const int grid = pw::blocks_for(rows * 32, 256);
+  if (const int v = pw::rows_v(cols, {x, g, h, d_x, d_g})) {
+    CG_ROWS_SWITCH(v, pw::rownorm_bwd_rows_kernel, grid, x, g, h, nullptr, rows, (int)cols, eps, d_x, d_g)
+  } else {
+    pw::rownorm_bwd_kernel<<<grid, 256, 0, s>>>(x, g, h, nullptr, rows, (int)cols, eps, d_x, d_g);
+  }
   CG_LAUNCHED("rownorm_bwd2");
   return kOk;
 }

@@ -18,7 +18,7 @@ from torch import Tensor
 from create_graph_b200 import native
 from create_graph_b200.errors import NativeError
 
-ACT_NONE, ACT_SILU, ACT_SILU_GRAD = native.ACT_NONE, native.ACT_SILU, native.ACT_SILU_GRAD
+ACT_NONE, ACT_SILU, ACT_SILU_GRAD, ACT_ADD = native.ACT_NONE, native.ACT_SILU, native.ACT_SILU_GRAD, native.ACT_ADD
 
 
 def _operand(t: Tensor, name: str) -> Tensor:

@@ -88,10 +88,12 @@ class Block(nn.Module):
 
     def forward(self, h: Tensor, bias: Tensor, env: Tensor, graph: cgnn.NeighborGraph) -> Tensor:
         # attention among the atom's edge tokens, pooled by the envelope, one fused op
-        m = cgnn.PooledTokenAttention.apply(self.qkv(self.norm1(h)), bias, env, graph, self.heads, self.scale,
-                                            self.precision)
-        h = h + self.out(m)
-        return h + self.ffn2(self.ffn1(self.norm2(h)))
+        # residual adds in the GEMM epilogues; each residual's two gradients meet
+        # inside the LayerNorm backward kernel
+        h, x = self.norm1.branch(h)
+        m = cgnn.PooledTokenAttention.apply(self.qkv(x), bias, env, graph, self.heads, self.scale, self.precision)
+        h, x = self.norm2.branch(self.out.residual(m, h))
+        return self.ffn2.residual(self.ffn1(x), h)
 
 
 class EnergyNetwork(nn.Module):

@@ -148,7 +148,7 @@ class GeomArgs(ctypes.Structure):
     ]
 
 
-ACT_NONE, ACT_SILU, ACT_SILU_GRAD = 0, 1, 2
+ACT_NONE, ACT_SILU, ACT_SILU_GRAD, ACT_ADD = 0, 1, 2, 3
 f32 = ctypes.c_float
 _I = ctypes.c_int
 
@@ -180,6 +180,7 @@ _SIGNATURES = {
     "cg_scale_shift": (_I, [vp, vp, vp, vp, i64, i64, vp]),
     "cg_rownorm_fwd": (_I, [vp, i64, i64, f32, vp, vp, vp]),
     "cg_rownorm_bwd1": (_I, [vp, vp, i64, i64, f32, vp, vp]),
+    "cg_rownorm_bwd1_add": (_I, [vp, vp, vp, i64, i64, f32, vp, vp]),
     "cg_rownorm_bwd2": (_I, [vp, vp, vp, i64, i64, f32, vp, vp, vp]),
     "cg_pool": (_I, [vp, vp, i64, i64, i64, vp, vp]),
     "cg_pool_outer": (_I, [vp, vp, i64, i64, i64, vp, vp]),

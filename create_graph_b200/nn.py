@@ -43,7 +43,7 @@ from create_graph_b200.edge_attn import (
     token_attention_forward1,
 )
 from create_graph_b200.errors import NativeError
-from create_graph_b200.gemm import ACT_SILU, gemm
+from create_graph_b200.gemm import ACT_ADD, ACT_SILU, gemm
 
 Function = torch.autograd.Function
 
@@ -208,6 +208,23 @@ class LinearFn(_Fused):
         return _linear_backward(ctx, g, x, w, ctx.has_bias)
 
 
+class LinearResidualFn(_Fused):
+    """y = r + x @ w.T + b: the residual add in the GEMM epilogue (reads r once,
+    no separate (rows, out) add); r's gradient is g itself."""
+
+    @staticmethod
+    def forward(ctx, x, w, b, r):
+        ctx.save_for_backward(x, w)
+        ctx.edges = _edges(x, w, b, r)
+        ctx.has_bias = b is not None
+        return mm_raw(x, w, bias=b, act=ACT_ADD, aux_in=_f32(r, "linear_residual"))
+
+    @staticmethod
+    def backward(ctx, g):
+        x, w = ctx.saved_tensors
+        return (*_linear_backward(ctx, g, x, w, ctx.has_bias), g if ctx.needs_input_grad[3] else None)
+
+
 class SiluGrad(_Fused):
     """out = g * silu'(z)."""
 
@@ -301,18 +318,45 @@ class RowNorm(_Fused):
     @staticmethod
     def backward(ctx, g):
         (x,) = ctx.saved_tensors
-        return RowNormGrad.apply(g, x, ctx.eps), None
+        return RowNormGrad.apply(g, x, ctx.eps, None), None
+
+
+class BranchNorm(_Fused):
+    """(x, rownorm(x)): a residual branch point. Backward sums the two branch
+    gradients inside the row-normalisation backward kernel (one pass, no
+    separate add of the residual gradient)."""
+
+    @staticmethod
+    def forward(ctx, x, eps):
+        x = _f32(x, "rownorm")
+        out = torch.empty_like(x)
+        native.call("cg_rownorm_fwd", x.data_ptr(), x.shape[0], x.shape[1], eps, out.data_ptr(), None,
+                    _stream())
+        ctx.save_for_backward(x)
+        ctx.eps = eps
+        ctx.set_materialize_grads(False)
+        return x.view_as(x), out
+
+    @staticmethod
+    def backward(ctx, g_x, g_norm):
+        (x,) = ctx.saved_tensors
+        if g_norm is None:
+            return g_x, None
+        return RowNormGrad.apply(g_norm, x, ctx.eps, g_x), None
 
 
 class RowNormGrad(_Fused):
-    """gx = J(x)^T g of the row normalisation; backward is the bwd2 kernel."""
+    """gx = J(x)^T g (+ add) of the row normalisation; backward is the bwd2
+    kernel (and add's gradient is h itself)."""
 
     @staticmethod
-    def forward(ctx, g, x, eps):
+    def forward(ctx, g, x, eps, add):
         g, x = _f32(g, "rownorm_bwd1"), _f32(x, "rownorm_bwd1")
+        if add is not None:
+            add = _f32(add, "rownorm_bwd1")
         out = torch.empty_like(g)
-        native.call("cg_rownorm_bwd1", x.data_ptr(), g.data_ptr(), x.shape[0], x.shape[1], eps, out.data_ptr(),
-                    _stream())
+        native.call("cg_rownorm_bwd1_add", x.data_ptr(), g.data_ptr(), native.ptr(add), x.shape[0], x.shape[1],
+                    eps, out.data_ptr(), _stream())
         ctx.save_for_backward(g, x)
         ctx.eps = eps
         return out
@@ -324,7 +368,7 @@ class RowNormGrad(_Fused):
         dx, dg = torch.empty_like(x), torch.empty_like(g)
         native.call("cg_rownorm_bwd2", x.data_ptr(), g.data_ptr(), h.data_ptr(), x.shape[0], x.shape[1], ctx.eps,
                     dx.data_ptr(), dg.data_ptr(), _stream())
-        return dg, dx, None
+        return dg, dx, None, h if ctx.needs_input_grad[3] else None
 
 
 # ---------------------------------------------------------------------------
@@ -697,6 +741,12 @@ class Linear(nn.Module):
             return LinearSiluFn.apply(x, self.weight, self.bias)[0]
         return LinearFn.apply(x, self.weight, self.bias)
 
+    def residual(self, x: Tensor, r: Tensor) -> Tensor:
+        """r + self(x) with the add in the GEMM epilogue."""
+        if self.silu:
+            raise NativeError("Linear.residual: no SiLU variant")
+        return LinearResidualFn.apply(x, self.weight, self.bias, r)
+
 
 class LayerNorm(nn.Module):
     """nn.LayerNorm over the last dimension: row normalisation + column affine."""
@@ -709,3 +759,9 @@ class LayerNorm(nn.Module):
 
     def forward(self, x: Tensor) -> Tensor:
         return ScaleShift.apply(RowNorm.apply(x, self.eps), self.weight, self.bias)
+
+    def branch(self, x: Tensor) -> tuple[Tensor, Tensor]:
+        """(x, LayerNorm(x)) for a residual block: x's two gradients meet inside
+        the normalisation backward kernel."""
+        x_res, xhat = BranchNorm.apply(x, self.eps)
+        return x_res, ScaleShift.apply(xhat, self.weight, self.bias)

@@ -175,6 +175,7 @@ int cg_pooled_attn_bwd2(const cg_pooled_attn_args* a, void* stream);
  *   CG_ACT_NONE       nothing;
  *   CG_ACT_SILU       aux_out[m, n] = x (pre-activation), x = silu(x);
  *   CG_ACT_SILU_GRAD  x *= silu'(aux_in[m, n]);
+ *   CG_ACT_ADD        x += aux_in[m, n] (a residual: y = h + x W^T + b);
  * then C = x, or C += x with accumulate. a, b 16-byte aligned; lda, ldb
  * multiples of 4. Replaces the nn.Linear (+ activation) GEMMs Inductor
  * generates inside a compiled region (src/create_graph/region.py:191-198).
@@ -182,6 +183,7 @@ int cg_pooled_attn_bwd2(const cg_pooled_attn_args* a, void* stream);
 #define CG_ACT_NONE 0
 #define CG_ACT_SILU 1
 #define CG_ACT_SILU_GRAD 2
+#define CG_ACT_ADD 3
 
 typedef struct cg_gemm_args {
   int64_t m, n, k;
@@ -192,7 +194,7 @@ typedef struct cg_gemm_args {
   float* c;
   int64_t ldc;
   const float* bias;     /* (n,) or NULL */
-  const float* aux_in;   /* CG_ACT_SILU_GRAD: pre-activation, pitch ld_aux */
+  const float* aux_in;   /* CG_ACT_SILU_GRAD: pre-activation; CG_ACT_ADD: residual; pitch ld_aux */
   float* aux_out;        /* CG_ACT_SILU: pre-activation out, pitch ld_aux; may be NULL */
   int64_t ld_aux;
   int32_t a_mn_major, b_mn_major;
@@ -274,6 +276,11 @@ int cg_rownorm_fwd(const float* x, int64_t rows, int64_t cols, float eps, float*
 /* gx = d xhat / dx applied to g */
 int cg_rownorm_bwd1(const float* x, const float* g, int64_t rows, int64_t cols, float eps, float* gx,
                     void* stream);
+/* gx = d xhat / dx applied to g, plus add (may be NULL): the gradient at a
+ * residual branch point x -> (x, rownorm(x)) in one pass (no reference
+ * counterpart: autograd adds the two branch gradients there). */
+int cg_rownorm_bwd1_add(const float* x, const float* g, const float* add, int64_t rows, int64_t cols, float eps,
+                        float* gx, void* stream);
 /* gradients of <h, gx(x, g)> w.r.t. x (d_x) and g (d_g) */
 int cg_rownorm_bwd2(const float* x, const float* g, const float* h, int64_t rows, int64_t cols, float eps,
                     float* d_x, float* d_g, void* stream);

@@ -14,7 +14,7 @@ import pytest
 import torch
 
 from create_graph_b200 import native
-from create_graph_b200.gemm import ACT_SILU, ACT_SILU_GRAD, gemm
+from create_graph_b200.gemm import ACT_ADD, ACT_SILU, ACT_SILU_GRAD, gemm
 
 pytestmark = pytest.mark.gpu
 TF32_TOL = 3e-3
@@ -73,6 +73,19 @@ def test_silu_gradient_epilogue_and_accumulate():
     acc = base.clone().cuda()
     gemm(a_dev, b_dev, b_t=True, out=acc, accumulate=True, alpha=0.5)
     assert rel(acc.cpu(), base.double() + 0.5 * a.double() @ b.double().T) < TF32_TOL
+
+
+@pytest.mark.parametrize("mnk", [(513, 384, 256), (12, 128, 20000)])
+def test_residual_add_epilogue(mnk):
+    """C = A B^T + bias + R (R read through the aux operand), also on the split-K path."""
+    m, n, k = mnk
+    a, b, a_dev, b_dev = operands(m, n, k, False, False, seed=6)
+    bias, r = torch.randn(n), torch.randn(m, n)
+    got = gemm(a_dev, b_dev, bias=bias.cuda(), act=ACT_ADD, aux_in=r.cuda())
+    torch.cuda.synchronize()
+    assert native.device_error() == 0
+    want = a.double() @ b.double().T + bias.double() + r.double()
+    assert rel(got.cpu(), want) < TF32_TOL
 
 
 def test_split_k_is_deterministic_and_uses_the_epilogue():

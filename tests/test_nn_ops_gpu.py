@@ -43,12 +43,40 @@ def test_mm_and_linear():
     check(twice_errors(silu_lin, lambda *a: F.silu(F.linear(*a)), [x, w, b]), TF32_TOL)
 
 
-def test_layer_norm():
-    x = randn(257, 192, seed=4, scale=2.0) + 0.5
-    gamma, beta = randn(192, seed=5), randn(192, seed=6)
+@pytest.mark.parametrize("cols", [192, 128, 768])
+def test_layer_norm(cols):
+    """192 columns take the strided row kernels, 128 and 768 the row-resident ones."""
+    x = randn(257, cols, seed=4, scale=2.0) + 0.5
+    gamma, beta = randn(cols, seed=5), randn(cols, seed=6)
     mine = lambda x, g, b: cgnn.ScaleShift.apply(cgnn.RowNorm.apply(x, 1e-5), g, b)  # noqa: E731
     ref = lambda x, g, b: F.layer_norm(x, (x.shape[-1],), g, b, 1e-5)  # noqa: E731
     check(twice_errors(mine, ref, [x, gamma, beta]), F32_TOL)
+
+
+@pytest.mark.parametrize("cols", [192, 256, 768])
+def test_residual_branch_and_linear_residual(cols):
+    """x + Linear(LayerNorm(x)) with the branch point's two gradients summed in
+    the normalisation backward kernel and the add in the GEMM epilogue."""
+    x = randn(257, cols, seed=9, scale=2.0) + 0.5
+    w, b = randn(cols, cols, seed=10, scale=1.0 / math.sqrt(cols)), randn(cols, seed=11)
+    gamma, beta = randn(cols, seed=12), randn(cols, seed=13)
+
+    def mine(x, w, b, g, be):
+        r, xhat = cgnn.BranchNorm.apply(x, 1e-5)
+        return cgnn.LinearResidualFn.apply(cgnn.ScaleShift.apply(xhat, g, be), w, b, r)
+
+    def ref(x, w, b, g, be):
+        return x + F.linear(F.layer_norm(x, (x.shape[-1],), g, be, 1e-5), w, b)
+
+    check(twice_errors(mine, ref, [x, w, b, gamma, beta]), TF32_TOL)
+
+
+def test_rownorm_backward_with_residual_matches_separate_add():
+    x, g, r = randn(300, 768, seed=14), randn(300, 768, seed=15), randn(300, 768, seed=16)
+    fused = cgnn.RowNormGrad.apply(g, x, 1e-5, r)
+    plain = cgnn.RowNormGrad.apply(g, x, 1e-5, None) + r
+    torch.cuda.synchronize()
+    assert (fused - plain).abs().max().item() <= 1e-5 * plain.abs().max().item()
 
 
 def test_column_ops():
