@@ -80,6 +80,7 @@ __device__ inline void epilogue_store(const Epilogue& ep, int64_t row, int col, 
     if (ep.aux_out) ep.aux_out[row * ep.ld_aux + col] = x;
     x = silu(x);
   } else if (ep.act == CG_ACT_SILU_GRAD) {
+    if (ep.aux_out) ep.aux_out[row * ep.ld_aux + col] = x;
     x *= silu_grad(ep.aux_in[row * ep.ld_aux + col]);
   } else if (ep.act == CG_ACT_ADD) {
     x += ep.aux_in[row * ep.ld_aux + col];
@@ -105,6 +106,7 @@ __device__ inline void epilogue_store4(const Epilogue& ep, int64_t row, int col,
 #pragma unroll
     for (int e = 0; e < 4; ++e) v[e] = silu(v[e]);
   } else if (ep.act == CG_ACT_SILU_GRAD) {
+    if (ep.aux_out) *reinterpret_cast<float4*>(ep.aux_out + row * ep.ld_aux + col) = make_float4(v[0], v[1], v[2], v[3]);
     v[0] *= silu_grad(aux.x);
     v[1] *= silu_grad(aux.y);
     v[2] *= silu_grad(aux.z);

@@ -75,11 +75,12 @@ def gemm(
     if bias is not None:
         bias = bias.contiguous()
         args.bias = bias.data_ptr()
-    aux = aux_in if aux_in is not None else aux_out
-    if aux is not None:
-        if aux.shape != (m, n) or aux.stride(1) != 1:
-            raise NativeError(f"gemm: aux must be ({m}, {n}) with unit column stride")
-        args.ld_aux = aux.stride(0)
+    auxes = [t for t in (aux_in, aux_out) if t is not None]
+    for aux in auxes:
+        if aux.shape != (m, n) or aux.stride(1) != 1 or aux.stride(0) != auxes[0].stride(0):
+            raise NativeError(f"gemm: aux_in / aux_out must be ({m}, {n}) with unit column stride and one row pitch")
+    if auxes:
+        args.ld_aux = auxes[0].stride(0)
     args.aux_in = None if aux_in is None else aux_in.data_ptr()
     args.aux_out = None if aux_out is None else aux_out.data_ptr()
     args.a_mn_major, args.b_mn_major = int(a_t), int(b_t)

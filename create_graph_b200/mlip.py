@@ -93,7 +93,8 @@ class Block(nn.Module):
         h, x = self.norm1.branch(h)
         m = cgnn.PooledTokenAttention.apply(self.qkv(x), bias, env, graph, self.heads, self.scale, self.precision)
         h, x = self.norm2.branch(self.out.residual(m, h))
-        return self.ffn2.residual(self.ffn1(x), h)
+        y, z = cgnn.LinearSiluFn.apply(x, self.ffn1.weight, self.ffn1.bias)
+        return self.ffn2.silu_residual(y, z, h)
 
 
 class EnergyNetwork(nn.Module):

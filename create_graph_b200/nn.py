@@ -43,7 +43,7 @@ from create_graph_b200.edge_attn import (
     token_attention_forward1,
 )
 from create_graph_b200.errors import NativeError
-from create_graph_b200.gemm import ACT_ADD, ACT_SILU, gemm
+from create_graph_b200.gemm import ACT_ADD, ACT_SILU, ACT_SILU_GRAD, gemm
 
 Function = torch.autograd.Function
 
@@ -275,6 +275,65 @@ class LinearSiluFn(_Fused):
         if g is None:
             return None, None, None
         return _linear_backward(ctx, g, x, w, ctx.has_bias)
+
+
+class MMSiluGrad(_Fused):
+    """out = (g @ w) * silu'(z): the input gradient of a linear layer applied
+    to silu(z), taken straight to z (the SiLU derivative in the GEMM epilogue)."""
+
+    @staticmethod
+    def forward(ctx, g, w, z, keep_u=False):
+        z = _f32(z, "mm_silu_grad")
+        # u = g @ w, the second-order term's factor, comes out of the same
+        # epilogue when the caller builds a graph through this node (keep_u)
+        u = torch.empty_like(z) if keep_u else None
+        out = mm_raw(g, w.t(), act=ACT_SILU_GRAD, aux_in=z, aux_out=u)
+        ctx.save_for_backward(g, w, z, u)
+        ctx.edges = _edges(g, w, z)
+        return out
+
+    @staticmethod
+    def backward(ctx, h):
+        g, w, z, u = ctx.saved_tensors
+        s = SiluGrad.apply(h, z) if (_wanted(ctx, 0) or _wanted(ctx, 1)) else None  # h * silu'(z)
+        dg = MM.apply(s, w) if _wanted(ctx, 0) else None
+        dw = MM.apply(g.t(), s.t()) if _wanted(ctx, 1) else None
+        dz = None
+        if _wanted(ctx, 2):
+            h = _f32(h, "mm_silu_grad2")
+            if u is None:
+                u = mm_raw(g, w.t())  # g @ w
+            dz = torch.empty_like(h)
+            native.call("cg_silu_grad2", h.data_ptr(), u.data_ptr(), z.data_ptr(), dz.data_ptr(), h.numel(),
+                        _stream())
+        return dg, dw, dz, None
+
+
+class SiluLinearResidualFn(_Fused):
+    """out = r + silu(z) @ w.T + b, given y = silu(z) (written by the producing
+    GEMM's epilogue). Backward sends the gradient to z through MMSiluGrad (one
+    GEMM with the SiLU derivative in its epilogue) and none to y, so the
+    producer's backward runs no separate SiLU-gradient pass. y must have no
+    other consumer; its second-order terms still flow through the weight
+    gradient, which reads y."""
+
+    @staticmethod
+    def forward(ctx, y, z, w, b, r):
+        ctx.save_for_backward(y, z, w)
+        ctx.edges = _edges(y, z, w, b, r)
+        ctx.has_bias = b is not None
+        return mm_raw(y, w, bias=b, act=ACT_ADD, aux_in=_f32(r, "silu_linear_residual"))
+
+    @staticmethod
+    def backward(ctx, g):
+        y, z, w = ctx.saved_tensors
+        # grad mode is on here exactly when this backward is being recorded
+        # (create_graph), i.e. when MMSiluGrad's own backward will run
+        gz = MMSiluGrad.apply(g, w, z, torch.is_grad_enabled()) if _wanted(ctx, 1) else None
+        gw = MM.apply(g.t(), y.t()) if _wanted(ctx, 2) else None
+        gb = ColSum.apply(g) if ctx.has_bias and _wanted(ctx, 3) else None
+        gr = g if ctx.needs_input_grad[4] else None
+        return None, gz, gw, gb, gr
 
 
 class SplitCols(_Fused):
@@ -746,6 +805,13 @@ class Linear(nn.Module):
         if self.silu:
             raise NativeError("Linear.residual: no SiLU variant")
         return LinearResidualFn.apply(x, self.weight, self.bias, r)
+
+    def silu_residual(self, y: Tensor, z: Tensor, r: Tensor) -> Tensor:
+        """r + self(silu(z)) for (y, z) = (silu(z), z) from a SiLU linear layer:
+        the SiLU derivative is applied in this layer's input-gradient GEMM."""
+        if self.silu:
+            raise NativeError("Linear.silu_residual: no SiLU variant")
+        return SiluLinearResidualFn.apply(y, z, self.weight, self.bias, r)
 
 
 class LayerNorm(nn.Module):

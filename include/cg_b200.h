@@ -174,7 +174,7 @@ int cg_pooled_attn_bwd2(const cg_pooled_attn_args* a, void* stream);
  * epi adds bias[n], then per act:
  *   CG_ACT_NONE       nothing;
  *   CG_ACT_SILU       aux_out[m, n] = x (pre-activation), x = silu(x);
- *   CG_ACT_SILU_GRAD  x *= silu'(aux_in[m, n]);
+ *   CG_ACT_SILU_GRAD  aux_out[m, n] = x when aux_out is set, x *= silu'(aux_in[m, n]);
  *   CG_ACT_ADD        x += aux_in[m, n] (a residual: y = h + x W^T + b);
  * then C = x, or C += x with accumulate. a, b 16-byte aligned; lda, ldb
  * multiples of 4. Replaces the nn.Linear (+ activation) GEMMs Inductor
@@ -195,7 +195,7 @@ typedef struct cg_gemm_args {
   int64_t ldc;
   const float* bias;     /* (n,) or NULL */
   const float* aux_in;   /* CG_ACT_SILU_GRAD: pre-activation; CG_ACT_ADD: residual; pitch ld_aux */
-  float* aux_out;        /* CG_ACT_SILU: pre-activation out, pitch ld_aux; may be NULL */
+  float* aux_out;        /* CG_ACT_SILU / CG_ACT_SILU_GRAD: x before the activation, pitch ld_aux; may be NULL */
   int64_t ld_aux;
   int32_t a_mn_major, b_mn_major;
   int32_t act, accumulate;

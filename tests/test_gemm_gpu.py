@@ -69,6 +69,11 @@ def test_silu_gradient_epilogue_and_accumulate():
     dsilu = s * (1 + z.double() * (1 - s))
     got = gemm(a_dev, b_dev, b_t=True, act=ACT_SILU_GRAD, aux_in=z.cuda())
     assert rel(got.cpu(), (a.double() @ b.double().T) * dsilu) < TF32_TOL
+    # the product before the derivative, written through aux_out
+    u = torch.empty(m, n, device="cuda")
+    again = gemm(a_dev, b_dev, b_t=True, act=ACT_SILU_GRAD, aux_in=z.cuda(), aux_out=u)
+    assert torch.equal(again, got)
+    assert rel(u.cpu(), a.double() @ b.double().T) < TF32_TOL
     base = torch.randn(m, n)
     acc = base.clone().cuda()
     gemm(a_dev, b_dev, b_t=True, out=acc, accumulate=True, alpha=0.5)

@@ -71,6 +71,23 @@ def test_residual_branch_and_linear_residual(cols):
     check(twice_errors(mine, ref, [x, w, b, gamma, beta]), TF32_TOL)
 
 
+def test_ffn_with_silu_gradient_in_the_epilogue():
+    """r + W2 silu(W1 x + b1) + b2 through LinearSiluFn and SiluLinearResidualFn
+    (the SiLU derivative applied in the second layer's input-gradient GEMM)."""
+    x, r = randn(257, 128, seed=17), randn(257, 128, seed=18)
+    w1, b1 = randn(512, 128, seed=19, scale=1.0 / math.sqrt(128)), randn(512, seed=20)
+    w2, b2 = randn(128, 512, seed=21, scale=1.0 / math.sqrt(512)), randn(128, seed=22)
+
+    def mine(x, w1, b1, w2, b2, r):
+        y, z = cgnn.LinearSiluFn.apply(x, w1, b1)
+        return cgnn.SiluLinearResidualFn.apply(y, z, w2, b2, r)
+
+    def ref(x, w1, b1, w2, b2, r):
+        return r + F.linear(F.silu(F.linear(x, w1, b1)), w2, b2)
+
+    check(twice_errors(mine, ref, [x, w1, b1, w2, b2, r]), TF32_TOL)
+
+
 def test_rownorm_backward_with_residual_matches_separate_add():
     x, g, r = randn(300, 768, seed=14), randn(300, 768, seed=15), randn(300, 768, seed=16)
     fused = cgnn.RowNormGrad.apply(g, x, 1e-5, r)
