@@ -240,6 +240,9 @@ def run_mine(args):
             "e2e": e2e,
             "gpu_launches": launches,
             "roofline": roofline,
+            # the GEMM entry point as a whole (every shape of the step) against the tf32 peak
+            "roofline_gemm": (_gemm_roofline(kernels["cg_gemm_tf32"]["calls"], bf16_sus, src)
+                              if "cg_gemm_tf32" in kernels else None),
             "kernels": {k: {"launches": v["launches"], "ms_per_step": v["ms"], "share": v["share"]}
                         for k, v in sorted(kernels.items(), key=lambda kv: -kv[1]["ms"])},
             "clocks": clocks.summary(),
@@ -330,21 +333,35 @@ def pooled_attn_bytes(info, name):
     return 6 * atom + 2 * key + 2 * tok + stats + atom + dqk + 2 * key + tok + atom
 
 
+def _gemm_roofline(rec, bf16_sus, src, name="cg_gemm_tf32"):
+    flops = sum(2 * m * n * k for _, _, (m, n, k) in rec)
+    secs = sum(a.elapsed_time(b) for a, b, _ in rec) / 1e3
+    achieved = flops / secs / 1e12
+    peak = bf16_sus / 2
+    return {"kernel": name, "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+            "frac": achieved / peak, "traffic": None, "peak_source": f"{src} bf16 sustained / 2 (dense tf32)"}
+
+
 def roofline_of(kernels, hbm, bf16, bf16_sus, src):
-    """Roofline of the dominant kernel family: HBM-bound edge attention, or the
-    tf32 GEMM against the tf32 tensor peak (half the measured bf16 figure)."""
+    """Roofline of the dominant kernel: the one kernel with the most device time
+    per step. The GEMM entry point runs a different kernel per shape (tile width,
+    operand majors, split), so its launches compete shape by shape; the HBM-bound
+    attention kernels are one kernel each."""
     if not kernels:
         return None
-    name = max(kernels, key=lambda k: kernels[k]["ms"])
-    rec = kernels[name]["calls"]
+    candidates = {}
+    for name, info in kernels.items():
+        if name == "cg_gemm_tf32":
+            shapes = {}
+            for call in info["calls"]:
+                shapes.setdefault(call[2], []).append(call)
+            for shape, rec in shapes.items():
+                candidates[("cg_gemm_tf32", shape)] = (sum(a.elapsed_time(b) for a, b, _ in rec), rec)
+        else:
+            candidates[(name, None)] = (info["ms"], info["calls"])
+    (name, shape), (_, rec) = max(candidates.items(), key=lambda kv: kv[1][0])
     if name == "cg_gemm_tf32":
-        flops = sum(2 * m * n * k for _, _, (m, n, k) in rec)
-        secs = sum(a.elapsed_time(b) for a, b, _ in rec) / 1e3
-        achieved = flops / secs / 1e12
-        peak = bf16_sus / 2
-        return {"kernel": name, "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak, "traffic": None,
-                "peak_source": f"{src} bf16 sustained / 2 (dense tf32)"}
+        return _gemm_roofline(rec, bf16_sus, src, name=f"cg_gemm_tf32 {shape}")
     if name.startswith("cg_edge_attn") or name.startswith("cg_pooled_attn"):
         count = attn_bytes if name.startswith("cg_edge_attn") else pooled_attn_bytes
         nbytes = sum(count(info, name) for _, _, info in rec)

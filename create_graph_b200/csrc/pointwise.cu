@@ -286,7 +286,10 @@ __global__ void rownorm_fwd_rows_kernel(const float* __restrict__ x, int64_t row
   }
 }
 
-template <int V>
+// SECOND = false: out_a = J^T g (+ add); true: out_a = d_x, out_b = d_g of
+// <h, J^T g> (no add). Separate instantiations keep the first-order kernel at
+// two row arrays of registers (higher residency).
+template <int V, bool SECOND>
 __global__ void rownorm_bwd_rows_kernel(const float* __restrict__ x, const float* __restrict__ g,
                                         const float* __restrict__ h, const float* __restrict__ add, int64_t rows,
                                         int cols, float eps, float* __restrict__ out_a, float* __restrict__ out_b) {
@@ -307,39 +310,44 @@ __global__ void rownorm_bwd_rows_kernel(const float* __restrict__ x, const float
       sgx += gv[e] * xh[e];
     }
     const float a = warp_sum(sg) / cols, b = warp_sum(sgx) / cols;
-    if (h == nullptr) {
-      float out[4 * V];
-      if (add != nullptr) load_row<V>(out, add + r * cols, lane);
+    if constexpr (!SECOND) {
+#pragma unroll
+      for (int e = 0; e < 4 * V; ++e) gv[e] = rstd * (gv[e] - a - xh[e] * b);
+      if (add != nullptr) {
+        load_row<V>(xh, add + r * cols, lane);  // xh is dead: reuse it for the residual row
+#pragma unroll
+        for (int e = 0; e < 4 * V; ++e) gv[e] += xh[e];
+      }
+      store_row<V>(out_a + r * cols, gv, lane);
+    } else {
+      float hv[4 * V];
+      load_row<V>(hv, h + r * cols, lane);
+      float sh = 0.0f, shx = 0.0f, shg = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 4 * V; ++e) {
+        sh += hv[e];
+        shx += hv[e] * xh[e];
+        shg += hv[e] * gv[e];
+      }
+      const float mh = warp_sum(sh) / cols, cc = warp_sum(shx) / cols, mhg = warp_sum(shg) / cols;
+      const float r2 = rstd * rstd;
 #pragma unroll
       for (int e = 0; e < 4 * V; ++e) {
         const float gx = rstd * (gv[e] - a - xh[e] * b);
-        out[e] = add != nullptr ? out[e] + gx : gx;
+        const float hx = rstd * (hv[e] - mh - xh[e] * cc);
+        hv[e] = hx;  // d_g
+        gv[e] = -xh[e] * (mhg - a * mh) * r2 - (cc * gx + b * hx) * rstd + b * cc * xh[e] * r2;  // d_x
       }
-      store_row<V>(out_a + r * cols, out, lane);
-      continue;
+      store_row<V>(out_b + r * cols, hv, lane);
+      store_row<V>(out_a + r * cols, gv, lane);
     }
-    float hv[4 * V];
-    load_row<V>(hv, h + r * cols, lane);
-    float sh = 0.0f, shx = 0.0f, shg = 0.0f;
-#pragma unroll
-    for (int e = 0; e < 4 * V; ++e) {
-      sh += hv[e];
-      shx += hv[e] * xh[e];
-      shg += hv[e] * gv[e];
-    }
-    const float mh = warp_sum(sh) / cols, cc = warp_sum(shx) / cols, mhg = warp_sum(shg) / cols;
-    const float r2 = rstd * rstd;
-#pragma unroll
-    for (int e = 0; e < 4 * V; ++e) {
-      const float gx = rstd * (gv[e] - a - xh[e] * b);
-      const float hx = rstd * (hv[e] - mh - xh[e] * cc);
-      hv[e] = hx;  // d_g
-      gv[e] = -xh[e] * (mhg - a * mh) * r2 - (cc * gx + b * hx) * rstd + b * cc * xh[e] * r2;  // d_x
-    }
-    store_row<V>(out_b + r * cols, hv, lane);
-    store_row<V>(out_a + r * cols, gv, lane);
   }
 }
+
+template <int V>
+constexpr auto rownorm_bwd1_rows = rownorm_bwd_rows_kernel<V, false>;
+template <int V>
+constexpr auto rownorm_bwd2_rows = rownorm_bwd_rows_kernel<V, true>;
 
 // V = cols / 128 when the row-resident kernels apply (every pointer 16-byte
 // aligned), else 0
@@ -541,7 +549,7 @@ int cg_rownorm_bwd1_add(const float* x, const float* g, const float* add, int64_
   const cudaStream_t s = as_stream(stream);
   const int grid = pw::blocks_for(rows * 32, 256);
   if (const int v = pw::rows_v(cols, {x, g, add, gx})) {
-    CG_ROWS_SWITCH(v, pw::rownorm_bwd_rows_kernel, grid, x, g, nullptr, add, rows, (int)cols, eps, gx, nullptr)
+    CG_ROWS_SWITCH(v, pw::rownorm_bwd1_rows, grid, x, g, nullptr, add, rows, (int)cols, eps, gx, nullptr)
   } else {
     pw::rownorm_bwd_kernel<<<grid, 256, 0, s>>>(x, g, nullptr, add, rows, (int)cols, eps, gx, nullptr);
   }
@@ -562,7 +570,7 @@ int cg_rownorm_bwd2(const float* x, const float* g, const float* h, int64_t rows
   const cudaStream_t s = as_stream(stream);
   const int grid = pw::blocks_for(rows * 32, 256);
   if (const int v = pw::rows_v(cols, {x, g, h, d_x, d_g})) {
-    CG_ROWS_SWITCH(v, pw::rownorm_bwd_rows_kernel, grid, x, g, h, nullptr, rows, (int)cols, eps, d_x, d_g)
+    CG_ROWS_SWITCH(v, pw::rownorm_bwd2_rows, grid, x, g, h, nullptr, rows, (int)cols, eps, d_x, d_g)
   } else {
     pw::rownorm_bwd_kernel<<<grid, 256, 0, s>>>(x, g, h, nullptr, rows, (int)cols, eps, d_x, d_g);
   }
