@@ -263,9 +263,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       item_coords(w, m0, n0, kt0, kt1);
       const int z = w / (m_tiles * n_tiles);
       const int b = j & 1, use = j >> 1;
-      // aux_in rows of a 32-column chunk (SiLU gradient, residual), loaded a
-      // chunk ahead so that their latency hides behind the accumulator wait
-      // and the previous chunk's stores; lane (l & 7) holds columns
+      // aux_in rows of a 32-column chunk (SiLU gradient, residual), loaded two
+      // chunks ahead so that their latency hides behind the accumulator wait
+      // and the previous chunks' stores (the four epilogue warps alone must
+      // keep enough loads in flight); lane (l & 7) holds columns
       // 4 (l & 7) .. +3 of rows (l >> 3) + 4 i
       const int cl = (lane & 7) * 4;
       const bool prefetch = ep.vec && partial == nullptr && reads_aux(ep);
@@ -278,8 +279,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
         }
       };
-      float4 aux[8];
-      if (prefetch) fetch_aux(aux, 0);
+      float4 aux[8], aux1[8];
+      if (prefetch) {
+        fetch_aux(aux, 0);
+        fetch_aux(aux1, 32);
+      }
       if (!mbar_wait(&acc_full[b], use & 1, &g_gemm_error)) break;
       tc_fence_after();
 #pragma unroll 1
@@ -292,8 +296,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<float4*>(stage + lane * kStagePitch + 4 * q) =
               make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
         __syncwarp();
-        float4 aux_next[8];
-        if (prefetch) fetch_aux(aux_next, c0 + 32);
+        float4 aux2[8];
+        if (prefetch) fetch_aux(aux2, c0 + 64);
         // each store instruction writes 4 full rows of 32 columns (8 lanes x 16 B per row)
         const int col = n0 + c0 + cl;
         if (ep.vec && c0 + cl < BN && col < N) {
@@ -339,7 +343,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (prefetch) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) aux[i] = aux_next[i];
+          for (int i = 0; i < 8; ++i) {
+            aux[i] = aux1[i];
+            aux1[i] = aux2[i];
+          }
         }
       }
       // the accumulator may be overwritten once every epilogue warp has read it
