@@ -34,7 +34,9 @@ using namespace cg::sm100;
 
 constexpr int BM = 128;
 constexpr int BK = 32;  // fp32 elements per k-slice: one 128-byte swizzle row
-constexpr int kThreads = 192;
+// warp 0 TMA producer, warp 1 UMMA issuer, then EPI epilogue warps (4, or 8 for
+// GEMMs whose epilogue streams extra operands: two warps per TMEM lane quarter)
+__host__ __device__ constexpr int threads_of(int epi) { return 32 * (2 + epi); }
 constexpr int kStagePitch = 36;  // floats per staged row: 16-byte rows, conflict-free 128-bit access
 
 struct Epilogue {
@@ -61,13 +63,13 @@ __device__ inline float silu_grad(float z) {
   return s * (1.0f + z * (1.0f - s));
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int EPI = 4>
 struct Smem {
   static constexpr int kA = BM * BK * 4;
   static constexpr int kB = BN * BK * 4;
   static constexpr int kStage = kA + kB;
   static constexpr int kTiles = STAGES * kStage;
-  static constexpr int kStaging = 4 * 32 * kStagePitch * 4;  // epilogue transpose, one 32 x 36 block per warp
+  static constexpr int kStaging = EPI * 32 * kStagePitch * 4;  // epilogue transpose, one 32 x 36 block per warp
   static constexpr int kBytes = kTiles + kStaging + 1024 /*alignment*/ + 256 /*barriers*/;
   static_assert(kBytes <= 227 * 1024, "shared memory budget");
 };
@@ -134,11 +136,12 @@ __device__ inline void epilogue_store4(const Epilogue& ep, int64_t row, int col,
 // tile to partial[z] (M x N); the reduction pass adds the splits in z order.
 // Two TMEM accumulators (2 * BN columns) let the epilogue of item j overlap
 // the UMMAs of item j + 1.
-template <int BN, int STAGES, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(threads_of(EPI), 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                      int M, int N, int K, int kt_per, int splits, float* partial, Epilogue ep) {
-  using S = Smem<BN, STAGES>;
+  static_assert(EPI == 4 || EPI == 8, "four or eight epilogue warps");
+  using S = Smem<BN, STAGES, EPI>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // tiles need 1024-byte alignment for the 128B swizzle pattern
   unsigned char* tiles = reinterpret_cast<unsigned char*>(
@@ -164,7 +167,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+      mbar_init(&acc_empty[b], EPI);  // one arrival per epilogue warp
     }
     fence_barrier_init();
   }
@@ -254,8 +257,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // chunk: tcgen05.ld (thread = row), transpose through shared memory, then
     // store row by row with the lanes along the columns: every store is one
     // coalesced 128-byte line.
-    const int quarter = warp & 3;
-    float* stage = staging + quarter * 32 * kStagePitch;
+    // with eight warps the two warps of a quarter take alternate 32-column chunks
+    const int quarter = warp & 3, e = warp - 2, first = 32 * (e >> 2), chunk_step = 32 * (EPI / 4);
+    float* stage = staging + e * 32 * kStagePitch;
     const int64_t mn = (int64_t)M * N;
     int j = 0;
     for (int w = blockIdx.x; w < items; w += gridDim.x, ++j) {
@@ -281,13 +285,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       float4 aux[8], aux1[8];
       if (prefetch) {
-        fetch_aux(aux, 0);
-        fetch_aux(aux1, 32);
+        fetch_aux(aux, first);
+        fetch_aux(aux1, first + chunk_step);
       }
       if (!mbar_wait(&acc_full[b], use & 1, &g_gemm_error)) break;
       tc_fence_after();
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      for (int c0 = first; c0 < BN; c0 += chunk_step) {
         float v[32];
         tmem_load_32(tmem + b * BN + ((uint32_t)(quarter * 32) << 16) + c0, v);
         // row `lane` of the warp's 32 x 32 block, as 8 16-byte stores
@@ -297,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
         __syncwarp();
         float4 aux2[8];
-        if (prefetch) fetch_aux(aux2, c0 + 64);
+        if (prefetch) fetch_aux(aux2, c0 + 2 * chunk_step);
         // each store instruction writes 4 full rows of 32 columns (8 lanes x 16 B per row)
         const int col = n0 + c0 + cl;
         if (ep.vec && c0 + cl < BN && col < N) {
@@ -488,7 +492,7 @@ static int64_t workspace_bytes(const cg_gemm_args& g) {
   return p.splits > 1 ? (int64_t)p.splits * g.m * g.n * (int64_t)sizeof(float) : 0;
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN>
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI = 4>
 static int launch(const cg_gemm_args& g, const Plan& p, cudaStream_t stream) {
   CUtensorMap ma, mb;
   int rc;
@@ -522,13 +526,13 @@ static int launch(const cg_gemm_args& g, const Plan& p, cudaStream_t stream) {
                p.splits, (long long)workspace_bytes(g));
     partial = g.workspace;
   }
-  using S = Smem<BN, STAGES>;
-  auto kernel = gemm_tf32_kernel<BN, STAGES, A_MN, B_MN>;
+  using S = Smem<BN, STAGES, EPI>;
+  auto kernel = gemm_tf32_kernel<BN, STAGES, A_MN, B_MN, EPI>;
   CG_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes));
   const int64_t items = ceil_div<int64_t>(g.m, BM) * ceil_div<int64_t>(g.n, BN) * p.splits;
   CG_REQUIRE(items < (1ll << 31), "gemm: too many tiles");
   const int grid = (int)(items < sm_count() ? items : sm_count());
-  kernel<<<grid, kThreads, S::kBytes, stream>>>(ma, mb, (int)g.m, (int)g.n, (int)g.k, p.kt_per, p.splits, partial,
+  kernel<<<grid, threads_of(EPI), S::kBytes, stream>>>(ma, mb, (int)g.m, (int)g.n, (int)g.k, p.kt_per, p.splits, partial,
                                                 ep);
   CG_LAUNCHED("gemm_tf32");
   if (p.splits > 1) {
@@ -546,12 +550,22 @@ static int launch(const cg_gemm_args& g, const Plan& p, cudaStream_t stream) {
   return kOk;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int EPI = 4>
 static int launch_majors(const cg_gemm_args& g, const Plan& p, cudaStream_t s) {
-  if (!g.a_mn_major && !g.b_mn_major) return launch<BN, STAGES, false, false>(g, p, s);
-  if (!g.a_mn_major && g.b_mn_major) return launch<BN, STAGES, false, true>(g, p, s);
-  if (g.a_mn_major && !g.b_mn_major) return launch<BN, STAGES, true, false>(g, p, s);
-  return launch<BN, STAGES, true, true>(g, p, s);
+  if (!g.a_mn_major && !g.b_mn_major) return launch<BN, STAGES, false, false, EPI>(g, p, s);
+  if (!g.a_mn_major && g.b_mn_major) return launch<BN, STAGES, false, true, EPI>(g, p, s);
+  if (g.a_mn_major && !g.b_mn_major) return launch<BN, STAGES, true, false, EPI>(g, p, s);
+  return launch<BN, STAGES, true, true, EPI>(g, p, s);
+}
+
+// Epilogues that read or write a second (M, N) stream (residual, SiLU
+// pre-activation in or out) run on eight epilogue warps, one stage fewer
+// making room for their staging blocks, when the main loop is short enough
+// (K <= 1024) for the epilogue to bound a tile; the wide-tile K-major-A
+// shapes the model runs them on. With long K the deeper pipeline wins.
+static bool heavy_epilogue(const cg_gemm_args& g, const Plan& p) {
+  return p.splits == 1 && (g.aux_in != nullptr || g.aux_out != nullptr) && !g.a_mn_major &&
+         (p.bn == 256 || p.bn == 192) && g.k <= 1024;
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -579,8 +593,14 @@ static int run(const cg_gemm_args* args, void* stream) {
     case 32: return launch_majors<32, 9>(g, p, s);
     case 64: return launch_majors<64, 8>(g, p, s);
     case 128: return launch_majors<128, 6>(g, p, s);
-    case 192: return launch_majors<192, 5>(g, p, s);
-    default: return launch_majors<256, 4>(g, p, s);
+    case 192:
+      if (heavy_epilogue(g, p))
+        return g.b_mn_major ? launch<192, 4, false, true, 8>(g, p, s) : launch<192, 4, false, false, 8>(g, p, s);
+      return launch_majors<192, 5>(g, p, s);
+    default:
+      if (heavy_epilogue(g, p))
+        return g.b_mn_major ? launch<256, 3, false, true, 8>(g, p, s) : launch<256, 3, false, false, 8>(g, p, s);
+      return launch_majors<256, 4>(g, p, s);
   }
 }
 

@@ -93,6 +93,36 @@ def test_residual_add_epilogue(mnk):
     assert rel(got.cpu(), want) < TF32_TOL
 
 
+@pytest.mark.parametrize("n,b_t,act", [(768, False, ACT_ADD), (768, True, ACT_SILU_GRAD), (3072, False, ACT_SILU),
+                                       (3072, True, ACT_ADD)])
+def test_wide_tile_epilogues_on_eight_warps(n, b_t, act):
+    """Output-heavy shapes (8280 rows, 192- and 256-column tiles) whose epilogue
+    streams a second (M, N) operand run on eight epilogue warps: every epilogue
+    form against float64, ragged last row tile."""
+    m, k = 8280, 256
+    a, b, a_dev, b_dev = operands(m, n, k, False, b_t, seed=8)
+    gen = torch.Generator().manual_seed(9)
+    bias, aux = torch.randn(n, generator=gen), torch.randn(m, n, generator=gen)
+    prod = a.double() @ b.double().T
+    x = prod + bias.double()
+    side = torch.full((m, n), float("nan"), device="cuda")
+    if act == ACT_ADD:
+        got = gemm(a_dev, b_dev, b_t=b_t, bias=bias.cuda(), act=act, aux_in=aux.cuda())
+        want, want_side = x + aux.double(), None
+    elif act == ACT_SILU:
+        got = gemm(a_dev, b_dev, b_t=b_t, bias=bias.cuda(), act=act, aux_out=side)
+        want, want_side = torch.nn.functional.silu(x), x
+    else:
+        s = torch.sigmoid(aux.double())
+        got = gemm(a_dev, b_dev, b_t=b_t, bias=bias.cuda(), act=act, aux_in=aux.cuda(), aux_out=side)
+        want, want_side = x * (s * (1 + aux.double() * (1 - s))), x
+    torch.cuda.synchronize()
+    assert native.device_error() == 0
+    assert rel(got.cpu(), want) < TF32_TOL
+    if want_side is not None:
+        assert rel(side.cpu(), want_side) < TF32_TOL
+
+
 def test_split_k_is_deterministic_and_uses_the_epilogue():
     """Weight-gradient shapes (small M x N, K = edges) split K across CTAs; the
     partial tiles are added in a fixed order."""
