@@ -457,7 +457,26 @@ static Plan plan_of(const cg_gemm_args& g) {
   if (g.n <= 16 && !g.b_mn_major) p.bn = 16;
   else if (g.n <= 32) p.bn = 32;
   else if (g.n <= 64) p.bn = 64;
-  else if (g.n >= 256 && mt * ceil_div<int64_t>(g.n, 256) < sms && ktiles >= 32) p.bn = 256;  // split K below
+  else if (g.n >= 256 && mt * ceil_div<int64_t>(g.n, 256) < sms && ktiles >= 32) {
+    // K is split below: the width whose split fills the SMs for the least
+    // time per wave (waves x width x k-tiles per split, 192 weighted for its
+    // lower flops per operand byte)
+    const int widths[2] = {256, 192};
+    const double weight[2] = {1.0, 1.05};
+    double best = 0.0;
+    for (int i = 0; i < 2; ++i) {
+      const int64_t tiles = mt * ceil_div<int64_t>(g.n, widths[i]);
+      int64_t splits = tiles < sms ? sms / tiles : 1;
+      if (splits > ktiles / 4) splits = ktiles / 4;
+      if (splits < 1) splits = 1;
+      const int64_t waves = ceil_div<int64_t>(tiles * splits, sms);
+      const double cost = (double)waves * widths[i] * (double)ceil_div<int64_t>(ktiles, splits) * weight[i];
+      if (best == 0.0 || cost < best) {
+        best = cost;
+        p.bn = widths[i];
+      }
+    }
+  }
   else if (g.n >= 192) {
     // the width whose waves of tiles take the least time: waves x width,
     // narrower tiles weighted for their lower flops per operand byte
@@ -558,14 +577,13 @@ static int launch_majors(const cg_gemm_args& g, const Plan& p, cudaStream_t s) {
   return launch<BN, STAGES, true, true, EPI>(g, p, s);
 }
 
-// Epilogues that read or write a second (M, N) stream (residual, SiLU
-// pre-activation in or out) run on eight epilogue warps, one stage fewer
-// making room for their staging blocks, when the main loop is short enough
-// (K <= 1024) for the epilogue to bound a tile; the wide-tile K-major-A
-// shapes the model runs them on. With long K the deeper pipeline wins.
+// Unsplit wide-tile GEMMs with a short main loop (K <= 1024) and K-major A
+// run on eight epilogue warps (one stage fewer makes room for their staging
+// blocks): their epilogue, the output plus any residual or SiLU stream,
+// bounds a tile, and four warps keep too few stores and loads in flight.
+// With long K the deeper pipeline wins.
 static bool heavy_epilogue(const cg_gemm_args& g, const Plan& p) {
-  return p.splits == 1 && (g.aux_in != nullptr || g.aux_out != nullptr) && !g.a_mn_major &&
-         (p.bn == 256 || p.bn == 192) && g.k <= 1024;
+  return p.splits == 1 && !g.a_mn_major && (p.bn == 256 || p.bn == 192) && g.k <= 1024;
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
