@@ -195,7 +195,8 @@ __device__ __forceinline__ void token_dots(float* out, const float* base, const 
 // ---------------------------------------------------------------------------
 
 template <int DP, bool X3>
-__global__ void __launch_bounds__(kThreads) pooled_fwd(const PParams P) {
+// 12 CTAs per SM (the shared-memory limit): registers capped at 85, no spills
+__global__ void __launch_bounds__(kThreads, 12) pooled_fwd(const PParams P) {
   using L = Layout<DP>;
   extern __shared__ __align__(16) float smem[];
   float* sQ = smem;
