@@ -9,8 +9,10 @@ atoms/A^3 (seed 1000 + rank), 12 blocks, hidden 768, 12 heads, FFN 3072,
 128-Gaussian RBF, cutoff 6 A, k <= 30 neighbours, 50 species, tf32 GEMMs with
 fp32 accumulation, CompileConfig(memory_budget=0.5, checkpoint=r"blocks\\.\\d+").
 A step is one cg.create_graph call (energy + forces), the MSE loss on both and
-loss.backward() (the parameter gradient through the force), plus one NCCL
-average of the fp32 gradients for N > 1. Synthetic data, random-init weights.
+loss.backward() (the parameter gradient through the force), one NCCL average
+of the fp32 gradients for N > 1, and an AdamW update of the parameters (one
+fused kernel; torch.optim.AdamW on the reference arm). Synthetic data,
+random-init weights.
 
 Rank 0 prints one JSON line. ``--impl reference`` times the reference's
 algorithm for the same step (eager create_graph over torch CPU ops, the
@@ -117,6 +119,7 @@ def run_mine(args):
     import create_graph_b200 as cg
     from create_graph_b200 import mlip, native
     from create_graph_b200.ddp import FlatGradients
+    from create_graph_b200.optim import FusedAdamW
     from create_graph_b200.graph import make_batch
 
     rank, world, local = env_rank()
@@ -136,6 +139,7 @@ def run_mine(args):
     config = cg.CompileConfig(memory_budget=0.5, checkpoint=r"blocks\.\d+")
     model = mlip.MLIP(spec, config=config).to(dev)
     grads = FlatGradients(model.parameters(), world if world > 1 else None)
+    opt = FusedAdamW(grads, **ADAMW)
     batch = make_batch(pos_h.to(dev), species_h.to(dev), sys_ptr_h.to(dev), spec.n_species)
     e_t, f_t = e_t_h.to(dev), f_t_h.to(dev)
 
@@ -143,6 +147,7 @@ def run_mine(args):
         grads.zero()
         loss = mlip.train_step(model, b, et, ft)
         grads.allreduce()
+        opt.step()
         return loss
 
     def barrier():
@@ -229,7 +234,7 @@ def run_mine(args):
             "config": {
                 "workload": f"{CONFIG_NAME}: ~{args.atoms} atoms/GPU as systems of U{{20..200}} atoms, "
                             "12 blocks, C 768, 12 heads, FFN 3072, 128 RBF, k<=30, memory_budget 0.5, "
-                            "per-block checkpoint",
+                            "per-block checkpoint; step = energy + forces + loss.backward() + AdamW update",
                 "atoms_per_step": total_atoms,
                 "systems_rank0": len(sizes),
                 "parallelism": f"dp{world}",
@@ -377,6 +382,24 @@ def roofline_of(kernels, hbm, bf16, bf16_sus, src):
             "traffic": None}
 
 
+# the optimizer update that closes every training step, on both arms
+ADAMW = {"lr": 1e-4, "betas": (0.9, 0.999), "eps": 1e-8, "weight_decay": 1e-2}
+
+
+def cpu_step(ostep, params, opt, spec, pos, species, sys_ptr, e_t, f_t):
+    """One step of the reference algorithm on the host: the oracle's eager
+    create_graph step, then torch.optim.AdamW on its gradients."""
+    out = ostep.train_step(params, spec, pos, species, sys_ptr, e_t, f_t)
+    for name, t in params.items():
+        t.grad = out["grads"][name]
+    opt.step()
+    return out
+
+
+def cpu_optimizer(params):
+    return torch.optim.AdamW(list(params.values()), **ADAMW)
+
+
 def cpu_baseline(spec, sizes, pos_h, species_h, sys_ptr_h, e_t_h, f_t_h, model, budget_s=20.0):
     """The oracle (reference algorithm, torch CPU, fp32) on a bounded sample:
     the first systems of rank 0's batch, about 10-30 s of CPU work."""
@@ -384,7 +407,8 @@ def cpu_baseline(spec, sizes, pos_h, species_h, sys_ptr_h, e_t_h, f_t_h, model, 
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    params = {n: p.detach().float().cpu() for n, p in model.named_parameters()}
+    params = {n: p.detach().float().cpu().clone() for n, p in model.named_parameters()}
+    opt = cpu_optimizer(params)
     sample, atoms = 0, 0
     while sample < len(sizes) and atoms < 160:
         atoms += sizes[sample]
@@ -392,16 +416,17 @@ def cpu_baseline(spec, sizes, pos_h, species_h, sys_ptr_h, e_t_h, f_t_h, model, 
     sys_ptr = sys_ptr_h[: sample + 1].clone()
     pos, species = pos_h[:atoms], species_h[:atoms]
     e_t, f_t = e_t_h[:sample], f_t_h[:atoms]
-    ostep.train_step(params, spec, pos, species, sys_ptr, e_t, f_t)  # warm-up
+    cpu_step(ostep, params, opt, spec, pos, species, sys_ptr, e_t, f_t)  # warm-up
     steps, t0 = 0, time.perf_counter()
     while True:
-        ostep.train_step(params, spec, pos, species, sys_ptr, e_t, f_t)
+        cpu_step(ostep, params, opt, spec, pos, species, sys_ptr, e_t, f_t)
         steps += 1
         if time.perf_counter() - t0 > budget_s / 2 or steps >= 5:
             break
     secs = (time.perf_counter() - t0) / steps
     return {"value": atoms / secs, "unit": "atoms/s", "cores": threads, "kind": "port",
-            "sample": f"{sample} systems, {atoms} atoms of rank 0's batch, {steps} timed steps, fp32 torch CPU"}
+            "sample": f"{sample} systems, {atoms} atoms of rank 0's batch, {steps} timed steps (step + AdamW), "
+                      "fp32 torch CPU"}
 
 
 # ---------------------------------------------------------------------------
@@ -424,6 +449,7 @@ def run_reference(args):
     e_t_h, f_t_h = mlip.make_targets(len(sizes), pos_h.shape[0], seed=2000)
     torch.manual_seed(0)
     params = {n: p.detach().float() for n, p in mlip.reference_parameters(spec).items()}
+    opt = cpu_optimizer(params)
     # each step: a bounded sample (the next few systems, ~160 atoms) of the workload
     starts = []
     b = 0
@@ -440,7 +466,7 @@ def run_reference(args):
         b0, b1 = starts[i % len(starts)]
         a0, a1 = int(sys_ptr_h[b0]), int(sys_ptr_h[b1])
         sys_ptr = sys_ptr_h[b0 : b1 + 1] - a0
-        ostep.train_step(params, spec, pos_h[a0:a1], species_h[a0:a1], sys_ptr, e_t_h[b0:b1], f_t_h[a0:a1])
+        cpu_step(ostep, params, opt, spec, pos_h[a0:a1], species_h[a0:a1], sys_ptr, e_t_h[b0:b1], f_t_h[a0:a1])
         return a1 - a0
 
     for i in range(args.warmup):
@@ -465,8 +491,8 @@ def run_reference(args):
         "dtype": "f32",
         "data": "synthetic (seeded random systems, random-init weights)",
         "config": {
-            "workload": f"{CONFIG_NAME}: the reference algorithm (eager create_graph over torch CPU ops) "
-                        "on bounded samples of ~160 atoms of the same batch",
+            "workload": f"{CONFIG_NAME}: the reference algorithm (eager create_graph over torch CPU ops, "
+                        "then torch.optim.AdamW) on bounded samples of ~160 atoms of the same batch",
             "parallelism": "host cores",
         },
         "cpu_baseline": {"value": value, "unit": "atoms/s", "cores": threads, "kind": "port",

@@ -370,6 +370,43 @@ inline int rows_v(int64_t cols, std::initializer_list<const void*> ptrs) {
     default: KERNEL<8><<<GRID, 256, 0, s>>>(__VA_ARGS__); break; \
   }
 
+// ---- AdamW step over flat parameter / gradient / moment buffers -----------------
+// torch.optim.AdamW (amsgrad off): p *= 1 - lr wd; m = lerp(m, g, 1 - b1);
+// v = b2 v + (1 - b2) g^2; p -= step_size m / (sqrt(v) / sqrt_bc2 + eps), with
+// step_size = lr / (1 - b1^t) and sqrt_bc2 = sqrt(1 - b2^t) from the host.
+struct AdamW {
+  float lr, b1, b2, eps, wd, step_size, sqrt_bc2;
+  __device__ __forceinline__ void update(float& p, float g, float& m, float& v) const {
+    p *= 1.0f - lr * wd;
+    m = fmaf(1.0f - b1, g - m, m);
+    v = fmaf(1.0f - b2, g * g, b2 * v);
+    p -= step_size * (m / (sqrtf(v) / sqrt_bc2 + eps));
+  }
+};
+
+__global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+                             float* __restrict__ v, int64_t n, AdamW a, bool vec) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t i0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (vec) {
+    for (int64_t i = i0; i < n / 4; i += stride) {
+      float4 pp = reinterpret_cast<float4*>(p)[i], mm = reinterpret_cast<float4*>(m)[i],
+             vv = reinterpret_cast<float4*>(v)[i];
+      const float4 gg = reinterpret_cast<const float4*>(g)[i];
+      a.update(pp.x, gg.x, mm.x, vv.x);
+      a.update(pp.y, gg.y, mm.y, vv.y);
+      a.update(pp.z, gg.z, mm.z, vv.z);
+      a.update(pp.w, gg.w, mm.w, vv.w);
+      reinterpret_cast<float4*>(p)[i] = pp;
+      reinterpret_cast<float4*>(m)[i] = mm;
+      reinterpret_cast<float4*>(v)[i] = vv;
+    }
+    for (int64_t i = n / 4 * 4 + i0; i < n; i += stride) a.update(p[i], g[i], m[i], v[i]);
+  } else {
+    for (int64_t i = i0; i < n; i += stride) a.update(p[i], g[i], m[i], v[i]);
+  }
+}
+
 // ---- envelope pooling over the k tokens of each n ------------------------------
 // pool:  out[n, c]    = sum_s w[n, s] x[n, s, c]
 // outer: out[n, s, c] = w[n, s] g[n, c]
@@ -575,6 +612,28 @@ int cg_rownorm_bwd2(const float* x, const float* g, const float* h, int64_t rows
     pw::rownorm_bwd_kernel<<<grid, 256, 0, s>>>(x, g, h, nullptr, rows, (int)cols, eps, d_x, d_g);
   }
   CG_LAUNCHED("rownorm_bwd2");
+  return kOk;
+}
+
+int cg_adamw_step(float* param, const float* grad, float* exp_avg, float* exp_avg_sq, int64_t n, float lr,
+                  float beta1, float beta2, float eps, float weight_decay, int64_t step, void* stream) {
+  CG_REQUIRE(n >= 0, "adamw: negative size");
+  CG_REQUIRE(step >= 1, "adamw: step = %lld, the first step is 1", (long long)step);
+  CG_REQUIRE(beta1 >= 0.0f && beta1 < 1.0f && beta2 >= 0.0f && beta2 < 1.0f, "adamw: betas outside [0, 1)");
+  if (n == 0) return kOk;
+  CG_REQUIRE(param && grad && exp_avg && exp_avg_sq, "adamw: null buffer");
+  pw::AdamW a;
+  a.lr = lr;
+  a.b1 = beta1;
+  a.b2 = beta2;
+  a.eps = eps;
+  a.wd = weight_decay;
+  a.step_size = (float)((double)lr / (1.0 - pow((double)beta1, (double)step)));
+  a.sqrt_bc2 = (float)sqrt(1.0 - pow((double)beta2, (double)step));
+  const bool vec = pw::al16(param) && pw::al16(grad) && pw::al16(exp_avg) && pw::al16(exp_avg_sq);
+  pw::adamw_kernel<<<pw::blocks_for(vec ? (n + 3) / 4 : n, 256), 256, 0, as_stream(stream)>>>(
+      param, grad, exp_avg, exp_avg_sq, n, a, vec);
+  CG_LAUNCHED("adamw");
   return kOk;
 }
 

@@ -27,6 +27,9 @@ import torch
 import torch.distributed as dist
 
 DEFAULT_BUCKET_BYTES = 64 << 20
+# each parameter's slice of the flat buffers starts on a 256-byte boundary, so
+# that views of it (weights read by TMA, gradients) keep an allocation's alignment
+ALIGN_BYTES = 256
 
 
 class FlatGradients:
@@ -36,15 +39,17 @@ class FlatGradients:
         device, dtype = self.params[0].device, self.params[0].dtype
         if any(p.dtype != dtype for p in self.params):
             raise ValueError("FlatGradients: all parameters must share one dtype")
-        total = sum(p.numel() for p in self.params)
-        self.flat = torch.zeros(total, dtype=dtype, device=device)
+        align = max(1, ALIGN_BYTES // self.params[0].element_size())
         offsets = []
         offset = 0
         for p in self.params:
-            n = p.numel()
+            offsets.append((offset, p.numel()))
+            offset += -(-p.numel() // align) * align
+        total = offset
+        self.flat = torch.zeros(total, dtype=dtype, device=device)
+        for p, (offset, n) in zip(self.params, offsets):
             p.grad = self.flat[offset : offset + n].view_as(p)
-            offsets.append((offset, n))
-            offset += n
+        self.offsets = offsets  # (start, numel) of each parameter; the gaps stay zero
         self.world = world
         # buckets of whole parameters from the end of the buffer backwards
         per = max(1, bucket_bytes // self.flat.element_size())

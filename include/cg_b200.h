@@ -284,6 +284,12 @@ int cg_rownorm_bwd1_add(const float* x, const float* g, const float* add, int64_
 /* gradients of <h, gx(x, g)> w.r.t. x (d_x) and g (d_g) */
 int cg_rownorm_bwd2(const float* x, const float* g, const float* h, int64_t rows, int64_t cols, float eps,
                     float* d_x, float* d_g, void* stream);
+/* One AdamW step (torch.optim.AdamW, amsgrad off) over n contiguous fp32
+ * parameters with their gradients and moment buffers, in place; step counts
+ * from 1. The optimizer update after loss.backward() in the training step:
+ * the reference leaves it to the user's torch optimizer. */
+int cg_adamw_step(float* param, const float* grad, float* exp_avg, float* exp_avg_sq, int64_t n, float lr,
+                  float beta1, float beta2, float eps, float weight_decay, int64_t step, void* stream);
 /* Envelope pooling of k tokens per row n (x contiguous (n, k, cols)):
  * pool: out[n, c] = sum_s w[n, s] x[n, s, c];  outer: out[n, s, c] = w[n, s] g[n, c];
  * dot: out[n, s] = sum_c g[n, c] x[n, s, c]. A family closed under differentiation. */

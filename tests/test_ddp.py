@@ -80,12 +80,19 @@ def worker(rank, world, port, path, fail_rank, bucket_bytes):
             step(model, rank_data(rank), fail=rank == fail_rank)
             in_backward = grads.launched_in_backward
             grads.allreduce()
-        flat = grads.flat.clone()
-        gathered = [torch.empty_like(flat) for _ in range(world)]
-        dist.all_gather(gathered, flat)
+        whole = grads.flat.clone()
+        gathered = [torch.empty_like(whole) for _ in range(world)]
+        dist.all_gather(gathered, whole)
+        # the parameters' gradients (each slice starts on a 256-byte boundary; the gaps stay zero)
+        flat = torch.cat([p.grad.flatten() for p in grads.params])
+        gaps = whole.clone()
+        for start, n in grads.offsets:
+            gaps[start : start + n] = 0
+        aligned = all((p.grad.data_ptr() - grads.flat.data_ptr()) % 256 == 0 for p in grads.params)
         if rank == 0:
             torch.save({"flat": flat, "identical": all(torch.equal(gathered[0], g) for g in gathered[1:]),
-                        "buckets": len(grads.buckets), "in_backward": in_backward}, path)
+                        "buckets": len(grads.buckets), "in_backward": in_backward,
+                        "gaps_zero": bool((gaps == 0).all()), "aligned": aligned}, path)
     except RuntimeError as error:
         torch.save({"error": str(error)}, f"{path}.{rank}")
     finally:
@@ -124,7 +131,7 @@ def test_averaged_gradients_match_eager_mean(bucket_bytes):
         path = os.path.join(tmp, "out.pt")
         mp.spawn(worker, args=(2, free_port(), path, -1, bucket_bytes), nprocs=2, join=True)
         got = torch.load(path)
-    assert got["identical"]
+    assert got["identical"] and got["gaps_zero"] and got["aligned"]
     assert ((got["flat"] - want).norm() / want.norm()).item() < 1e-10
     if bucket_bytes == 1:  # one bucket per parameter: most start inside backward
         assert got["buckets"] == 10
