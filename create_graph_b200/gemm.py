@@ -6,6 +6,12 @@ takes ``a`` as (K, M) and ``b_t=True`` takes ``b`` as (K, N), read in place
 (MN-major operands), so x W^T, g W and g^T x need no transposed copies.
 Arithmetic: tf32 products (fp32 operands rounded by the tensor core), fp32
 accumulation.
+
+Operands need 16-byte aligned bases and row pitches (the TMA rule); bases on
+256-byte boundaries, as separate allocations have, keep each 128-byte TMA row
+within one cache line: weights viewed at 16-byte offsets into a shared buffer
+measured 20% slower on the model's GEMMs (ddp.FlatGradients and
+optim.FusedAdamW lay their flat buffers out on 256-byte boundaries for this).
 """
 
 from __future__ import annotations
