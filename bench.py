@@ -173,6 +173,7 @@ def run_mine(args):
     torch.cuda.synchronize()
 
     # ---- device-resident throughput ----
+    torch.cuda.reset_peak_memory_stats(dev)
     launches0 = native.launch_count()
     with ClockSampler(local) as clocks:
         barrier()
@@ -185,6 +186,7 @@ def run_mine(args):
         torch.cuda.synchronize()
         barrier()
     launches = native.launch_count() - launches0
+    peak_gb = max_over_ranks(torch.cuda.max_memory_allocated(dev) / 1e9)
     ms = max_over_ranks(start.elapsed_time(end)) / args.steps
     total_atoms = sum_over_ranks(n_atoms)
     value = total_atoms / (ms / 1e3)
@@ -244,6 +246,9 @@ def run_mine(args):
             },
             "e2e": e2e,
             "gpu_launches": launches,
+            # torch.cuda.max_memory_allocated over the timed steps (max over ranks):
+            # parameters, gradients, AdamW moments and the step's activations
+            "peak_memory_gb": peak_gb,
             "roofline": roofline,
             # the GEMM entry point as a whole (every shape of the step) against the tf32 peak
             "roofline_gemm": (_gemm_roofline(kernels["cg_gemm_tf32"]["calls"], bf16_sus, src)

@@ -14,9 +14,21 @@ src/create_graph/compile_config.py:25-66. What they mean here:
 - ``dynamic``: accepted for compatibility. Every kernel takes its sizes at run
   time, so no batch size ever recompiles anything.
 - ``memory_budget``: fraction in (0, 1] of the activation bytes a region may
-  keep. Fused ops read it through ``active_memory_budget()``: below 1 they keep
-  only their inputs and recompute cheap intermediates (pre-activations,
-  softmax probabilities) inside their backward kernels.
+  keep (None: 1). The reference hands it to AOTAutograd's min-cut
+  partitioner; here the fused ops read it through ``active_memory_budget()``
+  when they record their saved tensors, and give up the intermediates that
+  are cheapest to rebuild, in three tiers:
+
+  - below 1: the FFN's second-order factor u = g W2 (rows x FFN width) is not
+    kept by the force pass; the parameter backward rebuilds it with one GEMM;
+  - 0.5 or less: also the FFN's SiLU activation (rows x FFN width), rebuilt
+    from its pre-activation by one elementwise kernel;
+  - 0.25 or less: also every LayerNorm output held for the gamma gradient
+    (rows x hidden), rebuilt from the normalisation input.
+
+  Rebuilt tensors equal the kept ones bit for bit (same kernels, same
+  inputs), so a budget changes peak memory and time, never results. Inside
+  ``checkpoint`` blocks it applies to the block being recomputed.
 - ``checkpoint``: regex of block module paths recomputed per block
   (create_graph_b200.checkpoint).
 - ``options``: free (key, value) pairs, kept sorted and hashable.

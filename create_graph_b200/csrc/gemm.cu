@@ -15,10 +15,18 @@
 // A and B are each either K-major (rows contiguous along K) or MN-major
 // (contiguous along M / N), so the forward (x W^T), the data gradient (g W)
 // and the weight gradient (g^T x) all read their operands in place.
+// Precision: CG_GEMM_TF32 makes one tf32 product per k-slice. CG_GEMM_FP32
+// adds a converter warpgroup (warps 2 + EPI ..): once a stage lands it
+// rewrites every operand x in place as hi = x truncated to tf32 and writes
+// lo = x - hi (exact) beside it; the issuer then accumulates A_lo B_hi +
+// A_hi B_lo + A_hi B_hi, which keeps fp32-level accuracy (the dropped
+// A_lo B_lo term and lo's own tf32 rounding are ~2^-21 relative).
 // Every mbarrier wait is bounded: on timeout the kernel records an error in
 // the device error word and unwinds, freeing its TMEM.
 #include <cudaTypedefs.h>
 #include <math.h>
+
+#include <atomic>
 
 #include "common.cuh"
 #include "sm100.cuh"
@@ -35,8 +43,10 @@ using namespace cg::sm100;
 constexpr int BM = 128;
 constexpr int BK = 32;  // fp32 elements per k-slice: one 128-byte swizzle row
 // warp 0 TMA producer, warp 1 UMMA issuer, then EPI epilogue warps (4, or 8 for
-// GEMMs whose epilogue streams extra operands: two warps per TMEM lane quarter)
-__host__ __device__ constexpr int threads_of(int epi) { return 32 * (2 + epi); }
+// GEMMs whose epilogue streams extra operands: two warps per TMEM lane quarter),
+// then, in the three-term split mode, CONV converter warps
+constexpr int CONV = 4;
+__host__ __device__ constexpr int threads_of(int epi, bool split = false) { return 32 * (2 + epi + (split ? CONV : 0)); }
 constexpr int kStagePitch = 36;  // floats per staged row: 16-byte rows, conflict-free 128-bit access
 
 struct Epilogue {
@@ -63,11 +73,22 @@ __device__ inline float silu_grad(float z) {
   return s * (1.0f + z * (1.0f - s));
 }
 
-template <int BN, int STAGES, int EPI = 4>
+// x = hi + lo with hi = x truncated to tf32 (the low 13 mantissa bits
+// cleared: exactly representable, so the tensor core's own tf32 conversion
+// leaves it alone) and lo = x - hi (exact in fp32). A non-finite operand makes
+// its products NaN in this mode (inf - inf, or inf times a zero lo term).
+__device__ inline void split_tf32(float x, float& hi, float& lo) {
+  hi = __uint_as_float(__float_as_uint(x) & 0xffffe000u);
+  lo = x - hi;
+}
+
+template <int BN, int STAGES, int EPI = 4, bool SPLIT = false>
 struct Smem {
   static constexpr int kA = BM * BK * 4;
   static constexpr int kB = BN * BK * 4;
-  static constexpr int kStage = kA + kB;
+  static constexpr int kLoad = kA + kB;                      // bytes TMA brings per stage
+  static constexpr int kStage = SPLIT ? 2 * kLoad : kLoad;   // + the lo copies of A and B
+  static_assert(kLoad % 1024 == 0, "lo tiles keep the 1024-byte swizzle alignment");
   static constexpr int kTiles = STAGES * kStage;
   static constexpr int kStaging = EPI * 32 * kStagePitch * 4;  // epilogue transpose, one 32 x 36 block per warp
   static constexpr int kBytes = kTiles + kStaging + 1024 /*alignment*/ + 256 /*barriers*/;
@@ -136,12 +157,12 @@ __device__ inline void epilogue_store4(const Epilogue& ep, int64_t row, int col,
 // tile to partial[z] (M x N); the reduction pass adds the splits in z order.
 // Two TMEM accumulators (2 * BN columns) let the epilogue of item j overlap
 // the UMMAs of item j + 1.
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(threads_of(EPI), 1)
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, bool SPLIT>
+__global__ void __launch_bounds__(threads_of(EPI, SPLIT), 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                      int M, int N, int K, int kt_per, int splits, float* partial, Epilogue ep) {
   static_assert(EPI == 4 || EPI == 8, "four or eight epilogue warps");
-  using S = Smem<BN, STAGES, EPI>;
+  using S = Smem<BN, STAGES, EPI, SPLIT>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // tiles need 1024-byte alignment for the 128B swizzle pattern
   unsigned char* tiles = reinterpret_cast<unsigned char*>(
@@ -151,7 +172,8 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* split_done = acc_empty + 2;  // SPLIT: stage s converted (one arrival per converter warp)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(split_done + (SPLIT ? STAGES : 0));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + BN - 1) / BN;
@@ -164,6 +186,7 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      if (SPLIT) mbar_init(&split_done[s], CONV);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
@@ -201,7 +224,7 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
         if (it >= STAGES && !(ok = mbar_wait(&empty[s], (round - 1) & 1, &g_gemm_error))) break;
         unsigned char* sa = tiles + s * S::kStage;
         unsigned char* sb = sa + S::kA;
-        mbar_arrive_expect_tx(&full[s], S::kStage);
+        mbar_arrive_expect_tx(&full[s], S::kLoad);
         const int k0 = kt * BK;
         if (!A_MN) {
           tma_load_2d(sa, &map_a, &full[s], k0, m0);
@@ -232,24 +255,69 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
       const uint32_t acc = tmem + b * BN;
       for (int kt = kt0; kt < kt1; ++kt, ++it) {
         const int s = it % STAGES;
-        if (!(ok = mbar_wait(&full[s], (it / STAGES) & 1, &g_gemm_error))) break;
+        if (!(ok = mbar_wait(SPLIT ? &split_done[s] : &full[s], (it / STAGES) & 1, &g_gemm_error))) break;
         tc_fence_after();
         const uint32_t sa = smem_u32(tiles + s * S::kStage);
         const uint32_t sb = sa + S::kA;
+        // K-major (128B swizzle, 8-row groups at 1024 B): advance 32 bytes
+        // along the row. MN-major (128B swizzle with 32 B granules, 4-row K
+        // groups at 512 B, 32-wide MN groups at BK * 128 B): advance 8 rows.
+        auto desc_a = [](uint32_t base, int kk) {
+          return A_MN ? smem_desc(base + kk * 1024, BK * 128, 512, kSwizzle128BBase32B)
+                      : smem_desc(base + kk * 32, 16, 1024, kSwizzle128B);
+        };
+        auto desc_b = [](uint32_t base, int kk) {
+          return B_MN ? smem_desc(base + kk * 1024, BK * 128, 512, kSwizzle128BBase32B)
+                      : smem_desc(base + kk * 32, 16, 1024, kSwizzle128B);
+        };
 #pragma unroll
         for (int kk = 0; kk < BK / 8; ++kk) {
-          // K-major (128B swizzle, 8-row groups at 1024 B): advance 32 bytes
-          // along the row. MN-major (128B swizzle with 32 B granules, 4-row K
-          // groups at 512 B, 32-wide MN groups at BK * 128 B): advance 8 rows.
-          const uint64_t ad = A_MN ? smem_desc(sa + kk * 1024, BK * 128, 512, kSwizzle128BBase32B)
-                                   : smem_desc(sa + kk * 32, 16, 1024, kSwizzle128B);
-          const uint64_t bd = B_MN ? smem_desc(sb + kk * 1024, BK * 128, 512, kSwizzle128BBase32B)
-                                   : smem_desc(sb + kk * 32, 16, 1024, kSwizzle128B);
-          umma_tf32(acc, ad, bd, idesc, kt > kt0 || kk > 0);
+          const bool acc_on = kt > kt0 || kk > 0;
+          if (SPLIT) {
+            // the small cross terms first, then the hi product
+            umma_tf32(acc, desc_a(sa + S::kLoad, kk), desc_b(sb, kk), idesc, acc_on);
+            umma_tf32(acc, desc_a(sa, kk), desc_b(sb + S::kLoad, kk), idesc, true);
+            umma_tf32(acc, desc_a(sa, kk), desc_b(sb, kk), idesc, true);
+          } else {
+            umma_tf32(acc, desc_a(sa, kk), desc_b(sb, kk), idesc, acc_on);
+          }
         }
         umma_commit(&empty[s]);
       }
       umma_commit(&acc_full[b]);
+    }
+  } else if (SPLIT && warp >= 2 + EPI) {
+    // ---------------- three-term split converter ----------------
+    // Stage s holds A then B as TMA wrote them (kLoad bytes, swizzled); the
+    // same bytes at +kLoad receive the lo parts. The transform is elementwise,
+    // so the swizzle carries over unchanged.
+    const int ct = threadIdx.x - 32 * (2 + EPI);
+    bool ok = true;
+    uint32_t it = 0;
+    for (int w = blockIdx.x; w < items && ok; w += gridDim.x) {
+      int m0, n0, kt0, kt1;
+      item_coords(w, m0, n0, kt0, kt1);
+      for (int kt = kt0; kt < kt1; ++kt, ++it) {
+        const int s = it % STAGES;
+        if (!(ok = mbar_wait(&full[s], (it / STAGES) & 1, &g_gemm_error))) break;
+        float4* hi = reinterpret_cast<float4*>(tiles + s * S::kStage);
+        float4* lo = reinterpret_cast<float4*>(tiles + s * S::kStage + S::kLoad);
+#pragma unroll 4
+        for (int i = ct; i < S::kLoad / 16; i += 32 * CONV) {
+          const float4 x = hi[i];
+          float4 h, l;
+          split_tf32(x.x, h.x, l.x);
+          split_tf32(x.y, h.y, l.y);
+          split_tf32(x.z, h.z, l.z);
+          split_tf32(x.w, h.w, l.w);
+          hi[i] = h;
+          lo[i] = l;
+        }
+        // make this thread's generic-proxy writes visible to the tensor core
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&split_done[s]);
+      }
     }
   } else if (warp >= 2) {
     // ---------------- epilogue ----------------
@@ -441,6 +509,7 @@ struct Plan {
   int bn;
   int splits;
   int kt_per;
+  bool split3;  // CG_GEMM_FP32: three-term tf32 split
 };
 
 // Tile width and split-K factor of a problem. Wide (128 x 256) tiles halve
@@ -493,6 +562,9 @@ static Plan plan_of(const cg_gemm_args& g) {
       }
     }
   } else p.bn = 128;
+  // the split mode keeps a lo copy of every stage: tiles up to 128 wide
+  p.split3 = g.precision == CG_GEMM_FP32;
+  if (p.split3 && p.bn > 128) p.bn = 128;
   const int64_t tiles = mt * ceil_div<int64_t>(g.n, p.bn);
   int64_t splits = 1;
   if (tiles < sms && ktiles >= 8) {
@@ -511,7 +583,7 @@ static int64_t workspace_bytes(const cg_gemm_args& g) {
   return p.splits > 1 ? (int64_t)p.splits * g.m * g.n * (int64_t)sizeof(float) : 0;
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI = 4>
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI = 4, bool SPLIT = false>
 static int launch(const cg_gemm_args& g, const Plan& p, cudaStream_t stream) {
   CUtensorMap ma, mb;
   int rc;
@@ -545,14 +617,14 @@ static int launch(const cg_gemm_args& g, const Plan& p, cudaStream_t stream) {
                p.splits, (long long)workspace_bytes(g));
     partial = g.workspace;
   }
-  using S = Smem<BN, STAGES, EPI>;
-  auto kernel = gemm_tf32_kernel<BN, STAGES, A_MN, B_MN, EPI>;
+  using S = Smem<BN, STAGES, EPI, SPLIT>;
+  auto kernel = gemm_tf32_kernel<BN, STAGES, A_MN, B_MN, EPI, SPLIT>;
   CG_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes));
   const int64_t items = ceil_div<int64_t>(g.m, BM) * ceil_div<int64_t>(g.n, BN) * p.splits;
   CG_REQUIRE(items < (1ll << 31), "gemm: too many tiles");
   const int grid = (int)(items < sm_count() ? items : sm_count());
-  kernel<<<grid, threads_of(EPI), S::kBytes, stream>>>(ma, mb, (int)g.m, (int)g.n, (int)g.k, p.kt_per, p.splits, partial,
-                                                ep);
+  kernel<<<grid, threads_of(EPI, SPLIT), S::kBytes, stream>>>(ma, mb, (int)g.m, (int)g.n, (int)g.k, p.kt_per,
+                                                             p.splits, partial, ep);
   CG_LAUNCHED("gemm_tf32");
   if (p.splits > 1) {
     if (ep.vec) {
@@ -569,12 +641,24 @@ static int launch(const cg_gemm_args& g, const Plan& p, cudaStream_t stream) {
   return kOk;
 }
 
-template <int BN, int STAGES, int EPI = 4>
+template <int BN, int STAGES, int EPI = 4, bool SPLIT = false>
 static int launch_majors(const cg_gemm_args& g, const Plan& p, cudaStream_t s) {
-  if (!g.a_mn_major && !g.b_mn_major) return launch<BN, STAGES, false, false, EPI>(g, p, s);
-  if (!g.a_mn_major && g.b_mn_major) return launch<BN, STAGES, false, true, EPI>(g, p, s);
-  if (g.a_mn_major && !g.b_mn_major) return launch<BN, STAGES, true, false, EPI>(g, p, s);
-  return launch<BN, STAGES, true, true, EPI>(g, p, s);
+  if (!g.a_mn_major && !g.b_mn_major) return launch<BN, STAGES, false, false, EPI, SPLIT>(g, p, s);
+  if (!g.a_mn_major && g.b_mn_major) return launch<BN, STAGES, false, true, EPI, SPLIT>(g, p, s);
+  if (g.a_mn_major && !g.b_mn_major) return launch<BN, STAGES, true, false, EPI, SPLIT>(g, p, s);
+  return launch<BN, STAGES, true, true, EPI, SPLIT>(g, p, s);
+}
+
+// Three-term split GEMMs (CG_GEMM_FP32): each stage is twice as large, so
+// fewer stages fit.
+static int run_split3(const cg_gemm_args& g, const Plan& p, cudaStream_t s) {
+  switch (p.bn) {
+    case 16:
+      return g.a_mn_major ? launch<16, 5, true, false, 4, true>(g, p, s) : launch<16, 5, false, false, 4, true>(g, p, s);
+    case 32: return launch_majors<32, 5, 4, true>(g, p, s);
+    case 64: return launch_majors<64, 4, 4, true>(g, p, s);
+    default: return launch_majors<128, 3, 4, true>(g, p, s);
+  }
 }
 
 // Unsplit wide-tile GEMMs with a short main loop (K <= 1024) and K-major A
@@ -604,8 +688,10 @@ static int run(const cg_gemm_args* args, void* stream) {
              "gemm: bad act");
   CG_REQUIRE((g.act != CG_ACT_SILU_GRAD && g.act != CG_ACT_ADD) || g.aux_in != nullptr,
              "gemm: the SiLU gradient and the residual add need aux_in");
+  CG_REQUIRE(g.precision == CG_GEMM_TF32 || g.precision == CG_GEMM_FP32, "gemm: bad precision %d", g.precision);
   cudaStream_t s = as_stream(stream);
   const Plan p = plan_of(g);
+  if (p.split3) return run_split3(g, p, s);
   switch (p.bn) {
     case 16: return g.a_mn_major ? launch<16, 10, true, false>(g, p, s) : launch<16, 10, false, false>(g, p, s);
     case 32: return launch_majors<32, 9>(g, p, s);
@@ -634,18 +720,23 @@ static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
 
 // Device address of the array on the current device, looked up once per device
 // (the first call on a device therefore runs a runtime query; make it before
-// any stream capture).
+// any stream capture). Concurrent first calls from several host threads may
+// each look the address up; they find the same value, and the slots are atomic.
+// A cudaDeviceReset while the library is in use leaves a stale address: the
+// cache is not refreshed.
 static int noalloc_scratch(float** out) {
-  static float* cached[64] = {nullptr};
+  static std::atomic<float*> cached[64];
   int dev = -1;
   CG_CUDA(cudaGetDevice(&dev));
   CG_REQUIRE(dev >= 0 && dev < 64, "gemm_noalloc: device index %d out of range", dev);
-  if (cached[dev] == nullptr) {
-    void* p = nullptr;
-    CG_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
-    cached[dev] = static_cast<float*>(p);
+  float* p = cached[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    void* found = nullptr;
+    CG_CUDA(cudaGetSymbolAddress(&found, g_noalloc_scratch));
+    p = static_cast<float*>(found);
+    cached[dev].store(p, std::memory_order_release);
   }
-  *out = cached[dev];
+  *out = p;
   return kOk;
 }
 

@@ -27,6 +27,9 @@ __device__ inline float silu_d2(float z) {
   const float s = sigm(z);
   return s * (1.0f - s) * (2.0f + z * (1.0f - 2.0f * s));
 }
+// silu itself, written exactly as the GEMM epilogue writes it, so that an
+// activation rebuilt here equals the one the GEMM produced bit for bit
+__device__ inline float silu_value(float z) { return __fdividef(z, 1.0f + __expf(-z)); }
 
 __device__ inline float warp_sum(float v) {
 #pragma unroll
@@ -47,13 +50,13 @@ inline int blocks_for(int64_t n, int threads) {
   return (int)(b < 1 ? 1 : (b < cap ? b : cap));
 }
 
-// mode 0: out = a * silu'(z); mode 1: out = a * b * silu''(z)
+// mode 0: out = a * silu'(z); mode 1: out = a * b * silu''(z); mode 2: out = silu(z)
 __global__ void silu_grad_kernel(const float* __restrict__ a, const float* __restrict__ b,
                                  const float* __restrict__ z, float* __restrict__ out, int64_t n,
                                  int mode) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
-    out[i] = mode == 0 ? a[i] * silu_d1(z[i]) : a[i] * b[i] * silu_d2(z[i]);
+    out[i] = mode == 2 ? silu_value(z[i]) : mode == 0 ? a[i] * silu_d1(z[i]) : a[i] * b[i] * silu_d2(z[i]);
   }
 }
 
@@ -61,7 +64,12 @@ __global__ void silu_grad_kernel(const float* __restrict__ a, const float* __res
 __global__ void silu_grad4_kernel(const float4* __restrict__ a, const float4* __restrict__ b,
                                   const float4* __restrict__ z, float4* __restrict__ out, int64_t n4, int mode) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
-    const float4 x = __ldg(a + i), zz = __ldg(z + i);
+    const float4 zz = __ldg(z + i);
+    if (mode == 2) {
+      out[i] = make_float4(silu_value(zz.x), silu_value(zz.y), silu_value(zz.z), silu_value(zz.w));
+      continue;
+    }
+    const float4 x = __ldg(a + i);
     float4 y;
     if (mode == 0) {
       y = make_float4(x.x * silu_d1(zz.x), x.y * silu_d1(zz.y), x.z * silu_d1(zz.z), x.w * silu_d1(zz.w));
@@ -506,6 +514,18 @@ int cg_silu_grad(const float* a, const float* z, float* out, int64_t n, void* st
   else
     pw::silu_grad_kernel<<<pw::blocks_for(n, 256), 256, 0, as_stream(stream)>>>(a, nullptr, z, out, n, 0);
   CG_LAUNCHED("silu_grad");
+  return kOk;
+}
+
+int cg_silu(const float* z, float* out, int64_t n, void* stream) {
+  CG_REQUIRE(n >= 0, "silu: negative size");
+  if (n == 0) return kOk;
+  if (n % 4 == 0 && pw::al16(z) && pw::al16(out))
+    pw::silu_grad4_kernel<<<pw::blocks_for(n / 4, 256), 256, 0, as_stream(stream)>>>(
+        nullptr, nullptr, reinterpret_cast<const float4*>(z), reinterpret_cast<float4*>(out), n / 4, 2);
+  else
+    pw::silu_grad_kernel<<<pw::blocks_for(n, 256), 256, 0, as_stream(stream)>>>(nullptr, nullptr, z, out, n, 2);
+  CG_LAUNCHED("silu");
   return kOk;
 }
 

@@ -91,6 +91,12 @@ __device__ inline void tmem_dealloc(uint32_t taddr, uint32_t cols) {
                : "memory");
 }
 
+// Order this thread's generic-proxy shared-memory writes before later
+// async-proxy reads of them (UMMA operands written by threads, not TMA).
+__device__ inline void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ inline void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }

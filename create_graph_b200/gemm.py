@@ -4,8 +4,12 @@ The tcgen05 GEMM of the dense projections (``cg_gemm_tf32``), on torch tensors.
 ``gemm(a, b)`` computes ``a @ b.T`` for a (M, K) and b (N, K); ``a_t=True``
 takes ``a`` as (K, M) and ``b_t=True`` takes ``b`` as (K, N), read in place
 (MN-major operands), so x W^T, g W and g^T x need no transposed copies.
-Arithmetic: tf32 products (fp32 operands rounded by the tensor core), fp32
-accumulation.
+Arithmetic: fp32 accumulation of tf32 products. ``precision="tf32"`` makes
+one product of tf32-rounded operands; ``precision="fp32"`` splits every
+operand into two tf32 terms on chip and accumulates three products
+(fp32-level accuracy, a third of the tf32 rate). Without an explicit
+argument the precision is the calling thread's current one
+(``gemm_precision``), "tf32" by default.
 
 Operands need 16-byte aligned bases and row pitches (the TMA rule); bases on
 256-byte boundaries, as separate allocations have, keep each 128-byte TMA row
@@ -16,7 +20,9 @@ optim.FusedAdamW lay their flat buffers out on 256-byte boundaries for this).
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
+import threading
 
 import torch
 from torch import Tensor
@@ -25,6 +31,29 @@ from create_graph_b200 import native
 from create_graph_b200.errors import NativeError
 
 ACT_NONE, ACT_SILU, ACT_SILU_GRAD, ACT_ADD = native.ACT_NONE, native.ACT_SILU, native.ACT_SILU_GRAD, native.ACT_ADD
+PRECISIONS = {"tf32": native.GEMM_TF32, "fp32": native.GEMM_FP32}
+
+_THREAD = threading.local()
+
+
+def current_precision() -> str:
+    """The GEMM precision of the calling thread ("tf32" unless set)."""
+    return getattr(_THREAD, "precision", "tf32")
+
+
+@contextlib.contextmanager
+def gemm_precision(precision: str):
+    """Run the GEMMs of this thread at ``precision`` ("tf32" or "fp32") inside
+    the block. Fused ops record the precision of their forward and re-enter it
+    in their backward, which autograd runs on its own threads."""
+    if precision not in PRECISIONS:
+        raise NativeError(f"gemm precision must be one of {sorted(PRECISIONS)}, got {precision!r}")
+    before = current_precision()
+    _THREAD.precision = precision
+    try:
+        yield
+    finally:
+        _THREAD.precision = before
 
 
 def _operand(t: Tensor, name: str) -> Tensor:
@@ -55,6 +84,7 @@ def gemm(
     out: Tensor | None = None,
     accumulate: bool = False,
     alpha: float = 1.0,
+    precision: str | None = None,
 ) -> Tensor:
     native.require_cuda(a, b, bias, aux_in, aux_out, out)
     a = _operand(a, "a")
@@ -91,6 +121,10 @@ def gemm(
     args.aux_out = None if aux_out is None else aux_out.data_ptr()
     args.a_mn_major, args.b_mn_major = int(a_t), int(b_t)
     args.act, args.accumulate, args.alpha = act, int(accumulate), float(alpha)
+    precision = current_precision() if precision is None else precision
+    if precision not in PRECISIONS:
+        raise NativeError(f"gemm: precision must be one of {sorted(PRECISIONS)}, got {precision!r}")
+    args.precision = PRECISIONS[precision]
     ws_bytes = native.lib().cg_gemm_workspace_bytes(ctypes.byref(args))
     workspace = None
     if ws_bytes > 0:

@@ -10,6 +10,7 @@ here and the CPU oracle in oracle/step.py, which restates it in plain torch.
         x   = LN(h);  qkv = x Wqkv^T + b            (n, 3C)       tcgen05 GEMM
         tok = qkv[nbr]  (read in place by the attention kernels through the index)
         bias = rbf Wb^T + bb                        (n*k, H)      per-key RBF bias
+                                                    (all blocks' Wb: one parameter)
         o   = attention among the k tokens of each atom, keys past counts masked
         m   = sum_s env[i, s] o[i, s]               (n, C)        envelope pooling
         h   = h + m Wo^T + bo
@@ -36,6 +37,7 @@ from torch import Tensor, nn
 
 import create_graph_b200 as cg
 from create_graph_b200 import nn as cgnn
+from create_graph_b200.gemm import gemm_precision
 from create_graph_b200.graph import AtomsBatch, build_graph, make_batch
 
 
@@ -50,8 +52,10 @@ class ModelSpec:
     cutoff: float
     k: int
     # tensor-core product precision of the edge attention: "fp32" (three-term
-    # tf32 split) or "tf32" (one product, the precision of the projections)
+    # tf32 split) or "tf32" (one product)
     attn_precision: str = "fp32"
+    # the same for the projections and FFNs (the tcgen05 GEMMs)
+    gemm_precision: str = "tf32"
 
     @property
     def head_dim(self) -> int:
@@ -63,9 +67,12 @@ class ModelSpec:
         return 0.5 / (step * step)
 
 
-SMALL_MLIP = ModelSpec(n_species=10, hidden=128, heads=4, blocks=4, ffn=512, n_rbf=64, cutoff=6.0, k=32)
+# the small MLIP is specified in fp32: every product at fp32 accuracy
+SMALL_MLIP = ModelSpec(n_species=10, hidden=128, heads=4, blocks=4, ffn=512, n_rbf=64, cutoff=6.0, k=32,
+                       attn_precision="fp32", gemm_precision="fp32")
+# the 85M model runs TF32 GEMMs with fp32 accumulation, and tf32 attention products
 ALLSCAIP_85M = ModelSpec(n_species=50, hidden=768, heads=12, blocks=12, ffn=3072, n_rbf=128, cutoff=6.0, k=30,
-                         attn_precision="tf32")
+                         attn_precision="tf32", gemm_precision="tf32")
 SPECS = {"small_mlip": SMALL_MLIP, "allscaip_85m": ALLSCAIP_85M}
 
 
@@ -76,17 +83,24 @@ class Block(nn.Module):
         self.heads = s.heads
         self.scale = 1.0 / math.sqrt(s.head_dim)
         self.precision = s.attn_precision
+        self.gemm_precision = s.gemm_precision
         self.norm1 = cgnn.LayerNorm(c)
         self.qkv = cgnn.Linear(c, 3 * c)
-        # per-key attention bias from the RBF features; applied for all blocks at
-        # once by EnergyNetwork (one GEMM over the shared RBF tensor)
-        self.rbf_bias = cgnn.Linear(s.n_rbf, s.heads)
+        # (the block's per-key attention bias from the RBF features is a row
+        # block of EnergyNetwork.rbf_bias: one GEMM over the RBF tensor serves
+        # every block)
         self.out = cgnn.Linear(c, c)
         self.norm2 = cgnn.LayerNorm(c)
         self.ffn1 = cgnn.Linear(c, s.ffn, silu=True)
         self.ffn2 = cgnn.Linear(s.ffn, c)
 
     def forward(self, h: Tensor, bias: Tensor, env: Tensor, graph: cgnn.NeighborGraph) -> Tensor:
+        # the precision is entered here, not by the caller, so that a checkpoint
+        # recompute of the block runs its GEMMs at the same precision
+        with gemm_precision(self.gemm_precision):
+            return self._forward(h, bias, env, graph)
+
+    def _forward(self, h: Tensor, bias: Tensor, env: Tensor, graph: cgnn.NeighborGraph) -> Tensor:
         # attention among the atom's edge tokens, pooled by the envelope, one fused op
         # residual adds in the GEMM epilogues; each residual's two gradients meet
         # inside the LayerNorm backward kernel
@@ -105,18 +119,23 @@ class EnergyNetwork(nn.Module):
         self.spec = s
         self.embed = nn.Parameter(torch.randn(s.n_species, s.hidden) * 0.5)
         self.blocks = nn.ModuleList(Block(s) for _ in range(s.blocks))
+        # rows b*H .. (b+1)*H - 1: block b's per-key attention bias (bias_b =
+        # rbf W_b^T + b_b); one parameter, so no per-step concatenation
+        self.rbf_bias = cgnn.Linear(s.n_rbf, s.blocks * s.heads)
         self.norm = cgnn.LayerNorm(s.hidden)
         self.readout = cgnn.Linear(s.hidden, 1)
 
     def forward(self, pos: Tensor, graph: cgnn.NeighborGraph, species_csr: cgnn.Csr, system_csr: cgnn.Csr) -> Tensor:
+        with gemm_precision(self.spec.gemm_precision):
+            return self._forward(pos, graph, species_csr, system_csr)
+
+    def _forward(self, pos: Tensor, graph: cgnn.NeighborGraph, species_csr: cgnn.Csr, system_csr: cgnn.Csr) -> Tensor:
         s = self.spec
         rbf, env = cgnn.EdgeGeometry.apply(pos, graph, s.n_rbf, s.cutoff, s.rbf_gamma)
         h = cgnn.Gather.apply(self.embed, species_csr)
-        # every block's rbf_bias projection in one GEMM over the RBF tensor, each
-        # block then reading its column block (bias = rbf W_b^T + b_b, as per block)
-        w = torch.cat([block.rbf_bias.weight for block in self.blocks])
-        b = torch.cat([block.rbf_bias.bias for block in self.blocks])
-        biases = cgnn.SplitCols.apply(cgnn.LinearFn.apply(rbf, w, b), s.heads)
+        # every block's bias projection in one GEMM over the RBF tensor, each
+        # block then reading its column block in place
+        biases = cgnn.SplitCols.apply(self.rbf_bias(rbf), s.heads)
         for block, bias in zip(self.blocks, biases):
             h = block(h, bias, env, graph)
         e_atom = self.readout(self.norm(h))

@@ -96,7 +96,7 @@ class GemmArgs(ctypes.Structure):
         ("act", i32),
         ("accumulate", i32),
         ("alpha", ctypes.c_float),
-        ("pad0", i32),
+        ("precision", i32),
         ("workspace", vp),
         ("workspace_bytes", i64),
     ]
@@ -149,6 +149,7 @@ class GeomArgs(ctypes.Structure):
 
 
 ACT_NONE, ACT_SILU, ACT_SILU_GRAD, ACT_ADD = 0, 1, 2, 3
+GEMM_TF32, GEMM_FP32 = 0, 1
 f32 = ctypes.c_float
 _I = ctypes.c_int
 
@@ -175,6 +176,7 @@ _SIGNATURES = {
     "cg_colsum": (_I, [vp, i64, i64, i64, vp, _I, vp, vp]),
     "cg_coldot_scratch_bytes": (i64, [i64, i64]),
     "cg_coldot": (_I, [vp, vp, i64, i64, vp, _I, vp, vp]),
+    "cg_silu": (_I, [vp, vp, i64, vp]),
     "cg_silu_grad": (_I, [vp, vp, vp, i64, vp]),
     "cg_silu_grad2": (_I, [vp, vp, vp, vp, i64, vp]),
     "cg_scale_shift": (_I, [vp, vp, vp, vp, i64, i64, vp]),

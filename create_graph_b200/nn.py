@@ -27,13 +27,14 @@ from __future__ import annotations
 
 import ctypes
 import dataclasses
+import functools
 import math
 
 import torch
 from torch import Tensor, nn
 
 from create_graph_b200 import native
-from create_graph_b200.compile_config import engine_will_execute, gradient_edge
+from create_graph_b200.compile_config import active_memory_budget, engine_will_execute, gradient_edge
 from create_graph_b200.edge_attn import (
     pooled_attention_backward1,
     pooled_attention_backward2,
@@ -43,7 +44,7 @@ from create_graph_b200.edge_attn import (
     token_attention_forward1,
 )
 from create_graph_b200.errors import NativeError
-from create_graph_b200.gemm import ACT_ADD, ACT_SILU, ACT_SILU_GRAD, gemm
+from create_graph_b200.gemm import ACT_ADD, ACT_SILU, ACT_SILU_GRAD, current_precision, gemm, gemm_precision
 
 Function = torch.autograd.Function
 
@@ -65,6 +66,24 @@ def _edges(*tensors):
 def _wanted(ctx, i: int) -> bool:
     """Whether input i's gradient is needed by the backward pass running now."""
     return ctx.needs_input_grad[i] and engine_will_execute(ctx.edges[i])
+
+
+def _keep_precision(ctx) -> None:
+    """Record the GEMM precision of a GEMM op's forward (see _at_forward_precision)."""
+    ctx.precision = current_precision()
+
+
+def _at_forward_precision(backward):
+    """Run a GEMM op's backward, and so every op it records, at the GEMM
+    precision of its forward: autograd calls backwards on its own threads,
+    where the forward thread's setting is not visible."""
+
+    @functools.wraps(backward)
+    def run(ctx, *grads):
+        with gemm_precision(ctx.precision):
+            return backward(ctx, *grads)
+
+    return run
 
 
 def _f32(t: Tensor, name: str) -> Tensor:
@@ -100,11 +119,13 @@ class MM(_Fused):
 
     @staticmethod
     def forward(ctx, a, b):
+        _keep_precision(ctx)
         ctx.save_for_backward(a, b)
         ctx.edges = _edges(a, b)
         return mm_raw(a, b)
 
     @staticmethod
+    @_at_forward_precision
     def backward(ctx, g):
         a, b = ctx.saved_tensors
         ga = MM.apply(g, b.t()) if _wanted(ctx, 0) else None
@@ -158,26 +179,36 @@ class ColDot(_Fused):
 
 
 class ScaleShift(_Fused):
-    """y[r, c] = x[r, c] * gamma[c] + beta[c] (beta optional)."""
+    """y[r, c] = x[r, c] * gamma[c] + beta[c] (beta optional).
+
+    When x is a row normalisation of ``src`` (LayerNorm) and the active memory
+    budget is 0.25 or less, x is not kept: the gamma gradient rebuilds it from
+    ``src`` (which the residual stream keeps alive anyway) with the same
+    normalisation kernel, bit for bit."""
 
     @staticmethod
-    def forward(ctx, x, gamma, beta):
+    def forward(ctx, x, gamma, beta, src=None, eps=None):
         x = _f32(x, "scale_shift")
         out = torch.empty_like(x)
         native.call("cg_scale_shift", x.data_ptr(), native.ptr(gamma), native.ptr(beta), out.data_ptr(),
                     x.shape[0], x.shape[1], _stream())
-        ctx.save_for_backward(x, gamma)
+        ctx.rebuild = src is not None and active_memory_budget() <= 0.25
+        ctx.eps = eps
+        ctx.save_for_backward(src if ctx.rebuild else x, gamma)
         ctx.edges = _edges(x, gamma, beta)
         ctx.has_beta = beta is not None
         return out
 
     @staticmethod
     def backward(ctx, g):
-        x, gamma = ctx.saved_tensors
+        kept, gamma = ctx.saved_tensors
         gx = ScaleShift.apply(g, gamma, None) if _wanted(ctx, 0) else None
-        gg = ColDot.apply(g, x) if _wanted(ctx, 1) else None
+        gg = None
+        if _wanted(ctx, 1):
+            x = RowNorm.apply(kept, ctx.eps) if ctx.rebuild else kept
+            gg = ColDot.apply(g, x)
         gb = ColSum.apply(g) if ctx.has_beta and _wanted(ctx, 2) else None
-        return gx, gg, gb
+        return gx, gg, gb, None, None
 
 
 # ---------------------------------------------------------------------------
@@ -197,12 +228,14 @@ class LinearFn(_Fused):
 
     @staticmethod
     def forward(ctx, x, w, b):
+        _keep_precision(ctx)
         ctx.save_for_backward(x, w)
         ctx.edges = _edges(x, w, b)
         ctx.has_bias = b is not None
         return mm_raw(x, w, bias=b)
 
     @staticmethod
+    @_at_forward_precision
     def backward(ctx, g):
         x, w = ctx.saved_tensors
         return _linear_backward(ctx, g, x, w, ctx.has_bias)
@@ -214,12 +247,14 @@ class LinearResidualFn(_Fused):
 
     @staticmethod
     def forward(ctx, x, w, b, r):
+        _keep_precision(ctx)
         ctx.save_for_backward(x, w)
         ctx.edges = _edges(x, w, b, r)
         ctx.has_bias = b is not None
         return mm_raw(x, w, bias=b, act=ACT_ADD, aux_in=_f32(r, "linear_residual"))
 
     @staticmethod
+    @_at_forward_precision
     def backward(ctx, g):
         x, w = ctx.saved_tensors
         return (*_linear_backward(ctx, g, x, w, ctx.has_bias), g if ctx.needs_input_grad[3] else None)
@@ -249,11 +284,29 @@ class SiluGrad(_Fused):
         return dg, dz
 
 
+class Silu(_Fused):
+    """y = silu(z), elementwise (rebuilds a SiLU activation that was not kept)."""
+
+    @staticmethod
+    def forward(ctx, z):
+        z = _f32(z, "silu")
+        out = torch.empty_like(z)
+        native.call("cg_silu", z.data_ptr(), out.data_ptr(), z.numel(), _stream())
+        ctx.save_for_backward(z)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        (z,) = ctx.saved_tensors
+        return SiluGrad.apply(g, z)
+
+
 class LinearSiluFn(_Fused):
     """(y, z) with z = x @ w.T + b and y = silu(z), from one GEMM."""
 
     @staticmethod
     def forward(ctx, x, w, b):
+        _keep_precision(ctx)
         z = torch.empty(x.shape[0], w.shape[0], device=x.device)
         y = mm_raw(x, w, bias=b, act=ACT_SILU, aux_out=z)
         ctx.save_for_backward(x, w, z)
@@ -265,6 +318,7 @@ class LinearSiluFn(_Fused):
         return y, z
 
     @staticmethod
+    @_at_forward_precision
     def backward(ctx, gy, gz):
         x, w, z = ctx.saved_tensors
         g = None
@@ -283,6 +337,7 @@ class MMSiluGrad(_Fused):
 
     @staticmethod
     def forward(ctx, g, w, z, keep_u=False):
+        _keep_precision(ctx)
         z = _f32(z, "mm_silu_grad")
         # u = g @ w, the second-order term's factor, comes out of the same
         # epilogue when the caller builds a graph through this node (keep_u)
@@ -293,6 +348,7 @@ class MMSiluGrad(_Fused):
         return out
 
     @staticmethod
+    @_at_forward_precision
     def backward(ctx, h):
         g, w, z, u = ctx.saved_tensors
         s = SiluGrad.apply(h, z) if (_wanted(ctx, 0) or _wanted(ctx, 1)) else None  # h * silu'(z)
@@ -315,22 +371,34 @@ class SiluLinearResidualFn(_Fused):
     GEMM with the SiLU derivative in its epilogue) and none to y, so the
     producer's backward runs no separate SiLU-gradient pass. y must have no
     other consumer; its second-order terms still flow through the weight
-    gradient, which reads y."""
+    gradient, which reads y.
+
+    Memory budget (the active region's CompileConfig.memory_budget): below 1
+    the second-order factor u = g @ w is not kept by the force pass (the
+    parameter backward recomputes it with one GEMM); at 0.5 or less y is not
+    kept either (the weight gradient rebuilds it from z, bit for bit)."""
 
     @staticmethod
     def forward(ctx, y, z, w, b, r):
-        ctx.save_for_backward(y, z, w)
+        _keep_precision(ctx)
+        budget = active_memory_budget()
+        ctx.keep_u = budget >= 1.0
+        ctx.save_for_backward(y if budget > 0.5 else None, z, w)
         ctx.edges = _edges(y, z, w, b, r)
         ctx.has_bias = b is not None
         return mm_raw(y, w, bias=b, act=ACT_ADD, aux_in=_f32(r, "silu_linear_residual"))
 
     @staticmethod
+    @_at_forward_precision
     def backward(ctx, g):
         y, z, w = ctx.saved_tensors
         # grad mode is on here exactly when this backward is being recorded
         # (create_graph), i.e. when MMSiluGrad's own backward will run
-        gz = MMSiluGrad.apply(g, w, z, torch.is_grad_enabled()) if _wanted(ctx, 1) else None
-        gw = MM.apply(g.t(), y.t()) if _wanted(ctx, 2) else None
+        keep_u = ctx.keep_u and torch.is_grad_enabled()
+        gz = MMSiluGrad.apply(g, w, z, keep_u) if _wanted(ctx, 1) else None
+        gw = None
+        if _wanted(ctx, 2):
+            gw = MM.apply(g.t(), (y if y is not None else Silu.apply(z)).t())
         gb = ColSum.apply(g) if ctx.has_bias and _wanted(ctx, 3) else None
         gr = g if ctx.needs_input_grad[4] else None
         return None, gz, gw, gb, gr
@@ -824,10 +892,10 @@ class LayerNorm(nn.Module):
         self.eps = eps
 
     def forward(self, x: Tensor) -> Tensor:
-        return ScaleShift.apply(RowNorm.apply(x, self.eps), self.weight, self.bias)
+        return ScaleShift.apply(RowNorm.apply(x, self.eps), self.weight, self.bias, x, self.eps)
 
     def branch(self, x: Tensor) -> tuple[Tensor, Tensor]:
         """(x, LayerNorm(x)) for a residual block: x's two gradients meet inside
         the normalisation backward kernel."""
         x_res, xhat = BranchNorm.apply(x, self.eps)
-        return x_res, ScaleShift.apply(xhat, self.weight, self.bias)
+        return x_res, ScaleShift.apply(xhat, self.weight, self.bias, x, self.eps)

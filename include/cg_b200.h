@@ -166,8 +166,9 @@ int cg_pooled_attn_bwd1(const cg_pooled_attn_args* a, void* stream);
 int cg_pooled_attn_bwd2(const cg_pooled_attn_args* a, void* stream);
 
 /* ------------------------------------------------------------------------
- * Dense projections on the tcgen05 tensor cores (kind::tf32: fp32 operands
- * rounded to tf32, fp32 accumulation in TMEM):
+ * Dense projections on the tcgen05 tensor cores (kind::tf32, fp32
+ * accumulation in TMEM; `precision` picks one tf32 product or the
+ * three-term split of fp32 accuracy):
  *   C[m, n] = epi( alpha * sum_k A(m, k) B(n, k) )
  * A(m, k) is a[m*lda + k] (K-major) or a[k*lda + m] (a_mn_major);
  * B(n, k) is b[n*ldb + k] (K-major) or b[k*ldb + n] (b_mn_major).
@@ -184,6 +185,10 @@ int cg_pooled_attn_bwd2(const cg_pooled_attn_args* a, void* stream);
 #define CG_ACT_SILU 1
 #define CG_ACT_SILU_GRAD 2
 #define CG_ACT_ADD 3
+/* product precision (cg_gemm_args.precision) */
+#define CG_GEMM_TF32 0 /* one product of tf32-rounded operands, fp32 accumulation */
+#define CG_GEMM_FP32 1 /* three-term tf32 split x = hi + lo: A_lo B_hi + A_hi B_lo + A_hi B_hi,
+                          fp32-level accuracy (<= 1e-5 relative) at a third of the tf32 rate */
 
 typedef struct cg_gemm_args {
   int64_t m, n, k;
@@ -200,7 +205,7 @@ typedef struct cg_gemm_args {
   int32_t a_mn_major, b_mn_major;
   int32_t act, accumulate;
   float alpha;
-  int32_t pad0;
+  int32_t precision;     /* CG_GEMM_TF32 (0) or CG_GEMM_FP32 (1) */
   float* workspace;         /* split-K partial tiles; cg_gemm_workspace_bytes() bytes */
   int64_t workspace_bytes;
 } cg_gemm_args;
@@ -220,10 +225,12 @@ int64_t cg_gemm_workspace_bytes(const cg_gemm_args* args);
  * (ignored); every GPU that loads the library holds that buffer until exit.
  * Shapes needing more scratch are rejected with an error before any launch.
  * The call allocates nothing; its first call on a device looks up the
- * buffer's address (make it before any stream capture). All calls share the
- * buffer, so calls that overlap on the GPU (other streams, other threads)
- * race; each call writes every scratch element it later reads, so nothing
- * needs clearing between calls. No counterpart in the reference. */
+ * buffer's address (make it before any stream capture) and caches it for the
+ * process (host threads may make first calls concurrently; a cudaDeviceReset
+ * while the library is in use leaves the cached address stale). All calls
+ * share the buffer, so calls that overlap on the GPU (other streams, other
+ * threads) race; each call writes every scratch element it later reads, so
+ * nothing needs clearing between calls. No counterpart in the reference. */
 int cg_gemm_tf32_noalloc(const cg_gemm_args* args, void* stream);
 
 /* ------------------------------------------------------------------------
@@ -263,6 +270,10 @@ int cg_coldot(const float* a, const float* b, int64_t rows, int64_t cols, float*
  * Pointwise and per-row kernels of the energy network (nn.SiLU, nn.LayerNorm
  * of the reference's test models, tests/test_semantics.py:51-69 there).
  * ---------------------------------------------------------------------- */
+/* out = silu(z) = z / (1 + exp(-z)), the same arithmetic as the GEMM's SiLU
+ * epilogue (a rebuilt activation equals the GEMM's bit for bit); rebuilds
+ * activations a memory budget below 1 did not keep. */
+int cg_silu(const float* z, float* out, int64_t n, void* stream);
 /* out = a * silu'(z) */
 int cg_silu_grad(const float* a, const float* z, float* out, int64_t n, void* stream);
 /* out = a * b * silu''(z) */

@@ -61,12 +61,14 @@ def energy(params: dict, spec, pos, species, sys_ptr, nbr, counts):
     rbf, env, valid, j = geometry(pos, nbr, spec.n_rbf, spec.cutoff, spec.rbf_gamma)
     h = p("embed")[species.long()]
     scale = 1.0 / math.sqrt(spec.head_dim)
+    w_bias, b_bias = p("rbf_bias.weight"), p("rbf_bias.bias")  # block b: rows b*H .. (b+1)*H - 1
+    H = spec.heads
     for b in range(spec.blocks):
         q = lambda name, b=b: p(f"blocks.{b}.{name}")  # noqa: E731
         x = F.layer_norm(h, (spec.hidden,), q("norm1.weight"), q("norm1.bias"), 1e-5)
         qkv = F.linear(x, q("qkv.weight"), q("qkv.bias"))
         tok = qkv[j] * valid[:, None]
-        bias = F.linear(rbf, q("rbf_bias.weight"), q("rbf_bias.bias"))
+        bias = F.linear(rbf, w_bias[b * H:(b + 1) * H], b_bias[b * H:(b + 1) * H])
         o = masked_attention(tok, bias, counts, spec.heads, scale, n, k)
         m = (env.view(n, k, 1) * o).sum(1)
         h = h + F.linear(m, q("out.weight"), q("out.bias"))

@@ -1,14 +1,17 @@
 """
 Generate the golden vectors under tests/golden/ by running the reference itself.
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <reference checkout>
 
 Imports the reference package read-only from its source tree (``src/`` and the
 repository root for ``kernels.edge_attn``) and records, for seeded inputs, what
 its own ``cg_kernels::edge_attn`` operators (forward1 / backward1 / backward2,
-kernels/edge_attn/ops.py) and its ``create_graph`` step (examples/mlp.py-style
-model) return. The fixtures are small ``.npz`` files; the GPU box never needs
-the reference. Re-running this script reproduces them bit for bit.
+kernels/edge_attn/ops.py) and its ``create_graph`` step return: on the
+examples/mlp.py-style model, and on the small edge-attention MLIP whose
+energy function is oracle/step.py's (so the fixture pins the oracle's step
+against the reference's own create_graph). The fixtures are small ``.npz``
+files; the GPU box never needs the reference. Re-running this script
+reproduces them bit for bit.
 """
 
 from __future__ import annotations
@@ -21,6 +24,7 @@ import numpy as np
 import torch
 
 HERE = pathlib.Path(__file__).resolve().parent
+REPO = HERE.parent.parent
 
 
 def import_reference(root: str):
@@ -139,13 +143,85 @@ def mlp_step_fixture(ref_cg) -> dict:
     return out
 
 
+MLIP_SEED = 7
+MLIP_SIZES = (64, 64, 64)
+
+
+def mlip_step_fixture(ref_cg) -> dict:
+    """One training step of the small edge-attention MLIP through the
+    reference's own create_graph: the small-MLIP spec (C 128, 4 heads of 32,
+    4 blocks, FFN 512, 64 RBF, 6 A cutoff, k <= 32, 10 species) on 3 of the
+    workload's 64-atom systems. Inside ``cg.compile`` runs oracle/step.py's
+    ``energy``; the neighbour lists come from oracle/neighbors.py outside the
+    region; loss = MSE(E) + MSE(F). Float64, compiled (aot_eager) and exact.
+
+    Parameters are the model's own initial draws under torch.manual_seed(seed)
+    (regenerated by the tests, with per-tensor sums stored to catch drift);
+    gradients of more than oracle.sketch.FULL_LIMIT elements are stored as
+    seeded sign-vector sketches."""
+    from torch import nn
+
+    from create_graph_b200 import mlip
+    from oracle import neighbors as onb
+    from oracle import step as ostep
+    from oracle.sketch import sketch
+
+    spec = mlip.SMALL_MLIP
+    torch.manual_seed(MLIP_SEED)
+    params = {name: t.double() for name, t in mlip.reference_parameters(spec).items()}
+    names = list(params)
+    pos, species, sys_ptr = mlip.synthetic_systems(list(MLIP_SIZES), spec.n_species, seed=MLIP_SEED)
+    e_target, f_target = mlip.make_targets(len(MLIP_SIZES), pos.shape[0], seed=MLIP_SEED + 1)
+    nbr, counts, _, _ = onb.neighbor_list(pos.numpy(), sys_ptr.numpy(), spec.cutoff, spec.k)
+    nbr_t, counts_t = torch.from_numpy(nbr), torch.from_numpy(counts)
+
+    class Network(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.weights = nn.ParameterList(nn.Parameter(params[n].clone()) for n in names)
+
+        def forward(self, x, species, sys_ptr, nbr, counts):
+            return ostep.energy(dict(zip(names, self.weights)), spec, x, species, sys_ptr, nbr, counts)
+
+    class Model(nn.Module):
+        def __init__(self, config):
+            super().__init__()
+            self.network = ref_cg.compile(Network(), config=config)
+
+        def forward(self, batch):
+            return {"energy": self.network(batch["pos"], batch["species"], batch["sys_ptr"], batch["nbr"],
+                                           batch["counts"])}
+
+    out = {
+        "seed": np.array(MLIP_SEED), "pos": pos.numpy(), "species": species.numpy(), "sys_ptr": sys_ptr.numpy(),
+        "nbr": nbr, "counts": counts, "e_target": e_target.numpy(), "f_target": f_target.numpy(),
+    }
+    for name in names:
+        out[f"param_sum.{name}"] = np.array([float(params[name].sum()), float(params[name].square().sum())])
+    batch = {"pos": pos.double(), "species": species, "sys_ptr": sys_ptr, "nbr": nbr_t, "counts": counts_t}
+    for label, exact in (("compiled", False), ("exact", True)):
+        model = Model(ref_cg.CompileConfig(backend="aot_eager"))
+        res, grads = ref_cg.create_graph(model, batch, exact=exact)
+        forces = -grads["pos"]
+        loss = (res["energy"] - e_target.double()).square().mean() + (forces - f_target.double()).square().mean()
+        loss.backward()
+        out[f"{label}.energy"] = res["energy"].detach().numpy()
+        out[f"{label}.forces"] = forces.detach().numpy()
+        out[f"{label}.loss"] = loss.detach().numpy()
+        for name, p in zip(names, model.network.module.weights):
+            out[f"{label}.grad.{name}"] = sketch(name, p.grad).numpy()
+    return out
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", required=True, help="root of the reference checkout (read-only)")
     args = parser.parse_args()
+    sys.path.insert(0, str(REPO))
     ref_cg, op = import_reference(args.reference)
     fixtures = edge_attn_fixtures(op)
     fixtures["mlp_step"] = mlp_step_fixture(ref_cg)
+    fixtures["mlip_step"] = mlip_step_fixture(ref_cg)
     for name, arrays in fixtures.items():
         path = HERE / f"{name}.npz"
         np.savez_compressed(path, **arrays)

@@ -143,3 +143,58 @@ def test_strided_operands_in_place():
     x = big[:, 96:192]
     got = gemm(x, w)
     assert rel(got.cpu(), x.double().cpu() @ w.double().cpu().T) < TF32_TOL
+
+
+# ---------------------------------------------------------------------------
+# fp32 precision: the three-term tf32 split (CG_GEMM_FP32)
+# ---------------------------------------------------------------------------
+
+FP32_TOL = 1e-5
+
+
+@pytest.mark.parametrize("a_t", [False, True])
+@pytest.mark.parametrize("b_t", [False, True])
+@pytest.mark.parametrize(
+    "mnk",
+    [(128, 64, 32), (300, 200, 100), (1000, 2304, 768), (768, 768, 4100), (77, 3072, 768), (12, 128, 20000),
+     (5000, 12, 128), (40, 24, 300), (4096, 512, 128)],
+)
+def test_fp32_precision_layouts_and_sizes(a_t, b_t, mnk):
+    m, n, k = mnk
+    a, b, a_dev, b_dev = operands(m, n, k, a_t, b_t, seed=3)
+    got = gemm(a_dev, b_dev, a_t=a_t, b_t=b_t, precision="fp32")
+    torch.cuda.synchronize()
+    assert native.device_error() == 0
+    err = rel(got.cpu(), a.double() @ b.double().T)
+    assert err < FP32_TOL, err
+
+
+def test_fp32_precision_epilogues():
+    m, n, k = 513, 384, 256
+    a, b, a_dev, b_dev = operands(m, n, k, False, False, seed=4)
+    bias = torch.randn(n)
+    pre = torch.empty(m, n, device="cuda")
+    got = gemm(a_dev, b_dev, bias=bias.cuda(), act=ACT_SILU, aux_out=pre, precision="fp32")
+    z = a.double() @ b.double().T + bias.double()
+    assert rel(pre.cpu(), z) < FP32_TOL
+    assert rel(got.cpu(), torch.nn.functional.silu(z)) < FP32_TOL
+    r = torch.randn(m, n)
+    got = gemm(a_dev, b_dev, act=ACT_ADD, aux_in=r.cuda(), precision="fp32")
+    assert rel(got.cpu(), r.double() + a.double() @ b.double().T) < FP32_TOL
+
+
+def test_fp32_precision_is_the_thread_default_inside_gemm_precision():
+    from create_graph_b200.gemm import current_precision, gemm_precision
+
+    a, b, a_dev, b_dev = operands(256, 256, 512, False, False, seed=5)
+    want = a.double() @ b.double().T
+    assert current_precision() == "tf32"
+    with gemm_precision("fp32"):
+        assert current_precision() == "fp32"
+        inside = gemm(a_dev, b_dev)
+    assert current_precision() == "tf32"
+    outside = gemm(a_dev, b_dev)
+    assert rel(inside.cpu(), want) < FP32_TOL
+    assert FP32_TOL < rel(outside.cpu(), want) < TF32_TOL
+    assert torch.equal(inside, gemm(a_dev, b_dev, precision="fp32"))
+

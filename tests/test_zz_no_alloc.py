@@ -2,10 +2,11 @@
 cg_gemm_tf32_noalloc: the GEMM entry point for callers that cannot allocate
 device memory (their device memory belongs to another allocator and they
 forbid cudaMalloc). Called through the C ABI on shapes that split K (so the
-static scratch buffer is used) and one that does not; each result must match
-the allocating entry point cg_gemm_tf32 within the tf32 tolerance of the GEMM
-tests, on two calls in a row (the second call reuses the scratch the first
-one left behind). A shape needing more than the static buffer is refused.
+static scratch buffer is used) and on one that does not (no scratch at all);
+each result must match the allocating entry point cg_gemm_tf32 and a float64
+torch product within the tf32 tolerance of the GEMM tests, on two calls in a
+row (the second call reuses the scratch the first one left behind). A shape
+needing more than the static buffer is refused.
 
 Kept in a file of its own that pytest collects last.
 """
@@ -29,11 +30,9 @@ def rel(a, b):
     return ((a - b).norm() / b.norm()).item()
 
 
-def noalloc_gemm(a_t: torch.Tensor, b_t: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
-    """a_t (K, M) and b_t (K, N) read MN-major: out = a_t.T @ b_t + bias."""
+def gemm_args(a_t: torch.Tensor, b_t: torch.Tensor, bias: torch.Tensor, out: torch.Tensor) -> native.GemmArgs:
     k, m = a_t.shape
     n = b_t.shape[1]
-    out = torch.empty(m, n, device=a_t.device)
     args = native.GemmArgs()
     args.m, args.n, args.k = m, n, k
     args.a, args.lda = a_t.data_ptr(), a_t.stride(0)
@@ -42,22 +41,38 @@ def noalloc_gemm(a_t: torch.Tensor, b_t: torch.Tensor, bias: torch.Tensor) -> to
     args.bias = bias.data_ptr()
     args.a_mn_major, args.b_mn_major = 1, 1
     args.alpha = 1.0
+    return args
+
+
+def noalloc_gemm(a_t: torch.Tensor, b_t: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """a_t (K, M) and b_t (K, N) read MN-major: out = a_t.T @ b_t + bias."""
+    out = torch.empty(a_t.shape[1], b_t.shape[1], device=a_t.device)
+    args = gemm_args(a_t, b_t, bias, out)
     native.check(native.lib().cg_gemm_tf32_noalloc(ctypes.byref(args), native.stream_ptr(a_t.device)))
     return out
 
 
-@pytest.mark.parametrize("mnk", [(12, 128, 50000), (128, 12, 250000), (300, 200, 1000)])
-def test_noalloc_matches_allocating_entry_point_twice(mnk):
+# (m, n, k, splits K): the first three use the static scratch, the last none
+@pytest.mark.parametrize(
+    "mnk, split", [((12, 128, 50000), True), ((128, 12, 250000), True), ((300, 200, 1000), True),
+                   ((1024, 1024, 128), False)])
+def test_noalloc_matches_allocating_entry_point_twice(mnk, split):
     m, n, k = mnk
     gen = torch.Generator().manual_seed(11)
-    a_t = torch.randn(k, m, generator=gen).cuda()
-    b_t = torch.randn(k, n, generator=gen).cuda()
-    bias = torch.randn(n, generator=gen).cuda()
+    a_host = torch.randn(k, m, generator=gen)
+    b_host = torch.randn(k, n, generator=gen)
+    bias_host = torch.randn(n, generator=gen)
+    a_t, b_t, bias = a_host.cuda(), b_host.cuda(), bias_host.cuda()
+    probe = gemm_args(a_t, b_t, bias, torch.empty(1, device="cuda"))
+    need = native.lib().cg_gemm_workspace_bytes(ctypes.byref(probe))
+    assert (need > 0) == split, need
     want = gemm(a_t, b_t, a_t=True, b_t=True, bias=bias)
+    exact = a_host.double().T @ b_host.double() + bias_host.double()
     for _ in range(2):
         got = noalloc_gemm(a_t, b_t, bias)
         torch.cuda.synchronize()
         assert rel(got, want) < TF32_TOL
+        assert rel(got.cpu(), exact) < TF32_TOL
     assert native.device_error() == 0
 
 
