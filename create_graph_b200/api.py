@@ -5,15 +5,23 @@ The entry points ``create_graph``, ``compile`` and ``reset``.
     loss = loss_fn(out, -grads["pos"])
     loss.backward()
 
-Behaviour follows src/create_graph/api.py:148-253: ``data.<input>`` (or
-``data[input]``) is swapped for a fresh leaf, ``model(data)`` runs once, and
-``grads[input]`` is the gradient of ``sum(out[outputs])`` w.r.t. it,
-differentiable w.r.t. the parameters when training.
+The contract is the reference's (src/create_graph/api.py:148-253 there): the
+named entries of ``data`` (dict keys or attributes) are differentiated,
+``model(data)`` runs once, and ``grads[name]`` is the gradient of
+``sum(out[outputs])`` with respect to ``data[name]``, differentiable with
+respect to the parameters in training. The arguments, defaults and
+``ContractError`` texts are kept so that user code and tests run unchanged.
+
+How it is done here: an ``_InputSwap`` puts fresh leaves into ``data`` for
+the duration of the model call (guarded so that the model itself cannot
+differentiate them); the one ``cg.compile`` region whose inputs depend on them
+records its differentiated output and the gradients of its inputs while it
+runs (create_graph_b200.region), and ``create_graph`` chains those back to
+the leaves.
 """
 
 from __future__ import annotations
 
-import contextlib
 import warnings
 from collections.abc import Callable, Sequence
 
@@ -37,32 +45,6 @@ from create_graph_b200.region import (
     select_output,
 )
 
-_grad = torch.autograd.grad
-
-
-def get_input(data, key: str) -> Tensor:
-    return data[key] if isinstance(data, dict) else getattr(data, key)
-
-
-def _set_input(data, key: str, value) -> None:
-    if isinstance(data, dict):
-        data[key] = value
-    else:
-        setattr(data, key, value)
-
-
-@contextlib.contextmanager
-def swapped_inputs(data, values: dict[str, Tensor]):
-    originals = {key: get_input(data, key) for key in values}
-    for key, value in values.items():
-        _set_input(data, key, value)
-    try:
-        yield
-    finally:
-        for key, value in originals.items():
-            _set_input(data, key, value)
-
-
 _GRAD_IN_MODEL = (
     "create_graph: the model computed a gradient w.r.t. a differentiated input during "
     "create_graph (torch.autograd.grad or backward). The model must only compute the "
@@ -71,57 +53,68 @@ _GRAD_IN_MODEL = (
 )
 
 
-def _forbidden_grad(grad):
+def get_input(data, key: str) -> Tensor:
+    """``data[key]`` for mappings, ``data.key`` otherwise."""
+    return data[key] if isinstance(data, dict) else getattr(data, key)
+
+
+class _InputSwap:
+    """Fresh leaves in place of the differentiated entries of ``data`` while the
+    model runs; the original tensors are back afterwards, whatever happens.
+    A hook on every leaf turns any gradient the model itself takes w.r.t. them
+    into the contract error (create_graph computes those gradients)."""
+
+    def __init__(self, data, names: Sequence[str]):
+        self.data = data
+        self.leaves = {name: get_input(data, name).detach().requires_grad_(True) for name in names}
+        self._saved: dict[str, Tensor] = {}
+        self._hooks: list = []
+
+    def _write(self, key: str, value) -> None:
+        if isinstance(self.data, dict):
+            self.data[key] = value
+        else:
+            setattr(self.data, key, value)
+
+    def __enter__(self) -> _InputSwap:
+        for key, leaf in self.leaves.items():
+            self._saved[key] = get_input(self.data, key)
+            self._write(key, leaf)
+            self._hooks.append(leaf.register_hook(_refuse_gradient))
+        return self
+
+    def __exit__(self, *exc) -> None:
+        for hook in self._hooks:
+            hook.remove()
+        for key, original in self._saved.items():
+            self._write(key, original)
+
+
+def _refuse_gradient(_grad):
     raise ContractError(_GRAD_IN_MODEL)
 
 
-@contextlib.contextmanager
-def _no_input_gradients(leaves: dict[str, Tensor]):
-    """While the model runs, nothing may differentiate w.r.t. the inputs."""
-    handles = [leaf.register_hook(_forbidden_grad) for leaf in leaves.values()]
-    try:
-        yield
-    finally:
-        for handle in handles:
-            handle.remove()
-
-
-def _same_entries(target: Tensor, selected: Tensor) -> bool:
-    """``target`` is ``selected`` or a view of it with the same elements."""
-    if target is selected:
-        return True
-    return (
-        target.numel() == selected.numel()
-        and target.data_ptr() == selected.data_ptr()
-        and target.untyped_storage().data_ptr() == selected.untyped_storage().data_ptr()
-    )
-
-
-def _reaches_inputs_besides(target: Tensor, selected: Tensor, state: State) -> bool:
-    """Whether ``target`` depends on the differentiated inputs other than through ``selected``."""
-    inputs = state.leaf_index()
-    stop = selected.grad_fn
-    todo = [target.grad_fn] if target.grad_fn is not None else []
-    seen = set()
-    while todo:
-        node = todo.pop()
-        if node is None or node is stop or node in seen:
-            continue
-        seen.add(node)
-        variable = getattr(node, "variable", None)
-        if variable is not None and id(variable) in inputs:
-            return True
-        todo.extend(child for child, _ in node.next_functions)
-    return False
+def _default_train(model) -> bool:
+    return torch.is_grad_enabled() and bool(getattr(model, "training", True))
 
 
 def _check_output(target: Tensor, state: State) -> None:
-    """The region's VJP is that of sum(selected): the model's output must have the
-    same entries, or add to them terms independent of the differentiated inputs
-    (src/create_graph/api.py:115-142). Returning the region's output itself
-    avoids the one host synchronisation this check can cost."""
+    """The region computed the VJP of sum(selected); the model's differentiated
+    output may be selected itself (or a view with its entries), or selected
+    plus terms that do not depend on the differentiated inputs.
+
+    The region ran on detached copies of its inputs, so selected's autograd
+    graph never reaches the create_graph leaves: one gradient query of
+    sum(target) w.r.t. (selected, leaves) gives both the coefficient of every
+    entry of selected (must be exactly 1) and whether target reaches a leaf
+    along some other path (any gradient that is not None). Returning the
+    region's output itself skips the query and its host synchronisation."""
     selected = state.region.selected
-    if _same_entries(target, selected):
+    if target is selected or (
+        target.numel() == selected.numel()
+        and target.data_ptr() == selected.data_ptr()
+        and target.untyped_storage().data_ptr() == selected.untyped_storage().data_ptr()
+    ):
         return
     message = (
         "create_graph: the differentiated model output is not the output of region "
@@ -129,22 +122,37 @@ def _check_output(target: Tensor, state: State) -> None:
     )
     if not (target.requires_grad and selected.requires_grad):
         raise ContractError(message + ".")
-    (weight,) = _grad(target.sum(), selected, retain_graph=True, allow_unused=True)
+    leaves = list(state.leaves.values())
+    weight, *through_leaves = torch.autograd.grad(
+        target.sum(), [selected, *leaves], retain_graph=True, allow_unused=True
+    )
     if weight is None:
         raise ContractError(message + ", and it is not computed from it.")
-    if _reaches_inputs_besides(target, selected, state):
+    if any(g is not None for g in through_leaves):
         raise ContractError(
             message + ": it also depends on the differentiated inputs through code after the "
             "region. Move that code into the region."
         )
-    if not bool(torch.all(weight == 1)):
+    if not bool((weight == 1).all()):
         raise ContractError(
             message + ": code after the region scales or drops entries of the region's output. "
             "Move that code into the region, or let the region return what the model returns."
         )
 
 
-_NO_REGION_WARNED: set[int] = set()
+_WARNED_NO_REGION: set[int] = set()
+
+
+def _warn_no_region(model, names) -> None:
+    if id(model) in _WARNED_NO_REGION:
+        return
+    _WARNED_NO_REGION.add(id(model))
+    warnings.warn(
+        "create_graph: the model ran no cg.compile region that depends on "
+        f"{', '.join(names)}, so the gradients come from eager create_graph. Mark the "
+        "part of the model that computes the energy with cg.compile.",
+        stacklevel=3,
+    )
 
 
 def create_graph(
@@ -167,46 +175,38 @@ def create_graph(
     the reference semantics for tests. Under DDP pass the wrapped model.
     """
     names = (inputs,) if isinstance(inputs, str) else tuple(inputs)
-    if train is None:
-        train = torch.is_grad_enabled() and bool(getattr(model, "training", True))
+    train = _default_train(model) if train is None else train
     if not exact and not supports_in_graph_grad():
         warn_eager_fallback("create_graph")
         exact = True
-    leaves = {name: get_input(data, name).detach().requires_grad_(True) for name in names}
-    state = State(leaves=leaves, train=train, exact=exact, outputs=outputs)
+    swap = _InputSwap(data, names)
+    state = State(leaves=swap.leaves, train=train, exact=exact, outputs=outputs)
     STATES.append(state)
     try:
-        with swapped_inputs(data, leaves), torch.enable_grad(), _no_input_gradients(leaves):
+        with swap, torch.enable_grad():
             out = model(data)
     except RuntimeError as error:
-        # the region works on detached copies, so a gradient taken inside the
-        # model w.r.t. an input surfaces as autograd's "not been used" error
+        # regions differentiate detached copies of their inputs, so a gradient
+        # the model takes w.r.t. an input reaches autograd as an unused tensor
         if "not have been used in the graph" in str(error):
             raise ContractError(_GRAD_IN_MODEL) from error
         raise
     finally:
         STATES.pop()
+
     target = select_output(out, outputs)
-    leaf_list = list(leaves.values())
+    leaves = list(swap.leaves.values())
     if state.exact or state.region is None:
-        if not exact and id(model) not in _NO_REGION_WARNED:
-            _NO_REGION_WARNED.add(id(model))
-            warnings.warn(
-                "create_graph: the model ran no cg.compile region that depends on "
-                f"{', '.join(names)}, so the gradients come from eager create_graph. Mark the "
-                "part of the model that computes the energy with cg.compile.",
-                stacklevel=2,
-            )
-        found = _grad(target.sum(), leaf_list, create_graph=train, allow_unused=True)
+        if not exact:
+            _warn_no_region(model, names)
+        found = torch.autograd.grad(target.sum(), leaves, create_graph=train, allow_unused=True)
         if not train:
-            out = tree_map_tensors(lambda t: t.detach(), out)
+            out = tree_map_tensors(Tensor.detach, out)
     else:
         _check_output(target, state)
-        found = state.region.input_grads(leaf_list, train)
-    grads = {
-        name: torch.zeros_like(leaf) if g is None else g
-        for (name, leaf), g in zip(leaves.items(), found)
-    }
+        found = state.region.input_grads(leaves, train)
+    grads = {name: g if g is not None else torch.zeros_like(leaf)
+             for (name, leaf), g in zip(swap.leaves.items(), found)}
     return out, grads
 
 
@@ -222,9 +222,7 @@ def compile(
     create_graph call's) and its VJP over the package's fused kernels."""
     if fn is None:
         return lambda f: compile(f, config=config, outputs=outputs)
-    if isinstance(fn, nn.Module):
-        return RegionModule(fn, config, outputs)
-    return Region(fn, config, outputs)
+    return RegionModule(fn, config, outputs) if isinstance(fn, nn.Module) else Region(fn, config, outputs)
 
 
 def reset() -> None:

@@ -392,8 +392,27 @@ struct AdamW {
   }
 };
 
+// Device-resident step count and bias corrections (cg_adamw_step_counted):
+// advanced by one single-thread kernel before each update, so a captured CUDA
+// graph replays the right step number every time.
+struct AdamWState {
+  int64_t step;
+  float step_size, sqrt_bc2;
+};
+
+__global__ void adamw_advance_kernel(AdamWState* st, float lr, float b1, float b2) {
+  const int64_t t = st->step + 1;
+  st->step = t;
+  st->step_size = (float)((double)lr / (1.0 - pow((double)b1, (double)t)));
+  st->sqrt_bc2 = (float)sqrt(1.0 - pow((double)b2, (double)t));
+}
+
 __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
-                             float* __restrict__ v, int64_t n, AdamW a, bool vec) {
+                             float* __restrict__ v, int64_t n, AdamW a, bool vec, const AdamWState* st = nullptr) {
+  if (st != nullptr) {
+    a.step_size = st->step_size;
+    a.sqrt_bc2 = st->sqrt_bc2;
+  }
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int64_t i0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (vec) {
@@ -653,6 +672,32 @@ int cg_adamw_step(float* param, const float* grad, float* exp_avg, float* exp_av
   const bool vec = pw::al16(param) && pw::al16(grad) && pw::al16(exp_avg) && pw::al16(exp_avg_sq);
   pw::adamw_kernel<<<pw::blocks_for(vec ? (n + 3) / 4 : n, 256), 256, 0, as_stream(stream)>>>(
       param, grad, exp_avg, exp_avg_sq, n, a, vec);
+  CG_LAUNCHED("adamw");
+  return kOk;
+}
+
+int cg_adamw_step_counted(float* param, const float* grad, float* exp_avg, float* exp_avg_sq, int64_t n, float lr,
+                          float beta1, float beta2, float eps, float weight_decay, void* state, void* stream) {
+  CG_REQUIRE(n >= 0, "adamw: negative size");
+  CG_REQUIRE(beta1 >= 0.0f && beta1 < 1.0f && beta2 >= 0.0f && beta2 < 1.0f, "adamw: betas outside [0, 1)");
+  CG_REQUIRE(state != nullptr, "adamw: state is NULL");
+  CG_REQUIRE((reinterpret_cast<uintptr_t>(state) & 7) == 0, "adamw: state must be 8-byte aligned");
+  if (n == 0) return kOk;
+  CG_REQUIRE(param && grad && exp_avg && exp_avg_sq, "adamw: null buffer");
+  pw::AdamW a;
+  a.lr = lr;
+  a.b1 = beta1;
+  a.b2 = beta2;
+  a.eps = eps;
+  a.wd = weight_decay;
+  a.step_size = 0.0f;
+  a.sqrt_bc2 = 1.0f;
+  auto* st = static_cast<pw::AdamWState*>(state);
+  pw::adamw_advance_kernel<<<1, 1, 0, as_stream(stream)>>>(st, lr, beta1, beta2);
+  CG_LAUNCHED("adamw counter");
+  const bool vec = pw::al16(param) && pw::al16(grad) && pw::al16(exp_avg) && pw::al16(exp_avg_sq);
+  pw::adamw_kernel<<<pw::blocks_for(vec ? (n + 3) / 4 : n, 256), 256, 0, as_stream(stream)>>>(
+      param, grad, exp_avg, exp_avg_sq, n, a, vec, st);
   CG_LAUNCHED("adamw");
   return kOk;
 }

@@ -329,10 +329,86 @@ int colsum_launch(const float* src, int64_t ld, int64_t rows, int64_t cols, floa
   return kOk;
 }
 
+
+// ---- CSR of a small many-to-one map (species and similar) -----------------------
+// One block of 1024 threads, rows <= kCsrMaxRows: counts per row (shared
+// atomics on integers: exact), an exclusive scan into row_ptr, then a stable
+// placement pass over 1024-element chunks in which each element's rank among
+// the chunk's elements of its row is its in-warp rank (match + popc) plus the
+// counts of the earlier warps, so perm lists every row's elements in
+// ascending order. No host synchronisation: sizes are known up front.
+constexpr int kCsrMaxRows = 256;
+constexpr int kCsrThreads = 1024;
+
+__global__ void __launch_bounds__(kCsrThreads) csr_small_kernel(const int32_t* __restrict__ index, int64_t n, int rows,
+                                                               int32_t* __restrict__ row_ptr,
+                                                               int32_t* __restrict__ perm) {
+  __shared__ int count[kCsrMaxRows];
+  __shared__ int start[kCsrMaxRows];
+  __shared__ int warp_count[kCsrThreads / 32][kCsrMaxRows];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int r = tid; r < rows; r += kCsrThreads) count[r] = 0;
+  __syncthreads();
+  for (int64_t e = tid; e < n; e += kCsrThreads) {
+    const int r = index[e];
+    if (r >= 0 && r < rows) atomicAdd(&count[r], 1);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int acc = 0;
+    for (int r = 0; r < rows; ++r) {
+      start[r] = acc;
+      row_ptr[r] = acc;
+      acc += count[r];
+    }
+    row_ptr[rows] = acc;
+  }
+  __syncthreads();
+  for (int64_t base = 0; base < n; base += kCsrThreads) {
+    const int64_t e = base + tid;
+    const int r = e < n ? index[e] : -1;
+    const bool ok = r >= 0 && r < rows;
+    for (int i = tid; i < (kCsrThreads / 32) * rows; i += kCsrThreads) warp_count[i / rows][i % rows] = 0;
+    __syncthreads();
+    const unsigned peers = __match_any_sync(0xffffffffu, ok ? r : -1);
+    const int in_warp = __popc(peers & ((1u << lane) - 1u));
+    if (ok && in_warp == 0) warp_count[warp][r] = __popc(peers);
+    __syncthreads();
+    if (ok) {
+      int before = 0;
+      for (int w = 0; w < warp; ++w) before += warp_count[w][r];
+      // in [0, n) by construction (counts of distinct elements); kept as a guard
+      const int64_t slot = (int64_t)start[r] + before + in_warp;
+      if (slot >= 0 && slot < n) perm[slot] = (int32_t)e;
+    }
+    __syncthreads();
+    // advance each row's start by this chunk's elements of it
+    for (int rr = tid; rr < rows; rr += kCsrThreads) {
+      int add = 0;
+      for (int w = 0; w < kCsrThreads / 32; ++w) add += warp_count[w][rr];
+      start[rr] += add;
+    }
+    __syncthreads();
+  }
+  // slots past the mapped elements (index outside [0, rows)) hold -1
+  for (int64_t e = (int64_t)row_ptr[rows] + tid; e < n; e += kCsrThreads) perm[e] = -1;
+}
+
 }  // namespace seg
 }  // namespace cg
 
 extern "C" {
+
+int cg_csr_from_index(const int32_t* index, int64_t n, int64_t rows, int32_t* row_ptr, int32_t* perm, void* stream) {
+  CG_REQUIRE(n >= 0 && n < (1ll << 31), "csr_from_index: n = %lld outside [0, 2^31)", (long long)n);
+  CG_REQUIRE(rows >= 0 && rows <= cg::seg::kCsrMaxRows, "csr_from_index: rows = %lld outside [0, %d]",
+             (long long)rows, cg::seg::kCsrMaxRows);
+  CG_REQUIRE(row_ptr != nullptr && (n == 0 || (index != nullptr && perm != nullptr)),
+             "csr_from_index: null buffer");
+  cg::seg::csr_small_kernel<<<1, cg::seg::kCsrThreads, 0, cg::as_stream(stream)>>>(index, n, (int)rows, row_ptr, perm);
+  CG_LAUNCHED("csr_from_index");
+  return cg::kOk;
+}
 
 int cg_gather_rows(const float* src, int64_t ld_src, const int32_t* index, int64_t n_out, int64_t cols,
                    float* out, int64_t ld_out, void* stream) {

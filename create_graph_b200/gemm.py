@@ -130,5 +130,5 @@ def gemm(
     if ws_bytes > 0:
         workspace = torch.empty(ws_bytes // 4, dtype=torch.float32, device=a.device)
         args.workspace, args.workspace_bytes = workspace.data_ptr(), ws_bytes
-    native.invoke("cg_gemm_tf32", ctypes.byref(args), native.stream_ptr(a.device), info=(m, n, k))
+    native.invoke("cg_gemm_tf32", ctypes.byref(args), native.stream_ptr(a.device), info=(m, n, k, precision))
     return out

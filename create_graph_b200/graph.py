@@ -42,12 +42,17 @@ def system_index(sys_ptr: Tensor, n_atoms: int) -> Tensor:
     return torch.repeat_interleave(torch.arange(len(counts), device=sys_ptr.device), counts, output_size=n_atoms)
 
 
-def make_batch(pos: Tensor, species: Tensor, sys_ptr: Tensor, n_species: int) -> AtomsBatch:
-    """Index structures of a batch (on the tensors' device)."""
+def make_batch(pos: Tensor, species: Tensor, sys_ptr: Tensor, n_species: int,
+               max_atoms: int | None = None) -> AtomsBatch:
+    """Index structures of a batch (on the tensors' device). ``max_atoms``
+    bounds the largest system (the neighbour-list kernel's shared tile); when
+    given, nothing is read back to the host, so the call can sit inside a
+    captured CUDA graph."""
     n = pos.shape[0]
     sys_ptr = sys_ptr.to(torch.int32)
     counts = sys_ptr[1:] - sys_ptr[:-1]
-    max_atoms = int(counts.max()) if counts.numel() else 0
+    if max_atoms is None:
+        max_atoms = int(counts.max()) if counts.numel() else 0
     species = species.to(torch.int32)
     sys_idx = system_index(sys_ptr, n).to(torch.int32)
     return AtomsBatch(

@@ -184,6 +184,8 @@ _SIGNATURES = {
     "cg_rownorm_bwd1": (_I, [vp, vp, i64, i64, f32, vp, vp]),
     "cg_rownorm_bwd1_add": (_I, [vp, vp, vp, i64, i64, f32, vp, vp]),
     "cg_adamw_step": (_I, [vp, vp, vp, vp, i64, f32, f32, f32, f32, f32, i64, vp]),
+    "cg_adamw_step_counted": (_I, [vp, vp, vp, vp, i64, f32, f32, f32, f32, f32, vp, vp]),
+    "cg_csr_from_index": (_I, [vp, i64, i64, vp, vp, vp]),
     "cg_rownorm_bwd2": (_I, [vp, vp, vp, i64, i64, f32, vp, vp, vp]),
     "cg_pool": (_I, [vp, vp, i64, i64, i64, vp, vp]),
     "cg_pool_outer": (_I, [vp, vp, i64, i64, i64, vp, vp]),

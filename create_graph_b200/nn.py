@@ -516,7 +516,17 @@ class Csr:
 
     @staticmethod
     def from_index(index: Tensor, rows: int) -> Csr:
-        """Build on the index's device with a stable sort (deterministic)."""
+        """Build on the index's device, deterministically. On a CUDA device with
+        rows <= 256 one kernel builds it without reading anything back to the
+        host (capturable in a CUDA graph); perm then has one slot per element,
+        -1 past the mapped ones. Otherwise a stable torch sort."""
+        if index.is_cuda and rows <= CSR_KERNEL_MAX_ROWS:
+            index = index.to(torch.int32).contiguous()
+            row_ptr = torch.empty(rows + 1, dtype=torch.int32, device=index.device)
+            perm = torch.empty(max(index.numel(), 1), dtype=torch.int32, device=index.device)
+            native.call("cg_csr_from_index", index.data_ptr(), index.numel(), rows, row_ptr.data_ptr(),
+                        perm.data_ptr(), _stream())
+            return Csr(index, row_ptr, perm, rows)
         index = index.to(torch.int64)
         valid = index >= 0
         order = torch.argsort(torch.where(valid, index, rows), stable=True)
@@ -525,6 +535,9 @@ class Csr:
         row_ptr[1:] = torch.cumsum(counts, 0)
         nnz = int(valid.sum())
         return Csr(index.to(torch.int32), row_ptr.to(torch.int32), order[:nnz].to(torch.int32).contiguous(), rows)
+
+
+CSR_KERNEL_MAX_ROWS = 256
 
 
 def gather_raw(src: Tensor, csr: Csr) -> Tensor:

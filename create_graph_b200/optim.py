@@ -39,11 +39,18 @@ class FusedAdamW:
         self.exp_avg = torch.zeros_like(self.flat)
         self.exp_avg_sq = torch.zeros_like(self.flat)
         self.lr, self.betas, self.eps, self.weight_decay = lr, betas, eps, weight_decay
-        self.steps = 0
+        # step count and bias corrections on the device (cg_adamw_step_counted),
+        # so that a CUDA graph holding the update replays the next step each time
+        self.state = torch.zeros(2, dtype=torch.int64, device=self.flat.device)
+
+    @property
+    def steps(self) -> int:
+        """Steps taken so far (reads the device counter: synchronises)."""
+        return int(self.state[0])
 
     @torch.no_grad()
     def step(self) -> None:
-        self.steps += 1
-        native.call("cg_adamw_step", self.flat.data_ptr(), self.grads.flat.data_ptr(), self.exp_avg.data_ptr(),
-                    self.exp_avg_sq.data_ptr(), self.flat.numel(), self.lr, self.betas[0], self.betas[1], self.eps,
-                    self.weight_decay, self.steps, native.stream_ptr(self.flat.device))
+        native.call("cg_adamw_step_counted", self.flat.data_ptr(), self.grads.flat.data_ptr(),
+                    self.exp_avg.data_ptr(), self.exp_avg_sq.data_ptr(), self.flat.numel(), self.lr, self.betas[0],
+                    self.betas[1], self.eps, self.weight_decay, self.state.data_ptr(),
+                    native.stream_ptr(self.flat.device))

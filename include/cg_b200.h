@@ -245,6 +245,12 @@ int cg_gather_rows(const float* src, int64_t ld_src, const int32_t* index, int64
                    float* out, int64_t ld_out, void* stream);
 /* out[r, :] (+)= sum_{e in [row_ptr[r], row_ptr[r+1])} src[perm ? perm[e] : e, :],
  * in increasing e; replaces index_add (tests/test_semantics.py:68-69 there). */
+/* CSR of a small many-to-one map: element e goes to row index[e] (outside
+ * [0, rows): nowhere). row_ptr (rows + 1) and perm (n; each row's elements in
+ * ascending order, then -1 for the unmapped ones) in one single-block kernel
+ * without host synchronisation; rows <= 256. Builds the species map of a
+ * batch (torch argsort + bincount there would read sizes back to the host). */
+int cg_csr_from_index(const int32_t* index, int64_t n, int64_t rows, int32_t* row_ptr, int32_t* perm, void* stream);
 int cg_segment_sum(const float* src, int64_t ld_src, const int32_t* row_ptr, const int32_t* perm,
                    int64_t n_rows, int64_t cols, float* out, int64_t ld_out, int accumulate,
                    void* stream);
@@ -301,6 +307,12 @@ int cg_rownorm_bwd2(const float* x, const float* g, const float* h, int64_t rows
  * the reference leaves it to the user's torch optimizer. */
 int cg_adamw_step(float* param, const float* grad, float* exp_avg, float* exp_avg_sq, int64_t n, float lr,
                   float beta1, float beta2, float eps, float weight_decay, int64_t step, void* stream);
+/* The same update with the step count kept on the device: `state` (16 bytes,
+ * 8-byte aligned, zeroed before the first step) holds the step count and its
+ * bias corrections; each call advances it on the stream before updating, so
+ * the call can sit in a captured CUDA graph and every replay is the next step. */
+int cg_adamw_step_counted(float* param, const float* grad, float* exp_avg, float* exp_avg_sq, int64_t n, float lr,
+                          float beta1, float beta2, float eps, float weight_decay, void* state, void* stream);
 /* Envelope pooling of k tokens per row n (x contiguous (n, k, cols)):
  * pool: out[n, c] = sum_s w[n, s] x[n, s, c];  outer: out[n, s, c] = w[n, s] g[n, c];
  * dot: out[n, s] = sum_c g[n, c] x[n, s, c]. A family closed under differentiation. */

@@ -1,9 +1,9 @@
 """
 Microbenchmarks of the hot kernels, timed with CUDA events.
 
-    python -m create_graph_b200.microbench attn [--n 4096] [--iters 10] [--precision fp32|tf32]
-    python -m create_graph_b200.microbench pooled [--n 8280] [--iters 10] [--precision tf32|fp32]
-    python -m create_graph_b200.microbench gemm M N K [--silu]
+    python microbench.py attn [--n 4096] [--iters 10] [--precision fp32|tf32]
+    python microbench.py pooled [--n 8280] [--iters 10] [--precision tf32|fp32]
+    python microbench.py gemm M N K [--silu]
 
 ``attn``: the masked edge-attention microbenchmark: n atoms x 8 heads x 32
 tokens x 32 dims, fp32, q/k/v ~ N(0, 1), bias ~ N(0, 0.1) per (n, h, i, j),
@@ -20,8 +20,12 @@ from __future__ import annotations
 
 import argparse
 import json
+import os
+import sys
 
 import torch
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
 from create_graph_b200.edge_attn import (
     attn_backward1,
@@ -34,13 +38,13 @@ from create_graph_b200.edge_attn import (
 from create_graph_b200.gemm import ACT_SILU, gemm
 
 
-def attn_inputs(n: int, h: int = 8, s: int = 32, d: int = 32, seed: int = 0):
+def attn_inputs(n: int, h: int = 8, s: int = 32, d: int = 32, seed: int = 0, device: str = "cuda"):
     gen = torch.Generator().manual_seed(seed)
-    q, k, v = (torch.randn(n, h, s, d, generator=gen).cuda() for _ in range(3))
-    bias = (0.1 * torch.randn(n, h, s, s, generator=gen)).cuda()
-    counts = torch.randint(8, s + 1, (n,), generator=gen, dtype=torch.int32).cuda()
-    g, hq, hk, hv = (torch.randn(n, h, s, d, generator=gen).cuda() for _ in range(4))
-    hb = torch.randn(n, h, s, s, generator=gen).cuda()
+    q, k, v = (torch.randn(n, h, s, d, generator=gen).to(device) for _ in range(3))
+    bias = (0.1 * torch.randn(n, h, s, s, generator=gen)).to(device)
+    counts = torch.randint(8, s + 1, (n,), generator=gen, dtype=torch.int32).to(device)
+    g, hq, hk, hv = (torch.randn(n, h, s, d, generator=gen).to(device) for _ in range(4))
+    hb = torch.randn(n, h, s, s, generator=gen).to(device)
     return q, k, v, bias, counts, g, hq, hk, hv, hb, d**-0.5
 
 
