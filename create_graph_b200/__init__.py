@@ -18,7 +18,7 @@ shared library (``include/cg_b200.h``) loaded by ``create_graph_b200.native``;
 the fused ops of the energy network are in ``create_graph_b200.nn``.
 """
 
-from create_graph_b200 import testing  # noqa: F401
+from create_graph_b200 import library, testing  # noqa: F401  (library: the torch.library operators)
 from create_graph_b200.api import compile, create_graph, reset
 from create_graph_b200.compile_config import CompileConfig, supports_in_graph_grad
 from create_graph_b200.errors import ContractError, NativeError

@@ -434,6 +434,59 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
   }
 }
 
+// ---- MSE loss on energies and forces (F = -grad) --------------------------------
+// loss = sum_b (E_b - Et_b)^2 / n_e + sum_i (g_i + Ft_i)^2 / n_f, g = dE/dpos.
+// One block: each thread sums a fixed strided subset, then a fixed-shape tree
+// over the block, so the value is bitwise reproducible.
+constexpr int kLossThreads = 1024;
+
+__global__ void __launch_bounds__(kLossThreads) mse_ef_kernel(const float* __restrict__ e, const float* __restrict__ et,
+                                                             int64_t n_e, const float* __restrict__ g,
+                                                             const float* __restrict__ ft, int64_t n_f,
+                                                             float* __restrict__ loss) {
+  __shared__ float part[kLossThreads / 32][2];
+  float se = 0.0f, sf = 0.0f;
+  for (int64_t i = threadIdx.x; i < n_e; i += kLossThreads) {
+    const float r = e[i] - et[i];
+    se = fmaf(r, r, se);
+  }
+  for (int64_t i = threadIdx.x; i < n_f; i += kLossThreads) {
+    const float r = g[i] + ft[i];
+    sf = fmaf(r, r, sf);
+  }
+  se = warp_sum(se);
+  sf = warp_sum(sf);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    part[warp][0] = se;
+    part[warp][1] = sf;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    se = warp_sum(part[lane][0]);
+    sf = warp_sum(part[lane][1]);
+    if (lane == 0) *loss = (n_e > 0 ? se / (float)n_e : 0.0f) + (n_f > 0 ? sf / (float)n_f : 0.0f);
+  }
+}
+
+// dE = 2 (E - Et) / n_e * gl, dg = 2 (g + Ft) / n_f * gl, gl = *grad_loss
+__global__ void mse_ef_bwd_kernel(const float* __restrict__ e, const float* __restrict__ et, int64_t n_e,
+                                  const float* __restrict__ g, const float* __restrict__ ft, int64_t n_f,
+                                  const float* __restrict__ grad_loss, float* __restrict__ de,
+                                  float* __restrict__ dg) {
+  const float gl = *grad_loss;
+  const float ce = n_e > 0 ? 2.0f * gl / (float)n_e : 0.0f, cf = n_f > 0 ? 2.0f * gl / (float)n_f : 0.0f;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n_e + n_f; i += stride) {
+    if (i < n_e) {
+      de[i] = ce * (e[i] - et[i]);
+    } else {
+      const int64_t j = i - n_e;
+      dg[j] = cf * (g[j] + ft[j]);
+    }
+  }
+}
+
 // ---- envelope pooling over the k tokens of each n ------------------------------
 // pool:  out[n, c]    = sum_s w[n, s] x[n, s, c]
 // outer: out[n, s, c] = w[n, s] g[n, c]
@@ -699,6 +752,33 @@ int cg_adamw_step_counted(float* param, const float* grad, float* exp_avg, float
   pw::adamw_kernel<<<pw::blocks_for(vec ? (n + 3) / 4 : n, 256), 256, 0, as_stream(stream)>>>(
       param, grad, exp_avg, exp_avg_sq, n, a, vec, st);
   CG_LAUNCHED("adamw");
+  return kOk;
+}
+
+int cg_mse_energy_force(const float* energy, const float* energy_target, int64_t n_energy, const float* grad_pos,
+                        const float* force_target, int64_t n_force, float* loss, void* stream) {
+  CG_REQUIRE(n_energy >= 0 && n_force >= 0, "mse_energy_force: negative size");
+  CG_REQUIRE(loss != nullptr && (n_energy == 0 || (energy && energy_target)) &&
+                 (n_force == 0 || (grad_pos && force_target)),
+             "mse_energy_force: null buffer");
+  pw::mse_ef_kernel<<<1, pw::kLossThreads, 0, as_stream(stream)>>>(energy, energy_target, n_energy, grad_pos,
+                                                                  force_target, n_force, loss);
+  CG_LAUNCHED("mse_energy_force");
+  return kOk;
+}
+
+int cg_mse_energy_force_bwd(const float* energy, const float* energy_target, int64_t n_energy, const float* grad_pos,
+                            const float* force_target, int64_t n_force, const float* grad_loss, float* d_energy,
+                            float* d_grad_pos, void* stream) {
+  CG_REQUIRE(n_energy >= 0 && n_force >= 0, "mse_energy_force_bwd: negative size");
+  CG_REQUIRE(grad_loss != nullptr, "mse_energy_force_bwd: grad_loss is NULL");
+  if (n_energy + n_force == 0) return kOk;
+  CG_REQUIRE((n_energy == 0 || (energy && energy_target && d_energy)) &&
+                 (n_force == 0 || (grad_pos && force_target && d_grad_pos)),
+             "mse_energy_force_bwd: null buffer");
+  pw::mse_ef_bwd_kernel<<<pw::blocks_for(n_energy + n_force, 256), 256, 0, as_stream(stream)>>>(
+      energy, energy_target, n_energy, grad_pos, force_target, n_force, grad_loss, d_energy, d_grad_pos);
+  CG_LAUNCHED("mse_energy_force_bwd");
   return kOk;
 }
 

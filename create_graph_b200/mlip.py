@@ -202,9 +202,10 @@ def loss_fn(energy: Tensor, forces: Tensor, e_target: Tensor, f_target: Tensor) 
 
 def train_step(model: MLIP, batch: AtomsBatch, e_target: Tensor, f_target: Tensor) -> Tensor:
     """One conservative-force training step: energy, forces = -dE/dpos through
-    create_graph, the loss and the parameter backward through the force."""
+    create_graph, the loss (loss_fn, as one fused kernel) and the parameter
+    backward through the force."""
     out, grads = cg.create_graph(model, batch, outputs="energy", inputs=("pos",))
-    loss = loss_fn(out["energy"], -grads["pos"], e_target, f_target)
+    loss = cgnn.energy_force_loss(out["energy"], grads["pos"], e_target, f_target)
     loss.backward()
     return loss.detach()
 

@@ -76,9 +76,9 @@ def synthetic_batch(spec: MLPSpec = MLPSpec(), seed: int = 0):
 
 
 def train_step(model: MLPModel, batch: dict, e_target: Tensor, f_target: Tensor) -> Tensor:
-    """Energy and forces through create_graph, MSE on both, loss.backward()."""
+    """Energy and forces through create_graph, MSE on both (one fused kernel),
+    loss.backward()."""
     out, grads = cg.create_graph(model, batch)
-    forces = -grads["pos"]
-    loss = (out["energy"] - e_target).square().mean() + (forces - f_target).square().mean()
+    loss = cgnn.energy_force_loss(out["energy"], grads["pos"], e_target, f_target)
     loss.backward()
     return loss.detach()

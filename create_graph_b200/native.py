@@ -187,6 +187,8 @@ _SIGNATURES = {
     "cg_adamw_step_counted": (_I, [vp, vp, vp, vp, i64, f32, f32, f32, f32, f32, vp, vp]),
     "cg_csr_from_index": (_I, [vp, i64, i64, vp, vp, vp]),
     "cg_rownorm_bwd2": (_I, [vp, vp, vp, i64, i64, f32, vp, vp, vp]),
+    "cg_mse_energy_force": (_I, [vp, vp, i64, vp, vp, i64, vp, vp]),
+    "cg_mse_energy_force_bwd": (_I, [vp, vp, i64, vp, vp, i64, vp, vp, vp, vp]),
     "cg_pool": (_I, [vp, vp, i64, i64, i64, vp, vp]),
     "cg_pool_outer": (_I, [vp, vp, i64, i64, i64, vp, vp]),
     "cg_pool_dot": (_I, [vp, vp, i64, i64, i64, vp, vp]),

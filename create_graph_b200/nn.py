@@ -137,19 +137,24 @@ def mm(a: Tensor, b: Tensor) -> Tensor:
     return MM.apply(a, b)
 
 
+def colsum_raw(x: Tensor) -> Tensor:
+    """out[c] = sum_r x[r, c] (deterministic two-pass reduction)."""
+    x = _f32(x, "colsum")
+    out = torch.empty(x.shape[1], device=x.device)
+    nbytes = native.lib().cg_colsum_scratch_bytes(x.shape[0], x.shape[1])
+    scratch = torch.empty(max(nbytes // 4, 1), device=x.device)
+    native.call("cg_colsum", x.data_ptr(), x.stride(0), x.shape[0], x.shape[1], out.data_ptr(), 0,
+                scratch.data_ptr(), _stream())
+    return out
+
+
 class ColSum(_Fused):
     """out[c] = sum_r x[r, c] (deterministic two-pass reduction)."""
 
     @staticmethod
     def forward(ctx, x):
-        x = _f32(x, "colsum")
         ctx.rows = x.shape[0]
-        out = torch.empty(x.shape[1], device=x.device)
-        nbytes = native.lib().cg_colsum_scratch_bytes(x.shape[0], x.shape[1])
-        scratch = torch.empty(max(nbytes // 4, 1), device=x.device)
-        native.call("cg_colsum", x.data_ptr(), x.stride(0), x.shape[0], x.shape[1], out.data_ptr(), 0,
-                    scratch.data_ptr(), _stream())
-        return out
+        return colsum_raw(x)
 
     @staticmethod
     def backward(ctx, h):
@@ -859,6 +864,44 @@ class PooledTokenAttentionGrad(_Fused):
             qkv, bias, env, lse, w, dm, h_qkv, h_bias, h_env, graph.tokens.index, graph.counts, graph.k, heads,
             scale, precision)
         return _pooled_qkv_grad(dqk, wv, dm, graph, heads), dbias, denv.view_as(env), None, None, ddm, None
+
+
+# ---------------------------------------------------------------------------
+# the training loss
+# ---------------------------------------------------------------------------
+
+
+class EnergyForceMSE(Function):
+    """loss = mean((E - Et)^2) + mean((F - Ft)^2) with F = -grad_pos, as one
+    kernel; backward one kernel (first order: the loss is differentiated once,
+    by loss.backward())."""
+
+    @staticmethod
+    def forward(ctx, energy, grad_pos, e_target, f_target):
+        e, g, et, ft = (_f32(t.detach(), "energy_force_mse") for t in (energy, grad_pos, e_target, f_target))
+        if e.numel() != et.numel() or g.numel() != ft.numel():
+            raise NativeError(f"energy_force_mse: energy {tuple(e.shape)} vs {tuple(et.shape)}, "
+                              f"forces {tuple(g.shape)} vs {tuple(ft.shape)}")
+        loss = torch.empty((), device=e.device)
+        native.call("cg_mse_energy_force", e.data_ptr(), et.data_ptr(), e.numel(), g.data_ptr(), ft.data_ptr(),
+                    g.numel(), loss.data_ptr(), _stream())
+        ctx.save_for_backward(e, g, et, ft)
+        return loss
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, grad_loss):
+        e, g, et, ft = ctx.saved_tensors
+        de, dg = torch.empty_like(e), torch.empty_like(g)
+        grad_loss = _f32(grad_loss, "energy_force_mse")
+        native.call("cg_mse_energy_force_bwd", e.data_ptr(), et.data_ptr(), e.numel(), g.data_ptr(),
+                    ft.data_ptr(), g.numel(), grad_loss.data_ptr(), de.data_ptr(), dg.data_ptr(), _stream())
+        return (de if ctx.needs_input_grad[0] else None, dg if ctx.needs_input_grad[1] else None, None, None)
+
+
+def energy_force_loss(energy: Tensor, grad_pos: Tensor, e_target: Tensor, f_target: Tensor) -> Tensor:
+    """MSE on energies plus MSE on forces F = -grad_pos, fused."""
+    return EnergyForceMSE.apply(energy, grad_pos, e_target, f_target)
 
 
 # ---------------------------------------------------------------------------

@@ -316,6 +316,19 @@ int cg_adamw_step_counted(float* param, const float* grad, float* exp_avg, float
 /* Envelope pooling of k tokens per row n (x contiguous (n, k, cols)):
  * pool: out[n, c] = sum_s w[n, s] x[n, s, c];  outer: out[n, s, c] = w[n, s] g[n, c];
  * dot: out[n, s] = sum_c g[n, c] x[n, s, c]. A family closed under differentiation. */
+/* The training loss on energies and forces, F = -dE/dpos:
+ *   loss = mean_b (E_b - Et_b)^2 + mean_i (F_i - Ft_i)^2,
+ * given grad_pos = dE/dpos (the sign is folded in). One block, fixed
+ * reduction order (bitwise reproducible). Replaces the MSE losses the
+ * reference's training steps build from torch ops (tests/test_semantics.py,
+ * examples/mlp.py there). */
+int cg_mse_energy_force(const float* energy, const float* energy_target, int64_t n_energy, const float* grad_pos,
+                        const float* force_target, int64_t n_force, float* loss, void* stream);
+/* Its gradient: d_energy = 2 (E - Et) / n_energy * g, d_grad_pos = 2 (grad_pos +
+ * Ft) / n_force * g, with g = *grad_loss read on the device. */
+int cg_mse_energy_force_bwd(const float* energy, const float* energy_target, int64_t n_energy, const float* grad_pos,
+                            const float* force_target, int64_t n_force, const float* grad_loss, float* d_energy,
+                            float* d_grad_pos, void* stream);
 int cg_pool(const float* x, const float* w, int64_t n, int64_t k, int64_t cols, float* out, void* stream);
 int cg_pool_outer(const float* w, const float* g, int64_t n, int64_t k, int64_t cols, float* out,
                   void* stream);
