@@ -57,19 +57,25 @@ def attn_algorithmic_bytes(n: int, h: int = 8, s: int = 32, d: int = 32) -> dict
     }
 
 
-def _time(fn, iters: int) -> float:
+def _time(fn, iters: int, batches: int = 3) -> float:
+    """Milliseconds per call: the median over `batches` of `iters` back-to-back
+    calls between two CUDA events. Calls are queued without synchronising, so
+    the Python work that prepares each launch overlaps the previous kernel
+    and the figure is the kernels' device time (timing calls one at a time
+    would add that host time whenever it exceeds the queue)."""
     for _ in range(3):
         fn()
     torch.cuda.synchronize()
-    times = []
-    for _ in range(iters):
+    per_call = []
+    for _ in range(batches):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        fn()
+        for _ in range(iters):
+            fn()
         b.record()
         torch.cuda.synchronize()
-        times.append(a.elapsed_time(b))
-    return sorted(times)[len(times) // 2]
+        per_call.append(a.elapsed_time(b) / iters)
+    return sorted(per_call)[len(per_call) // 2]
 
 
 def attn(n: int = 4096, iters: int = 10, hbm_gbs: float | None = None, which=("fwd1", "bwd1", "bwd2"),
