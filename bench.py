@@ -154,6 +154,15 @@ class Job:
         self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
 
+    def gather(self, x: float) -> list[float]:
+        """x from every rank, in rank order."""
+        if self.world == 1:
+            return [x]
+        t = torch.tensor([x], device=self.dev, dtype=torch.float64)
+        out = [torch.empty_like(t) for _ in range(self.world)]
+        self.dist.all_gather(out, t)
+        return [float(o.item()) for o in out]
+
     def sum(self, x: int) -> int:
         if self.world == 1:
             return x
@@ -161,9 +170,10 @@ class Job:
         self.dist.all_reduce(t)
         return int(t.item())
 
-    def timed(self, step, steps: int) -> float:
+    def timed(self, step, steps: int, per_rank: list | None = None) -> float:
         """ms per step of `steps` calls, CUDA events on this rank's stream,
-        barrier + synchronize on both sides, max over ranks."""
+        barrier + synchronize on both sides, max over ranks (every rank's own
+        figure appended to per_rank when given)."""
         self.barrier()
         torch.cuda.synchronize()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -173,7 +183,11 @@ class Job:
         end.record()
         torch.cuda.synchronize()
         self.barrier()
-        return self.max(start.elapsed_time(end)) / steps
+        mine = start.elapsed_time(end) / steps
+        everyone = self.gather(mine)
+        if per_rank is not None:
+            per_rank.extend(everyone)
+        return max(everyone)
 
     def close(self):
         if self.world > 1:
@@ -320,56 +334,66 @@ def roofline_of(kernels, hbm, bf16, bf16_sus, src):
 ADAMW = {"lr": 1e-4, "betas": (0.9, 0.999), "eps": 1e-8, "weight_decay": 1e-2}
 
 
-def mlip_workload(job, name, atoms_target, config):
-    """Model, flat gradients, optimizer and device batch of one rank."""
+def headline_workload(job, atoms, config, captured: bool):
+    """The 85M workload of one rank (its balanced share of the global pool of
+    systems): model, gradient buffer, host inputs, their device buffers and
+    the training step (CUDA graphs, or eager with the all-reduce overlapped)."""
     from create_graph_b200 import mlip
     from create_graph_b200.ddp import FlatGradients
     from create_graph_b200.graph import make_batch
     from create_graph_b200.optim import FusedAdamW
 
-    spec = mlip.SPECS[name]
-    sizes = mlip.workload_sizes(name, seed=1000 + job.rank, atoms_target=atoms_target)
-    pos_h, species_h, sys_ptr_h = mlip.synthetic_systems(sizes, spec.n_species, seed=1000 + job.rank)
+    spec = mlip.SPECS[CONFIG_NAME]
+    sizes, pos_h, species_h, sys_ptr_h = mlip.sharded_workload(CONFIG_NAME, job.rank, job.world, atoms)
     e_t_h, f_t_h = mlip.make_targets(len(sizes), pos_h.shape[0], seed=2000 + job.rank)
     torch.manual_seed(0)  # identical initial weights on every rank
     model = mlip.MLIP(spec, config=config).to(job.dev)
+    host = (pos_h, species_h, sys_ptr_h, e_t_h, f_t_h)
+    bufs = [t.to(job.dev) for t in host]
+    pos, species, sys_ptr, e_t, f_t = bufs
+    if captured:
+        def loss_fn():
+            # index structures and neighbour lists rebuilt from the buffers on every replay
+            batch = make_batch(pos, species, sys_ptr, spec.n_species, max_atoms=max(sizes))
+            return mlip.train_step(model, batch, e_t, f_t)
+
+        step, kernels, grads = captured_training(job, model, loss_fn)
+        return spec, sizes, model, grads, host, bufs, step, kernels
     grads = FlatGradients(model.parameters(), job.world if job.world > 1 else None)
     opt = FusedAdamW(grads, **ADAMW)
-    host = (pos_h, species_h, sys_ptr_h, e_t_h, f_t_h)
-    batch = make_batch(pos_h.to(job.dev), species_h.to(job.dev), sys_ptr_h.to(job.dev), spec.n_species)
-    e_t, f_t = e_t_h.to(job.dev), f_t_h.to(job.dev)
 
-    def step(b=batch, et=e_t, ft=f_t):
+    def step():
         grads.zero()
-        loss = mlip.train_step(model, b, et, ft)
+        batch = make_batch(pos, species, sys_ptr, spec.n_species)
+        loss = mlip.train_step(model, batch, e_t, f_t)
         grads.allreduce()
         opt.step()
         return loss
 
-    return spec, sizes, model, grads, host, step
+    return spec, sizes, model, grads, host, bufs, step, None
 
 
 def run_mine(args):
     import create_graph_b200 as cg
     from create_graph_b200 import native
-    from create_graph_b200.graph import make_batch
 
     job = Job()
     hbm, bf16, bf16_sus, src = peaks()
     config = cg.CompileConfig(memory_budget=0.5, checkpoint=r"blocks\.\d+")
-    spec, sizes, model, grads, host, step = mlip_workload(job, CONFIG_NAME, args.atoms, config)
+    captured = not args.eager
+    spec, sizes, model, grads, host, bufs, step, kernels_per_step = headline_workload(job, args.atoms, config,
+                                                                                      captured)
     n_atoms = host[0].shape[0]
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
 
     # ---- device-resident throughput ----
-    torch.cuda.reset_peak_memory_stats(job.dev)
     launches0 = native.launch_count()
-    last = {}
+    last, per_rank = {}, []
     with ClockSampler(job.local) as clocks:
-        ms = job.timed(lambda: last.__setitem__("loss", step()), args.steps)
-    launches = native.launch_count() - launches0
+        ms = job.timed(lambda: last.__setitem__("loss", step()), args.steps, per_rank)
+    launches = kernels_per_step * args.steps if captured else native.launch_count() - launches0
     peak_gb = job.max(torch.cuda.max_memory_allocated(job.dev) / 1e9)
     total_atoms = job.sum(n_atoms)
     value = total_atoms / (ms / 1e3)
@@ -379,9 +403,9 @@ def run_mine(args):
     h2d = sum(t.numel() * t.element_size() for t in pinned)
 
     def e2e_step():
-        pos, species, sys_ptr, et, ft = (t.to(job.dev, non_blocking=True) for t in pinned)
-        b = make_batch(pos, species, sys_ptr, spec.n_species)
-        last["host_loss"] = step(b, et, ft).to("cpu")
+        for dst, src in zip(bufs, pinned):
+            dst.copy_(src, non_blocking=True)
+        last["host_loss"] = step().to("cpu")
 
     e_ms = job.timed(e2e_step, args.steps)
     e2e = {
@@ -391,8 +415,26 @@ def run_mine(args):
         "d2h_bytes_per_step": last["host_loss"].numel() * last["host_loss"].element_size(),
     }
 
-    # ---- kernel breakdown (instrumented step after the timed region) ----
-    kernels = kernel_breakdown(native, step)
+    # ---- the gradient average's own device time, per step (max over ranks) ----
+    allreduce_ms = None
+    if job.world > 1 and captured:
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        job.barrier()
+        torch.cuda.synchronize()
+        a0.record()
+        for _ in range(3):
+            grads.allreduce()
+        a1.record()
+        torch.cuda.synchronize()
+        allreduce_ms = job.max(a0.elapsed_time(a1) / 3)
+
+    # ---- kernel breakdown (one instrumented eager step after the timed region) ----
+    from create_graph_b200 import mlip
+    from create_graph_b200.graph import make_batch
+
+    pos, species, sys_ptr, e_t, f_t = bufs
+    kernels = kernel_breakdown(native, lambda: mlip.train_step(
+        model, make_batch(pos, species, sys_ptr, spec.n_species, max_atoms=max(sizes)), e_t, f_t))
     shapes = {} if args.headline_only else other_shapes(job, args, hbm, bf16, bf16_sus, src)
     if job.rank == 0:
         line = {
@@ -411,24 +453,35 @@ def run_mine(args):
             "config": {
                 "workload": f"{CONFIG_NAME}: ~{args.atoms} atoms/GPU as systems of U{{20..200}} atoms, "
                             "12 blocks, C 768, 12 heads, FFN 3072, 128 RBF, k<=30, memory_budget 0.5, "
-                            "per-block checkpoint; step = energy + forces + loss.backward() + AdamW update",
+                            "per-block checkpoint; step = neighbour lists + energy + forces + loss.backward() "
+                            "+ AdamW update",
                 "atoms_per_step": total_atoms,
                 "systems_rank0": len(sizes),
+                "sharding": "one global pool of systems, least-loaded assignment by atoms (equal work per rank)",
                 "parallelism": f"dp{job.world}",
-                "allreduce": (f"{len(grads.buckets)} buckets (<= 64 MiB) of the flat fp32 gradients, NCCL "
-                              "all-reduce launched from backward hooks" if job.world > 1 else "none (1 rank)"),
+                "execution": ("CUDA graphs: create_graph + loss.backward() captured as one graph, the AdamW "
+                              "update as another" if captured else "eager, all-reduce buckets overlapped with "
+                              "backward"),
+                "allreduce": ("none (1 rank)" if job.world == 1 else
+                              "NCCL average of the flat fp32 gradients between the two graphs" if captured else
+                              f"{len(grads.buckets)} buckets (<= 64 MiB) of the flat fp32 gradients, NCCL "
+                              "all-reduce launched from backward hooks"),
                 "l2": "working set of several GB per step (larger than L2)",
             },
             "e2e": e2e,
             "gpu_launches": launches,
-            # torch.cuda.max_memory_allocated over the timed steps (max over ranks):
-            # parameters, gradients, AdamW moments and the step's activations
+            "per_rank_ms_per_step": per_rank,
+            "allreduce_ms_per_step": allreduce_ms,
+            # torch.cuda.max_memory_allocated since the start of the run (max over ranks):
+            # parameters, gradients, AdamW moments and the step's activations (a
+            # captured graph's buffers are allocated during its warm-up and capture)
             "peak_memory_gb": peak_gb,
             "roofline": roofline_of(kernels, hbm, bf16, bf16_sus, src),
             # the GEMM entry point as a whole (every shape of the step) against the tf32 peak
             "roofline_gemm": (gemm_roofline(kernels["cg_gemm_tf32"]["calls"], bf16_sus, src)
                               if "cg_gemm_tf32" in kernels else None),
             "kernels": kernel_table(kernels),
+            "kernels_note": "per-kernel device times from one eager step, CUDA events around each launch",
             "clocks": clocks.summary(),
             "loss": float(last["loss"].item()),
         }
@@ -482,7 +535,7 @@ def captured_training(job, model, loss_fn):
         second()
         return loss
 
-    return step, first.kernels + second.kernels
+    return step, first.kernels + second.kernels, grads
 
 
 def bench_small_mlip(job, args, hbm, bf16, bf16_sus, src) -> dict:
@@ -503,7 +556,7 @@ def bench_small_mlip(job, args, hbm, bf16, bf16_sus, src) -> dict:
         batch = make_batch(pos, species, sys_ptr, spec.n_species, max_atoms=max(sizes))
         return mlip.train_step(model, batch, e_t, f_t)
 
-    step, kernels = captured_training(job, model, loss_fn)
+    step, kernels, _ = captured_training(job, model, loss_fn)
     for _ in range(args.warmup):
         step()
     steps = max(args.steps, 20)
@@ -534,7 +587,7 @@ def bench_mlp(job, args, hbm, bf16, bf16_sus, src) -> dict:
     model = mlp.MLPModel(spec).to(job.dev)
     pos, e_t, f_t = (t.to(job.dev) for t in mlp.synthetic_batch(spec, seed=job.rank))
     batch = {"pos": pos, "molecules": mlp.molecules_csr(spec, job.dev)}
-    step, kernels = captured_training(job, model, lambda: mlp.train_step(model, batch, e_t, f_t))
+    step, kernels, _ = captured_training(job, model, lambda: mlp.train_step(model, batch, e_t, f_t))
     for _ in range(max(args.warmup, 3)):
         step()
     steps = max(args.steps, 200)
@@ -804,8 +857,7 @@ def run_reference(args):
 
     threads = _cpu_threads()
     spec = mlip.SPECS[CONFIG_NAME]
-    sizes = mlip.workload_sizes(CONFIG_NAME, seed=1000, atoms_target=args.atoms)
-    pos, species, sys_ptr = mlip.synthetic_systems(sizes, spec.n_species, seed=1000)
+    sizes, pos, species, sys_ptr = mlip.sharded_workload(CONFIG_NAME, 0, 1, args.atoms)
     host = (pos, species, sys_ptr, *mlip.make_targets(len(sizes), pos.shape[0], seed=2000))
     torch.manual_seed(0)
     params = {n: p.detach().float() for n, p in mlip.reference_parameters(spec).items()}
@@ -848,6 +900,8 @@ def main():
     parser.add_argument("--atoms", type=int, default=ATOMS_PER_RANK, help="atoms per GPU (headline workload)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--headline-only", action="store_true", help="skip the other named workloads")
+    parser.add_argument("--eager", action="store_true",
+                        help="run the headline step eagerly (all-reduce buckets overlapped with backward)")
     args = parser.parse_args()
     if args.impl == "reference":
         run_reference(args)

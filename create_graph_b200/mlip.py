@@ -190,6 +190,33 @@ def workload_sizes(name: str, seed: int = 0, atoms_target: int | None = None) ->
     return sizes
 
 
+def sharded_workload(name: str, rank: int, world: int, atoms_per_rank: int, seed: int = 1000):
+    """One rank's share of a data-parallel workload: (sizes, pos, species,
+    sys_ptr) on the CPU. Every rank draws the same global pool of systems
+    (``workload_sizes(name, seed, world * atoms_per_rank)``, positions and
+    species from ``seed``) and takes the systems that a least-loaded
+    assignment in decreasing size gives it, kept in pool order. Per-rank atom
+    counts then differ by less than one system's size; every kernel of the
+    step works per atom or per padded neighbour slot (k per atom), so equal
+    atoms are equal work. With world = 1 the share is the whole pool."""
+    sizes = workload_sizes(name, seed=seed, atoms_target=world * atoms_per_rank)
+    spec = SPECS[name]
+    pos, species, sys_ptr = synthetic_systems(sizes, spec.n_species, seed=seed)
+    load = [0] * world
+    owner = [0] * len(sizes)
+    for b in sorted(range(len(sizes)), key=lambda i: (-sizes[i], i)):
+        r = min(range(world), key=lambda j: (load[j], j))
+        owner[b] = r
+        load[r] += sizes[b]
+    mine = [b for b in range(len(sizes)) if owner[b] == rank]
+    ptr = sys_ptr.tolist()
+    atoms = torch.cat([torch.arange(ptr[b], ptr[b + 1]) for b in mine])
+    my_sizes = [sizes[b] for b in mine]
+    my_ptr = torch.zeros(len(mine) + 1, dtype=torch.int32)
+    my_ptr[1:] = torch.cumsum(torch.tensor(my_sizes), 0)
+    return my_sizes, pos[atoms], species[atoms], my_ptr
+
+
 def make_targets(n_systems: int, n_atoms: int, seed: int = 1):
     gen = torch.Generator().manual_seed(seed)
     return torch.randn(n_systems, generator=gen), torch.randn(n_atoms, 3, generator=gen)
