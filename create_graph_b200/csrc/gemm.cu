@@ -47,7 +47,14 @@ constexpr int BK = 32;  // fp32 elements per k-slice: one 128-byte swizzle row
 // then, in the three-term split mode, CONV converter warps
 constexpr int CONV = 4;
 __host__ __device__ constexpr int threads_of(int epi, bool split = false) { return 32 * (2 + epi + (split ? CONV : 0)); }
-constexpr int kStagePitch = 36;  // floats per staged row: 16-byte rows, conflict-free 128-bit access
+// floats per staged epilogue row (a 32 x 32 block per warp); the row's eight
+// 16-byte chunks are XOR-swizzled by (row & 7), so both the row-per-lane
+// writes and the 4-rows-per-instruction reads are free of bank conflicts
+// without padding
+constexpr int kStagePitch = 32;
+__device__ __forceinline__ int stage_idx(int r, int c) {
+  return r * kStagePitch + ((((c >> 2) ^ (r & 7)) << 2) | (c & 3));
+}
 
 struct Epilogue {
   float* c;
@@ -90,7 +97,7 @@ struct Smem {
   static constexpr int kStage = SPLIT ? 2 * kLoad : kLoad;   // + the lo copies of A and B
   static_assert(kLoad % 1024 == 0, "lo tiles keep the 1024-byte swizzle alignment");
   static constexpr int kTiles = STAGES * kStage;
-  static constexpr int kStaging = EPI * 32 * kStagePitch * 4;  // epilogue transpose, one 32 x 36 block per warp
+  static constexpr int kStaging = EPI * 32 * kStagePitch * 4;  // epilogue transpose, one 32 x 32 block per warp
   static constexpr int kBytes = kTiles + kStaging + 1024 /*alignment*/ + 256 /*barriers*/;
   static_assert(kBytes <= 227 * 1024, "shared memory budget");
 };
@@ -365,7 +372,7 @@ __global__ void __launch_bounds__(threads_of(EPI, SPLIT), 1)
         // row `lane` of the warp's 32 x 32 block, as 8 16-byte stores
 #pragma unroll
         for (int q = 0; q < 8; ++q)
-          *reinterpret_cast<float4*>(stage + lane * kStagePitch + 4 * q) =
+          *reinterpret_cast<float4*>(stage + stage_idx(lane, 4 * q)) =
               make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
         __syncwarp();
         float4 aux2[8];
@@ -380,7 +387,7 @@ __global__ void __launch_bounds__(threads_of(EPI, SPLIT), 1)
               const int r = (lane >> 3) + 4 * i;
               const int row = m0 + quarter * 32 + r;
               if (row >= M) break;
-              const float4 x = *reinterpret_cast<const float4*>(stage + r * kStagePitch + cl);
+              const float4 x = *reinterpret_cast<const float4*>(stage + stage_idx(r, cl));
               epilogue_store4(ep, row, col, x, bias, aux[i]);
             }
           } else {
@@ -389,7 +396,7 @@ __global__ void __launch_bounds__(threads_of(EPI, SPLIT), 1)
             for (int r = lane >> 3; r < 32; r += 4) {
               const int row = m0 + quarter * 32 + r;
               if (row >= M) break;
-              const float4 x = *reinterpret_cast<const float4*>(stage + r * kStagePitch + cl);
+              const float4 x = *reinterpret_cast<const float4*>(stage + stage_idx(r, cl));
               if (partial) {
                 *reinterpret_cast<float4*>(partial + z * mn + (int64_t)row * N + col) = x;
               } else {
@@ -404,7 +411,7 @@ __global__ void __launch_bounds__(threads_of(EPI, SPLIT), 1)
           for (int r = 0; r < 32; ++r) {
             const int row = m0 + quarter * 32 + r;
             if (!ok_c || row >= M) continue;
-            const float x = stage[r * kStagePitch + lane];
+            const float x = stage[stage_idx(r, lane)];
             if (partial) {
               partial[z * mn + (int64_t)row * N + colc] = x;
             } else {
@@ -662,10 +669,10 @@ static int run_split3(const cg_gemm_args& g, const Plan& p, cudaStream_t s) {
 }
 
 // Unsplit wide-tile GEMMs with a short main loop (K <= 1024) and K-major A
-// run on eight epilogue warps (one stage fewer makes room for their staging
-// blocks): their epilogue, the output plus any residual or SiLU stream,
-// bounds a tile, and four warps keep too few stores and loads in flight.
-// With long K the deeper pipeline wins.
+// run on eight epilogue warps: their epilogue, the output plus any residual
+// or SiLU stream, bounds a tile, and four warps keep too few stores and loads
+// in flight. (The 192-wide tile gives up a stage for the extra staging
+// blocks; with long K the deeper pipeline wins.)
 static bool heavy_epilogue(const cg_gemm_args& g, const Plan& p) {
   return p.splits == 1 && !g.a_mn_major && (p.bn == 256 || p.bn == 192) && g.k <= 1024;
 }
@@ -703,7 +710,7 @@ static int run(const cg_gemm_args* args, void* stream) {
       return launch_majors<192, 5>(g, p, s);
     default:
       if (heavy_epilogue(g, p))
-        return g.b_mn_major ? launch<256, 3, false, true, 8>(g, p, s) : launch<256, 3, false, false, 8>(g, p, s);
+        return g.b_mn_major ? launch<256, 4, false, true, 8>(g, p, s) : launch<256, 4, false, false, 8>(g, p, s);
       return launch_majors<256, 4>(g, p, s);
   }
 }
