@@ -14,9 +14,13 @@ over ``named_modules()``) becomes one ``BlockFn`` node of the autograd graph:
   its first-order gradients.
 
 So a block's forward runs four times and its VJP twice, and at most one
-block's activations are alive at a time. The block's fused ops are the same
-sm_100a kernels as elsewhere; the recompute runs under the region's config,
-so its memory budget applies inside the blocks too.
+block's activations are alive at a time. Each call keeps a RecomputeCache:
+ops whose outputs are cheap to rebuild from a few small statistics (the
+pooled attention's softmax weights) keep those from the first forward, so
+the three recomputes skip the statistics' own computation; the memory budget
+decides whether they may (create_graph_b200.nn). The block's fused ops are
+the same sm_100a kernels as elsewhere; the recompute runs under the region's
+config, so its memory budget applies inside the blocks too.
 """
 
 from __future__ import annotations
@@ -35,6 +39,32 @@ from create_graph_b200.pytree import flatten, is_float, unflatten
 _grad = torch.autograd.grad
 
 FORCES_PASS: list[bool] = [False]
+
+
+class RecomputeCache:
+    """Small results a checkpointed block's ops keep across the recomputes of
+    one block call (its first forward and every recompute see the same inputs,
+    so they produce the same values): ops ask for a slot in call order and
+    either find what the first run left there or fill it."""
+
+    def __init__(self):
+        self.slots: dict[int, object] = {}
+        self._next = 0
+
+    def start(self) -> None:
+        self._next = 0
+
+    def slot(self) -> int:
+        self._next += 1
+        return self._next - 1
+
+
+_CACHES: list[RecomputeCache] = []
+
+
+def active_recompute_cache() -> RecomputeCache | None:
+    """The cache of the checkpointed block call whose forward is running, if any."""
+    return _CACHES[-1] if _CACHES else None
 
 
 @contextlib.contextmanager
@@ -64,6 +94,7 @@ class _BlockCall:
         self.out_leaves: list = []
         self.out_spec = None
         self.out_slots: tuple[int, ...] = ()
+        self.cache = RecomputeCache()
 
     @property
     def inputs(self) -> list[Tensor]:
@@ -75,8 +106,13 @@ class _BlockCall:
         for i, t in zip(self.slots, tensors):
             leaves[i] = t
         args, kwargs = unflatten(self.spec, leaves)
-        with compile_context(self.config):
-            return type(self.block).forward(self.block, *args, **kwargs)
+        self.cache.start()
+        _CACHES.append(self.cache)
+        try:
+            with compile_context(self.config):
+                return type(self.block).forward(self.block, *args, **kwargs)
+        finally:
+            _CACHES.pop()
 
     def vjp(self, tensors, g_outs, create: bool):
         """Cotangents of the block inputs for output cotangents ``g_outs``."""

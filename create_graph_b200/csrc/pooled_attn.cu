@@ -55,6 +55,22 @@ extern "C" {
 
 int cg_pooled_attn_fwd(const cg_pooled_attn_args* a, void* stream) { return cg::pooled::run(0, a, stream); }
 
+int cg_pooled_attn_out(const cg_pooled_attn_args* a, void* stream) {
+  CG_REQUIRE(a != nullptr, "pooled_attn_out: args is NULL");
+  CG_REQUIRE(a->n >= 0 && a->h >= 1 && a->k >= 1 && a->k <= cg::attn_tc::KP && a->d >= 1 && a->d <= 64,
+             "pooled_attn_out: bad sizes (n %lld, h %d, k %d, d %d)", (long long)a->n, a->h, a->k, a->d);
+  if (a->n == 0) return cg::kOk;
+  CG_REQUIRE(a->token_index && a->key_count && a->qkv && a->w && a->out,
+             "pooled_attn_out: token_index, key_count, qkv, w and out are required");
+  CG_REQUIRE(a->ld_qkv >= 3 * (int64_t)a->h * a->d, "pooled_attn_out: ld_qkv below 3*h*d");
+  const int64_t warps = a->n * a->h;
+  const int64_t blocks = (warps * 32 + 255) / 256;
+  const int64_t cap = (int64_t)cg::sm_count() * 16;
+  cg::pooled::pooled_out_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, cg::as_stream(stream)>>>(*a);
+  CG_LAUNCHED("pooled_attn_out");
+  return cg::kOk;
+}
+
 int cg_pooled_attn_bwd1(const cg_pooled_attn_args* a, void* stream) { return cg::pooled::run(1, a, stream); }
 
 int cg_pooled_attn_bwd2(const cg_pooled_attn_args* a, void* stream) { return cg::pooled::run(2, a, stream); }

@@ -530,6 +530,34 @@ __global__ void __launch_bounds__(kThreads) pooled_bwd2(const PParams P) {
   }
 }
 
+// out[n, h*d + c] = sum_{j < kc} w[n, h, j] v_j[h*d + c] over the atom's valid
+// keys, v_j read from the per-atom rows through the token index: the forward's
+// output for known weights w (a checkpoint recompute of the same inputs reuses
+// the first forward's w and lse). One warp per (atom, head), lanes over the
+// columns; the sum runs in the forward kernel's order with its arithmetic, so
+// the result equals the forward's output bit for bit.
+static __global__ void pooled_out_kernel(const cg_pooled_attn_args a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int k = a.k, d = a.d, H = a.h;
+  const int64_t C = (int64_t)H * d;
+  for (int64_t task = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; task < a.n * H; task += warps) {
+    const int64_t n = task / H;
+    const int hh = (int)(task % H);
+    const int kc = key_count(a, n);
+    const float* w = a.w + (n * H + hh) * k;
+    const float* vbase = a.qkv + 2 * C + (int64_t)hh * d;
+    for (int c = lane; c < d; c += 32) {
+      float acc = 0.0f;
+      for (int j = 0; j < kc; ++j) {
+        const int32_t t = a.token_index[n * k + j];
+        if (t >= 0) acc += w[j] * __ldg(vbase + (int64_t)t * a.ld_qkv + c);
+      }
+      a.out[n * C + (int64_t)hh * d + c] = acc;
+    }
+  }
+}
+
 #undef CG_A_ROWS
 #undef CG_B_ROWS
 #undef CG_B_COLS

@@ -413,6 +413,25 @@ def pooled_attention_forward(qkv, bias, env, index, counts, k, heads, scale, pre
     return out, lse, w
 
 
+def pooled_attention_out(qkv, w, index, counts, k, heads):
+    """out (n, h*d) = sum_j w[n, h, j] v_j for known weights w (n, h, k): the
+    forward's output, bit for bit, without recomputing the softmax."""
+    qkv = qkv.contiguous()
+    native.require_cuda(qkv, w, index, counts)
+    n = counts.shape[0]
+    d = qkv.shape[1] // (3 * heads)
+    if w.shape != (n, heads, k) or not w.is_contiguous():
+        raise NativeError(f"pooled attention: w {tuple(w.shape)} must be a contiguous ({n}, {heads}, {k})")
+    a = native.PooledAttnArgs()
+    a.n, a.h, a.k, a.d = n, heads, k, d
+    a.token_index, a.key_count = index.data_ptr(), counts.data_ptr()
+    a.qkv, a.ld_qkv, a.w = qkv.data_ptr(), qkv.stride(0), w.data_ptr()
+    out = torch.empty(n, heads * d, device=qkv.device)
+    a.out = out.data_ptr()
+    _run("cg_pooled_attn_out", a, qkv.device)
+    return out
+
+
 def pooled_attention_backward1(qkv, bias, env, lse, w, dout, index, counts, k, heads, scale, precision="fp32"):
     """(dqk (n*k, 2*h*d) per-token [dq | dk], wv (n*k, h), dbias (n*k, h), denv (n, k))."""
     qkv, bias, env, dout = qkv.contiguous(), _rows(bias), env.contiguous(), dout.contiguous()

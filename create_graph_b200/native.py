@@ -172,6 +172,7 @@ _SIGNATURES = {
     "cg_pooled_attn_fwd": (_I, [ctypes.POINTER(PooledAttnArgs), vp]),
     "cg_pooled_attn_bwd1": (_I, [ctypes.POINTER(PooledAttnArgs), vp]),
     "cg_pooled_attn_bwd2": (_I, [ctypes.POINTER(PooledAttnArgs), vp]),
+    "cg_pooled_attn_out": (_I, [ctypes.POINTER(PooledAttnArgs), vp]),
     "cg_colsum_scratch_bytes": (i64, [i64, i64]),
     "cg_colsum": (_I, [vp, i64, i64, i64, vp, _I, vp, vp]),
     "cg_coldot_scratch_bytes": (i64, [i64, i64]),

@@ -34,11 +34,13 @@ import torch
 from torch import Tensor, nn
 
 from create_graph_b200 import native
+from create_graph_b200.checkpoint import active_recompute_cache
 from create_graph_b200.compile_config import active_memory_budget, engine_will_execute, gradient_edge
 from create_graph_b200.edge_attn import (
     pooled_attention_backward1,
     pooled_attention_backward2,
     pooled_attention_forward,
+    pooled_attention_out,
     token_attention_backward1,
     token_attention_backward2,
     token_attention_forward1,
@@ -827,8 +829,21 @@ class PooledTokenAttention(_Fused):
     @staticmethod
     def forward(ctx, qkv, bias, env, graph, heads, scale, precision="fp32"):
         meta = (graph, heads, scale, precision)
-        out, lse, w = pooled_attention_forward(qkv, bias, env, graph.tokens.index, graph.counts, graph.k, heads,
-                                               scale, precision)
+        args = (graph.tokens.index, graph.counts, graph.k, heads)
+        # inside a checkpointed block call, a recompute on the same inputs
+        # reuses the first forward's softmax statistics (lse, w) and only
+        # forms out = sum_j w_j v_j, bit for bit the same; a memory budget of
+        # 0.25 or less keeps nothing across recomputes
+        cache = active_recompute_cache() if active_memory_budget() > 0.25 else None
+        slot = cache.slot() if cache is not None else None
+        kept = cache.slots.get(slot) if cache is not None else None
+        if kept is not None and kept[1].shape == (graph.n_atoms, heads, graph.k):
+            lse, w = kept
+            out = pooled_attention_out(qkv, w, *args)
+        else:
+            out, lse, w = pooled_attention_forward(qkv, bias, env, *args[:3], heads, scale, precision)
+            if cache is not None:
+                cache.slots[slot] = (lse, w)
         ctx.save_for_backward(qkv, bias, env, lse, w)
         ctx.meta = meta
         return out

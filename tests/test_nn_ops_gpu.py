@@ -328,3 +328,21 @@ def test_pooled_token_attention_strided_bias(precision, tol):
         return (e.view(n, k, 1) * o).sum(1)
 
     check(twice_errors(mine, ref, [qkv, bias, env]), tol)
+
+
+def test_pooled_output_from_known_weights_equals_the_forward():
+    """cg_pooled_attn_out (a checkpoint recompute's attention output from the
+    first forward's weights) equals the forward kernel's output bit for bit."""
+    from create_graph_b200.edge_attn import pooled_attention_forward, pooled_attention_out
+
+    gen = torch.Generator().manual_seed(9)
+    for n, h, k, d, prec in ((300, 12, 30, 64, "tf32"), (200, 4, 32, 32, "fp32"), (50, 2, 12, 16, "fp32")):
+        qkv = torch.randn(n, 3 * h * d, generator=gen).cuda()
+        bias = (0.1 * torch.randn(n * k, h, generator=gen)).cuda()
+        env = torch.rand(n * k, generator=gen).cuda()
+        counts = torch.randint(1, k + 1, (n,), generator=gen, dtype=torch.int32).cuda()
+        index = torch.randint(0, n, (n, k), generator=gen, dtype=torch.int32).cuda()
+        index[torch.arange(k, device="cuda")[None, :] >= counts[:, None]] = -1
+        out, lse, w = pooled_attention_forward(qkv, bias, env, index.view(-1), counts, k, h, d ** -0.5, prec)
+        again = pooled_attention_out(qkv, w, index.view(-1), counts, k, h)
+        assert torch.equal(again, out)
