@@ -541,19 +541,42 @@ static __global__ void pooled_out_kernel(const cg_pooled_attn_args a) {
   const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const int k = a.k, d = a.d, H = a.h;
   const int64_t C = (int64_t)H * d;
+  // d = 64 on 16-byte aligned rows: each lane owns two adjacent columns
+  const bool pairs = d == 64 && (a.ld_qkv & 1) == 0 && (reinterpret_cast<uintptr_t>(a.qkv) & 7) == 0 &&
+                     (reinterpret_cast<uintptr_t>(a.out) & 7) == 0;
   for (int64_t task = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; task < a.n * H; task += warps) {
     const int64_t n = task / H;
     const int hh = (int)(task % H);
     const int kc = key_count(a, n);
-    const float* w = a.w + (n * H + hh) * k;
+    // the atom's token rows and this head's weights, one per lane, then broadcast
+    const int32_t my_t = lane < k ? a.token_index[n * k + lane] : -1;
+    const float my_w = lane < k ? a.w[(n * H + hh) * k + lane] : 0.0f;
     const float* vbase = a.qkv + 2 * C + (int64_t)hh * d;
-    for (int c = lane; c < d; c += 32) {
-      float acc = 0.0f;
+    float* dst = a.out + n * C + (int64_t)hh * d;
+    if (pairs) {
+      float acc0 = 0.0f, acc1 = 0.0f;
+#pragma unroll 8
       for (int j = 0; j < kc; ++j) {
-        const int32_t t = a.token_index[n * k + j];
-        if (t >= 0) acc += w[j] * __ldg(vbase + (int64_t)t * a.ld_qkv + c);
+        const int32_t t = __shfl_sync(0xffffffffu, my_t, j);
+        const float wj = __shfl_sync(0xffffffffu, my_w, j);
+        if (t >= 0) {
+          const float2 v = __ldg(reinterpret_cast<const float2*>(vbase + (int64_t)t * a.ld_qkv) + lane);
+          acc0 += wj * v.x;
+          acc1 += wj * v.y;
+        }
       }
-      a.out[n * C + (int64_t)hh * d + c] = acc;
+      reinterpret_cast<float2*>(dst)[lane] = make_float2(acc0, acc1);
+    } else {
+      for (int c0 = 0; c0 < d; c0 += 32) {
+        const int c = c0 + lane;
+        float acc = 0.0f;
+        for (int j = 0; j < kc; ++j) {
+          const int32_t t = __shfl_sync(0xffffffffu, my_t, j);
+          const float wj = __shfl_sync(0xffffffffu, my_w, j);
+          if (t >= 0 && c < d) acc += wj * __ldg(vbase + (int64_t)t * a.ld_qkv + c);
+        }
+        if (c < d) dst[c] = acc;
+      }
     }
   }
 }
