@@ -17,8 +17,11 @@ So a block's forward runs four times and its VJP twice, and at most one
 block's activations are alive at a time. Each call keeps a RecomputeCache:
 ops whose outputs are cheap to rebuild from a few small statistics (the
 pooled attention's softmax weights) keep those from the first forward, so
-the three recomputes skip the statistics' own computation; the memory budget
-decides whether they may (create_graph_b200.nn). The block's fused ops are
+the three recomputes skip the statistics' own computation, and the costliest
+step of the VJP (the pooled attention's backward1) keeps its outputs from the
+force pass for the VJP's rebuild in the parameter backward, which takes them
+instead of recomputing; the memory budget decides whether they may
+(create_graph_b200.nn). The block's fused ops are
 the same sm_100a kernels as elsewhere; the recompute runs under the region's
 config, so its memory budget applies inside the blocks too.
 """
@@ -48,8 +51,11 @@ class RecomputeCache:
     either find what the first run left there or fill it."""
 
     def __init__(self):
-        self.slots: dict[int, object] = {}
+        self.slots: dict[object, object] = {}
         self._next = 0
+        # set while the block's VJP (create_graph's force pass, or its rebuild
+        # in the parameter backward) runs: both see the same output cotangents
+        self.in_vjp = False
 
     def start(self) -> None:
         self._next = 0
@@ -121,13 +127,17 @@ class _BlockCall:
             pairs = [(o, g) for o, g in zip(outs, g_outs) if o.requires_grad]
             if not pairs:
                 return [None] * len(tensors)
-            return _grad(
-                [o for o, _ in pairs],
-                list(tensors),
-                [g for _, g in pairs],
-                create_graph=create,
-                allow_unused=True,
-            )
+            self.cache.in_vjp = True
+            try:
+                return _grad(
+                    [o for o, _ in pairs],
+                    list(tensors),
+                    [g for _, g in pairs],
+                    create_graph=create,
+                    allow_unused=True,
+                )
+            finally:
+                self.cache.in_vjp = False
 
     def keep_output(self, out) -> tuple[Tensor, ...]:
         """The block's float outputs become the node's outputs, except tensors it

@@ -846,12 +846,16 @@ class PooledTokenAttention(_Fused):
                 cache.slots[slot] = (lse, w)
         ctx.save_for_backward(qkv, bias, env, lse, w)
         ctx.meta = meta
+        ctx.cache, ctx.slot = cache, slot
         return out
 
     @staticmethod
     def backward(ctx, dm):
         qkv, bias, env, lse, w = ctx.saved_tensors
-        d_qkv, dbias, denv = PooledTokenAttentionGrad.apply(qkv, bias, env, lse, w, dm, ctx.meta)
+        # inside the block's VJP (force pass or its rebuild): the rebuild sees
+        # the force pass's cotangent again and takes its kept result
+        reuse = (ctx.cache, ("backward1", ctx.slot)) if ctx.cache is not None and ctx.cache.in_vjp else None
+        d_qkv, dbias, denv = PooledTokenAttentionGrad.apply(qkv, bias, env, lse, w, dm, ctx.meta, reuse)
         return d_qkv, dbias, denv, None, None, None, None
 
 
@@ -861,13 +865,22 @@ class PooledTokenAttentionGrad(_Fused):
     statistics, not differentiated)."""
 
     @staticmethod
-    def forward(ctx, qkv, bias, env, lse, w, dm, meta):
+    def forward(ctx, qkv, bias, env, lse, w, dm, meta, reuse=None):
         graph, heads, scale, precision = meta
-        dqk, wv, dbias, denv = pooled_attention_backward1(qkv, bias, env, lse, w, dm, graph.tokens.index,
-                                                          graph.counts, graph.k, heads, scale, precision)
         ctx.save_for_backward(qkv, bias, env, lse, w, dm)
         ctx.meta = meta
-        return _pooled_qkv_grad(dqk, wv, dm, graph, heads), dbias, denv.view_as(env)
+        if reuse is not None:
+            cache, key = reuse
+            kept = cache.slots.pop(key, None)
+            if kept is not None:
+                # the same op on the same inputs earlier in this block call
+                return tuple(t.detach() for t in kept)
+        dqk, wv, dbias, denv = pooled_attention_backward1(qkv, bias, env, lse, w, dm, graph.tokens.index,
+                                                          graph.counts, graph.k, heads, scale, precision)
+        out = (_pooled_qkv_grad(dqk, wv, dm, graph, heads), dbias, denv.view_as(env))
+        if reuse is not None:
+            cache.slots[key] = out
+        return out
 
     @staticmethod
     def backward(ctx, h_qkv, h_bias, h_env):
@@ -878,7 +891,7 @@ class PooledTokenAttentionGrad(_Fused):
         dqk, wv, dbias, denv, ddm = pooled_attention_backward2(
             qkv, bias, env, lse, w, dm, h_qkv, h_bias, h_env, graph.tokens.index, graph.counts, graph.k, heads,
             scale, precision)
-        return _pooled_qkv_grad(dqk, wv, dm, graph, heads), dbias, denv.view_as(env), None, None, ddm, None
+        return _pooled_qkv_grad(dqk, wv, dm, graph, heads), dbias, denv.view_as(env), None, None, ddm, None, None
 
 
 # ---------------------------------------------------------------------------
