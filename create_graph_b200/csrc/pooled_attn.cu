@@ -63,10 +63,24 @@ int cg_pooled_attn_out(const cg_pooled_attn_args* a, void* stream) {
   CG_REQUIRE(a->token_index && a->key_count && a->qkv && a->w && a->out,
              "pooled_attn_out: token_index, key_count, qkv, w and out are required");
   CG_REQUIRE(a->ld_qkv >= 3 * (int64_t)a->h * a->d, "pooled_attn_out: ld_qkv below 3*h*d");
-  const int64_t warps = a->n * a->h;
-  const int64_t blocks = (warps * 32 + 255) / 256;
-  const int64_t cap = (int64_t)cg::sm_count() * 16;
-  cg::pooled::pooled_out_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, cg::as_stream(stream)>>>(*a);
+  const int64_t C = (int64_t)a->h * a->d;
+  const bool rows = a->d % 4 == 0 && C % 128 == 0 && C / 128 <= cg::pooled::kOutRowsQMax && a->ld_qkv % 4 == 0 &&
+                    (reinterpret_cast<uintptr_t>(a->qkv) & 15) == 0 && (reinterpret_cast<uintptr_t>(a->out) & 15) == 0;
+  if (rows) {
+    // one warp per atom, all heads
+    using cg::pooled::kOutRowsWarps;
+    const int64_t blocks = (a->n + kOutRowsWarps - 1) / kOutRowsWarps;
+    const int64_t cap = (int64_t)cg::sm_count() * 8;
+    const size_t smem = (size_t)kOutRowsWarps * a->h * a->k * sizeof(float);
+    CG_REQUIRE(smem <= 48 * 1024, "pooled_attn_out: h * k too large (%d x %d)", a->h, a->k);
+    cg::pooled::pooled_out_rows_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 32 * kOutRowsWarps, smem,
+                                         cg::as_stream(stream)>>>(*a);
+  } else {
+    const int64_t warps = a->n * a->h;
+    const int64_t blocks = (warps * 32 + 255) / 256;
+    const int64_t cap = (int64_t)cg::sm_count() * 16;
+    cg::pooled::pooled_out_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, cg::as_stream(stream)>>>(*a);
+  }
   CG_LAUNCHED("pooled_attn_out");
   return cg::kOk;
 }

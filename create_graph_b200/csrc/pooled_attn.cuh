@@ -581,6 +581,60 @@ static __global__ void pooled_out_kernel(const cg_pooled_attn_args a) {
   }
 }
 
+// The same output for all heads at once when every head's columns split into
+// 16-byte groups (d % 4 == 0, h*d a multiple of 128, aligned rows): one warp
+// per atom reads each valid token's whole v row (h*d contiguous floats) once
+// with coalesced 16-byte loads, lane l owning column groups l, l + 32, ...
+// (QMAX at most), with the atom's weights w[n, :, :] staged in shared memory.
+// Per column the sum runs over j ascending with the forward kernel's
+// arithmetic, so the result equals the forward's output bit for bit.
+constexpr int kOutRowsWarps = 8;
+constexpr int kOutRowsQMax = 8;  // h*d <= 1024
+
+static __global__ void __launch_bounds__(32 * kOutRowsWarps) pooled_out_rows_kernel(const cg_pooled_attn_args a) {
+  extern __shared__ float sw_all[];  // kOutRowsWarps x (h*k)
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int k = a.k, d = a.d, H = a.h;
+  const int64_t C = (int64_t)H * d;
+  const int q_count = (int)(C / 128);
+  float* sw = sw_all + wid * H * k;
+  int hk[kOutRowsQMax];
+#pragma unroll
+  for (int q = 0; q < kOutRowsQMax; ++q) hk[q] = q < q_count ? (4 * (lane + 32 * q)) / d * k : 0;
+  const int64_t warps = (int64_t)gridDim.x * kOutRowsWarps;
+  for (int64_t n = blockIdx.x * (int64_t)kOutRowsWarps + wid; n < a.n; n += warps) {
+    const int kc = key_count(a, n);
+    const int32_t my_t = lane < k ? a.token_index[n * k + lane] : -1;
+    __syncwarp();  // the previous atom's weights are no longer read
+    for (int i = lane; i < H * k; i += 32) sw[i] = a.w[n * H * k + i];
+    __syncwarp();
+    float4 acc[kOutRowsQMax];
+#pragma unroll
+    for (int q = 0; q < kOutRowsQMax; ++q) acc[q] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const float4* vbase = reinterpret_cast<const float4*>(a.qkv + 2 * C);
+    for (int j = 0; j < kc; ++j) {
+      const int32_t t = __shfl_sync(0xffffffffu, my_t, j);
+      if (t < 0) continue;
+      const float4* vrow = vbase + (int64_t)t * (a.ld_qkv / 4);
+#pragma unroll
+      for (int q = 0; q < kOutRowsQMax; ++q) {
+        if (q < q_count) {
+          const float wj = sw[hk[q] + j];
+          const float4 v = __ldg(vrow + lane + 32 * q);
+          acc[q].x += wj * v.x;
+          acc[q].y += wj * v.y;
+          acc[q].z += wj * v.z;
+          acc[q].w += wj * v.w;
+        }
+      }
+    }
+    float4* dst = reinterpret_cast<float4*>(a.out + n * C);
+#pragma unroll
+    for (int q = 0; q < kOutRowsQMax; ++q)
+      if (q < q_count) dst[lane + 32 * q] = acc[q];
+  }
+}
+
 #undef CG_A_ROWS
 #undef CG_B_ROWS
 #undef CG_B_COLS

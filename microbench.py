@@ -34,6 +34,7 @@ from create_graph_b200.edge_attn import (
     pooled_attention_backward1,
     pooled_attention_backward2,
     pooled_attention_forward,
+    pooled_attention_out,
 )
 from create_graph_b200.gemm import ACT_SILU, gemm
 
@@ -123,6 +124,7 @@ def pooled(n: int = 8280, iters: int = 10, precision: str = "tf32") -> dict:
         "fwd": lambda: pooled_attention_forward(qkv, bias, env, *args),
         "bwd1": lambda: pooled_attention_backward1(qkv, bias, env, lse, w, dm, *args),
         "bwd2": lambda: pooled_attention_backward2(qkv, bias, env, lse, w, dm, hqkv, hb, he, *args),
+        "out": lambda: pooled_attention_out(qkv, w, index, counts, k, h),
     }
     return {name: {"us": _time(fn, iters) * 1e3} for name, fn in fns.items()}
 
