@@ -11,6 +11,36 @@ int launch_fp32(int which, const PParams& P, int dp, cudaStream_t stream) {
 
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// Whether the per-atom row kernels (one warp per atom over all heads, 16-byte
+// column groups) apply: d % 4 == 0, h*d a multiple of 128 and at most
+// 128 * kOutRowsQMax, 16-byte aligned qkv rows.
+static bool rows_eligible(const cg_pooled_attn_args& a) {
+  const int64_t C = (int64_t)a.h * a.d;
+  return a.d % 4 == 0 && C % 128 == 0 && C / 128 <= kOutRowsQMax && a.ld_qkv % 4 == 0 && al16(a.qkv);
+}
+
+static unsigned rows_grid(int64_t n) {
+  const int64_t blocks = (n + kOutRowsWarps - 1) / kOutRowsWarps;
+  const int64_t cap = (int64_t)sm_count() * 8;
+  return (unsigned)(blocks < cap ? blocks : cap);
+}
+
+// out[n, :] = sum_j w_j v_j for every head, from the weights w.
+static int launch_out(const cg_pooled_attn_args& a, cudaStream_t s) {
+  if (rows_eligible(a) && al16(a.out)) {
+    const size_t smem = (size_t)kOutRowsWarps * a.h * a.k * sizeof(float);
+    CG_REQUIRE(smem <= 48 * 1024, "pooled_attn_out: h * k too large (%d x %d)", a.h, a.k);
+    pooled_out_rows_kernel<<<rows_grid(a.n), 32 * kOutRowsWarps, smem, s>>>(a);
+  } else {
+    const int64_t warps = a.n * a.h;
+    const int64_t blocks = (warps * 32 + 255) / 256;
+    const int64_t cap = (int64_t)sm_count() * 16;
+    pooled_out_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, s>>>(a);
+  }
+  CG_LAUNCHED("pooled_attn_out");
+  return kOk;
+}
+
 static int run(int which, const cg_pooled_attn_args* args, void* stream) {
   CG_REQUIRE(args != nullptr, "pooled_attn: args is NULL");
   const cg_pooled_attn_args& a = *args;
@@ -45,7 +75,9 @@ static int run(int which, const cg_pooled_attn_args* args, void* stream) {
   if (which != 0) vec = vec && a.ld_dqk % 4 == 0 && al16(a.dqk) && al16(a.dout);
   P.vec = vec ? 1 : 0;
   const cudaStream_t s = as_stream(stream);
-  return a.precision == CG_ATTN_TF32 ? launch_tf32(which, P, dp, s) : launch_fp32(which, P, dp, s);
+  const int rc = a.precision == CG_ATTN_TF32 ? launch_tf32(which, P, dp, s) : launch_fp32(which, P, dp, s);
+  if (rc != kOk || which != 0) return rc;
+  return launch_out(a, s);
 }
 
 }  // namespace pooled
@@ -63,26 +95,7 @@ int cg_pooled_attn_out(const cg_pooled_attn_args* a, void* stream) {
   CG_REQUIRE(a->token_index && a->key_count && a->qkv && a->w && a->out,
              "pooled_attn_out: token_index, key_count, qkv, w and out are required");
   CG_REQUIRE(a->ld_qkv >= 3 * (int64_t)a->h * a->d, "pooled_attn_out: ld_qkv below 3*h*d");
-  const int64_t C = (int64_t)a->h * a->d;
-  const bool rows = a->d % 4 == 0 && C % 128 == 0 && C / 128 <= cg::pooled::kOutRowsQMax && a->ld_qkv % 4 == 0 &&
-                    (reinterpret_cast<uintptr_t>(a->qkv) & 15) == 0 && (reinterpret_cast<uintptr_t>(a->out) & 15) == 0;
-  if (rows) {
-    // one warp per atom, all heads
-    using cg::pooled::kOutRowsWarps;
-    const int64_t blocks = (a->n + kOutRowsWarps - 1) / kOutRowsWarps;
-    const int64_t cap = (int64_t)cg::sm_count() * 8;
-    const size_t smem = (size_t)kOutRowsWarps * a->h * a->k * sizeof(float);
-    CG_REQUIRE(smem <= 48 * 1024, "pooled_attn_out: h * k too large (%d x %d)", a->h, a->k);
-    cg::pooled::pooled_out_rows_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 32 * kOutRowsWarps, smem,
-                                         cg::as_stream(stream)>>>(*a);
-  } else {
-    const int64_t warps = a->n * a->h;
-    const int64_t blocks = (warps * 32 + 255) / 256;
-    const int64_t cap = (int64_t)cg::sm_count() * 16;
-    cg::pooled::pooled_out_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, cg::as_stream(stream)>>>(*a);
-  }
-  CG_LAUNCHED("pooled_attn_out");
-  return cg::kOk;
+  return cg::pooled::launch_out(*a, cg::as_stream(stream));
 }
 
 int cg_pooled_attn_bwd1(const cg_pooled_attn_args* a, void* stream) { return cg::pooled::run(1, a, stream); }

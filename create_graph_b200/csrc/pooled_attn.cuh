@@ -8,9 +8,10 @@
 // as mma fragments, operands gathered through the staged token index into
 // swizzled shared memory, tf32 or three-term products). What pooling changes:
 // - forward: w_j = sum_i env_i P_ij is a column sum of the fragments (quad
-//   shuffles over g, then the two bands in a fixed order) and
-//   out = sum_j w_j v_j a per-column FMA loop reading v straight from the
-//   atom rows; the P v product and the staging of v disappear;
+//   shuffles over g, then the two bands in a fixed order); the forward kernel
+//   writes lse and w, and out = sum_j w_j v_j follows in the output kernel
+//   (one pass over each token's v row for all heads); the P v product and the
+//   staging of v disappear;
 // - backward1: the token cotangent is env_i dm, so grad_probs = env_i u_j
 //   with u = V dm, dv_j = w_j dm is rank one (left to cg_segment_sum_scaled
 //   as the weight w) and only S, dq and dk are products;
@@ -165,7 +166,9 @@ __device__ __forceinline__ void load_rows2_async(float* s1, const float* b1, flo
 // u_j = row_j . x for the atom's tokens, read straight from the per-atom rows
 // (L2) while the operand copies are in flight: two threads per token j =
 // tid / 2 (alternate 4-column chunks, then one shuffle), zero for padding
-// and past k. vec: 16-byte rows and x.
+// and past k. vec: 16-byte rows and x, d == DP; its loop has a compile-time
+// trip count and is unrolled, so a thread's loads are in flight together.
+template <int DP>
 __device__ __forceinline__ void token_dots(float* out, const float* base, const int64_t* srow, const float* x, int d,
                                            bool vec) {
   const int j = threadIdx.x >> 1, half = threadIdx.x & 1;
@@ -174,7 +177,8 @@ __device__ __forceinline__ void token_dots(float* out, const float* base, const 
   if (off >= 0) {
     const float* row = base + off;
     if (vec) {
-      for (int q = half; q < d / 4; q += 2) {
+#pragma unroll
+      for (int q = half; q < DP / 4; q += 2) {
         const float4 v = __ldg(reinterpret_cast<const float4*>(row) + q);
         const float4 m = __ldg(reinterpret_cast<const float4*>(x) + q);
         acc += v.x * m.x + v.y * m.y + v.z * m.z + v.w * m.w;
@@ -246,21 +250,9 @@ __global__ void __launch_bounds__(kThreads, 12) pooled_fwd(const PParams P) {
       if (threadIdx.x < KP) {
         const float wj = sW[threadIdx.x] + sW[KP + threadIdx.x];
         if ((int)threadIdx.x < k) a.w[(n * H + hh) * k + threadIdx.x] = wj;
-        sW[threadIdx.x] = wj;  // each thread rewrites only the entry it read
       }
-      __syncthreads();
-      // out = sum_j w_j v_j over the valid keys (w_j = 0 past kc), v read
-      // straight from the atom rows (coalesced over c)
-      const float* vbase = a.qkv + 2 * C + (int64_t)hh * d;
-      for (int c = threadIdx.x; c < d; c += kThreads) {
-        float acc = 0.0f;
-#pragma unroll 8
-        for (int j = 0; j < kc; ++j) {
-          const int64_t off = sRow[j];
-          if (off >= 0) acc += sW[j] * __ldg(vbase + off + c);
-        }
-        a.out[n * C + (int64_t)hh * d + c] = acc;
-      }
+      // out = sum_j w_j v_j is formed afterwards from w (pooled_out_*_kernel),
+      // one pass over each token's whole v row for all heads
     }
   }
 }
@@ -305,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 10) pooled_bwd1(const PParams P) {
         sLse[i] = i < k ? a.lse[(n * H + hh) * k + i] : INFINITY;
         sW[i] = i < k ? a.w[(n * H + hh) * k + i] : 0.0f;
       }
-      token_dots(sU, hq + 2 * C, sRow, a.dout + n * C + (int64_t)hh * d, d, vec);  // u = V dm
+      token_dots<DP>(sU, hq + 2 * C, sRow, a.dout + n * C + (int64_t)hh * d, d, vec);  // u = V dm
       cp_async_wait<0>();
       __syncthreads();
       float S[4][4], p[4][4], lse[2];
@@ -415,8 +407,8 @@ __global__ void __launch_bounds__(kThreads) pooled_bwd2(const PParams P) {
         sW[i] = i < k ? a.w[(n * H + hh) * k + i] : 0.0f;
       }
       const float* dm = a.dout + n * C + (int64_t)hh * d;
-      token_dots(sU, hq + 2 * C, sRow, dm, d, vec);  // u = V dm
-      token_dots(sT, nq + 2 * C, sRow, dm, d, vec);  // t = HV dm
+      token_dots<DP>(sU, hq + 2 * C, sRow, dm, d, vec);  // u = V dm
+      token_dots<DP>(sT, nq + 2 * C, sRow, dm, d, vec);  // t = HV dm
       cp_async_wait<0>();
       __syncthreads();
       float S[4][4], A[4][4], p[4][4], lse[2];

@@ -165,8 +165,9 @@ int cg_pooled_attn_fwd(const cg_pooled_attn_args* a, void* stream);
 int cg_pooled_attn_bwd1(const cg_pooled_attn_args* a, void* stream);
 int cg_pooled_attn_bwd2(const cg_pooled_attn_args* a, void* stream);
 /* The forward's output for known weights: out[n, h] = sum_j w[n, h, j] v_j over
- * the valid keys (qkv, token_index, key_count, w, out used), in the forward's
- * order and arithmetic (equal to cg_pooled_attn_fwd's out bit for bit). A
+ * the valid keys (qkv, token_index, key_count, w, out used); cg_pooled_attn_fwd
+ * forms its out with this same kernel after writing lse and w, so the two are
+ * equal bit for bit. A
  * checkpoint recompute of a block on the same inputs reuses the first
  * forward's w and lse through it instead of recomputing the softmax. No
  * counterpart in the reference (its recompute reruns the whole forward). */
