@@ -145,20 +145,22 @@ __device__ __forceinline__ void kstep(float (&acc)[NT][4], LA la, LB lb, int k0,
 }
 
 // acc += A(16 x 8*KT) * B(8*KT x 8*NT); the tf32 loop is unrolled, the
-// three-term one (three times the code per step) is not.
-template <bool X3, int NT, int KT, class LA, class LB>
+// three-term one (three times the code per step) only where FULL asks for it
+// (kernels whose register budget holds it: the unrolled steps pipeline their
+// fragment loads and splits across k).
+template <bool X3, int NT, int KT, bool FULL = !X3, class LA, class LB>
 __device__ __forceinline__ void band_mma(float (&acc)[NT][4], LA la, LB lb, int g, int t) {
-  constexpr int U = X3 ? 1 : KT;
+  constexpr int U = FULL ? KT : 1;
 #pragma unroll U
   for (int kt = 0; kt < KT; ++kt) kstep<X3>(acc, la, lb, kt * 8, g, t);
 }
 
 // Two independent products in one k loop: twice the accumulator chains in
 // flight per warp.
-template <bool X3, int NT, int KT, class LA1, class LB1, class LA2, class LB2>
+template <bool X3, int NT, int KT, bool FULL = !X3, class LA1, class LB1, class LA2, class LB2>
 __device__ __forceinline__ void band_mma2(float (&acc1)[NT][4], LA1 la1, LB1 lb1, float (&acc2)[NT][4], LA2 la2,
                                           LB2 lb2, int g, int t) {
-  constexpr int U = X3 ? 1 : KT;
+  constexpr int U = FULL ? KT : 1;
 #pragma unroll U
   for (int kt = 0; kt < KT; ++kt) {
     kstep<X3>(acc1, la1, lb1, kt * 8, g, t);
@@ -546,7 +548,7 @@ __global__ void __launch_bounds__(kThreads) fwd1_tc(const Params P) {
     const int kc = valid_keys(P, n);
     float S[4][4], p[4][4], lse[2];
     zero(S);
-    band_mma<X3, 4, DP / 8>(S, CG_A_ROWS(sQ), CG_B_ROWS(sK), g, t);
+    band_mma<X3, 4, DP / 8, true>(S, CG_A_ROWS(sQ), CG_B_ROWS(sK), g, t);
     band_softmax<!X3>(p, S, sP, brow, band, g, t, scale, kc, nullptr, lse);
     cp_async_wait<0>();
     __syncthreads();  // V landed
@@ -695,7 +697,7 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
       float p[4][4], lse[2], A[4][4], B[4][4];
       zero(A);  // scores
       zero(B);  // grad_probs = grad_out v^T
-      band_mma2<X3, 4, DP / 8>(A, CG_A_ROWS(sQ), CG_B_ROWS(sK), B, CG_A_ROWS(sG), CG_B_ROWS(sV), g, t);
+      band_mma2<X3, 4, DP / 8, true>(A, CG_A_ROWS(sQ), CG_B_ROWS(sK), B, CG_A_ROWS(sG), CG_B_ROWS(sV), g, t);
       band_softmax<!X3>(p, A, sBias, brow, band, g, t, scale, kc, sLse, lse);
       float rs[2];
       row_dot(rs, p, B);
@@ -708,8 +710,8 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
       __syncthreads();
       zero(A);  // d_logits = scale * (hq k^T + q hk^T) + hb
       zero(B);  // grad_out hv^T
-      band_mma2<X3, 4, DP / 8>(A, CG_A_ROWS(sHQ), CG_B_ROWS(sK), B, CG_A_ROWS(sG), CG_B_ROWS(sHV), g, t);
-      band_mma<X3, 4, DP / 8>(A, CG_A_ROWS(sQ), CG_B_ROWS(sHK), g, t);
+      band_mma2<X3, 4, DP / 8, true>(A, CG_A_ROWS(sHQ), CG_B_ROWS(sK), B, CG_A_ROWS(sG), CG_B_ROWS(sHV), g, t);
+      band_mma<X3, 4, DP / 8, true>(A, CG_A_ROWS(sQ), CG_B_ROWS(sHK), g, t);
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
@@ -757,8 +759,8 @@ __global__ void __launch_bounds__(kThreads) bwd2_tc(const Params P) {
       float DK[DP / 8][4], DV[DP / 8][4];
       zero(DK);  // grad_k = scale * (grad_logits^T hq + d_scores^T q)
       zero(DV);  // grad_v = d_grad_probs^T grad_out
-      band_mma2<X3, DP / 8, 4>(DK, CG_A_KKT(sGL), CG_B_COLS(sHQ), DV, CG_A_KKT(sDG), CG_B_COLS(sG), g, t);
-      band_mma<X3, DP / 8, 4>(DK, CG_A_KKT(sDS), CG_B_COLS(sQ), g, t);
+      band_mma2<X3, DP / 8, 4, true>(DK, CG_A_KKT(sGL), CG_B_COLS(sHQ), DV, CG_A_KKT(sDG), CG_B_COLS(sG), g, t);
+      band_mma<X3, DP / 8, 4, true>(DK, CG_A_KKT(sDS), CG_B_COLS(sQ), g, t);
       store_band<DP / 8>(a.dk, n, h, band, k, d, DK, g, t, scale, vec);
       store_band<DP / 8>(a.dv, n, h, band, k, d, DV, g, t, 1.0f, vec);
     }
