@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 12) pooled_fwd(const PParams P) {
       __syncthreads();
       float S[4][4], p[4][4], lse[2];
       zero(S);
-      band_mma<X3, 4, DP / 8>(S, CG_A_ROWS(sQ), CG_B_ROWS(sK), g, t);
+      band_mma<X3, 4, DP / 8, true>(S, CG_A_ROWS(sQ), CG_B_ROWS(sK), g, t);
       band_softmax<!X3>(p, S, sB, 0, band, g, t, scale, kc, nullptr, lse);
       const float e0 = sE[band * 16 + g], e1 = sE[band * 16 + g + 8];
 #pragma unroll
@@ -302,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 10) pooled_bwd1(const PParams P) {
       __syncthreads();
       float S[4][4], p[4][4], lse[2];
       zero(S);
-      band_mma<X3, 4, DP / 8>(S, CG_A_ROWS(sQ), CG_B_ROWS(sK), g, t);
+      band_mma<X3, 4, DP / 8, true>(S, CG_A_ROWS(sQ), CG_B_ROWS(sK), g, t);
       band_softmax<!X3>(p, S, sB, 0, band, g, t, scale, kc, sLse, lse);
       float uc[4][2];
 #pragma unroll
@@ -332,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 10) pooled_bwd1(const PParams P) {
       put_band(sGL, S, band, g, t);
       __syncthreads();
       zero(O);  // dk = scale dL^T q
-      band_mma<X3, DP / 8, 4>(O, CG_A_KKT(sGL), CG_B_COLS(sQ), g, t);
+      band_mma<X3, DP / 8, 4, true>(O, CG_A_KKT(sGL), CG_B_COLS(sQ), g, t);
       store_band<DP / 8>(tk, n, hh, band, k, d, O, g, t, scale, vec);
       if (warp == 0) {
         if (a.dbias != nullptr) {

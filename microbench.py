@@ -115,9 +115,9 @@ def pooled_inputs(n: int, h: int = 12, k: int = 30, d: int = 64, seed: int = 0):
     return cuda, k, h
 
 
-def pooled(n: int = 8280, iters: int = 10, precision: str = "tf32") -> dict:
-    """Median launch time of the pooled attention kernels at the model shape."""
-    (qkv, bias, env, index, counts, dm, hqkv, hb, he), k, h = pooled_inputs(n)
+def pooled(n: int = 8280, iters: int = 10, precision: str = "tf32", heads: int = 12, k: int = 30, d: int = 64) -> dict:
+    """Median launch time of the pooled attention kernels (default: the 85M model's shape)."""
+    (qkv, bias, env, index, counts, dm, hqkv, hb, he), k, h = pooled_inputs(n, heads, k, d)
     args = (index, counts, k, h, 0.125, precision)
     _, lse, w = pooled_attention_forward(qkv, bias, env, *args)
     fns = {
@@ -154,6 +154,9 @@ def main() -> None:
     p_pool.add_argument("--n", type=int, default=8280)
     p_pool.add_argument("--iters", type=int, default=10)
     p_pool.add_argument("--precision", choices=("fp32", "tf32"), default="tf32")
+    p_pool.add_argument("--heads", type=int, default=12)
+    p_pool.add_argument("--k", type=int, default=30)
+    p_pool.add_argument("--d", type=int, default=64)
     p_gemm = sub.add_parser("gemm")
     p_gemm.add_argument("shape", type=int, nargs=3)
     p_gemm.add_argument("--silu", action="store_true")
@@ -163,7 +166,7 @@ def main() -> None:
     if args.what == "attn":
         print(json.dumps(attn(args.n, args.iters, precision=args.precision)))
     elif args.what == "pooled":
-        print(json.dumps(pooled(args.n, args.iters, args.precision)))
+        print(json.dumps(pooled(args.n, args.iters, args.precision, args.heads, args.k, args.d)))
     else:
         print(json.dumps(gemm_bench(*args.shape, silu=args.silu, a_mn=args.a_mn, b_mn=args.b_mn)))
 
