@@ -19,6 +19,7 @@ namespace cg {
 namespace nbl {
 
 constexpr int KMAX = 64;
+constexpr int64_t kReverseSmemMax = 160 * 1024;  // staged slots of one system in shared memory
 
 __device__ inline float d2_exact(float xi, float yi, float zi, float xj, float yj, float zj) {
   const float dx = __fsub_rn(xj, xi), dy = __fsub_rn(yj, yi), dz = __fsub_rn(zj, zi);
@@ -69,6 +70,90 @@ __global__ void select_kernel(const float* __restrict__ pos, const int32_t* __re
   if (threadIdx.x == 0) sys_edges[b] = total;
 }
 
+// Systems of at most kSmallSystemSel atoms: one warp per atom. The system's
+// positions are staged in shared memory; lane l scores candidates l, l + 32,
+// ... (8 per lane) as 64-bit keys (bits of d2 << 32 | j; d2 >= 0, so the
+// integer order is the (d2, j) order; non-candidates get the largest key)
+// and the warp sorts the 256 keys with a bitonic network (element p = 8 lane
+// + r: strides below 8 inside a lane, the others across lanes by shuffles).
+// The first k keys are the kept neighbours in (d2, j) order: the same list
+// as select_kernel's, from the same d2 bits.
+constexpr int kSmallSystemSel = 256;
+constexpr int kSelectWarps = 4;
+
+__global__ void __launch_bounds__(32 * kSelectWarps) select_small_kernel(
+    const float* __restrict__ pos, const int32_t* __restrict__ sys_ptr, int k, float cutoff2,
+    int32_t* __restrict__ nbr, int32_t* __restrict__ counts, int32_t* __restrict__ sys_edges) {
+  __shared__ float sp[3 * kSmallSystemSel];
+  __shared__ int total;
+  const int b = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int a0 = sys_ptr[b], n = sys_ptr[b + 1] - a0;
+  if (threadIdx.x == 0) total = 0;
+  for (int e = threadIdx.x; e < 3 * n; e += 32 * kSelectWarps) sp[e] = pos[3 * (int64_t)a0 + e];
+  __syncthreads();
+  int mine = 0;
+  for (int li = warp; li < n; li += kSelectWarps) {
+    const float xi = sp[3 * li], yi = sp[3 * li + 1], zi = sp[3 * li + 2];
+    unsigned long long key[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int c = lane + 32 * r;
+      key[r] = ~0ull;
+      if (c < n && c != li) {
+        const float d = d2_exact(xi, yi, zi, sp[3 * c], sp[3 * c + 1], sp[3 * c + 2]);
+        if (d < cutoff2) key[r] = ((unsigned long long)__float_as_uint(d) << 32) | (unsigned)(a0 + c);
+      }
+    }
+    // bitonic sort, ascending over p = 8 lane + r
+#pragma unroll
+    for (int size = 2; size <= 256; size <<= 1) {
+#pragma unroll
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        if (stride >= 8) {
+          const int other_lane = lane ^ (stride >> 3);
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            const unsigned long long o = __shfl_xor_sync(0xffffffffu, key[r], stride >> 3);
+            const bool up = ((8 * lane + r) & size) == 0;
+            const bool keep_min = (lane < other_lane) == up;
+            key[r] = keep_min ? (o < key[r] ? o : key[r]) : (o > key[r] ? o : key[r]);
+          }
+        } else {
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            const int q = r ^ stride;
+            if (q > r) {
+              const bool up = ((8 * lane + r) & size) == 0;
+              const unsigned long long lo = key[r] < key[q] ? key[r] : key[q];
+              const unsigned long long hi = key[r] < key[q] ? key[q] : key[r];
+              key[r] = up ? lo : hi;
+              key[q] = up ? hi : lo;
+            }
+          }
+        }
+      }
+    }
+    const int i = a0 + li;
+    int kept = 0;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int p = 8 * lane + r;
+      const bool valid = key[r] != ~0ull;
+      if (p < k) {
+        nbr[(int64_t)i * k + p] = valid ? (int32_t)(key[r] & 0xffffffffull) : -1;
+        kept += valid;
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) kept += __shfl_xor_sync(0xffffffffu, kept, off);
+    if (lane == 0) counts[i] = kept;
+    mine += lane == 0 ? kept : 0;
+  }
+  if (lane == 0) atomicAdd(&total, mine);  // integer count: order does not matter
+  __syncthreads();
+  if (threadIdx.x == 0) sys_edges[b] = total;
+}
+
 // Exclusive scan of the per-system slot totals (one thread: a few hundred systems).
 __global__ void scan_systems_kernel(const int32_t* __restrict__ sys_edges, int n_sys,
                                     int32_t* __restrict__ sys_offset) {
@@ -83,19 +168,30 @@ __global__ void scan_systems_kernel(const int32_t* __restrict__ sys_edges, int n
 
 // One block per system: reverse CSR of its slots. Thread t owns targets
 // j = a0 + t, a0 + t + blockDim, ...; each walks the system's slots in
-// ascending order, so every segment is sorted.
+// ascending order, so every segment is sorted. Slots past an atom's count
+// hold -1 (select_kernel), so the walk covers all n*k slots without reading
+// the counts. With `staged`, the system's slots are first copied to shared
+// memory (after the n per-target words) and the walks read them there.
 __global__ void reverse_kernel(const int32_t* __restrict__ sys_ptr, const int32_t* __restrict__ sys_offset,
-                               const int32_t* __restrict__ nbr, const int32_t* __restrict__ counts, int k,
-                               int n_atoms, int32_t* __restrict__ rev_ptr, int32_t* __restrict__ rev_idx) {
+                               const int32_t* __restrict__ nbr, int k, int n_atoms, int staged_stride,
+                               int32_t* __restrict__ rev_ptr, int32_t* __restrict__ rev_idx) {
   const int b = blockIdx.x;
   const int a0 = sys_ptr[b], a1 = sys_ptr[b + 1];
-  extern __shared__ int32_t scan[];  // per-target counts, then offsets
+  extern __shared__ int32_t scan[];  // per-target counts, then offsets; then the staged slots
   const int n = a1 - a0;
+  const int slots = n * k;
+  const int32_t* src = nbr + (int64_t)a0 * k;
+  if (staged_stride > 0) {
+    int32_t* staged = scan + staged_stride;
+    for (int e = threadIdx.x; e < slots; e += blockDim.x) staged[e] = src[e];
+    src = staged;
+    __syncthreads();
+  }
   for (int t = threadIdx.x; t < n; t += blockDim.x) {
     const int j = a0 + t;
     int c = 0;
-    for (int i = a0; i < a1; ++i)
-      for (int s = 0; s < counts[i]; ++s) c += nbr[(int64_t)i * k + s] == j;
+#pragma unroll 4
+    for (int e = 0; e < slots; ++e) c += src[e] == j;
     scan[t] = c;
   }
   __syncthreads();
@@ -112,11 +208,72 @@ __global__ void reverse_kernel(const int32_t* __restrict__ sys_ptr, const int32_
     const int j = a0 + t;
     int32_t w = scan[t];
     rev_ptr[j] = w;
-    for (int i = a0; i < a1; ++i)
-      for (int s = 0; s < counts[i]; ++s)
-        if (nbr[(int64_t)i * k + s] == j) rev_idx[w++] = (int32_t)((int64_t)i * k + s);
+    for (int e = 0; e < slots; ++e)
+      if (src[e] == j) rev_idx[w++] = (int32_t)((int64_t)a0 * k + e);
   }
   if (b == gridDim.x - 1 && threadIdx.x == 0) rev_ptr[n_atoms] = sys_offset[gridDim.x];
+}
+
+// Systems of at most kSmallSystem atoms: the same reverse CSR by a stable
+// counting sort in O(slots) per system (the kernel above walks all slots
+// once per target). Integer shared atomics count slots per target; an
+// exclusive scan gives each target's start; slots are then placed in
+// chunks of the block's width in ascending order, a slot's rank among the
+// chunk's slots of its target being its rank within its warp (match + popc)
+// plus the counts of that target in the chunk's earlier warps. Placement
+// depends only on slot order: identical output on every run, equal to the
+// kernel above.
+constexpr int kSmallSystem = 256;
+constexpr int kReverseThreads = 128;
+
+__global__ void __launch_bounds__(kReverseThreads) reverse_small_kernel(
+    const int32_t* __restrict__ sys_ptr, const int32_t* __restrict__ sys_offset, const int32_t* __restrict__ nbr,
+    int k, int n_atoms, int32_t* __restrict__ rev_ptr, int32_t* __restrict__ rev_idx) {
+  constexpr int W = kReverseThreads / 32;
+  __shared__ int32_t start[kSmallSystem];
+  __shared__ int32_t wcount[W][kSmallSystem];
+  const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int a0 = sys_ptr[b], n = sys_ptr[b + 1] - a0;
+  const int slots = n * k;
+  const int32_t* src = nbr + (int64_t)a0 * k;
+  for (int t = tid; t < n; t += kReverseThreads) start[t] = 0;
+  __syncthreads();
+  for (int e = tid; e < slots; e += kReverseThreads) {
+    const int32_t j = src[e];
+    if (j >= 0) atomicAdd(&start[j - a0], 1);  // integer counts: order does not matter
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int32_t run = sys_offset[b];
+    for (int t = 0; t < n; ++t) {
+      const int32_t c = start[t];
+      start[t] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  for (int t = tid; t < n; t += kReverseThreads) rev_ptr[a0 + t] = start[t];
+  const uint32_t lower_lanes = (1u << lane) - 1u;
+  for (int c0 = 0; c0 < slots; c0 += kReverseThreads) {
+    const int e = c0 + tid;
+    const int32_t j = e < slots ? src[e] : -1;
+    const int t = j >= 0 ? j - a0 : -1;
+    const uint32_t same = __match_any_sync(0xffffffffu, t);
+    const int rank = __popc(same & lower_lanes);
+    for (int i = tid; i < W * kSmallSystem; i += kReverseThreads) (&wcount[0][0])[i] = 0;
+    __syncthreads();
+    if (t >= 0 && rank == 0) wcount[warp][t] = __popc(same);
+    __syncthreads();
+    if (t >= 0) {
+      int32_t before = 0;
+      for (int w = 0; w < warp; ++w) before += wcount[w][t];
+      rev_idx[start[t] + before + rank] = (int32_t)((int64_t)a0 * k + e);
+    }
+    __syncthreads();
+    if (t >= 0 && rank == 0) atomicAdd(&start[t], __popc(same));  // integer: exact
+    __syncthreads();
+  }
+  if (b == gridDim.x - 1 && tid == 0) rev_ptr[n_atoms] = sys_offset[gridDim.x];
 }
 
 }  // namespace nbl
@@ -144,13 +301,28 @@ int cg_neighbor_list(const float* pos, const int32_t* sys_ptr, int64_t n_systems
   int32_t* sys_offset = workspace + n_systems;
   const float cutoff2 = cutoff * cutoff;
   cudaStream_t s = as_stream(stream);
-  nbl::select_kernel<<<(unsigned)n_systems, 128, 0, s>>>(pos, sys_ptr, k, cutoff2, nbr, counts, sys_edges);
+  if (max_atoms_per_system <= nbl::kSmallSystemSel && k <= 256)
+    nbl::select_small_kernel<<<(unsigned)n_systems, 32 * nbl::kSelectWarps, 0, s>>>(pos, sys_ptr, k, cutoff2, nbr,
+                                                                                   counts, sys_edges);
+  else
+    nbl::select_kernel<<<(unsigned)n_systems, 128, 0, s>>>(pos, sys_ptr, k, cutoff2, nbr, counts, sys_edges);
   CG_LAUNCHED("neighbor_list select");
   nbl::scan_systems_kernel<<<1, 32, 0, s>>>(sys_edges, (int)n_systems, sys_offset);
   CG_LAUNCHED("neighbor_list scan");
-  const size_t smem = (size_t)(max_atoms_per_system > 0 ? max_atoms_per_system : 1) * sizeof(int32_t);
-  nbl::reverse_kernel<<<(unsigned)n_systems, 128, smem, s>>>(sys_ptr, sys_offset, nbr, counts, k, (int)n_atoms,
-                                                             rev_ptr, rev_idx);
+  if (max_atoms_per_system <= nbl::kSmallSystem) {
+    nbl::reverse_small_kernel<<<(unsigned)n_systems, nbl::kReverseThreads, 0, s>>>(sys_ptr, sys_offset, nbr, k,
+                                                                                  (int)n_atoms, rev_ptr, rev_idx);
+    CG_LAUNCHED("neighbor_list reverse");
+    return kOk;
+  }
+  // the per-target words, then (when they fit) the largest system's slots
+  const int64_t words = max_atoms_per_system > 0 ? max_atoms_per_system : 1;
+  const int64_t stride = (words + 3) / 4 * 4;
+  const bool staged = (stride + words * k) * (int64_t)sizeof(int32_t) <= nbl::kReverseSmemMax;
+  const size_t smem = (size_t)(staged ? stride + words * k : words) * sizeof(int32_t);
+  CG_CUDA(cudaFuncSetAttribute(nbl::reverse_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  nbl::reverse_kernel<<<(unsigned)n_systems, 128, smem, s>>>(sys_ptr, sys_offset, nbr, k, (int)n_atoms,
+                                                             staged ? (int)stride : 0, rev_ptr, rev_idx);
   CG_LAUNCHED("neighbor_list reverse");
   return kOk;
 }

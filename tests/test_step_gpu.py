@@ -51,9 +51,25 @@ def tiny_inputs(seed=0, sizes=(20, 31, 25, 40, 3)):
     return pos, species, sys_ptr, e_t, f_t
 
 
+def _lattice(nx, ny, nz, spacing=1.0):
+    """Atoms on a cubic grid: many exactly equal distances (the (d2, j) tie rule)."""
+    g = torch.stack(torch.meshgrid(torch.arange(nx), torch.arange(ny), torch.arange(nz), indexing="ij"), -1)
+    return spacing * g.reshape(-1, 3).float()
+
+
 def test_neighbor_list_bit_exact():
-    for seed, sizes, k in [(0, [20, 31, 25, 40, 3], 12), (1, [200, 150, 64], 30), (2, [1, 2, 64], 32)]:
-        pos, species, sys_ptr = mlip.synthetic_systems(sizes, 5, seed=seed)
+    """Systems of up to 256 atoms take the warp-per-atom selection and the
+    counting-sort reverse; larger ones the per-thread kernels: both against
+    the oracle, on random systems and on lattices full of equal distances."""
+    cases = []
+    for seed, sizes, k in [(0, [20, 31, 25, 40, 3], 12), (1, [200, 150, 64], 30), (2, [1, 2, 64], 32),
+                           (3, [256, 30], 30), (4, [300, 40], 20), (5, [257], 64)]:
+        pos, _, sys_ptr = mlip.synthetic_systems(sizes, 5, seed=seed)
+        cases.append((pos, sys_ptr, sizes, k))
+    for dims in ((4, 4, 4), (7, 7, 6)):
+        pos = _lattice(*dims)
+        cases.append((pos, torch.tensor([0, pos.shape[0]], dtype=torch.int32), [pos.shape[0]], 26))
+    for pos, sys_ptr, sizes, k in cases:
         g = build_graph(pos.cuda(), sys_ptr.cuda(), len(sizes), max(sizes), 6.0, k)
         nbr, counts, rev_ptr, rev_idx = onb.neighbor_list(pos.numpy(), sys_ptr.numpy(), 6.0, k)
         assert np.array_equal(g.nbr.cpu().numpy(), nbr)
