@@ -6,8 +6,13 @@
 // is evaluated with round-to-nearest single operations (no FMA contraction),
 // so a CPU evaluating the same expression gets the same bits. The k nearest
 // by (d2, j) are kept in that order. The reverse CSR (slots grouped by
-// neighbour, slots ascending) is filled in a fixed order. Nothing is atomic:
-// the output is identical on every run.
+// neighbour, slots ascending) lists every segment in ascending slot order.
+// Integer atomics only count or place entries whose final order is fixed
+// afterwards: the output is identical on every run.
+//
+// Systems of up to 256 atoms (the batches of small molecules the models
+// train on) run per system in shared memory; larger ones (up to 12000
+// atoms) run over the whole batch with the candidates read from L2.
 //
 // The reference leaves neighbour lists to model code before its region
 // (README.md:28 there); this is the GPU builder of the padded layout the
@@ -19,72 +24,85 @@ namespace cg {
 namespace nbl {
 
 constexpr int KMAX = 64;
-constexpr int64_t kReverseSmemMax = 160 * 1024;  // staged slots of one system in shared memory
 
 __device__ inline float d2_exact(float xi, float yi, float zi, float xj, float yj, float zj) {
   const float dx = __fsub_rn(xj, xi), dy = __fsub_rn(yj, yi), dz = __fsub_rn(zj, zi);
   return __fadd_rn(__fadd_rn(__fmul_rn(dx, dx), __fmul_rn(dy, dy)), __fmul_rn(dz, dz));
 }
 
-__device__ inline bool before(float da, int ja, float db, int jb) {
-  return da < db || (da == db && ja < jb);
-}
-
-// One block per system: the k nearest neighbours of every atom, and the
-// number of kept slots of the system.
-__global__ void select_kernel(const float* __restrict__ pos, const int32_t* __restrict__ sys_ptr, int k,
-                              float cutoff2, int32_t* __restrict__ nbr, int32_t* __restrict__ counts,
-                              int32_t* __restrict__ sys_edges) {
-  const int b = blockIdx.x;
-  const int a0 = sys_ptr[b], a1 = sys_ptr[b + 1];
-  __shared__ int total;
-  if (threadIdx.x == 0) total = 0;
-  __syncthreads();
-  int mine = 0;
-  for (int i = a0 + threadIdx.x; i < a1; i += blockDim.x) {
-    float bd[KMAX];
-    int bj[KMAX];
-    int n = 0;
-    const float xi = pos[3 * i], yi = pos[3 * i + 1], zi = pos[3 * i + 2];
-    for (int j = a0; j < a1; ++j) {
-      if (j == i) continue;
-      const float d = d2_exact(xi, yi, zi, pos[3 * j], pos[3 * j + 1], pos[3 * j + 2]);
-      if (!(d < cutoff2)) continue;
-      if (n == k && !before(d, j, bd[k - 1], bj[k - 1])) continue;
-      int p = n < k ? n : k - 1;  // insertion position from the end
-      while (p > 0 && before(d, j, bd[p - 1], bj[p - 1])) {
-        bd[p] = bd[p - 1];
-        bj[p] = bj[p - 1];
-        --p;
+// Ascending bitonic sort of the warp's 256 keys, element p = 8 lane + r in
+// key[r]: strides below 8 inside a lane, the others across lanes by shuffles.
+__device__ __forceinline__ void warp_sort256(unsigned long long (&key)[8], int lane) {
+#pragma unroll
+  for (int size = 2; size <= 256; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      if (stride >= 8) {
+        const int other_lane = lane ^ (stride >> 3);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          const unsigned long long o = __shfl_xor_sync(0xffffffffu, key[r], stride >> 3);
+          const bool up = ((8 * lane + r) & size) == 0;
+          const bool keep_min = (lane < other_lane) == up;
+          key[r] = keep_min ? (o < key[r] ? o : key[r]) : (o > key[r] ? o : key[r]);
+        }
+      } else {
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          const int q = r ^ stride;
+          if (q > r) {
+            const bool up = ((8 * lane + r) & size) == 0;
+            const unsigned long long lo = key[r] < key[q] ? key[r] : key[q];
+            const unsigned long long hi = key[r] < key[q] ? key[q] : key[r];
+            key[r] = up ? lo : hi;
+            key[q] = up ? hi : lo;
+          }
+        }
       }
-      bd[p] = d;
-      bj[p] = j;
-      if (n < k) ++n;
     }
-    for (int s = 0; s < k; ++s) nbr[(int64_t)i * k + s] = s < n ? bj[s] : -1;
-    counts[i] = n;
-    mine += n;
   }
-  atomicAdd(&total, mine);  // integer count: order does not matter
-  __syncthreads();
-  if (threadIdx.x == 0) sys_edges[b] = total;
 }
 
-// Systems of at most kSmallSystemSel atoms: one warp per atom. The system's
-// positions are staged in shared memory; lane l scores candidates l, l + 32,
-// ... (8 per lane) as 64-bit keys (bits of d2 << 32 | j; d2 >= 0, so the
-// integer order is the (d2, j) order; non-candidates get the largest key)
-// and the warp sorts the 256 keys with a bitonic network (element p = 8 lane
-// + r: strides below 8 inside a lane, the others across lanes by shuffles).
-// The first k keys are the kept neighbours in (d2, j) order: the same list
-// as select_kernel's, from the same d2 bits.
-constexpr int kSmallSystemSel = 256;
+// Key of candidate j for atom i: bits of d2 << 32 | j (d2 >= 0, so the
+// integer order is the (d2, j) order), or the largest key when j is not a
+// candidate (j == i, or d2 not below the cutoff).
+__device__ __forceinline__ unsigned long long cand_key(float xi, float yi, float zi, float xj, float yj, float zj,
+                                                       int i, int j, float cutoff2) {
+  if (j == i) return ~0ull;
+  const float d = d2_exact(xi, yi, zi, xj, yj, zj);
+  return d < cutoff2 ? ((unsigned long long)__float_as_uint(d) << 32) | (unsigned)j : ~0ull;
+}
+
+// Writes the first k sorted keys (lanes 0..7 hold positions 0..63) as atom
+// i's neighbour row; returns the number kept (on every lane).
+__device__ __forceinline__ int write_row(const unsigned long long (&key)[8], int lane, int64_t i, int k,
+                                         int32_t* __restrict__ nbr) {
+  int kept = 0;
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const int p = 8 * lane + r;
+    const bool valid = key[r] != ~0ull;
+    if (p < k) {
+      nbr[i * k + p] = valid ? (int32_t)(key[r] & 0xffffffffull) : -1;
+      kept += valid;
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) kept += __shfl_xor_sync(0xffffffffu, kept, off);
+  return kept;
+}
+
+// Systems of at most kSmallSystem atoms: one block per system, one warp per
+// atom. The system's positions are staged in shared memory; lane l scores
+// candidates l, l + 32, ... (8 per lane) and the warp sorts the 256 keys; the
+// first k are the kept neighbours in (d2, j) order.
+constexpr int kSmallSystem = 256;
 constexpr int kSelectWarps = 4;
 
 __global__ void __launch_bounds__(32 * kSelectWarps) select_small_kernel(
     const float* __restrict__ pos, const int32_t* __restrict__ sys_ptr, int k, float cutoff2,
     int32_t* __restrict__ nbr, int32_t* __restrict__ counts, int32_t* __restrict__ sys_edges) {
-  __shared__ float sp[3 * kSmallSystemSel];
+  __shared__ float sp[3 * kSmallSystem];
   __shared__ int total;
   const int b = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int a0 = sys_ptr[b], n = sys_ptr[b + 1] - a0;
@@ -98,60 +116,56 @@ __global__ void __launch_bounds__(32 * kSelectWarps) select_small_kernel(
 #pragma unroll
     for (int r = 0; r < 8; ++r) {
       const int c = lane + 32 * r;
-      key[r] = ~0ull;
-      if (c < n && c != li) {
-        const float d = d2_exact(xi, yi, zi, sp[3 * c], sp[3 * c + 1], sp[3 * c + 2]);
-        if (d < cutoff2) key[r] = ((unsigned long long)__float_as_uint(d) << 32) | (unsigned)(a0 + c);
-      }
+      key[r] = c < n ? cand_key(xi, yi, zi, sp[3 * c], sp[3 * c + 1], sp[3 * c + 2], li, c, cutoff2) : ~0ull;
+      if (key[r] != ~0ull) key[r] += (unsigned)a0;  // local to global atom index (no carry: c + a0 < 2^31)
     }
-    // bitonic sort, ascending over p = 8 lane + r
-#pragma unroll
-    for (int size = 2; size <= 256; size <<= 1) {
-#pragma unroll
-      for (int stride = size >> 1; stride > 0; stride >>= 1) {
-        if (stride >= 8) {
-          const int other_lane = lane ^ (stride >> 3);
-#pragma unroll
-          for (int r = 0; r < 8; ++r) {
-            const unsigned long long o = __shfl_xor_sync(0xffffffffu, key[r], stride >> 3);
-            const bool up = ((8 * lane + r) & size) == 0;
-            const bool keep_min = (lane < other_lane) == up;
-            key[r] = keep_min ? (o < key[r] ? o : key[r]) : (o > key[r] ? o : key[r]);
-          }
-        } else {
-#pragma unroll
-          for (int r = 0; r < 8; ++r) {
-            const int q = r ^ stride;
-            if (q > r) {
-              const bool up = ((8 * lane + r) & size) == 0;
-              const unsigned long long lo = key[r] < key[q] ? key[r] : key[q];
-              const unsigned long long hi = key[r] < key[q] ? key[q] : key[r];
-              key[r] = up ? lo : hi;
-              key[q] = up ? hi : lo;
-            }
-          }
-        }
-      }
-    }
-    const int i = a0 + li;
-    int kept = 0;
-#pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      const int p = 8 * lane + r;
-      const bool valid = key[r] != ~0ull;
-      if (p < k) {
-        nbr[(int64_t)i * k + p] = valid ? (int32_t)(key[r] & 0xffffffffull) : -1;
-        kept += valid;
-      }
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) kept += __shfl_xor_sync(0xffffffffu, kept, off);
-    if (lane == 0) counts[i] = kept;
+    warp_sort256(key, lane);
+    const int kept = write_row(key, lane, a0 + li, k, nbr);
+    if (lane == 0) counts[a0 + li] = kept;
     mine += lane == 0 ? kept : 0;
   }
   if (lane == 0) atomicAdd(&total, mine);  // integer count: order does not matter
   __syncthreads();
   if (threadIdx.x == 0) sys_edges[b] = total;
+}
+
+// Any system size: one warp per atom of the batch (its system found by a
+// binary search of sys_ptr), candidates read from L2. The first chunk is 256
+// candidates; each later chunk brings 192 more into lanes 8..31 while lanes
+// 0..7 keep the 64 smallest keys so far, and the warp re-sorts. k <= 64.
+__global__ void __launch_bounds__(32 * kSelectWarps) select_chunked_kernel(
+    const float* __restrict__ pos, const int32_t* __restrict__ sys_ptr, int n_sys, int64_t n_atoms, int k,
+    float cutoff2, int32_t* __restrict__ nbr, int32_t* __restrict__ counts) {
+  const int lane = threadIdx.x & 31;
+  const int64_t i = (int64_t)blockIdx.x * kSelectWarps + (threadIdx.x >> 5);
+  if (i >= n_atoms) return;
+  int lo = 0, hi = n_sys;  // the system b with sys_ptr[b] <= i < sys_ptr[b + 1]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (sys_ptr[mid] <= i) lo = mid;
+    else hi = mid;
+  }
+  const int a0 = sys_ptr[lo], n = sys_ptr[lo + 1] - a0, li = (int)(i - a0);
+  const float xi = pos[3 * i], yi = pos[3 * i + 1], zi = pos[3 * i + 2];
+  auto key_of = [&](int c) {
+    if (c >= n) return ~0ull;
+    const int64_t j = a0 + c;
+    const unsigned long long kk = cand_key(xi, yi, zi, pos[3 * j], pos[3 * j + 1], pos[3 * j + 2], li, c, cutoff2);
+    return kk == ~0ull ? kk : kk + (unsigned)a0;
+  };
+  unsigned long long key[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) key[r] = key_of(lane + 32 * r);
+  warp_sort256(key, lane);
+  for (int base = 256; base < n; base += 192) {
+    if (lane >= 8) {
+#pragma unroll
+      for (int r = 0; r < 8; ++r) key[r] = key_of(base + (lane - 8) + 24 * r);
+    }
+    warp_sort256(key, lane);
+  }
+  const int kept = write_row(key, lane, i, k, nbr);
+  if (lane == 0) counts[i] = kept;
 }
 
 // Exclusive scan of the per-system slot totals (one thread: a few hundred systems).
@@ -166,54 +180,6 @@ __global__ void scan_systems_kernel(const int32_t* __restrict__ sys_edges, int n
   sys_offset[n_sys] = run;
 }
 
-// One block per system: reverse CSR of its slots. Thread t owns targets
-// j = a0 + t, a0 + t + blockDim, ...; each walks the system's slots in
-// ascending order, so every segment is sorted. Slots past an atom's count
-// hold -1 (select_kernel), so the walk covers all n*k slots without reading
-// the counts. With `staged`, the system's slots are first copied to shared
-// memory (after the n per-target words) and the walks read them there.
-__global__ void reverse_kernel(const int32_t* __restrict__ sys_ptr, const int32_t* __restrict__ sys_offset,
-                               const int32_t* __restrict__ nbr, int k, int n_atoms, int staged_stride,
-                               int32_t* __restrict__ rev_ptr, int32_t* __restrict__ rev_idx) {
-  const int b = blockIdx.x;
-  const int a0 = sys_ptr[b], a1 = sys_ptr[b + 1];
-  extern __shared__ int32_t scan[];  // per-target counts, then offsets; then the staged slots
-  const int n = a1 - a0;
-  const int slots = n * k;
-  const int32_t* src = nbr + (int64_t)a0 * k;
-  if (staged_stride > 0) {
-    int32_t* staged = scan + staged_stride;
-    for (int e = threadIdx.x; e < slots; e += blockDim.x) staged[e] = src[e];
-    src = staged;
-    __syncthreads();
-  }
-  for (int t = threadIdx.x; t < n; t += blockDim.x) {
-    const int j = a0 + t;
-    int c = 0;
-#pragma unroll 4
-    for (int e = 0; e < slots; ++e) c += src[e] == j;
-    scan[t] = c;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int32_t run = sys_offset[b];
-    for (int t = 0; t < n; ++t) {
-      const int32_t c = scan[t];
-      scan[t] = run;
-      run += c;
-    }
-  }
-  __syncthreads();
-  for (int t = threadIdx.x; t < n; t += blockDim.x) {
-    const int j = a0 + t;
-    int32_t w = scan[t];
-    rev_ptr[j] = w;
-    for (int e = 0; e < slots; ++e)
-      if (src[e] == j) rev_idx[w++] = (int32_t)((int64_t)a0 * k + e);
-  }
-  if (b == gridDim.x - 1 && threadIdx.x == 0) rev_ptr[n_atoms] = sys_offset[gridDim.x];
-}
-
 // Systems of at most kSmallSystem atoms: the same reverse CSR by a stable
 // counting sort in O(slots) per system (the kernel above walks all slots
 // once per target). Integer shared atomics count slots per target; an
@@ -223,7 +189,6 @@ __global__ void reverse_kernel(const int32_t* __restrict__ sys_ptr, const int32_
 // plus the counts of that target in the chunk's earlier warps. Placement
 // depends only on slot order: identical output on every run, equal to the
 // kernel above.
-constexpr int kSmallSystem = 256;
 constexpr int kReverseThreads = 128;
 
 __global__ void __launch_bounds__(kReverseThreads) reverse_small_kernel(
@@ -276,6 +241,69 @@ __global__ void __launch_bounds__(kReverseThreads) reverse_small_kernel(
   if (b == gridDim.x - 1 && tid == 0) rev_ptr[n_atoms] = sys_offset[gridDim.x];
 }
 
+// Any system size, over the whole batch: slots per target counted with
+// integer atomics into rev_ptr, an inclusive scan, each slot placed at
+// atomicSub(end of its target) - 1 (which leaves rev_ptr[j] at the target's
+// start), then every segment sorted by slot index, which fixes the order.
+__global__ void count_targets_kernel(const int32_t* __restrict__ nbr, int64_t slots, int32_t* __restrict__ cnt) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < slots; e += (int64_t)gridDim.x * blockDim.x) {
+    const int32_t j = nbr[e];
+    if (j >= 0) atomicAdd(&cnt[j], 1);
+  }
+}
+
+// In place inclusive scan of x[0, n) by one block of kScanThreads threads
+// (a contiguous chunk each, then a scan of the chunk totals); x[n] = total.
+constexpr int kScanThreads = 1024;
+__global__ void __launch_bounds__(kScanThreads) scan_inclusive_kernel(int32_t* __restrict__ x, int64_t n) {
+  __shared__ int32_t part[kScanThreads];
+  const int t = threadIdx.x;
+  const int64_t per = (n + kScanThreads - 1) / kScanThreads;
+  const int64_t b0 = t * per, b1 = b0 + per < n ? b0 + per : n;
+  int32_t sum = 0;
+  for (int64_t e = b0; e < b1; ++e) sum += x[e];
+  part[t] = sum;
+  __syncthreads();
+  for (int off = 1; off < kScanThreads; off <<= 1) {  // Hillis-Steele over the chunk totals
+    const int32_t v = t >= off ? part[t - off] : 0;
+    __syncthreads();
+    part[t] += v;
+    __syncthreads();
+  }
+  int32_t run = t > 0 ? part[t - 1] : 0;
+  for (int64_t e = b0; e < b1; ++e) {
+    run += x[e];
+    x[e] = run;
+  }
+  if (t == kScanThreads - 1) x[n] = part[t];
+}
+
+__global__ void scatter_slots_kernel(const int32_t* __restrict__ nbr, int64_t slots, int32_t* __restrict__ end,
+                                     int32_t* __restrict__ rev_idx) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < slots; e += (int64_t)gridDim.x * blockDim.x) {
+    const int32_t j = nbr[e];
+    if (j >= 0) rev_idx[atomicSub(&end[j], 1) - 1] = (int32_t)e;
+  }
+}
+
+// Insertion sort of each target's segment (its in-degree entries, about k).
+__global__ void sort_segments_kernel(const int32_t* __restrict__ rev_ptr, int64_t n_atoms,
+                                     int32_t* __restrict__ rev_idx) {
+  for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < n_atoms;
+       j += (int64_t)gridDim.x * blockDim.x) {
+    const int32_t s0 = rev_ptr[j], s1 = rev_ptr[j + 1];
+    for (int32_t a = s0 + 1; a < s1; ++a) {
+      const int32_t v = rev_idx[a];
+      int32_t b = a;
+      while (b > s0 && rev_idx[b - 1] > v) {
+        rev_idx[b] = rev_idx[b - 1];
+        --b;
+      }
+      rev_idx[b] = v;
+    }
+  }
+}
+
 }  // namespace nbl
 }  // namespace cg
 
@@ -291,7 +319,8 @@ int cg_neighbor_list(const float* pos, const int32_t* sys_ptr, int64_t n_systems
   CG_REQUIRE(k >= 1 && k <= nbl::KMAX, "neighbor_list: k = %d outside [1, %d]", k, nbl::KMAX);
   CG_REQUIRE(cutoff > 0.0f, "neighbor_list: cutoff must be positive");
   CG_REQUIRE(max_atoms_per_system >= 0 && max_atoms_per_system <= 12000,
-             "neighbor_list: systems of up to 12000 atoms (shared-memory scan)");
+             "neighbor_list: systems of up to 12000 atoms (O(n^2) distances per system)");
+  CG_REQUIRE(n_atoms * (int64_t)k < (1ll << 31), "neighbor_list: n_atoms * k must stay below 2^31 slots");
   if (n_systems == 0) {
     if (n_atoms == 0) CG_CUDA(cudaMemsetAsync(rev_ptr, 0, sizeof(int32_t), as_stream(stream)));
     return kOk;
@@ -301,28 +330,35 @@ int cg_neighbor_list(const float* pos, const int32_t* sys_ptr, int64_t n_systems
   int32_t* sys_offset = workspace + n_systems;
   const float cutoff2 = cutoff * cutoff;
   cudaStream_t s = as_stream(stream);
-  if (max_atoms_per_system <= nbl::kSmallSystemSel && k <= 256)
+  if (max_atoms_per_system <= nbl::kSmallSystem) {
     nbl::select_small_kernel<<<(unsigned)n_systems, 32 * nbl::kSelectWarps, 0, s>>>(pos, sys_ptr, k, cutoff2, nbr,
                                                                                    counts, sys_edges);
-  else
-    nbl::select_kernel<<<(unsigned)n_systems, 128, 0, s>>>(pos, sys_ptr, k, cutoff2, nbr, counts, sys_edges);
-  CG_LAUNCHED("neighbor_list select");
-  nbl::scan_systems_kernel<<<1, 32, 0, s>>>(sys_edges, (int)n_systems, sys_offset);
-  CG_LAUNCHED("neighbor_list scan");
-  if (max_atoms_per_system <= nbl::kSmallSystem) {
+    CG_LAUNCHED("neighbor_list select");
+    nbl::scan_systems_kernel<<<1, 32, 0, s>>>(sys_edges, (int)n_systems, sys_offset);
+    CG_LAUNCHED("neighbor_list scan");
     nbl::reverse_small_kernel<<<(unsigned)n_systems, nbl::kReverseThreads, 0, s>>>(sys_ptr, sys_offset, nbr, k,
                                                                                   (int)n_atoms, rev_ptr, rev_idx);
     CG_LAUNCHED("neighbor_list reverse");
     return kOk;
   }
-  // the per-target words, then (when they fit) the largest system's slots
-  const int64_t words = max_atoms_per_system > 0 ? max_atoms_per_system : 1;
-  const int64_t stride = (words + 3) / 4 * 4;
-  const bool staged = (stride + words * k) * (int64_t)sizeof(int32_t) <= nbl::kReverseSmemMax;
-  const size_t smem = (size_t)(staged ? stride + words * k : words) * sizeof(int32_t);
-  CG_CUDA(cudaFuncSetAttribute(nbl::reverse_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  nbl::reverse_kernel<<<(unsigned)n_systems, 128, smem, s>>>(sys_ptr, sys_offset, nbr, k, (int)n_atoms,
-                                                             staged ? (int)stride : 0, rev_ptr, rev_idx);
+  const int64_t slots = n_atoms * k;
+  const unsigned sel_blocks = (unsigned)((n_atoms + nbl::kSelectWarps - 1) / nbl::kSelectWarps);
+  nbl::select_chunked_kernel<<<sel_blocks, 32 * nbl::kSelectWarps, 0, s>>>(pos, sys_ptr, (int)n_systems, n_atoms,
+                                                                          k, cutoff2, nbr, counts);
+  CG_LAUNCHED("neighbor_list select");
+  CG_CUDA(cudaMemsetAsync(rev_ptr, 0, (n_atoms + 1) * sizeof(int32_t), s));
+  const int64_t grid_cap = (int64_t)sm_count() * 8;
+  const int64_t slot_blocks = (slots + 255) / 256 < grid_cap ? (slots + 255) / 256 : grid_cap;
+  nbl::count_targets_kernel<<<(unsigned)(slot_blocks > 0 ? slot_blocks : 1), 256, 0, s>>>(nbr, slots, rev_ptr);
+  CG_LAUNCHED("neighbor_list count");
+  nbl::scan_inclusive_kernel<<<1, nbl::kScanThreads, 0, s>>>(rev_ptr, n_atoms);
+  CG_LAUNCHED("neighbor_list scan");
+  nbl::scatter_slots_kernel<<<(unsigned)(slot_blocks > 0 ? slot_blocks : 1), 256, 0, s>>>(nbr, slots, rev_ptr,
+                                                                                         rev_idx);
+  CG_LAUNCHED("neighbor_list scatter");
+  const int64_t atom_blocks = (n_atoms + 255) / 256 < grid_cap ? (n_atoms + 255) / 256 : grid_cap;
+  nbl::sort_segments_kernel<<<(unsigned)(atom_blocks > 0 ? atom_blocks : 1), 256, 0, s>>>(rev_ptr, n_atoms,
+                                                                                         rev_idx);
   CG_LAUNCHED("neighbor_list reverse");
   return kOk;
 }
