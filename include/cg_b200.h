@@ -378,8 +378,10 @@ int cg_edge_geom_bwd2(const cg_geom_args* a, const float* g_rbf, const float* g_
  * that order; nbr (n_atoms, k) padded with -1, counts (n_atoms). rev_ptr
  * (n_atoms + 1) / rev_idx (sum of counts) is the reverse CSR, slots grouped by
  * neighbour in ascending slot order. workspace: cg_neighbor_list_workspace()
- * int32s. Bit-exact and deterministic. The reference leaves neighbour lists
- * to model code before its region (README.md:28 there).
+ * int32s. Bit-exact and deterministic. Limits: k <= 64, systems of up to
+ * 12000 atoms (max_atoms_per_system must bound every system), n_atoms * k
+ * below 2^31; the distance work is O(n^2) per system. The reference leaves
+ * neighbour lists to model code before its region (README.md:28 there).
  * ---------------------------------------------------------------------- */
 int cg_neighbor_list_workspace(int64_t n_systems);
 int cg_neighbor_list(const float* pos, const int32_t* sys_ptr, int64_t n_systems, int64_t n_atoms,
