@@ -67,6 +67,11 @@ void colsum_plan(int64_t rows, int64_t cols, int64_t* chunks, int64_t* rows_per)
 // matrices into partial[chunk, c]; false (nothing launched) when not 16-byte aligned
 bool colsum4_launch(const float* a, const float* b, int64_t rows, int64_t cols, int64_t chunks, int64_t rows_per,
                     float* partial, cudaStream_t s);
+// CSR of element -> row index[e] (rows outside [0, rows) skipped): row_ptr
+// (rows + 1) and perm (n: each row's elements ascending, then -1), any size,
+// deterministic (segment.cu).
+int csr_build_launch(const int32_t* index, int64_t n, int64_t rows, int32_t* row_ptr, int32_t* perm,
+                     cudaStream_t s);
 }  // namespace seg
 
 }  // namespace cg

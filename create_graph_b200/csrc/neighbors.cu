@@ -241,69 +241,6 @@ __global__ void __launch_bounds__(kReverseThreads) reverse_small_kernel(
   if (b == gridDim.x - 1 && tid == 0) rev_ptr[n_atoms] = sys_offset[gridDim.x];
 }
 
-// Any system size, over the whole batch: slots per target counted with
-// integer atomics into rev_ptr, an inclusive scan, each slot placed at
-// atomicSub(end of its target) - 1 (which leaves rev_ptr[j] at the target's
-// start), then every segment sorted by slot index, which fixes the order.
-__global__ void count_targets_kernel(const int32_t* __restrict__ nbr, int64_t slots, int32_t* __restrict__ cnt) {
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < slots; e += (int64_t)gridDim.x * blockDim.x) {
-    const int32_t j = nbr[e];
-    if (j >= 0) atomicAdd(&cnt[j], 1);
-  }
-}
-
-// In place inclusive scan of x[0, n) by one block of kScanThreads threads
-// (a contiguous chunk each, then a scan of the chunk totals); x[n] = total.
-constexpr int kScanThreads = 1024;
-__global__ void __launch_bounds__(kScanThreads) scan_inclusive_kernel(int32_t* __restrict__ x, int64_t n) {
-  __shared__ int32_t part[kScanThreads];
-  const int t = threadIdx.x;
-  const int64_t per = (n + kScanThreads - 1) / kScanThreads;
-  const int64_t b0 = t * per, b1 = b0 + per < n ? b0 + per : n;
-  int32_t sum = 0;
-  for (int64_t e = b0; e < b1; ++e) sum += x[e];
-  part[t] = sum;
-  __syncthreads();
-  for (int off = 1; off < kScanThreads; off <<= 1) {  // Hillis-Steele over the chunk totals
-    const int32_t v = t >= off ? part[t - off] : 0;
-    __syncthreads();
-    part[t] += v;
-    __syncthreads();
-  }
-  int32_t run = t > 0 ? part[t - 1] : 0;
-  for (int64_t e = b0; e < b1; ++e) {
-    run += x[e];
-    x[e] = run;
-  }
-  if (t == kScanThreads - 1) x[n] = part[t];
-}
-
-__global__ void scatter_slots_kernel(const int32_t* __restrict__ nbr, int64_t slots, int32_t* __restrict__ end,
-                                     int32_t* __restrict__ rev_idx) {
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < slots; e += (int64_t)gridDim.x * blockDim.x) {
-    const int32_t j = nbr[e];
-    if (j >= 0) rev_idx[atomicSub(&end[j], 1) - 1] = (int32_t)e;
-  }
-}
-
-// Insertion sort of each target's segment (its in-degree entries, about k).
-__global__ void sort_segments_kernel(const int32_t* __restrict__ rev_ptr, int64_t n_atoms,
-                                     int32_t* __restrict__ rev_idx) {
-  for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < n_atoms;
-       j += (int64_t)gridDim.x * blockDim.x) {
-    const int32_t s0 = rev_ptr[j], s1 = rev_ptr[j + 1];
-    for (int32_t a = s0 + 1; a < s1; ++a) {
-      const int32_t v = rev_idx[a];
-      int32_t b = a;
-      while (b > s0 && rev_idx[b - 1] > v) {
-        rev_idx[b] = rev_idx[b - 1];
-        --b;
-      }
-      rev_idx[b] = v;
-    }
-  }
-}
-
 }  // namespace nbl
 }  // namespace cg
 
@@ -346,19 +283,9 @@ int cg_neighbor_list(const float* pos, const int32_t* sys_ptr, int64_t n_systems
   nbl::select_chunked_kernel<<<sel_blocks, 32 * nbl::kSelectWarps, 0, s>>>(pos, sys_ptr, (int)n_systems, n_atoms,
                                                                           k, cutoff2, nbr, counts);
   CG_LAUNCHED("neighbor_list select");
-  CG_CUDA(cudaMemsetAsync(rev_ptr, 0, (n_atoms + 1) * sizeof(int32_t), s));
-  const int64_t grid_cap = (int64_t)sm_count() * 8;
-  const int64_t slot_blocks = (slots + 255) / 256 < grid_cap ? (slots + 255) / 256 : grid_cap;
-  nbl::count_targets_kernel<<<(unsigned)(slot_blocks > 0 ? slot_blocks : 1), 256, 0, s>>>(nbr, slots, rev_ptr);
-  CG_LAUNCHED("neighbor_list count");
-  nbl::scan_inclusive_kernel<<<1, nbl::kScanThreads, 0, s>>>(rev_ptr, n_atoms);
-  CG_LAUNCHED("neighbor_list scan");
-  nbl::scatter_slots_kernel<<<(unsigned)(slot_blocks > 0 ? slot_blocks : 1), 256, 0, s>>>(nbr, slots, rev_ptr,
-                                                                                         rev_idx);
-  CG_LAUNCHED("neighbor_list scatter");
-  const int64_t atom_blocks = (n_atoms + 255) / 256 < grid_cap ? (n_atoms + 255) / 256 : grid_cap;
-  nbl::sort_segments_kernel<<<(unsigned)(atom_blocks > 0 ? atom_blocks : 1), 256, 0, s>>>(rev_ptr, n_atoms,
-                                                                                         rev_idx);
+  // the reverse CSR over the whole batch: row j = the slots whose neighbour is j
+  const int rc = seg::csr_build_launch(nbr, slots, n_atoms, rev_ptr, rev_idx, s);
+  if (rc != kOk) return rc;
   CG_LAUNCHED("neighbor_list reverse");
   return kOk;
 }

@@ -175,7 +175,6 @@ __global__ void segment_sum_scaled_kernel(const float* __restrict__ w, const flo
 // [chunk*rows_per, (chunk+1)*rows_per) of 32 columns into partial[chunk, :];
 // then one thread per column adds the partials in chunk order.
 constexpr int kColTile = 32;
-constexpr int kRowsPerThread = 8;
 
 __global__ void colsum_partial_kernel(const float* __restrict__ src, int64_t ld, int64_t rows,
                                       int64_t cols, int64_t rows_per, float* __restrict__ partial) {
@@ -394,6 +393,91 @@ __global__ void __launch_bounds__(kCsrThreads) csr_small_kernel(const int32_t* _
   for (int64_t e = (int64_t)row_ptr[rows] + tid; e < n; e += kCsrThreads) perm[e] = -1;
 }
 
+// CSR of any many-to-one map over the whole input: element e goes to row
+// index[e] (outside [0, rows): nowhere). Counts per row with integer
+// atomics into row_ptr, an inclusive scan, each element placed at
+// atomicSub(end of its row) - 1 (which leaves row_ptr[r] at the row's start),
+// then every row sorted by element index, which fixes the order: perm lists
+// each row's elements in ascending order on every run.
+__global__ void count_rows_kernel(const int32_t* __restrict__ index, int64_t n, int64_t rows,
+                                  int32_t* __restrict__ cnt) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+    const int32_t r = index[e];
+    if (r >= 0 && r < rows) atomicAdd(&cnt[r], 1);
+  }
+}
+
+// In place inclusive scan of x[0, n) by one block of kScanThreads threads
+// (a contiguous chunk each, then a scan of the chunk totals); x[n] = total.
+constexpr int kScanThreads = 1024;
+__global__ void __launch_bounds__(kScanThreads) scan_inclusive_kernel(int32_t* __restrict__ x, int64_t n) {
+  __shared__ int32_t part[kScanThreads];
+  const int t = threadIdx.x;
+  const int64_t per = (n + kScanThreads - 1) / kScanThreads;
+  const int64_t b0 = t * per < n ? t * per : n, b1 = b0 + per < n ? b0 + per : n;
+  int32_t sum = 0;
+  for (int64_t e = b0; e < b1; ++e) sum += x[e];
+  part[t] = sum;
+  __syncthreads();
+  for (int off = 1; off < kScanThreads; off <<= 1) {  // Hillis-Steele over the chunk totals
+    const int32_t v = t >= off ? part[t - off] : 0;
+    __syncthreads();
+    part[t] += v;
+    __syncthreads();
+  }
+  int32_t run = t > 0 ? part[t - 1] : 0;
+  for (int64_t e = b0; e < b1; ++e) {
+    run += x[e];
+    x[e] = run;
+  }
+  if (t == kScanThreads - 1) x[n] = part[t];
+}
+
+__global__ void place_rows_kernel(const int32_t* __restrict__ index, int64_t n, int64_t rows,
+                                  int32_t* __restrict__ end, int32_t* __restrict__ perm) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+    const int32_t r = index[e];
+    if (r >= 0 && r < rows) perm[atomicSub(&end[r], 1) - 1] = (int32_t)e;
+  }
+}
+
+// Insertion sort of each row's segment of perm.
+__global__ void sort_rows_kernel(const int32_t* __restrict__ row_ptr, int64_t rows, int32_t* __restrict__ perm) {
+  for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < rows; j += (int64_t)gridDim.x * blockDim.x) {
+    const int32_t s0 = row_ptr[j], s1 = row_ptr[j + 1];
+    for (int32_t a = s0 + 1; a < s1; ++a) {
+      const int32_t v = perm[a];
+      int32_t b = a;
+      while (b > s0 && perm[b - 1] > v) {
+        perm[b] = perm[b - 1];
+        --b;
+      }
+      perm[b] = v;
+    }
+  }
+}
+
+int csr_build_launch(const int32_t* index, int64_t n, int64_t rows, int32_t* row_ptr, int32_t* perm,
+                     cudaStream_t s) {
+  CG_CUDA(cudaMemsetAsync(row_ptr, 0, (rows + 1) * sizeof(int32_t), s));
+  if (n == 0) return kOk;
+  CG_CUDA(cudaMemsetAsync(perm, 0xff, n * sizeof(int32_t), s));  // -1 past the mapped elements
+  const int64_t cap = (int64_t)sm_count() * 8;
+  auto grid = [&](int64_t items) {
+    const int64_t b = (items + 255) / 256;
+    return (unsigned)(b < 1 ? 1 : (b < cap ? b : cap));
+  };
+  count_rows_kernel<<<grid(n), 256, 0, s>>>(index, n, rows, row_ptr);
+  CG_LAUNCHED("csr count");
+  scan_inclusive_kernel<<<1, kScanThreads, 0, s>>>(row_ptr, rows);
+  CG_LAUNCHED("csr scan");
+  place_rows_kernel<<<grid(n), 256, 0, s>>>(index, n, rows, row_ptr, perm);
+  CG_LAUNCHED("csr place");
+  sort_rows_kernel<<<grid(rows), 256, 0, s>>>(row_ptr, rows, perm);
+  CG_LAUNCHED("csr sort");
+  return kOk;
+}
+
 }  // namespace seg
 }  // namespace cg
 
@@ -401,10 +485,10 @@ extern "C" {
 
 int cg_csr_from_index(const int32_t* index, int64_t n, int64_t rows, int32_t* row_ptr, int32_t* perm, void* stream) {
   CG_REQUIRE(n >= 0 && n < (1ll << 31), "csr_from_index: n = %lld outside [0, 2^31)", (long long)n);
-  CG_REQUIRE(rows >= 0 && rows <= cg::seg::kCsrMaxRows, "csr_from_index: rows = %lld outside [0, %d]",
-             (long long)rows, cg::seg::kCsrMaxRows);
+  CG_REQUIRE(rows >= 0 && rows < (1ll << 31), "csr_from_index: rows = %lld outside [0, 2^31)", (long long)rows);
   CG_REQUIRE(row_ptr != nullptr && (n == 0 || (index != nullptr && perm != nullptr)),
              "csr_from_index: null buffer");
+  if (rows > cg::seg::kCsrMaxRows) return cg::seg::csr_build_launch(index, n, rows, row_ptr, perm, cg::as_stream(stream));
   cg::seg::csr_small_kernel<<<1, cg::seg::kCsrThreads, 0, cg::as_stream(stream)>>>(index, n, (int)rows, row_ptr, perm);
   CG_LAUNCHED("csr_from_index");
   return cg::kOk;

@@ -523,11 +523,11 @@ class Csr:
 
     @staticmethod
     def from_index(index: Tensor, rows: int) -> Csr:
-        """Build on the index's device, deterministically. On a CUDA device with
-        rows <= 256 one kernel builds it without reading anything back to the
-        host (capturable in a CUDA graph); perm then has one slot per element,
-        -1 past the mapped ones. Otherwise a stable torch sort."""
-        if index.is_cuda and rows <= CSR_KERNEL_MAX_ROWS:
+        """Build on the index's device, deterministically. On a CUDA device the
+        kernels build it without reading anything back to the host (capturable
+        in a CUDA graph); perm then has one slot per element, -1 past the
+        mapped ones. A CPU index takes a stable torch sort."""
+        if index.is_cuda:
             index = index.to(torch.int32).contiguous()
             row_ptr = torch.empty(rows + 1, dtype=torch.int32, device=index.device)
             perm = torch.empty(max(index.numel(), 1), dtype=torch.int32, device=index.device)
@@ -542,9 +542,6 @@ class Csr:
         row_ptr[1:] = torch.cumsum(counts, 0)
         nnz = int(valid.sum())
         return Csr(index.to(torch.int32), row_ptr.to(torch.int32), order[:nnz].to(torch.int32).contiguous(), rows)
-
-
-CSR_KERNEL_MAX_ROWS = 256
 
 
 def gather_raw(src: Tensor, csr: Csr) -> Tensor:

@@ -253,11 +253,13 @@ int cg_gather_rows(const float* src, int64_t ld_src, const int32_t* index, int64
                    float* out, int64_t ld_out, void* stream);
 /* out[r, :] (+)= sum_{e in [row_ptr[r], row_ptr[r+1])} src[perm ? perm[e] : e, :],
  * in increasing e; replaces index_add (tests/test_semantics.py:68-69 there). */
-/* CSR of a small many-to-one map: element e goes to row index[e] (outside
+/* CSR of a many-to-one map: element e goes to row index[e] (outside
  * [0, rows): nowhere). row_ptr (rows + 1) and perm (n; each row's elements in
- * ascending order, then -1 for the unmapped ones) in one single-block kernel
- * without host synchronisation; rows <= 256. Builds the species map of a
- * batch (torch argsort + bincount there would read sizes back to the host). */
+ * ascending order, then -1 for the unmapped ones), without host
+ * synchronisation: one single-block kernel for rows <= 256, else a count /
+ * scan / place / sort-rows sequence (integer atomics, order fixed by the
+ * final sort: deterministic). Builds the species map of a batch (torch
+ * argsort + bincount there would read sizes back to the host). */
 int cg_csr_from_index(const int32_t* index, int64_t n, int64_t rows, int32_t* row_ptr, int32_t* perm, void* stream);
 int cg_segment_sum(const float* src, int64_t ld_src, const int32_t* row_ptr, const int32_t* perm,
                    int64_t n_rows, int64_t cols, float* out, int64_t ld_out, int accumulate,

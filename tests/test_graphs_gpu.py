@@ -27,8 +27,10 @@ from create_graph_b200.optim import FusedAdamW
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("n, rows", [(1, 1), (777, 10), (8280, 50), (5000, 256), (3000, 3)])
+@pytest.mark.parametrize("n, rows", [(1, 1), (777, 10), (8280, 50), (5000, 256), (3000, 3), (20000, 257),
+                                     (248400, 8280), (100, 5000), (0, 300)])
 def test_csr_from_index_kernel_is_a_stable_sort(n, rows):
+    """rows <= 256: the single-block kernel; more: count / scan / place / sort-rows."""
     gen = torch.Generator().manual_seed(n + rows)
     index = torch.randint(-1, rows, (n,), generator=gen, dtype=torch.int32)
     got = Csr.from_index(index.cuda(), rows)
