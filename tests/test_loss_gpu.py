@@ -27,7 +27,7 @@ def test_fused_loss_matches_torch(n_sys, n_atoms):
     e64, g64 = e.double().requires_grad_(True), g.double().requires_grad_(True)
     want = (e64 - et.double()).square().mean() + (-g64 - ft.double()).square().mean()
     (0.5 * want).backward()
-    assert abs(float(loss) - float(want)) <= 2e-6 * abs(float(want))
+    assert abs(loss.item() - want.item()) <= 2e-6 * abs(want.item())
     assert torch.allclose(e_d.grad.cpu().double(), e64.grad, rtol=1e-5, atol=1e-7)
     assert torch.allclose(g_d.grad.cpu().double(), g64.grad, rtol=1e-5, atol=1e-9)
     again = energy_force_loss(e_d.detach(), g_d.detach(), et.cuda(), ft.cuda())
