@@ -40,7 +40,6 @@ from create_graph_b200.edge_attn import (
     pooled_attention_backward1,
     pooled_attention_backward2,
     pooled_attention_forward,
-    pooled_attention_out,
     token_attention_backward1,
     token_attention_backward2,
     token_attention_forward1,
@@ -828,19 +827,20 @@ class PooledTokenAttention(_Fused):
         meta = (graph, heads, scale, precision)
         args = (graph.tokens.index, graph.counts, graph.k, heads)
         # inside a checkpointed block call, a recompute on the same inputs
-        # reuses the first forward's softmax statistics (lse, w) and only
-        # forms out = sum_j w_j v_j, bit for bit the same; a memory budget of
-        # 0.25 or less keeps nothing across recomputes
+        # reuses the first forward's softmax statistics (lse, w) and its
+        # output (copied: each recompute's node owns its output), bit for bit
+        # the same; a memory budget of 0.25 or less keeps nothing across
+        # recomputes
         cache = active_recompute_cache() if active_memory_budget() > 0.25 else None
         slot = cache.slot() if cache is not None else None
         kept = cache.slots.get(slot) if cache is not None else None
         if kept is not None and kept[1].shape == (graph.n_atoms, heads, graph.k):
-            lse, w = kept
-            out = pooled_attention_out(qkv, w, *args)
+            lse, w, first = kept
+            out = first.clone()
         else:
             out, lse, w = pooled_attention_forward(qkv, bias, env, *args[:3], heads, scale, precision)
             if cache is not None:
-                cache.slots[slot] = (lse, w)
+                cache.slots[slot] = (lse, w, out.detach())
         ctx.save_for_backward(qkv, bias, env, lse, w)
         ctx.meta = meta
         ctx.cache, ctx.slot = cache, slot
