@@ -247,6 +247,24 @@ class LinearFn(_Fused):
         return _linear_backward(ctx, g, x, w, ctx.has_bias)
 
 
+def _kept_across_recomputes(compute):
+    """The op's output from ``compute()``; inside a checkpointed block call
+    whose memory budget is above 0.25, a recompute on the same inputs takes a
+    copy of what the call's first forward computed instead (bit for bit the
+    same; each recompute's node owns its output). For ops whose backward reads
+    only their inputs, so the kept output is all a recompute needs."""
+    cache = active_recompute_cache() if active_memory_budget() > 0.25 else None
+    if cache is None:
+        return compute()
+    slot = cache.slot()
+    kept = cache.slots.get(slot)
+    if kept is not None:
+        return kept.clone()
+    out = compute()
+    cache.slots[slot] = out.detach()
+    return out
+
+
 class LinearResidualFn(_Fused):
     """y = r + x @ w.T + b: the residual add in the GEMM epilogue (reads r once,
     no separate (rows, out) add); r's gradient is g itself."""
@@ -257,7 +275,7 @@ class LinearResidualFn(_Fused):
         ctx.save_for_backward(x, w)
         ctx.edges = _edges(x, w, b, r)
         ctx.has_bias = b is not None
-        return mm_raw(x, w, bias=b, act=ACT_ADD, aux_in=_f32(r, "linear_residual"))
+        return _kept_across_recomputes(lambda: mm_raw(x, w, bias=b, act=ACT_ADD, aux_in=_f32(r, "linear_residual")))
 
     @staticmethod
     @_at_forward_precision
@@ -392,7 +410,8 @@ class SiluLinearResidualFn(_Fused):
         ctx.save_for_backward(y if budget > 0.5 else None, z, w)
         ctx.edges = _edges(y, z, w, b, r)
         ctx.has_bias = b is not None
-        return mm_raw(y, w, bias=b, act=ACT_ADD, aux_in=_f32(r, "silu_linear_residual"))
+        return _kept_across_recomputes(
+            lambda: mm_raw(y, w, bias=b, act=ACT_ADD, aux_in=_f32(r, "silu_linear_residual")))
 
     @staticmethod
     @_at_forward_precision
