@@ -16,8 +16,9 @@ over ``named_modules()``) becomes one ``BlockFn`` node of the autograd graph:
 So a block's forward runs four times and its VJP twice, and at most one
 block's activations are alive at a time. Each call keeps a RecomputeCache:
 the pooled attention keeps its softmax statistics and its output (n x C)
-from the first forward, so the three recomputes copy them instead of
-running the attention again, and the costliest step of the VJP (the pooled
+from the first forward, and the linear layers whose backward reads only
+their inputs their outputs, so the three recomputes copy them instead of
+running those kernels again, and the costliest step of the VJP (the pooled
 attention's backward1) keeps its outputs from the force pass for the VJP's
 rebuild in the parameter backward, which takes them instead of recomputing;
 the memory budget decides whether they may (create_graph_b200.nn). The block's fused ops are

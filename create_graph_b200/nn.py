@@ -238,7 +238,9 @@ class LinearFn(_Fused):
         ctx.save_for_backward(x, w)
         ctx.edges = _edges(x, w, b)
         ctx.has_bias = b is not None
-        return mm_raw(x, w, bias=b)
+        # inside checkpointed blocks at a budget of 0.5 or more, the recomputes
+        # take the first forward's projection (the q/k/v rows: 3C floats per atom)
+        return _kept_across_recomputes(lambda: mm_raw(x, w, bias=b), min_budget=0.5)
 
     @staticmethod
     @_at_forward_precision
@@ -247,13 +249,17 @@ class LinearFn(_Fused):
         return _linear_backward(ctx, g, x, w, ctx.has_bias)
 
 
-def _kept_across_recomputes(compute):
+def _kept_across_recomputes(compute, min_budget: float | None = None):
     """The op's output from ``compute()``; inside a checkpointed block call
-    whose memory budget is above 0.25, a recompute on the same inputs takes a
-    copy of what the call's first forward computed instead (bit for bit the
-    same; each recompute's node owns its output). For ops whose backward reads
-    only their inputs, so the kept output is all a recompute needs."""
-    cache = active_recompute_cache() if active_memory_budget() > 0.25 else None
+    whose memory budget is above 0.25 (and at least ``min_budget`` when given,
+    for outputs that cost more memory per microsecond saved), a recompute on
+    the same inputs takes a copy of what the call's first forward computed
+    instead (bit for bit the same; each recompute's node owns its output). For
+    ops whose backward reads only their inputs, so the kept output is all a
+    recompute needs."""
+    budget = active_memory_budget()
+    keep = budget > 0.25 and (min_budget is None or budget >= min_budget)
+    cache = active_recompute_cache() if keep else None
     if cache is None:
         return compute()
     slot = cache.slot()
