@@ -17,7 +17,7 @@ So a block's forward runs four times and its VJP twice, and at most one
 block's activations are alive at a time. Each call keeps a RecomputeCache:
 the pooled attention keeps its softmax statistics and its output (n x C)
 from the first forward, and the linear layers whose backward reads only
-their inputs their outputs, so the three recomputes copy them instead of
+their inputs their outputs, so the three recomputes take them instead of
 running those kernels again, and the costliest step of the VJP (the pooled
 attention's backward1) keeps its outputs from the force pass for the VJP's
 rebuild in the parameter backward, which takes them instead of recomputing;

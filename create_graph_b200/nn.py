@@ -253,10 +253,11 @@ def _kept_across_recomputes(compute, min_budget: float | None = None):
     """The op's output from ``compute()``; inside a checkpointed block call
     whose memory budget is above 0.25 (and at least ``min_budget`` when given,
     for outputs that cost more memory per microsecond saved), a recompute on
-    the same inputs takes a copy of what the call's first forward computed
-    instead (bit for bit the same; each recompute's node owns its output). For
-    ops whose backward reads only their inputs, so the kept output is all a
-    recompute needs."""
+    the same inputs takes what the call's first forward computed instead (bit
+    for bit the same), as an alias of its storage: each recompute's node gets
+    its own tensor, and nothing writes these outputs in place. For ops whose
+    backward reads only their inputs, so the kept output is all a recompute
+    needs."""
     budget = active_memory_budget()
     keep = budget > 0.25 and (min_budget is None or budget >= min_budget)
     cache = active_recompute_cache() if keep else None
@@ -265,7 +266,7 @@ def _kept_across_recomputes(compute, min_budget: float | None = None):
     slot = cache.slot()
     kept = cache.slots.get(slot)
     if kept is not None:
-        return kept.clone()
+        return kept.detach()
     out = compute()
     cache.slots[slot] = out.detach()
     return out
@@ -853,15 +854,15 @@ class PooledTokenAttention(_Fused):
         args = (graph.tokens.index, graph.counts, graph.k, heads)
         # inside a checkpointed block call, a recompute on the same inputs
         # reuses the first forward's softmax statistics (lse, w) and its
-        # output (copied: each recompute's node owns its output), bit for bit
-        # the same; a memory budget of 0.25 or less keeps nothing across
-        # recomputes
+        # output (an alias of its storage, a tensor of this node's own), bit
+        # for bit the same; a memory budget of 0.25 or less keeps nothing
+        # across recomputes
         cache = active_recompute_cache() if active_memory_budget() > 0.25 else None
         slot = cache.slot() if cache is not None else None
         kept = cache.slots.get(slot) if cache is not None else None
         if kept is not None and kept[1].shape == (graph.n_atoms, heads, graph.k):
             lse, w, first = kept
-            out = first.clone()
+            out = first.detach()
         else:
             out, lse, w = pooled_attention_forward(qkv, bias, env, *args[:3], heads, scale, precision)
             if cache is not None:
