@@ -18,8 +18,8 @@ block's activations are alive at a time. Each call keeps a RecomputeCache:
 the pooled attention keeps its softmax statistics and its output (n x C)
 from the first forward, and the linear layers whose backward reads only
 their inputs their outputs, so the three recomputes take them instead of
-running those kernels again, and the costliest step of the VJP (the pooled
-attention's backward1) keeps its outputs from the force pass for the VJP's
+running those kernels again, and the VJP's pooled-attention backward1 and
+input-gradient GEMMs keep their outputs from the force pass for the VJP's
 rebuild in the parameter backward, which takes them instead of recomputing;
 the memory budget decides whether they may (create_graph_b200.nn). The block's fused ops are
 the same sm_100a kernels as elsewhere; the recompute runs under the region's

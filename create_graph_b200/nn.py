@@ -119,11 +119,12 @@ class MM(_Fused):
     """C = a @ b.T (a (M, K), b (N, K)); backward: g @ b and g.T @ a."""
 
     @staticmethod
-    def forward(ctx, a, b):
+    def forward(ctx, a, b, reuse=None):
+        """reuse: (cache, key) inside a checkpointed block's VJP (_vjp_reuse)."""
         _keep_precision(ctx)
         ctx.save_for_backward(a, b)
         ctx.edges = _edges(a, b)
-        return mm_raw(a, b)
+        return _reused_in_rebuild(reuse, lambda: mm_raw(a, b))
 
     @staticmethod
     @_at_forward_precision
@@ -131,11 +132,45 @@ class MM(_Fused):
         a, b = ctx.saved_tensors
         ga = MM.apply(g, b.t()) if _wanted(ctx, 0) else None
         gb = MM.apply(g.t(), a.t()) if _wanted(ctx, 1) else None
-        return ga, gb
+        return ga, gb, None
 
 
 def mm(a: Tensor, b: Tensor) -> Tensor:
     return MM.apply(a, b)
+
+
+def _block_slot():
+    """(cache, slot) of the checkpointed block call whose forward is running
+    (memory budget above 0.25), else (None, None). Ops take their slot in
+    call order, the same in the call's first forward and its recomputes."""
+    cache = active_recompute_cache() if active_memory_budget() > 0.25 else None
+    return (cache, cache.slot()) if cache is not None else (None, None)
+
+
+def _vjp_reuse(ctx, what: str):
+    """(cache, key) when an op's backward runs inside its block call's VJP:
+    the force pass, or the VJP's rebuild in the parameter backward, which sees
+    the same inputs and cotangents. The force pass leaves its result there and
+    the rebuild takes it (_reused_in_rebuild); None elsewhere."""
+    cache, slot = getattr(ctx, "block", (None, None))
+    if cache is None or not cache.in_vjp:
+        return None
+    return cache, (what, slot)
+
+
+def _reused_in_rebuild(reuse, compute):
+    """compute(), kept for the VJP's rebuild when ``reuse`` is set; in the
+    rebuild, the force pass's result (an alias of its storage, a tensor of
+    this node's own; bit for bit what compute() gives), which is then dropped."""
+    if reuse is None:
+        return compute()
+    cache, key = reuse
+    kept = cache.slots.pop(key, None)
+    if kept is not None:
+        return kept.detach()
+    out = compute()
+    cache.slots[key] = out.detach()
+    return out
 
 
 def colsum_raw(x: Tensor) -> Tensor:
@@ -223,7 +258,7 @@ class ScaleShift(_Fused):
 
 
 def _linear_backward(ctx, g, x, w, has_bias):
-    gx = MM.apply(g, w.t()) if _wanted(ctx, 0) else None
+    gx = MM.apply(g, w.t(), _vjp_reuse(ctx, "gx")) if _wanted(ctx, 0) else None
     gw = MM.apply(g.t(), x.t()) if _wanted(ctx, 1) else None
     gb = ColSum.apply(g) if has_bias and _wanted(ctx, 2) else None
     return gx, gw, gb
@@ -240,7 +275,8 @@ class LinearFn(_Fused):
         ctx.has_bias = b is not None
         # inside checkpointed blocks at a budget of 0.5 or more, the recomputes
         # take the first forward's projection (the q/k/v rows: 3C floats per atom)
-        return _kept_across_recomputes(lambda: mm_raw(x, w, bias=b), min_budget=0.5)
+        ctx.block = _block_slot()
+        return _kept_across_recomputes(lambda: mm_raw(x, w, bias=b), ctx.block, min_budget=0.5)
 
     @staticmethod
     @_at_forward_precision
@@ -249,21 +285,19 @@ class LinearFn(_Fused):
         return _linear_backward(ctx, g, x, w, ctx.has_bias)
 
 
-def _kept_across_recomputes(compute, min_budget: float | None = None):
+def _kept_across_recomputes(compute, where, min_budget: float | None = None):
     """The op's output from ``compute()``; inside a checkpointed block call
-    whose memory budget is above 0.25 (and at least ``min_budget`` when given,
+    (``where`` = _block_slot()) whose memory budget is above 0.25 (and at
+    least ``min_budget`` when given,
     for outputs that cost more memory per microsecond saved), a recompute on
     the same inputs takes what the call's first forward computed instead (bit
     for bit the same), as an alias of its storage: each recompute's node gets
     its own tensor, and nothing writes these outputs in place. For ops whose
     backward reads only their inputs, so the kept output is all a recompute
     needs."""
-    budget = active_memory_budget()
-    keep = budget > 0.25 and (min_budget is None or budget >= min_budget)
-    cache = active_recompute_cache() if keep else None
-    if cache is None:
+    cache, slot = where
+    if cache is None or (min_budget is not None and active_memory_budget() < min_budget):
         return compute()
-    slot = cache.slot()
     kept = cache.slots.get(slot)
     if kept is not None:
         return kept.detach()
@@ -282,7 +316,9 @@ class LinearResidualFn(_Fused):
         ctx.save_for_backward(x, w)
         ctx.edges = _edges(x, w, b, r)
         ctx.has_bias = b is not None
-        return _kept_across_recomputes(lambda: mm_raw(x, w, bias=b, act=ACT_ADD, aux_in=_f32(r, "linear_residual")))
+        ctx.block = _block_slot()
+        return _kept_across_recomputes(
+            lambda: mm_raw(x, w, bias=b, act=ACT_ADD, aux_in=_f32(r, "linear_residual")), ctx.block)
 
     @staticmethod
     @_at_forward_precision
@@ -343,6 +379,7 @@ class LinearSiluFn(_Fused):
         ctx.save_for_backward(x, w, z)
         ctx.edges = _edges(x, w, b)
         ctx.has_bias = b is not None
+        ctx.block = _block_slot()  # its backward's input gradient is kept for the VJP's rebuild
         # z is usually unused: its gradient arrives as None, not as a zero-filled
         # (rows, out) tensor added to the SiLU gradient
         ctx.set_materialize_grads(False)
@@ -367,13 +404,17 @@ class MMSiluGrad(_Fused):
     to silu(z), taken straight to z (the SiLU derivative in the GEMM epilogue)."""
 
     @staticmethod
-    def forward(ctx, g, w, z, keep_u=False):
+    def forward(ctx, g, w, z, keep_u=False, reuse=None):
+        """reuse: (cache, key) inside a checkpointed block's VJP (_vjp_reuse)."""
         _keep_precision(ctx)
         z = _f32(z, "mm_silu_grad")
         # u = g @ w, the second-order term's factor, comes out of the same
-        # epilogue when the caller builds a graph through this node (keep_u)
-        u = torch.empty_like(z) if keep_u else None
-        out = mm_raw(g, w.t(), act=ACT_SILU_GRAD, aux_in=z, aux_out=u)
+        # epilogue when the caller builds a graph through this node (keep_u);
+        # a result taken from the force pass comes without it (the backward
+        # then forms u with one GEMM)
+        kept = reuse is not None and reuse[1] in reuse[0].slots
+        u = torch.empty_like(z) if keep_u and not kept else None
+        out = _reused_in_rebuild(reuse, lambda: mm_raw(g, w.t(), act=ACT_SILU_GRAD, aux_in=z, aux_out=u))
         ctx.save_for_backward(g, w, z, u)
         ctx.edges = _edges(g, w, z)
         return out
@@ -393,7 +434,7 @@ class MMSiluGrad(_Fused):
             dz = torch.empty_like(h)
             native.call("cg_silu_grad2", h.data_ptr(), u.data_ptr(), z.data_ptr(), dz.data_ptr(), h.numel(),
                         _stream())
-        return dg, dw, dz, None
+        return dg, dw, dz, None, None
 
 
 class SiluLinearResidualFn(_Fused):
@@ -417,8 +458,9 @@ class SiluLinearResidualFn(_Fused):
         ctx.save_for_backward(y if budget > 0.5 else None, z, w)
         ctx.edges = _edges(y, z, w, b, r)
         ctx.has_bias = b is not None
+        ctx.block = _block_slot()
         return _kept_across_recomputes(
-            lambda: mm_raw(y, w, bias=b, act=ACT_ADD, aux_in=_f32(r, "silu_linear_residual")))
+            lambda: mm_raw(y, w, bias=b, act=ACT_ADD, aux_in=_f32(r, "silu_linear_residual")), ctx.block)
 
     @staticmethod
     @_at_forward_precision
@@ -427,7 +469,10 @@ class SiluLinearResidualFn(_Fused):
         # grad mode is on here exactly when this backward is being recorded
         # (create_graph), i.e. when MMSiluGrad's own backward will run
         keep_u = ctx.keep_u and torch.is_grad_enabled()
-        gz = MMSiluGrad.apply(g, w, z, keep_u) if _wanted(ctx, 1) else None
+        # below a memory budget of 1 (no u kept) the VJP's rebuild takes the
+        # force pass's gz; at 1 the rebuild runs the GEMM again for its u
+        reuse = None if ctx.keep_u else _vjp_reuse(ctx, "gz")
+        gz = MMSiluGrad.apply(g, w, z, keep_u, reuse) if _wanted(ctx, 1) else None
         gw = None
         if _wanted(ctx, 2):
             gw = MM.apply(g.t(), (y if y is not None else Silu.apply(z)).t())

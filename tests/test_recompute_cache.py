@@ -12,7 +12,7 @@ import torch
 import create_graph_b200 as cg
 from create_graph_b200 import checkpoint
 from create_graph_b200.compile_config import compile_context
-from create_graph_b200.nn import _kept_across_recomputes
+from create_graph_b200.nn import _block_slot, _kept_across_recomputes
 
 
 class Counter:
@@ -32,7 +32,7 @@ def _run_block(cache, counter, values):
     cache.start()
     checkpoint._CACHES.append(cache)
     try:
-        return [_kept_across_recomputes(counter(v)) for v in values]
+        return [_kept_across_recomputes(counter(v), _block_slot()) for v in values]
     finally:
         checkpoint._CACHES.pop()
 
@@ -62,6 +62,6 @@ def test_budget_of_a_quarter_or_less_keeps_nothing():
 def test_outside_a_block_call_every_call_computes():
     counter = Counter()
     with compile_context(cg.CompileConfig(memory_budget=1.0)):
-        a = _kept_across_recomputes(counter(1))
-        b = _kept_across_recomputes(counter(2))
+        a = _kept_across_recomputes(counter(1), _block_slot())
+        b = _kept_across_recomputes(counter(2), _block_slot())
     assert counter.calls == 2 and float(a[0]) == 1.0 and float(b[0]) == 2.0

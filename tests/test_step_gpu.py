@@ -166,12 +166,18 @@ def _budget_run(spec, sizes, budget, checkpoint):
 def test_memory_budget_lowers_peak_memory(checkpoint):
     """Below 1 the force pass keeps no second-order FFN factor, at 0.5 no SiLU
     activation, at 0.25 no LayerNorm output: each is rebuilt bit for bit
-    where a backward needs it, so the results stay identical."""
+    where a backward needs it, so the results stay identical. With
+    checkpointed blocks, budgets above 0.25 also keep the force pass's input
+    gradients for the parameter backward; they set the peak at the end of the
+    force pass, which is then the same at 1 and 0.5."""
     sizes = mlip.workload_sizes("allscaip_85m", seed=0, atoms_target=3000)
     runs = {b: _budget_run(BLOCKS_85M, sizes, b, checkpoint) for b in (1.0, 0.5, 0.25)}
     peaks = {b: runs[b][0] for b in runs}
     print("peak MB:", {b: round(p / 2**20, 1) for b, p in peaks.items()})
-    assert peaks[1.0] > peaks[0.5] > peaks[0.25]
+    if checkpoint:
+        assert peaks[1.0] >= peaks[0.5] > peaks[0.25]
+    else:
+        assert peaks[1.0] > peaks[0.5] > peaks[0.25]
     ref = runs[1.0][1]
     for b in (0.5, 0.25):
         got = runs[b][1]
