@@ -249,6 +249,7 @@ def attn_bytes(info, name):
 # traffic is this figure times its atoms.
 TRAFFIC_PER_ATOM = {
     ("cg_pooled_attn_bwd1", 12, 30, 64): (53.767680e6 + 329.964032e6) / 2048,  # tf32
+    ("cg_pooled_attn_bwd2", 12, 30, 64): (127.4e6 + 346.0e6) / 2048,           # tf32
 }
 # the edge-attention backward2 microbenchmark kernel, 8 heads x 32 tokens x 32 dims, tf32
 EDGE_BWD2_TRAFFIC_PER_ATOM = (303.211264e6 + 133.112064e6) / 1024

@@ -21,7 +21,19 @@ their inputs their outputs, so the three recomputes take them instead of
 running those kernels again, and the VJP's pooled-attention backward1 and
 input-gradient GEMMs keep their outputs from the force pass for the VJP's
 rebuild in the parameter backward, which takes them instead of recomputing;
-the memory budget decides whether they may (create_graph_b200.nn). The block's fused ops are
+the memory budget decides whether they may (create_graph_b200.nn).
+
+Deferred first-order backward (budget above 0.25): VjpFn.backward
+differentiates the block's VJP; the second-order terms that reach the forward
+tensors the VJP's ops read would run the block's forward ops' backward, which
+BlockFn.backward runs again on the energy's cotangent. So while the VJP is
+rebuilt the ops read those tensors through leaves, VjpFn.backward stops at
+them, and the cotangents they receive are added by each op's backward inside
+BlockFn.backward (backward is linear in its cotangents): the forward ops'
+backward runs once per block. Block i's own backward waits for the gradient
+of its output, which the VJP of block i+1 produces after block i's, so the
+deferred cotangents are there; if the block's backward ever ran first,
+VjpFn.backward does the whole differentiation itself. The block's fused ops are
 the same sm_100a kernels as elsewhere; the recompute runs under the region's
 config, so its memory budget applies inside the blocks too.
 """
@@ -53,16 +65,30 @@ class RecomputeCache:
     def __init__(self):
         self.slots: dict[object, object] = {}
         self._next = 0
+        self._next_op = 0
         # set while the block's VJP (create_graph's force pass, or its rebuild
         # in the parameter backward) runs: both see the same output cotangents
         self.in_vjp = False
+        # deferred first-order backward (VjpFn.backward / BlockFn.backward):
+        # while ``cutting``, ops building the VJP's graph read their forward
+        # tensors through leaves (``cuts``, keyed by (op, role)); the cotangents
+        # those leaves receive wait in ``pending`` for the block's own backward
+        self.cutting = False
+        self.cuts: dict[tuple[int, str], Tensor] = {}
+        self.pending: dict[tuple[int, str], Tensor] = {}
 
     def start(self) -> None:
         self._next = 0
+        self._next_op = 0
 
     def slot(self) -> int:
         self._next += 1
         return self._next - 1
+
+    def op(self) -> int:
+        """The next op's index in this forward (the same in every run of the call)."""
+        self._next_op += 1
+        return self._next_op - 1
 
 
 _CACHES: list[RecomputeCache] = []
@@ -101,6 +127,16 @@ class _BlockCall:
         self.out_spec = None
         self.out_slots: tuple[int, ...] = ()
         self.cache = RecomputeCache()
+        # whether the parameter backward has run this call's first-order
+        # backward (BlockFn.backward) yet
+        self.backward_done = False
+
+    def defers(self) -> bool:
+        """Whether VjpFn.backward may leave the forward ops' part of its
+        backward to BlockFn.backward: the block's own backward is still to
+        come and the memory budget (above 0.25) allows holding the cotangents."""
+        budget = self.config.memory_budget
+        return not self.backward_done and (budget is None or budget > 0.25)
 
     @property
     def inputs(self) -> list[Tensor]:
@@ -189,20 +225,37 @@ class VjpFn(torch.autograd.Function):
         saved = ctx.saved_tensors
         n = len(call.slots)
         inputs, g_outs = saved[:n], saved[n:]
+        cache = call.cache
+        cache.pending = {}
         with torch.enable_grad():
             li = [_leaf(t, True) for t in inputs]
             lg = [_leaf(g, True) for g in g_outs]
-            outs = call.vjp(li, lg, True)
+            # deferred: the ops that build the VJP's graph read their forward
+            # tensors through leaves, so this backward stops at them; the
+            # cotangents the leaves get are the forward ops' share, which the
+            # block's own backward (BlockFn.backward) adds to its output
+            # cotangents' so that the forward ops' backward runs once
+            cache.cutting, cache.cuts = call.defers(), {}
+            try:
+                outs = call.vjp(li, lg, True)
+            finally:
+                cache.cutting = False
+            cuts = [(key, leaf) for key, leaf in cache.cuts.items() if leaf.requires_grad]
+            cache.cuts = {}
             pairs = [
                 (o, gg)
                 for o, gg in zip(outs, ggs)
                 if o is not None and gg is not None and o.requires_grad
             ]
-            wanted = [*li, *lg, *call.params]
+            wanted = [*li, *lg, *call.params, *(leaf for _, leaf in cuts)]
             if pairs:
                 grads = _grad([o for o, _ in pairs], wanted, [gg for _, gg in pairs], allow_unused=True)
             else:
                 grads = [None] * len(wanted)
+        if cuts:
+            found = grads[len(grads) - len(cuts):]
+            cache.pending = {key: g for (key, _), g in zip(cuts, found) if g is not None}
+            grads = grads[: len(grads) - len(cuts)]
         return (None, None, *grads)
 
 
@@ -226,9 +279,15 @@ class BlockFn(torch.autograd.Function):
         if in_forces_pass():
             grads_in = VjpFn.apply(call, len(g_outs), *inputs, *g_outs, *call.params)
             return (None, *grads_in, *([None] * n_params))
+        call.backward_done = True
+        pending = call.cache.pending
         with torch.enable_grad():
             leaves = [_leaf(t) for t in inputs]
             outs = call.selected(call.run(leaves))
+            if pending:
+                # the VJP's deferred cotangents enter inside the block (each op's
+                # backward adds its own): every op must be reached
+                g_outs = [torch.zeros_like(o) if g is None and o.requires_grad else g for o, g in zip(outs, g_outs)]
             pairs = [(o, g) for o, g in zip(outs, g_outs) if g is not None and o.requires_grad]
             every = [*leaves, *call.params]
             wanted = [t for t in every if t.requires_grad]
@@ -237,6 +296,10 @@ class BlockFn(torch.autograd.Function):
             else:
                 found = iter([None] * len(wanted))
             grads = [next(found) if t.requires_grad else None for t in every]
+        if pending:
+            left = sorted(pending)
+            pending.clear()
+            raise RuntimeError(f"checkpoint: deferred cotangents of {left} reached no op of the block's backward")
         return (None, *grads)
 
 

@@ -27,8 +27,11 @@ src/create_graph/compile_config.py:25-66. What they mean here:
     (rows x hidden), rebuilt from the normalisation input.
 
   Rebuilt tensors equal the kept ones bit for bit (same kernels, same
-  inputs), so a budget changes peak memory and time, never results. Inside
-  ``checkpoint`` blocks it applies to the block being recomputed.
+  inputs), so a budget changes peak memory and time, not results. Inside
+  ``checkpoint`` blocks it applies to the block being recomputed; above 0.25
+  checkpointed blocks also keep results across their recomputes and defer
+  part of the parameter backward (create_graph_b200.checkpoint), which sums
+  the parameter gradients in another order than at 0.25 or less.
 - ``checkpoint``: regex of block module paths recomputed per block
   (create_graph_b200.checkpoint).
 - ``options``: free (key, value) pairs, kept sorted and hashable.

@@ -115,15 +115,68 @@ def mm_raw(a: Tensor, b: Tensor, **kw) -> Tensor:
     return gemm(A, B, a_t=at, b_t=bt, **kw)
 
 
+# ---------------------------------------------------------------------------
+# Deferred first-order backward inside checkpointed blocks
+#
+# The parameter backward differentiates a block's VJP (VjpFn.backward); the
+# second-order terms that reach the forward tensors the VJP's ops read would
+# then run the block's forward ops' backward, which the block's own backward
+# (BlockFn.backward, on the energy's cotangent) runs again later. Instead the
+# VJP's ops read those tensors through leaves (_cut), and the cotangents the
+# leaves receive are added where the block's own backward passes the same
+# tensors (_deferred), so the forward ops' backward runs once.
+# ---------------------------------------------------------------------------
+
+
+def _op_slot():
+    """(cache, index) of an op inside a checkpointed block call (the same in
+    every run of the call's forward), else None."""
+    cache = active_recompute_cache()
+    return (cache, cache.op()) if cache is not None else None
+
+
+def _cut(ctx, role: str, t: Tensor | None) -> Tensor | None:
+    """t, or a leaf standing for it while the block's VJP is rebuilt with its
+    forward ops' share deferred (one leaf per op and role)."""
+    op = getattr(ctx, "op", None)
+    if op is None or t is None or not op[0].cutting:
+        return t
+    cache, index = op
+    leaf = cache.cuts.get((index, role))
+    if leaf is None:
+        leaf = t.detach().requires_grad_(t.requires_grad)
+        cache.cuts[(index, role)] = leaf
+    return leaf
+
+
+def _deferred(ctx, role: str) -> Tensor | None:
+    """The deferred cotangent of the op's tensor ``role``, taken once (in the
+    block's own backward), or None."""
+    op = getattr(ctx, "op", None)
+    if op is None or not op[0].pending:
+        return None
+    cache, index = op
+    return cache.pending.pop((index, role), None)
+
+
+def _plus(g: Tensor | None, c: Tensor | None) -> Tensor | None:
+    if c is None:
+        return g
+    return c if g is None else g + c
+
+
 class MM(_Fused):
-    """C = a @ b.T (a (M, K), b (N, K)); backward: g @ b and g.T @ a."""
+    """C = a @ b.T (+ add) (a (M, K), b (N, K)); backward: g @ b and g.T @ a.
+    ``add`` (M, N) enters through the GEMM epilogue."""
 
     @staticmethod
-    def forward(ctx, a, b, reuse=None):
+    def forward(ctx, a, b, reuse=None, add=None):
         """reuse: (cache, key) inside a checkpointed block's VJP (_vjp_reuse)."""
         _keep_precision(ctx)
         ctx.save_for_backward(a, b)
         ctx.edges = _edges(a, b)
+        if add is not None:
+            return mm_raw(a, b, act=ACT_ADD, aux_in=_f32(add, "mm_add"))
         return _reused_in_rebuild(reuse, lambda: mm_raw(a, b))
 
     @staticmethod
@@ -132,7 +185,8 @@ class MM(_Fused):
         a, b = ctx.saved_tensors
         ga = MM.apply(g, b.t()) if _wanted(ctx, 0) else None
         gb = MM.apply(g.t(), a.t()) if _wanted(ctx, 1) else None
-        return ga, gb, None
+        g_add = g if len(ctx.needs_input_grad) > 3 and ctx.needs_input_grad[3] else None
+        return ga, gb, None, g_add
 
 
 def mm(a: Tensor, b: Tensor) -> Tensor:
@@ -238,18 +292,24 @@ class ScaleShift(_Fused):
         ctx.save_for_backward(src if ctx.rebuild else x, gamma)
         ctx.edges = _edges(x, gamma, beta)
         ctx.has_beta = beta is not None
+        ctx.op = _op_slot()
         return out
 
     @staticmethod
     def backward(ctx, g):
         kept, gamma = ctx.saved_tensors
+        role = "src" if ctx.rebuild else "x"
+        c = _deferred(ctx, role)
         gx = ScaleShift.apply(g, gamma, None) if _wanted(ctx, 0) else None
         gg = None
         if _wanted(ctx, 1):
+            kept = _cut(ctx, role, kept)
             x = RowNorm.apply(kept, ctx.eps) if ctx.rebuild else kept
             gg = ColDot.apply(g, x)
         gb = ColSum.apply(g) if ctx.has_beta and _wanted(ctx, 2) else None
-        return gx, gg, gb, None, None
+        if ctx.rebuild:
+            return gx, gg, gb, c, None
+        return _plus(gx, c), gg, gb, None, None
 
 
 # ---------------------------------------------------------------------------
@@ -258,8 +318,11 @@ class ScaleShift(_Fused):
 
 
 def _linear_backward(ctx, g, x, w, has_bias):
-    gx = MM.apply(g, w.t(), _vjp_reuse(ctx, "gx")) if _wanted(ctx, 0) else None
-    gw = MM.apply(g.t(), x.t()) if _wanted(ctx, 1) else None
+    """(gx, gw, gb); gx takes the deferred cotangent of x in its epilogue, gw
+    reads x through _cut."""
+    c = _deferred(ctx, "x")
+    gx = MM.apply(g, w.t(), _vjp_reuse(ctx, "gx"), c) if _wanted(ctx, 0) else None
+    gw = MM.apply(g.t(), _cut(ctx, "x", x).t()) if _wanted(ctx, 1) else None
     gb = ColSum.apply(g) if has_bias and _wanted(ctx, 2) else None
     return gx, gw, gb
 
@@ -276,6 +339,7 @@ class LinearFn(_Fused):
         # inside checkpointed blocks at a budget of 0.5 or more, the recomputes
         # take the first forward's projection (the q/k/v rows: 3C floats per atom)
         ctx.block = _block_slot()
+        ctx.op = _op_slot()
         return _kept_across_recomputes(lambda: mm_raw(x, w, bias=b), ctx.block, min_budget=0.5)
 
     @staticmethod
@@ -317,6 +381,7 @@ class LinearResidualFn(_Fused):
         ctx.edges = _edges(x, w, b, r)
         ctx.has_bias = b is not None
         ctx.block = _block_slot()
+        ctx.op = _op_slot()
         return _kept_across_recomputes(
             lambda: mm_raw(x, w, bias=b, act=ACT_ADD, aux_in=_f32(r, "linear_residual")), ctx.block)
 
@@ -380,6 +445,7 @@ class LinearSiluFn(_Fused):
         ctx.edges = _edges(x, w, b)
         ctx.has_bias = b is not None
         ctx.block = _block_slot()  # its backward's input gradient is kept for the VJP's rebuild
+        ctx.op = _op_slot()
         # z is usually unused: its gradient arrives as None, not as a zero-filled
         # (rows, out) tensor added to the SiLU gradient
         ctx.set_materialize_grads(False)
@@ -389,13 +455,14 @@ class LinearSiluFn(_Fused):
     @_at_forward_precision
     def backward(ctx, gy, gz):
         x, w, z = ctx.saved_tensors
+        gz = _plus(gz, _deferred(ctx, "z"))
         g = None
         if gy is not None:
-            g = SiluGrad.apply(gy, z)
+            g = SiluGrad.apply(gy, _cut(ctx, "z", z))
         if gz is not None:
             g = gz if g is None else g + gz
         if g is None:
-            return None, None, None
+            return _deferred(ctx, "x"), None, None
         return _linear_backward(ctx, g, x, w, ctx.has_bias)
 
 
@@ -459,6 +526,7 @@ class SiluLinearResidualFn(_Fused):
         ctx.edges = _edges(y, z, w, b, r)
         ctx.has_bias = b is not None
         ctx.block = _block_slot()
+        ctx.op = _op_slot()
         return _kept_across_recomputes(
             lambda: mm_raw(y, w, bias=b, act=ACT_ADD, aux_in=_f32(r, "silu_linear_residual")), ctx.block)
 
@@ -472,13 +540,16 @@ class SiluLinearResidualFn(_Fused):
         # below a memory budget of 1 (no u kept) the VJP's rebuild takes the
         # force pass's gz; at 1 the rebuild runs the GEMM again for its u
         reuse = None if ctx.keep_u else _vjp_reuse(ctx, "gz")
-        gz = MMSiluGrad.apply(g, w, z, keep_u, reuse) if _wanted(ctx, 1) else None
+        # deferred cotangents: z's joins gz; y's is y's gradient (through the
+        # producer's SiLU derivative)
+        cy, cz = _deferred(ctx, "y"), _deferred(ctx, "z")
+        gz = _plus(MMSiluGrad.apply(g, w, _cut(ctx, "z", z), keep_u, reuse), cz) if _wanted(ctx, 1) else None
         gw = None
         if _wanted(ctx, 2):
-            gw = MM.apply(g.t(), (y if y is not None else Silu.apply(z)).t())
+            gw = MM.apply(g.t(), (_cut(ctx, "y", y) if y is not None else Silu.apply(_cut(ctx, "z", z))).t())
         gb = ColSum.apply(g) if ctx.has_bias and _wanted(ctx, 3) else None
         gr = g if ctx.needs_input_grad[4] else None
-        return None, gz, gw, gb, gr
+        return cy, gz, gw, gb, gr
 
 
 class SplitCols(_Fused):
@@ -539,14 +610,16 @@ class BranchNorm(_Fused):
         ctx.save_for_backward(x)
         ctx.eps = eps
         ctx.set_materialize_grads(False)
+        ctx.op = _op_slot()
         return x.view_as(x), out
 
     @staticmethod
     def backward(ctx, g_x, g_norm):
         (x,) = ctx.saved_tensors
+        c = _deferred(ctx, "x")
         if g_norm is None:
-            return g_x, None
-        return RowNormGrad.apply(g_norm, x, ctx.eps, g_x), None
+            return _plus(g_x, c), None
+        return _plus(RowNormGrad.apply(g_norm, _cut(ctx, "x", x), ctx.eps, g_x), c), None
 
 
 class RowNormGrad(_Fused):
@@ -870,21 +943,23 @@ class TokenAttentionGrad(_Fused):
         return segment_sum_raw(dtok, graph.tokens), dbias, None, dg, None
 
 
-def _pooled_qkv_grad(dqk: Tensor, wv: Tensor, dm: Tensor, graph, heads: int) -> Tensor:
+def _pooled_qkv_grad(dqk: Tensor, wv: Tensor, dm: Tensor, graph, heads: int, into: Tensor | None = None) -> Tensor:
     """Per-atom q/k/v gradient (n_atoms, 3C) of the pooled attention: the
     per-token [dq | dk] rows and the rank-one v rows wv[token, h] * dm[atom of
-    token, h], each reduced to atoms in a fixed order."""
+    token, h], each reduced to atoms in a fixed order; added to ``into`` (a
+    gradient of the caller's own, overwritten) when given."""
     csr = graph.tokens
     C = dm.shape[1]
     d = C // heads
-    out = torch.empty(csr.rows, 3 * C, device=dm.device)
+    acc = int(into is not None and into.is_contiguous() and into.shape == (csr.rows, 3 * C))
+    out = into if acc else torch.empty(csr.rows, 3 * C, device=dm.device)
     native.call("cg_segment_sum", dqk.data_ptr(), dqk.stride(0), csr.row_ptr.data_ptr(), csr.perm.data_ptr(),
-                csr.rows, 2 * C, out.data_ptr(), out.stride(0), 0, _stream())
+                csr.rows, 2 * C, out.data_ptr(), out.stride(0), acc, _stream())
     dm = _f32(dm, "segment_sum_scaled")
     native.call("cg_segment_sum_scaled", wv.data_ptr(), dm.data_ptr(), dm.stride(0), graph.k, heads, d,
                 csr.row_ptr.data_ptr(), csr.perm.data_ptr(), csr.rows, out.data_ptr() + 2 * C * out.element_size(),
-                out.stride(0), 0, _stream())
-    return out
+                out.stride(0), acc, _stream())
+    return out if acc or into is None else out + into
 
 
 class PooledTokenAttention(_Fused):
@@ -915,6 +990,7 @@ class PooledTokenAttention(_Fused):
         ctx.save_for_backward(qkv, bias, env, lse, w)
         ctx.meta = meta
         ctx.cache, ctx.slot = cache, slot
+        ctx.op = _op_slot()
         return out
 
     @staticmethod
@@ -923,8 +999,11 @@ class PooledTokenAttention(_Fused):
         # inside the block's VJP (force pass or its rebuild): the rebuild sees
         # the force pass's cotangent again and takes its kept result
         reuse = (ctx.cache, ("backward1", ctx.slot)) if ctx.cache is not None and ctx.cache.in_vjp else None
-        d_qkv, dbias, denv = PooledTokenAttentionGrad.apply(qkv, bias, env, lse, w, dm, ctx.meta, reuse)
-        return d_qkv, dbias, denv, None, None, None, None
+        c = [_deferred(ctx, role) for role in ("qkv", "bias", "env")]
+        qkv, bias, env = (_cut(ctx, role, t) for role, t in zip(("qkv", "bias", "env"), (qkv, bias, env)))
+        # (the deferred q/k/v cotangent is the reduction's starting value)
+        d_qkv, dbias, denv = PooledTokenAttentionGrad.apply(qkv, bias, env, lse, w, dm, ctx.meta, reuse, c[0])
+        return d_qkv, _plus(dbias, c[1]), _plus(denv, c[2]), None, None, None, None
 
 
 class PooledTokenAttentionGrad(_Fused):
@@ -933,7 +1012,8 @@ class PooledTokenAttentionGrad(_Fused):
     statistics, not differentiated)."""
 
     @staticmethod
-    def forward(ctx, qkv, bias, env, lse, w, dm, meta, reuse=None):
+    def forward(ctx, qkv, bias, env, lse, w, dm, meta, reuse=None, d_qkv_into=None):
+        """d_qkv_into: a q/k/v gradient the result is added to (overwritten)."""
         graph, heads, scale, precision = meta
         ctx.save_for_backward(qkv, bias, env, lse, w, dm)
         ctx.meta = meta
@@ -942,10 +1022,13 @@ class PooledTokenAttentionGrad(_Fused):
             kept = cache.slots.pop(key, None)
             if kept is not None:
                 # the same op on the same inputs earlier in this block call
-                return tuple(t.detach() for t in kept)
+                out = tuple(t.detach() for t in kept)
+                return out if d_qkv_into is None else (out[0] + d_qkv_into, *out[1:])
         dqk, wv, dbias, denv = pooled_attention_backward1(qkv, bias, env, lse, w, dm, graph.tokens.index,
                                                           graph.counts, graph.k, heads, scale, precision)
-        out = (_pooled_qkv_grad(dqk, wv, dm, graph, heads), dbias, denv.view_as(env))
+        out = (_pooled_qkv_grad(dqk, wv, dm, graph, heads, d_qkv_into), dbias, denv.view_as(env))
+        if out[0] is d_qkv_into:
+            ctx.mark_dirty(d_qkv_into)
         if reuse is not None:
             cache.slots[key] = out
         return out
@@ -959,7 +1042,7 @@ class PooledTokenAttentionGrad(_Fused):
         dqk, wv, dbias, denv, ddm = pooled_attention_backward2(
             qkv, bias, env, lse, w, dm, h_qkv, h_bias, h_env, graph.tokens.index, graph.counts, graph.k, heads,
             scale, precision)
-        return _pooled_qkv_grad(dqk, wv, dm, graph, heads), dbias, denv.view_as(env), None, None, ddm, None, None
+        return _pooled_qkv_grad(dqk, wv, dm, graph, heads), dbias, denv.view_as(env), None, None, ddm, None, None, None
 
 
 # ---------------------------------------------------------------------------

@@ -1,0 +1,122 @@
+"""
+The deferred first-order backward of checkpointed blocks, on the CPU in
+float64 (host logic only). A toy fused op uses the same hooks as the package's
+fused ops (_op_slot / _cut / _deferred): while the parameter backward
+differentiates a block's VJP, the op's backward reads its forward tensors
+through leaves, and the cotangents they receive are added where the block's
+own backward passes them. Results must equal eager create_graph at 1e-10 with
+the deferral on (budget above 0.25) and off, and the op's backward must run
+once less per block with it on.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+from torch import nn
+
+import create_graph_b200 as cg
+from create_graph_b200.nn import _cut, _deferred, _Fused, _op_slot, _plus
+from create_graph_b200.testing import check_create_graph
+
+F64 = torch.float64
+
+
+class ToyLayer(_Fused):
+    """out = x + tanh(x @ w.T) * s; backward from torch ops (differentiable
+    when recorded), reading x and s through _cut."""
+
+    calls = 0
+
+    @staticmethod
+    def forward(ctx, x, w, s):
+        ctx.op = _op_slot()
+        ctx.save_for_backward(x, w, s)
+        return x + torch.tanh(x @ w.t()) * s
+
+    @staticmethod
+    def backward(ctx, g):
+        ToyLayer.calls += 1
+        x, w, s = ctx.saved_tensors
+        cx, cs = _deferred(ctx, "x"), _deferred(ctx, "s")
+        x, s = _cut(ctx, "x", x), _cut(ctx, "s", s)
+        t = torch.tanh(x @ w.t())
+        u = g * s * (1 - t * t)
+        gx = g + u @ w
+        gw = u.t() @ x
+        gs = (g * t).sum(-1, keepdim=True)
+        return _plus(gx, cx), gw, _plus(gs, cs)
+
+
+class ToyBlock(nn.Module):
+    def __init__(self, width):
+        super().__init__()
+        self.norm = nn.LayerNorm(width)  # plain torch: its tensors are not cut
+        self.w1 = nn.Parameter(torch.randn(width, width) / width**0.5)
+        self.w2 = nn.Parameter(torch.randn(width, width) / width**0.5)
+
+    def forward(self, h, dist):
+        s = torch.cos(dist)[:, None]
+        return h + ToyLayer.apply(ToyLayer.apply(self.norm(h), self.w1, s), self.w2, s)
+
+
+class ToyStack(nn.Module):
+    def __init__(self, width=8, depth=3):
+        super().__init__()
+        self.inp = nn.Linear(4, width)
+        self.blocks = nn.ModuleList(ToyBlock(width) for _ in range(depth))
+        self.out = nn.Linear(width, 1)
+
+    def forward(self, vec, dist, system, n_systems):
+        h = self.inp(torch.cat([vec, dist[:, None]], dim=-1))
+        for block in self.blocks:
+            h = block(h, dist)
+        return torch.zeros(n_systems, dtype=h.dtype).index_add(0, system, self.out(h).squeeze(-1))
+
+
+class ToyModel(nn.Module):
+    def __init__(self, budget):
+        super().__init__()
+        config = cg.CompileConfig(backend="eager", checkpoint=r"blocks\.\d+", memory_budget=budget)
+        self.region = cg.compile(ToyStack(), config=config)
+
+    def forward(self, data):
+        vec = data["pos"][data["dst"]] - data["pos"][data["src"]]
+        return {"energy": self.region(vec, vec.norm(dim=-1), data["system"], data["n_systems"])}
+
+
+def toy_data(e=24, n=9, systems=3, seed=0):
+    gen = torch.Generator().manual_seed(seed)
+    src = torch.randint(0, n, (e,), generator=gen)
+    dst = (src + torch.randint(1, n, (e,), generator=gen)) % n
+    return {"pos": torch.randn(n, 3, generator=gen, dtype=F64), "src": src, "dst": dst,
+            "system": torch.arange(e) * systems // e, "n_systems": systems}
+
+
+@pytest.mark.parametrize("budget", [1.0, 0.5, 0.25])
+def test_deferred_backward_matches_eager(budget):
+    torch.manual_seed(0)
+    model = ToyModel(budget).to(F64)
+    errors = check_create_graph(model, toy_data())
+    bad = {k: v for k, v in errors.items() if v > 1e-10}
+    assert not bad, errors
+
+
+def _backward_calls(budget):
+    torch.manual_seed(0)
+    model = ToyModel(budget).to(F64)
+    data = toy_data(seed=1)
+    out, grads = cg.create_graph(model, data)
+    ToyLayer.calls = 0
+    (out["energy"].sum() + grads["pos"].square().sum()).backward()
+    return ToyLayer.calls
+
+
+def test_deferral_runs_the_forward_ops_backward_once():
+    depth = len(ToyStack().blocks)
+    # per block: the VJP's rebuild (both layers), its differentiation through
+    # the first layer, whose output the second layer's backward reads (only
+    # without the deferral), then the block's own backward (both layers)
+    assert _backward_calls(0.25) == 5 * depth
+    assert _backward_calls(0.5) == 4 * depth
+    assert _backward_calls(1.0) == 4 * depth

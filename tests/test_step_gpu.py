@@ -168,8 +168,11 @@ def test_memory_budget_lowers_peak_memory(checkpoint):
     activation, at 0.25 no LayerNorm output: each is rebuilt bit for bit
     where a backward needs it, so the results stay identical. With
     checkpointed blocks, budgets above 0.25 also keep the force pass's input
-    gradients for the parameter backward; they set the peak at the end of the
-    force pass, which is then the same at 1 and 0.5."""
+    gradients for the parameter backward and defer the forward ops' share of
+    the VJP's differentiation to the block's own backward (holding its
+    cotangents); they set the peak, the same at 1 and 0.5. Without the
+    deferral (0.25) the parameter gradients are summed in another order: equal
+    to the tf32 products' rounding, not bit for bit."""
     sizes = mlip.workload_sizes("allscaip_85m", seed=0, atoms_target=3000)
     runs = {b: _budget_run(BLOCKS_85M, sizes, b, checkpoint) for b in (1.0, 0.5, 0.25)}
     peaks = {b: runs[b][0] for b in runs}
@@ -179,12 +182,19 @@ def test_memory_budget_lowers_peak_memory(checkpoint):
     else:
         assert peaks[1.0] > peaks[0.5] > peaks[0.25]
     ref = runs[1.0][1]
+    scale = torch.cat([g.flatten() for g in ref["grads"].values()]).norm()
     for b in (0.5, 0.25):
         got = runs[b][1]
         for key in ("energy", "forces", "loss"):
             assert torch.equal(got[key], ref[key]), (b, key)
         for name, g in ref["grads"].items():
-            assert torch.equal(got["grads"][name], g), (b, name)
+            if b == 0.5 or not checkpoint:
+                assert torch.equal(got["grads"][name], g), (b, name)
+            else:
+                # gradients that nearly cancel (the attention-bias bias sums
+                # softmax gradients) are compared against the whole gradient's norm
+                err = (got["grads"][name] - g).norm()
+                assert err <= 1e-3 * max(g.norm(), 1e-2 * scale), (b, name, float(err), float(g.norm()))
 
 
 def test_eval_mode_forces_first_order():
