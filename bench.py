@@ -196,7 +196,8 @@ class Job:
 
 def kernel_breakdown(native, step, n_steps=1):
     """Per entry point: launches, device time per step (CUDA events around each
-    launch on its stream) and share of the instrumented step."""
+    launch on its stream) and share of the library's device time in the step
+    (the instrumented step's wall time is host-bound, so it is no denominator)."""
     names = [n for n in native.exported_symbols() if n.startswith("cg_") and n not in
              ("cg_last_error", "cg_version", "cg_launch_count", "cg_device_error") and
              not n.endswith("_bytes") and not n.endswith("_workspace")]
@@ -215,7 +216,10 @@ def kernel_breakdown(native, step, n_steps=1):
         if not rec:
             continue
         ms = sum(a.elapsed_time(b) for a, b, _ in rec) / n_steps
-        out[name] = {"launches": len(rec) // n_steps, "ms": ms, "share": ms / total, "calls": rec}
+        out[name] = {"launches": len(rec) // n_steps, "ms": ms, "calls": rec}
+    device_ms = sum(v["ms"] for v in out.values()) or total
+    for v in out.values():
+        v["share"] = v["ms"] / device_ms
     native.time_entry_points(names, enable=False)
     return out
 
@@ -482,7 +486,7 @@ def run_mine(args):
             "roofline_gemm": (gemm_roofline(kernels["cg_gemm_tf32"]["calls"], bf16_sus, src)
                               if "cg_gemm_tf32" in kernels else None),
             "kernels": kernel_table(kernels),
-            "kernels_note": "per-kernel device times from one eager step, CUDA events around each launch",
+            "kernels_note": "per-kernel device times from one eager step, CUDA events around each launch; share of the library kernels' summed device time",
             "clocks": clocks.summary(),
             "loss": float(last["loss"].item()),
         }

@@ -16,8 +16,8 @@ over ``named_modules()``) becomes one ``BlockFn`` node of the autograd graph:
 So a block's forward runs four times and its VJP twice, and at most one
 block's activations are alive at a time. Each call keeps a RecomputeCache:
 the pooled attention keeps its softmax statistics and its output (n x C)
-from the first forward, and the linear layers whose backward reads only
-their inputs their outputs, so the three recomputes take them instead of
+from the first forward, and the linear layers and LayerNorms their outputs
+(the larger ones from a memory budget of 0.5), so the three recomputes take them instead of
 running those kernels again, and the VJP's pooled-attention backward1 and
 input-gradient GEMMs keep their outputs from the force pass for the VJP's
 rebuild in the parameter backward, which takes them instead of recomputing;

@@ -284,9 +284,16 @@ class ScaleShift(_Fused):
     @staticmethod
     def forward(ctx, x, gamma, beta, src=None, eps=None):
         x = _f32(x, "scale_shift")
-        out = torch.empty_like(x)
-        native.call("cg_scale_shift", x.data_ptr(), native.ptr(gamma), native.ptr(beta), out.data_ptr(),
-                    x.shape[0], x.shape[1], _stream())
+
+        def compute():
+            out = torch.empty_like(x)
+            native.call("cg_scale_shift", x.data_ptr(), native.ptr(gamma), native.ptr(beta), out.data_ptr(),
+                        x.shape[0], x.shape[1], _stream())
+            return out
+
+        # a LayerNorm's output inside checkpointed blocks at a budget of 0.5 or
+        # more: the recomputes take the first forward's
+        out = _kept_across_recomputes(compute, _block_slot() if src is not None else (None, None), min_budget=0.5)
         ctx.rebuild = src is not None and active_memory_budget() <= 0.25
         ctx.eps = eps
         ctx.save_for_backward(src if ctx.rebuild else x, gamma)
@@ -364,9 +371,9 @@ def _kept_across_recomputes(compute, where, min_budget: float | None = None):
         return compute()
     kept = cache.slots.get(slot)
     if kept is not None:
-        return kept.detach()
+        return tuple(t.detach() for t in kept) if isinstance(kept, tuple) else kept.detach()
     out = compute()
-    cache.slots[slot] = out.detach()
+    cache.slots[slot] = tuple(t.detach() for t in out) if isinstance(out, tuple) else out.detach()
     return out
 
 
@@ -439,12 +446,19 @@ class LinearSiluFn(_Fused):
     @staticmethod
     def forward(ctx, x, w, b):
         _keep_precision(ctx)
-        z = torch.empty(x.shape[0], w.shape[0], device=x.device)
-        y = mm_raw(x, w, bias=b, act=ACT_SILU, aux_out=z)
+
+        def compute():
+            z = torch.empty(x.shape[0], w.shape[0], device=x.device)
+            return mm_raw(x, w, bias=b, act=ACT_SILU, aux_out=z), z
+
+        # inside checkpointed blocks: the recomputes take the first forward's
+        # (y, z) at a budget of 0.5 or more, and its backward's input gradient
+        # is kept for the VJP's rebuild
+        ctx.block = _block_slot()
+        y, z = _kept_across_recomputes(compute, ctx.block, min_budget=0.5)
         ctx.save_for_backward(x, w, z)
         ctx.edges = _edges(x, w, b)
         ctx.has_bias = b is not None
-        ctx.block = _block_slot()  # its backward's input gradient is kept for the VJP's rebuild
         ctx.op = _op_slot()
         # z is usually unused: its gradient arrives as None, not as a zero-filled
         # (rows, out) tensor added to the SiLU gradient
@@ -604,9 +618,16 @@ class BranchNorm(_Fused):
     @staticmethod
     def forward(ctx, x, eps):
         x = _f32(x, "rownorm")
-        out = torch.empty_like(x)
-        native.call("cg_rownorm_fwd", x.data_ptr(), x.shape[0], x.shape[1], eps, out.data_ptr(), None,
-                    _stream())
+
+        def compute():
+            out = torch.empty_like(x)
+            native.call("cg_rownorm_fwd", x.data_ptr(), x.shape[0], x.shape[1], eps, out.data_ptr(), None,
+                        _stream())
+            return out
+
+        # inside checkpointed blocks at a budget of 0.5 or more the recomputes
+        # take the first forward's normalised rows
+        out = _kept_across_recomputes(compute, _block_slot(), min_budget=0.5)
         ctx.save_for_backward(x)
         ctx.eps = eps
         ctx.set_materialize_grads(False)
