@@ -120,3 +120,36 @@ def test_deferral_runs_the_forward_ops_backward_once():
     assert _backward_calls(0.25) == 5 * depth
     assert _backward_calls(0.5) == 4 * depth
     assert _backward_calls(1.0) == 4 * depth
+
+
+class ForgetfulLayer(ToyLayer):
+    """A planted mistake: reads x through _cut but never adds its deferred
+    cotangent back."""
+
+    @staticmethod
+    def backward(ctx, g):
+        x, w, s = ctx.saved_tensors
+        x = _cut(ctx, "x", x)
+        t = torch.tanh(x @ w.t())
+        u = g * s * (1 - t * t)
+        return g + u @ w, u.t() @ x, (g * t).sum(-1, keepdim=True)
+
+
+def test_an_unconsumed_deferred_cotangent_is_an_error(monkeypatch):
+    monkeypatch.setattr(ToyLayer, "apply", ForgetfulLayer.apply)
+    torch.manual_seed(0)
+    model = ToyModel(0.5).to(F64)
+    out, grads = cg.create_graph(model, toy_data())
+    with pytest.raises(RuntimeError, match="deferred cotangents"):
+        (out["energy"].sum() + grads["pos"].square().sum()).backward()
+
+
+def test_defers_only_above_a_quarter_and_before_the_block_backward():
+    from create_graph_b200.checkpoint import _BlockCall
+
+    block = nn.Linear(2, 2)
+    for budget, want in ((None, True), (1.0, True), (0.5, True), (0.25, False), (0.1, False)):
+        call = _BlockCall(block, cg.CompileConfig(memory_budget=budget), (torch.zeros(1, 2),), {})
+        assert call.defers() is want, budget
+        call.backward_done = True
+        assert not call.defers()

@@ -65,3 +65,24 @@ def test_outside_a_block_call_every_call_computes():
         a = _kept_across_recomputes(counter(1), _block_slot())
         b = _kept_across_recomputes(counter(2), _block_slot())
     assert counter.calls == 2 and float(a[0]) == 1.0 and float(b[0]) == 2.0
+
+
+def test_ops_with_several_outputs_keep_each_of_them():
+    cache, calls = checkpoint.RecomputeCache(), []
+
+    def pair():
+        calls.append(1)
+        return torch.full((2,), 1.0), torch.full((3,), 2.0)
+
+    with compile_context(cg.CompileConfig(memory_budget=0.5)):
+        for _ in range(3):
+            cache.start()
+            checkpoint._CACHES.append(cache)
+            try:
+                y, z = _kept_across_recomputes(pair, _block_slot())
+            finally:
+                checkpoint._CACHES.pop()
+    assert len(calls) == 1
+    assert torch.equal(y, torch.full((2,), 1.0)) and torch.equal(z, torch.full((3,), 2.0))
+    kept_y, kept_z = cache.slots[0]
+    assert y is not kept_y and y.data_ptr() == kept_y.data_ptr() and z.data_ptr() == kept_z.data_ptr()
