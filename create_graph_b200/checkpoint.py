@@ -99,6 +99,60 @@ def active_recompute_cache() -> RecomputeCache | None:
     return _CACHES[-1] if _CACHES else None
 
 
+# ---------------------------------------------------------------------------
+# Deferred first-order backward: the hooks an op uses to take part
+#
+# The parameter backward differentiates a block's VJP (VjpFn.backward); the
+# second-order terms that reach the forward tensors the VJP's ops read would
+# then run the block's forward ops' backward, which the block's own backward
+# (BlockFn.backward, on the energy's cotangent) runs again later. An op that
+# takes part records ``ctx.op = deferral_slot()`` in its forward; its backward
+# reads the forward tensors it builds on through ``cut_forward_tensor`` (leaves
+# while the VJP is rebuilt, so the differentiation stops there) and adds
+# ``deferred_cotangent`` (what those leaves received, handed out once in the
+# block's own backward) to the gradient of the same tensor. Ops without the
+# hooks are differentiated in full, which is also correct.
+# ---------------------------------------------------------------------------
+
+
+def deferral_slot():
+    """(cache, index) of an op inside a checkpointed block call (the same in
+    every run of the call's forward), else None."""
+    cache = active_recompute_cache()
+    return (cache, cache.op()) if cache is not None else None
+
+
+def cut_forward_tensor(ctx, role: str, t: Tensor | None) -> Tensor | None:
+    """t, or a leaf standing for it while the block's VJP is rebuilt with its
+    forward ops' share deferred (one leaf per op and role)."""
+    op = getattr(ctx, "op", None)
+    if op is None or t is None or not op[0].cutting:
+        return t
+    cache, index = op
+    leaf = cache.cuts.get((index, role))
+    if leaf is None:
+        leaf = t.detach().requires_grad_(t.requires_grad)
+        cache.cuts[(index, role)] = leaf
+    return leaf
+
+
+def deferred_cotangent(ctx, role: str) -> Tensor | None:
+    """The deferred cotangent of the op's tensor ``role``, taken once (in the
+    block's own backward), or None."""
+    op = getattr(ctx, "op", None)
+    if op is None or not op[0].pending:
+        return None
+    cache, index = op
+    return cache.pending.pop((index, role), None)
+
+
+def plus(g: Tensor | None, c: Tensor | None) -> Tensor | None:
+    """g + c where either may be None."""
+    if c is None:
+        return g
+    return c if g is None else g + c
+
+
 @contextlib.contextmanager
 def forces_pass():
     """Marks the region's force pass (the VJP create_graph computes)."""

@@ -34,7 +34,13 @@ import torch
 from torch import Tensor, nn
 
 from create_graph_b200 import native
-from create_graph_b200.checkpoint import active_recompute_cache
+from create_graph_b200.checkpoint import (
+    active_recompute_cache,
+    cut_forward_tensor,
+    deferral_slot,
+    deferred_cotangent,
+    plus,
+)
 from create_graph_b200.compile_config import active_memory_budget, engine_will_execute, gradient_edge
 from create_graph_b200.edge_attn import (
     pooled_attention_backward1,
@@ -115,54 +121,10 @@ def mm_raw(a: Tensor, b: Tensor, **kw) -> Tensor:
     return gemm(A, B, a_t=at, b_t=bt, **kw)
 
 
-# ---------------------------------------------------------------------------
-# Deferred first-order backward inside checkpointed blocks
-#
-# The parameter backward differentiates a block's VJP (VjpFn.backward); the
-# second-order terms that reach the forward tensors the VJP's ops read would
-# then run the block's forward ops' backward, which the block's own backward
-# (BlockFn.backward, on the energy's cotangent) runs again later. Instead the
-# VJP's ops read those tensors through leaves (_cut), and the cotangents the
-# leaves receive are added where the block's own backward passes the same
-# tensors (_deferred), so the forward ops' backward runs once.
-# ---------------------------------------------------------------------------
-
-
-def _op_slot():
-    """(cache, index) of an op inside a checkpointed block call (the same in
-    every run of the call's forward), else None."""
-    cache = active_recompute_cache()
-    return (cache, cache.op()) if cache is not None else None
-
-
-def _cut(ctx, role: str, t: Tensor | None) -> Tensor | None:
-    """t, or a leaf standing for it while the block's VJP is rebuilt with its
-    forward ops' share deferred (one leaf per op and role)."""
-    op = getattr(ctx, "op", None)
-    if op is None or t is None or not op[0].cutting:
-        return t
-    cache, index = op
-    leaf = cache.cuts.get((index, role))
-    if leaf is None:
-        leaf = t.detach().requires_grad_(t.requires_grad)
-        cache.cuts[(index, role)] = leaf
-    return leaf
-
-
-def _deferred(ctx, role: str) -> Tensor | None:
-    """The deferred cotangent of the op's tensor ``role``, taken once (in the
-    block's own backward), or None."""
-    op = getattr(ctx, "op", None)
-    if op is None or not op[0].pending:
-        return None
-    cache, index = op
-    return cache.pending.pop((index, role), None)
-
-
-def _plus(g: Tensor | None, c: Tensor | None) -> Tensor | None:
-    if c is None:
-        return g
-    return c if g is None else g + c
+# the deferred first-order backward inside checkpointed blocks: ops read the
+# forward tensors their backward builds on through _cut, and add what
+# _deferred hands them (create_graph_b200.checkpoint)
+_op_slot, _cut, _deferred, _plus = deferral_slot, cut_forward_tensor, deferred_cotangent, plus
 
 
 class MM(_Fused):

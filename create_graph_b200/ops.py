@@ -45,6 +45,7 @@ import typing
 import torch
 from torch import Tensor
 
+from create_graph_b200.checkpoint import cut_forward_tensor, deferral_slot, deferred_cotangent, plus
 from create_graph_b200.errors import ContractError
 
 # schema types of the non-tensor arguments forward1 may take
@@ -194,7 +195,11 @@ class FusedOp:
         return self._shapes_of(self.plan.tensors, count)
 
     def _link_first_derivative(self) -> None:
-        """forward1's backward is backward1 on the saved tensors."""
+        """forward1's backward is backward1 on the saved tensors. Inside
+        checkpointed blocks the op takes part in the deferred first-order
+        backward (create_graph_b200.checkpoint): backward1 reads the saved
+        tensors through cut_forward_tensor, and the deferred cotangents of saved
+        inputs join their gradients, those of saved outputs their cotangents."""
         plan = self.plan
         backward1_op = self.backward1_op
 
@@ -206,11 +211,15 @@ class FusedOp:
             statistics = [values[n] for n in plan.nondiff if n in plan.outputs]
             if statistics:
                 ctx.mark_non_differentiable(*statistics)
+            ctx.op = deferral_slot()
 
         def backward(ctx, *cotangents):
-            wanted = [c for o, c in zip(plan.outputs, cotangents) if o not in plan.nondiff]
-            grads = dict(zip(plan.tensors, _as_tuple(backward1_op(*ctx.saved_tensors, *wanted, *ctx.scalars))))
-            return tuple(grads.get(p) for p in plan.params)
+            saved = [cut_forward_tensor(ctx, n, t) for n, t in zip(plan.save, ctx.saved_tensors)]
+            wanted = [plus(c, deferred_cotangent(ctx, o)) if o in plan.save else c
+                      for o, c in zip(plan.outputs, cotangents) if o not in plan.nondiff]
+            grads = dict(zip(plan.tensors, _as_tuple(backward1_op(*saved, *wanted, *ctx.scalars))))
+            return tuple(plus(grads.get(p), deferred_cotangent(ctx, p)) if p in plan.save else grads.get(p)
+                         for p in plan.params)
 
         self.op.register_autograd(backward, setup_context=setup)
 

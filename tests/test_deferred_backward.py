@@ -17,7 +17,7 @@ from torch import nn
 
 import create_graph_b200 as cg
 from create_graph_b200.nn import _cut, _deferred, _Fused, _op_slot, _plus
-from create_graph_b200.testing import check_create_graph
+from create_graph_b200.testing import check_create_graph, check_op
 
 F64 = torch.float64
 
@@ -153,3 +153,104 @@ def test_defers_only_above_a_quarter_and_before_the_block_backward():
         assert call.defers() is want, budget
         call.backward_done = True
         assert not call.defers()
+
+
+# ---------------------------------------------------------------------------
+# cg.custom_op operators take part as well
+# ---------------------------------------------------------------------------
+
+
+BACKWARD1_CALLS = [0]
+
+
+@cg.custom_op("cg_b200_tests::scaled_tanh")
+class ScaledTanh:
+    """y = x + a * tanh(x * w) over rows x (n, C) and w (C,); t = tanh(x * w)
+    is a statistic kept for backward1."""
+
+    outputs = ("y", "t")
+    save = ("x", "w", "t")
+    nondiff = ("t",)
+
+    @staticmethod
+    def forward1(x: torch.Tensor, w: torch.Tensor, a: float) -> tuple[torch.Tensor, torch.Tensor]:
+        t = torch.tanh(x * w)
+        return x + a * t, t
+
+    @staticmethod
+    def fake(x, w, a):
+        return torch.empty_like(x), torch.empty_like(x)
+
+    @staticmethod
+    def backward1(x, w, t, grad_y, a):
+        BACKWARD1_CALLS[0] += 1
+        d = 1 - t * t
+        return grad_y * (1 + a * d * w), (grad_y * a * d * x).sum(0)
+
+    @staticmethod
+    def backward2(x, w, t, grad_y, a, gg_x, gg_w):
+        d = 1 - t * t
+        dd = -2 * t * d           # d(1 - tanh^2) / dz
+        u = gg_x * w + gg_w * x   # <gg, (gx, gw)> = sum grad_y * (gg_x + a * d * u)
+        dx = grad_y * a * (u * dd * w + gg_w * d)
+        dw = (grad_y * a * (u * dd * x + gg_x * d)).sum(0)
+        return dx, dw, gg_x + a * d * u
+
+
+def scaled_tanh_ref(x, w, a):
+    t = torch.tanh(x * w)
+    return x + a * t, t
+
+
+class OpBlock(nn.Module):
+    def __init__(self, width):
+        super().__init__()
+        self.lin = nn.Linear(width, width)
+        self.w1 = nn.Parameter(torch.randn(width) * 0.7)
+        self.w2 = nn.Parameter(torch.randn(width) * 0.7)
+
+    def forward(self, h, dist):
+        y1, _ = ScaledTanh(self.lin(h), self.w1, 0.7)
+        y2, _ = ScaledTanh(y1, self.w2, 0.3)
+        # (no plain op here whose backward reads y2: it would take the VJP's
+        # differentiation through both ops whatever they do)
+        return h + y2
+
+
+class OpModel(ToyModel):
+    def __init__(self, budget):
+        nn.Module.__init__(self)
+        stack = ToyStack()
+        stack.blocks = nn.ModuleList(OpBlock(8) for _ in range(len(stack.blocks)))
+        config = cg.CompileConfig(backend="eager", checkpoint=r"blocks\.\d+", memory_budget=budget)
+        self.region = cg.compile(stack, config=config)
+
+
+def test_custom_op_kernels_match_reference():
+    gen = torch.Generator().manual_seed(0)
+    args = (torch.randn(5, 4, generator=gen, dtype=F64), torch.randn(4, generator=gen, dtype=F64), 0.7)
+    errors = check_op(ScaledTanh, scaled_tanh_ref, args)
+    assert max(errors.values()) < 1e-10, errors
+
+
+@pytest.mark.parametrize("budget", [0.5, 0.25])
+def test_custom_op_deferred_backward_matches_eager(budget):
+    torch.manual_seed(0)
+    model = OpModel(budget).to(F64)
+    errors = check_create_graph(model, toy_data())
+    bad = {k: v for k, v in errors.items() if v > 1e-10}
+    assert not bad, errors
+
+
+def test_custom_op_backward1_runs_once_less_per_block():
+    def calls(budget):
+        torch.manual_seed(0)
+        model = OpModel(budget).to(F64)
+        out, grads = cg.create_graph(model, toy_data(seed=1))
+        BACKWARD1_CALLS[0] = 0
+        (out["energy"].sum() + grads["pos"].square().sum()).backward()
+        return BACKWARD1_CALLS[0]
+
+    depth = len(ToyStack().blocks)
+    assert calls(0.25) == 5 * depth
+    assert calls(0.5) == 4 * depth
