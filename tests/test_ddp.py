@@ -9,7 +9,9 @@ test asserts (tests/test_ddp.py there) -- for one bucket and for buckets of a
 single parameter, and with small buckets some all-reduces must have started
 before backward returned. A second case has one rank raise before its first
 collective and checks the other fails with an error instead of waiting
-forever.
+forever. A third case checkpoints the layers (memory budget 0.5) with ops that
+take part in the deferred first-order backward: each parameter's gradient
+still completes once, so the same buckets and averages follow.
 """
 
 from __future__ import annotations
@@ -26,6 +28,7 @@ import torch.multiprocessing as mp
 from torch import nn
 
 import create_graph_b200 as cg
+from create_graph_b200.checkpoint import cut_forward_tensor, deferral_slot, deferred_cotangent, plus
 from create_graph_b200.ddp import FlatGradients
 
 pytestmark = [pytest.mark.ddp, pytest.mark.slow]
@@ -49,6 +52,46 @@ class Net(nn.Module):
         return {"energy": self.region(vec, vec.norm(dim=-1))}
 
 
+class TanhResidual(torch.autograd.Function):
+    """x + tanh(x @ w.T), its backward from torch ops, with the deferral hooks."""
+
+    @staticmethod
+    def forward(ctx, x, w):
+        ctx.op = deferral_slot()
+        ctx.save_for_backward(x, w)
+        return x + torch.tanh(x @ w.t())
+
+    @staticmethod
+    def backward(ctx, g):
+        x, w = ctx.saved_tensors
+        c = deferred_cotangent(ctx, "x")
+        x = cut_forward_tensor(ctx, "x", x)
+        t = torch.tanh(x @ w.t())
+        u = g * (1 - t * t)
+        return plus(g + u @ w, c), u.t() @ x
+
+
+class DeferBlock(nn.Module):
+    def __init__(self, width):
+        super().__init__()
+        self.w1 = nn.Parameter(torch.randn(width, width) / width**0.5)
+        self.w2 = nn.Parameter(torch.randn(width, width) / width**0.5)
+
+    def forward(self, h):
+        return TanhResidual.apply(TanhResidual.apply(h, self.w1), self.w2)
+
+
+class CheckpointedNet(Net):
+    def __init__(self):
+        super().__init__()
+        self.layers = nn.ModuleList(DeferBlock(32) for _ in range(3))
+        config = cg.CompileConfig(backend="eager", checkpoint=r"layers\.\d+", memory_budget=0.5)
+        self.region = cg.compile(self._energy, config=config)
+
+
+MODELS = {"plain": Net, "checkpointed": CheckpointedNet}
+
+
 def rank_data(rank):
     gen = torch.Generator().manual_seed(100 + rank)
     n = 9
@@ -67,12 +110,12 @@ def step(model, data, exact=False, fail=False):
     (out["energy"].sum() + grads["pos"].square().sum()).backward()
 
 
-def worker(rank, world, port, path, fail_rank, bucket_bytes):
+def worker(rank, world, port, path, fail_rank, bucket_bytes, model_name="plain"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
     torch.set_default_dtype(torch.float64)
     torch.manual_seed(0)
-    model = Net()
+    model = MODELS[model_name]()
     grads = FlatGradients(model.parameters(), world, bucket_bytes=bucket_bytes)
     try:
         for _ in range(2):  # a second step reuses the hooks and buckets
@@ -108,11 +151,11 @@ def free_port() -> int:
         return s.getsockname()[1]
 
 
-def expected_flat():
+def expected_flat(model_name="plain"):
     torch.set_default_dtype(torch.float64)
     try:
         torch.manual_seed(0)
-        model = Net()
+        model = MODELS[model_name]()
         total = None
         for rank in range(2):
             model.zero_grad()
@@ -145,3 +188,14 @@ def test_failing_rank_ends_the_other_with_an_error():
         assert "injected failure" in torch.load(f"{path}.1")["error"]
         # rank 0 is left alone in the collective: gloo ends it with an error, not a hang
         assert os.path.exists(f"{path}.0")
+
+
+def test_checkpointed_layers_with_deferred_backward():
+    want = expected_flat("checkpointed")
+    with tempfile.TemporaryDirectory() as tmp:
+        path = os.path.join(tmp, "out.pt")
+        mp.spawn(worker, args=(2, free_port(), path, -1, 1, "checkpointed"), nprocs=2, join=True)
+        got = torch.load(path)
+    assert got["identical"] and got["gaps_zero"] and got["aligned"]
+    assert ((got["flat"] - want).norm() / want.norm()).item() < 1e-10
+    assert got["buckets"] == 10 and got["in_backward"] >= 5
