@@ -1,7 +1,9 @@
 """
 The deferred first-order backward of checkpointed blocks, on the CPU in
 float64 (host logic only). A toy fused op uses the same hooks as the package's
-fused ops (_op_slot / _cut / _deferred): while the parameter backward
+fused ops (checkpoint.deferral_slot / cut_forward_tensor / deferred_cotangent,
+which create_graph_b200.nn names _op_slot / _cut / _deferred), and a
+cg.custom_op operator takes part by itself: while the parameter backward
 differentiates a block's VJP, the op's backward reads its forward tensors
 through leaves, and the cotangents they receive are added where the block's
 own backward passes them. Results must equal eager create_graph at 1e-10 with
